@@ -1,0 +1,431 @@
+"""Benchmark of the quantization hot path on B200 (one JSON line on rank 0).
+
+Headline workload ("C2"): quantize float32 weights
+[11008, 4096] ~ N(0, 0.02^2) three ways per step, through the reference's op
+API (torch.ops.quantized_ops):
+  * NF4 per-group 64: quantize_mx(w, lut4 index table, [-1], 64, 1.0)
+    (block absmax scale computed in the same pass),
+  * posit8_1 per-tensor: quantize(w, amax/4096, qmap=posit8_1),
+  * int8 per-output-channel: quantize(w, row_amax/127, qmap=int8).
+metric = algorithmic GB/s over the three (8.0625 + 8 + 8 bytes per element),
+whole job (all ranks).  Multi-GPU: every rank quantizes its own weight matrix
+(weak scaling, no collective on the data path).
+
+Secondary results in the same line ("secondary"): C1 NVFP4 round trip GB/s
+and C3 MXFP8 quantized-linear TFLOP/s on one GPU.
+
+--impl reference times the reference algorithm's CPU restatement (the oracle
+port under oracle/) on this host's cores, on a bounded row sample of the
+same workload.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "voyager-compiler_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+ROWS, COLS = 11008, 4096
+BYTES_PER_ELEM = {"nf4_g64": 4 + 4 + 4.0 / 64, "posit8_tensor": 8.0, "int8_channel": 8.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle port, threaded over row chunks
+# ---------------------------------------------------------------------------
+def cpu_step(w_rows, tables, threads):
+    """One C2 step on a row sample with the oracle (all host threads)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    import oracle
+
+    idx_tab, posit_tab, int8_tab = tables
+    sp = np.array(np.abs(w_rows).max() / np.float32(4096.0), dtype=np.float32).reshape(())
+    si = (np.abs(w_rows).max(axis=1, keepdims=True) / np.float32(127.0)).astype(np.float32)
+    n = w_rows.shape[0]
+    bounds = np.linspace(0, n, threads + 1).astype(int)
+
+    def work(i):
+        lo, hi = bounds[i], bounds[i + 1]
+        oracle.quantize_mx(w_rows[lo:hi], idx_tab, [-1], 64, 1.0)
+        oracle.quantize(w_rows[lo:hi], sp, qmap=posit_tab)
+        oracle.quantize(w_rows[lo:hi], si[lo:hi], qmap=int8_tab)
+
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(work, range(threads)))
+
+
+def cpu_tables():
+    from oracle.numerics import index_table, quantization_map
+
+    return index_table(quantization_map("lut4")), quantization_map("posit8_1"), quantization_map("int8")
+
+
+def bytes_per_row():
+    return COLS * sum(BYTES_PER_ELEM.values())
+
+
+def cpu_baseline(sample_rows=1024, reps=3):
+    from voyager_b200 import synth
+
+    threads = os.cpu_count() or 1
+    w = synth.c2_weight()[:sample_rows]
+    tabs = cpu_tables()
+    cpu_step(w, tabs, threads)  # warm
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        cpu_step(w, tabs, threads)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(sample_rows * bytes_per_row() / dt / 1e9, 3), "unit": "GB/s",
+            "cores": threads, "kind": "port",
+            "sample": f"{sample_rows} of {ROWS} rows of the C2 weight, 3 quantizations, "
+                      f"mean of {reps} reps"}
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from voyager_b200 import synth
+
+    threads = os.cpu_count() or 1
+    sample_rows = 768
+    w_full = synth.c2_weight()
+    tabs = cpu_tables()
+    for i in range(args.warmup):
+        cpu_step(w_full[:sample_rows], tabs, threads)
+    times = []
+    for i in range(args.steps):
+        lo = (i * sample_rows) % (ROWS - sample_rows)
+        t0 = time.perf_counter()
+        cpu_step(w_full[lo:lo + sample_rows], tabs, threads)
+        times.append(time.perf_counter() - t0)
+    dt = sum(times) / len(times)
+    val = sample_rows * bytes_per_row() / dt / 1e9
+    line = {
+        "impl": "reference", "metric": "C2 weight quantize throughput (NF4 g64 + posit8 "
+        "per-tensor + int8 per-channel)", "value": round(val, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": "C2 fp32 [11008,4096] N(0,0.02): NF4 g64 / posit8_1 "
+                   "per-tensor / int8 per-channel", "sample_rows_per_step": sample_rows},
+        "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": f"{sample_rows} rows per step"},
+        "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            self.path = f"/tmp/vq_clocks_{os.getpid()}.csv"
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=clocks.sm,clocks.max.sm,"
+                 "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 7:
+                continue
+            try:
+                sm.append(float(p[0]))
+                mx = float(p[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.remove(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def run_ours(args):
+    import torch
+
+    rank, world, local = dist_env()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py: needs a CUDA GPU (the CUDA path has no fallback)")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        pg = dist
+    import voyager_b200  # noqa: F401
+    from voyager_b200 import synth
+    from voyager_b200.tables import get_quantization_map, index_table
+
+    Q = torch.ops.quantized_ops
+    peaks = {}
+    pth = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pth):
+        peaks = json.load(open(pth))
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+
+    w_host = synth.c2_weight()
+    w = torch.from_numpy(w_host).to(dev)
+    idx_tab = index_table(get_quantization_map("lut4")).to(dev)
+    posit = get_quantization_map("posit8_1", dev)
+    i8 = get_quantization_map("int8", dev)
+    sp = w.abs().amax() / 4096.0
+    si = w.abs().amax(dim=1, keepdim=True) / 127.0
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        Q.quantize_mx(w, idx_tab, [-1], 64, 1.0, False)
+        Q.quantize(w, sp, qmap=posit)
+        Q.quantize(w, si, qmap=i8)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+
+    # per-kernel launch times (CUDA events on the launching stream)
+    names = list(BYTES_PER_ELEM)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            Q.quantize_mx(w, idx_tab, [-1], 64, 1.0, False)
+            ev[i][1].record(stream)
+            Q.quantize(w, sp, qmap=posit)
+            ev[i][2].record(stream)
+            Q.quantize(w, si, qmap=i8)
+            ev[i][3].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    ms = t_start.elapsed_time(t_end)
+    per = {n: [ev[i][j].elapsed_time(ev[i][j + 1]) for i in range(args.steps)]
+           for j, n in enumerate(names)}
+    if pg:
+        t = torch.tensor([ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    elems = ROWS * COLS
+    total_bytes = elems * sum(BYTES_PER_ELEM.values()) * world * args.steps
+    value = total_bytes / (ms / 1e3) / 1e9
+    mean_ms = {n: sum(v) / len(v) for n, v in per.items()}
+    dom = max(mean_ms, key=mean_ms.get)
+    achieved = elems * BYTES_PER_ELEM[dom] / (mean_ms[dom] / 1e3) / 1e9
+    kernels = {n: {"ms": round(mean_ms[n], 4),
+                   "GB/s": round(elems * BYTES_PER_ELEM[n] / (mean_ms[n] / 1e3) / 1e9, 1)}
+               for n in names}
+
+    # end-to-end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        pinned = torch.from_numpy(w_host).pin_memory()
+        outs_host = [torch.empty((ROWS, COLS), dtype=torch.float32).pin_memory() for _ in range(3)]
+        sc_host = torch.empty((ROWS, COLS // 64), dtype=torch.float32).pin_memory()
+        wd = torch.empty_like(w)
+
+        def e2e_step():
+            wd.copy_(pinned, non_blocking=True)
+            s, c = Q.quantize_mx(wd, idx_tab, [-1], 64, 1.0, False)
+            c1 = Q.quantize(wd, sp, qmap=posit)
+            c2 = Q.quantize(wd, si, qmap=i8)
+            sc_host.copy_(s, non_blocking=True)
+            outs_host[0].copy_(c, non_blocking=True)
+            outs_host[1].copy_(c1, non_blocking=True)
+            outs_host[2].copy_(c2, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        k = max(2, min(args.steps, 5))
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(k):
+            e2e_step()
+        a1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = a0.elapsed_time(a1) / k
+        if pg:
+            t = torch.tensor([e_ms], device=dev)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": round(elems * sum(BYTES_PER_ELEM.values()) * world / (e_ms / 1e3) / 1e9, 3),
+               "unit": "GB/s", "ms_per_step": round(e_ms, 3),
+               "h2d_bytes_per_step": elems * 4,
+               "d2h_bytes_per_step": elems * 4 * 3 + ROWS * (COLS // 64) * 4}
+
+    secondary = {}
+    if not args.no_secondary and rank == 0:
+        secondary = run_secondary(dev, hbm_peak, peaks)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()
+
+    if rank == 0:
+        line = {
+            "metric": "C2 weight quantize throughput (NF4 g64 + posit8 per-tensor + int8 "
+                      "per-channel), algorithmic bytes",
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded PCG64 N(0,0.02^2))",
+            "config": {"workload": "C2 fp32 [11008,4096]: NF4 g64 quantize_mx / posit8_1 "
+                                   "per-tensor / int8 per-channel quantize",
+                       "per_gpu_bytes_per_step": int(elems * sum(BYTES_PER_ELEM.values())),
+                       "l2": "inputs (180 MB) and outputs larger than the 126 MB L2",
+                       "parallelism": f"replicas x{world} (row-sharded weak scaling)"},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
+                         "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
+                         "traffic": None},
+            "kernels": kernels,
+            "clocks": clk.summary(),
+            "gpu_launches": 3 * args.steps,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "secondary": secondary,
+        }
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+def _time_ms(fn, stream, reps=10, warm=3):
+    import torch
+
+    for _ in range(warm):
+        fn()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record(stream)
+    for _ in range(reps):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def run_secondary(dev, hbm_peak, peaks):
+    import torch
+
+    from voyager_b200 import synth
+    from voyager_b200.tables import get_quantization_map
+
+    Q = torch.ops.quantized_ops
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+    # C1 NVFP4 round trip (bf16 [4096,4096], bs 16, e2m1 + e4m3 scale)
+    x = torch.from_numpy(synth.c1_input().view(np.int16)).view(torch.bfloat16).to(dev)
+    e2m1 = get_quantization_map("fp4_e2m1", dev)
+    e4m3 = get_quantization_map("fp8_e4m3", dev)
+    s, c = Q.quantize_mx(x, e2m1, [-1], 16, 6.0, False, e4m3)
+    tq = _time_ms(lambda: Q.quantize_mx(x, e2m1, [-1], 16, 6.0, False, e4m3), stream, reps=20)
+    td = _time_ms(lambda: Q.dequantize(c, s, None, [-1], 16), stream, reps=20)
+    n = x.numel()
+    out["c1_quantize_mx_GBps"] = round(n * 4.125 / (tq / 1e3) / 1e9, 1)
+    out["c1_dequantize_GBps"] = round(n * 4.125 / (td / 1e3) / 1e9, 1)
+    out["c1_quantize_mx_frac_hbm"] = round(out["c1_quantize_mx_GBps"] / hbm_peak, 3)
+    out["c1_note"] = "16.8M elems, 69 MB per launch (fits L2: warm-L2 figure)"
+    # C3 MXFP8 linear
+    try:
+        a_np, w_np = synth.c3_operands()
+        a = torch.from_numpy(a_np.view(np.int16)).view(torch.bfloat16).to(dev)
+        wq = torch.from_numpy(w_np.view(np.int16)).view(torch.bfloat16).to(dev)
+        sa, ca = Q.quantize_mx(a, e4m3, [-1], 32, 448.0, True)
+        sw, cw = Q.quantize_mx(wq, e4m3, [-1], 32, 448.0, True)
+        tl = _time_ms(lambda: Q.linear_mx(ca, cw, None, input_scale=sa, weight_scale=sw,
+                                          block_size=32), stream, reps=10)
+        fl = 2 * 8192 * 4096 * 11008
+        out["c3_linear_mx_TFLOPs"] = round(fl / (tl / 1e3) / 1e12, 1)
+        from voyager_b200 import mxgemm
+
+        out["c3_path"] = "tcgen05 mxf8f6f4" if mxgemm.applies(
+            ca, cw, sa, sw, 32, None, None, "kc", "linear") else "dequant + cuBLAS bf16"
+    except Exception as e:  # report, do not hide
+        out["c3_error"] = repr(e)[:200]
+    return out
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

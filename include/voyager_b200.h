@@ -1,0 +1,176 @@
+/*
+ * voyager_b200 -- C ABI of the B200 (sm_100a) quantization numerics library.
+ *
+ * Each entry point replaces one op of the reference's `quantized_ops`
+ * torch.library (Joejoedesu/voyager-compiler,
+ * src/voyager_compiler/ops/quantized.py) on CUDA tensors.  The reference binds
+ * these ops from Python; the matching ctypes binding lives in
+ * voyager_b200/_lib.py and the torch.library registration that makes exported
+ * graphs dispatch here in voyager_b200/ops.py.
+ *
+ * Conventions
+ *   - Tensors are dense, row-major (C-contiguous) device buffers described by
+ *     vq_tensor; the caller allocates every output.  Entry points that launch
+ *     work never allocate, never synchronise the host and are ordered on the
+ *     `stream` argument (a cudaStream_t; NULL = the legacy default stream).
+ *   - bfloat16 values are carried as their 16-bit patterns.
+ *   - Every function returns a vq_status; nothing traps on the device.
+ *     vq_status_string() names a status.  Invalid shapes, dtypes and sizes are
+ *     rejected before any launch.
+ *   - Rounding is bit-exact with the reference's eager CPU ops: binary ops are
+ *     evaluated in float32 and rounded once to the result dtype (a 0-d scale
+ *     keeps its float32 value and does not promote the result), and the
+ *     element rounding is the reference's 65,536-entry bf16-indexed table,
+ *     which vq_rounder_from_table() turns into a rounder the kernels evaluate.
+ */
+#ifndef VOYAGER_B200_H_
+#define VOYAGER_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum vq_status {
+  VQ_OK = 0,
+  VQ_ERR_INVALID = 1,      /* bad argument value (sizes, block size, axes) */
+  VQ_ERR_UNSUPPORTED = 2,  /* dtype / layout combination not provided      */
+  VQ_ERR_ALIGNMENT = 3,    /* pointer or extent alignment not met          */
+  VQ_ERR_CUDA = 4,         /* a CUDA runtime call failed                   */
+  VQ_ERR_SHAPE = 5,        /* shapes do not broadcast as the op requires   */
+  VQ_ERR_NULL = 6,         /* required pointer is NULL                     */
+  VQ_ERR_TIMEOUT = 7       /* a bounded device wait gave up                */
+} vq_status;
+
+typedef enum vq_dtype {
+  VQ_BF16 = 0,
+  VQ_F32 = 1,
+  VQ_F16 = 2,
+  VQ_I64 = 3,
+  VQ_U8 = 4,
+  VQ_I32 = 5
+} vq_dtype;
+
+#define VQ_MAX_DIMS 8
+
+/* A dense row-major device tensor.  ndim == 0 is a 0-d (scalar) tensor. */
+typedef struct vq_tensor {
+  void* data;
+  int32_t dtype; /* vq_dtype */
+  int32_t ndim;
+  int64_t shape[VQ_MAX_DIMS];
+} vq_tensor;
+
+/* How a bfloat16 bit pattern maps to its table entry (bf16 bits).
+ *
+ * vq_rounder_from_table() classifies a 65,536-entry table into the cheapest
+ * exact form and verifies it against every entry:
+ *   IDENTITY   entry == input bits
+ *   MINIFLOAT  round-half-even to a minifloat with saturation
+ *              (src/voyager_compiler/quantization/dtypes/fp8.py:69-133)
+ *   INT        clamp(round-half-even(x), qmin, qmax)
+ *              (src/voyager_compiler/quantization/fake_quantize.py:67-68)
+ *   POSIT      posit<nbits,es> rounding (dtypes/posit.py:8-73)
+ *   STEP       a step function of the sortable key with <= 64 breakpoints
+ *              (NormalFloat / codebook index tables)
+ *   TABLE      anything else: a gather from the device copy in `table`.   */
+typedef enum vq_rounder_kind {
+  VQ_R_IDENTITY = 0,
+  VQ_R_MINIFLOAT = 1,
+  VQ_R_INT = 2,
+  VQ_R_POSIT = 3,
+  VQ_R_STEP = 4,
+  VQ_R_TABLE = 5
+} vq_rounder_kind;
+
+#define VQ_STEP_MAX 64
+
+typedef struct vq_rounder {
+  int32_t kind;
+  /* MINIFLOAT */
+  int32_t ebits, mbits, is_signed, min_exp;
+  float max_norm;
+  /* INT */
+  float qmin, qmax;
+  /* POSIT */
+  int32_t nbits, es;
+  /* NaN output pattern (MINIFLOAT / INT / POSIT) */
+  uint32_t nan_bits;
+  /* STEP: keys ascending; output step_vals[j] for keys in
+   * [step_keys[j-1], step_keys[j]) with step_keys[-1] = 0, and
+   * step_vals[nsteps] for keys >= step_keys[nsteps-1]. */
+  int32_t nsteps;
+  uint16_t step_keys[VQ_STEP_MAX];
+  uint16_t step_vals[VQ_STEP_MAX + 1];
+  uint16_t pad_;
+  /* TABLE: device pointer to 65,536 bf16 entries (caller-owned). */
+  const uint16_t* table;
+} vq_rounder;
+
+/* Name of a status code (static string). */
+const char* vq_status_string(int status);
+
+/* Library version string. */
+const char* vq_version(void);
+
+/* Classify a 65,536-entry bf16 table held in HOST memory (host-only, no
+ * CUDA).  On return `out` evaluates exactly like the table for all inputs.
+ * For VQ_R_TABLE the caller sets out->table to a device copy of the table.
+ * Replaces the reference's per-call gather `qmap[bits & 0xFFFF]`
+ * (src/voyager_compiler/ops/quantized.py:174-203). */
+int vq_rounder_from_table(const uint16_t* host_table, vq_rounder* out);
+
+/* Evaluate a rounder on the host for one bf16 pattern (test hook; the
+ * device code runs the same function). */
+uint16_t vq_rounder_eval_host(const vq_rounder* r, uint16_t bits);
+
+/* Host evaluation of the power-of-two block scale for one block amax
+ * (test hook for calculate_mx_qparam(force_scale_power_of_two=True),
+ * src/voyager_compiler/ops/quantized.py:823-840,850).  `amax_bits` is a bf16
+ * pattern when dtype == VQ_BF16, else float32 bits.  Returns the scale's bits
+ * in the same dtype. */
+uint32_t vq_pow2_scale_host(uint32_t amax_bits, int32_t dtype, int32_t floor_log2_qmax);
+
+/* quantized_ops::quantize (src/voyager_compiler/ops/quantized.py:340-397):
+ *   out = table[bf16(input / scale [+ zero_point])]
+ * `scale` / `zero_point` broadcast as the op does: with block_size > 0 a dim
+ * whose size differs from the input's repeats block_size times (expand(),
+ * quantized.py:158-171); otherwise ordinary broadcasting.  `zero_point` may
+ * be NULL.  `out` has the promoted dtype and the input's shape. */
+int vq_quantize(const vq_tensor* input, const vq_tensor* scale,
+                const vq_tensor* zero_point, int64_t block_size,
+                const vq_rounder* qmap, vq_tensor* out, void* stream);
+
+/* quantized_ops::dequantize (quantized.py:400-452):
+ *   out = output_qmap[(input_qmap[input] [- zero_point]) * scale]
+ * Either rounder may be NULL. */
+int vq_dequantize(const vq_tensor* input, const vq_tensor* scale,
+                  const vq_tensor* zero_point, int64_t block_size,
+                  const vq_rounder* input_qmap, const vq_rounder* output_qmap,
+                  vq_tensor* out, void* stream);
+
+/* quantized_ops::calculate_mx_qparam (quantized.py:787-851): one scale per
+ * block of `block_size` elements along each axis in `axes`.  `scale_qmap`
+ * may be NULL.  `floor_log2_qmax` = floor(log2(quant_max)) as the reference
+ * computes it (math.floor(math.log2(quant_max))).  `out` has the input's
+ * dtype and the blocked shape. */
+int vq_calculate_mx_qparam(const vq_tensor* input, const int64_t* axes, int32_t naxes,
+                           int64_t block_size, float quant_max, int32_t pow2,
+                           int32_t floor_log2_qmax, const vq_rounder* scale_qmap,
+                           vq_tensor* scale_out, void* stream);
+
+/* quantized_ops::quantize_mx (quantized.py:854-881): calculate_mx_qparam
+ * then quantize, fused into one pass over the input when the blocks run
+ * along the last dim.  Writes `scale_out` (blocked shape) and `codes_out`
+ * (input shape), both in the input dtype. */
+int vq_quantize_mx(const vq_tensor* input, const vq_rounder* qmap, const int64_t* axes,
+                   int32_t naxes, int64_t block_size, float quant_max, int32_t pow2,
+                   int32_t floor_log2_qmax, const vq_rounder* scale_qmap,
+                   vq_tensor* scale_out, vq_tensor* codes_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VOYAGER_B200_H_ */

@@ -1,0 +1,954 @@
+// Quantize / dequantize / microscaling kernels for sm_100a and their C ABI.
+//
+// Three kernels cover the reference's quantized_ops numerics
+// (src/voyager_compiler/ops/quantized.py):
+//
+//   k_qmx_last   quantize_mx / calculate_mx_qparam with blocks along the last
+//                dim: one pass over HBM, 16-byte loads, the block amax reduced
+//                with warp shuffles, scale and codes written in the same pass.
+//   k_qparam     calculate_mx_qparam for blocks along any one or two axes
+//                (one thread per block).
+//   k_elem       quantize / dequantize with any broadcast or expand()ed
+//                scale / zero point (16-byte loads when the inner dim allows).
+//
+// Element rounding is a vq_rounder (vq_numerics.cuh): analytic for
+// minifloat and integer tables, a shared-memory copy of the 65,536-entry bf16
+// table otherwise.  Every launch validates its arguments on the host first,
+// returns a status and never traps on the device.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "vq_numerics.cuh"
+
+namespace vq {
+
+// ---------------------------------------------------------------------------
+// Small helpers
+// ---------------------------------------------------------------------------
+constexpr int kTableBytes = 65536 * 2;
+
+// Division by a run-time invariant (Granlund-Montgomery, round-up variant):
+// q = (umulhi(n, m) + n) >> s, exact for every 32-bit n.
+struct FastDiv {
+  uint32_t d, m, s;
+  static FastDiv make(uint32_t d) {
+    FastDiv f;
+    f.d = d;
+    uint32_t l = 0;
+    while ((1ull << l) < d) ++l;
+    f.s = l;
+    f.m = (uint32_t)((((1ull << 32) * ((1ull << l) - d)) / d) + 1);
+    return f;
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    uint32_t hi = __umulhi(n, m);
+    return (uint32_t)(((uint64_t)hi + n) >> s);
+  }
+};
+
+__device__ __forceinline__ float ld_f(const void* p, int64_t i, bool bf) {
+  if (bf) return bf2f(((const uint16_t*)p)[i]);
+  return ((const float*)p)[i];
+}
+
+int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+// Element rounder specialised at compile time.  TABLE reads the shared-memory
+// copy of the bf16 table.
+template <int K>
+__device__ __forceinline__ uint32_t round_elem(const vq_rounder& r, uint32_t b,
+                                               const uint16_t* stab) {
+  if (K == VQ_R_IDENTITY) return b & 0xFFFFu;
+  if (K == VQ_R_MINIFLOAT) return round_minifloat(r, b);
+  if (K == VQ_R_INT) return round_int(r, b);
+  return stab[b & 0xFFFFu];
+}
+
+// Copy the 128 KB table into shared memory (TABLE kind only).
+template <int K>
+__device__ __forceinline__ void stage_table(const vq_rounder& r, uint16_t* stab) {
+  if (K != VQ_R_TABLE) return;
+  const uint4* src = reinterpret_cast<const uint4*>(r.table);
+  uint4* dst = reinterpret_cast<uint4*>(stab);
+  for (int i = threadIdx.x; i < kTableBytes / 16; i += blockDim.x) dst[i] = __ldg(src + i);
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// k_qmx_last: fused block scale + quantize, blocks along the last dim
+// ---------------------------------------------------------------------------
+struct QmxArgs {
+  const void* in;
+  void* codes;      // may be null (calculate_mx_qparam only)
+  void* scale;
+  uint32_t ngroups; // rows * nb
+  uint32_t C;       // row length (elements)
+  uint32_t bs;      // block size (elements)
+  FastDiv nb;       // blocks per row
+  float quant_max;
+  int32_t pow2;
+  int32_t fl2q;
+  int32_t has_sq;
+  const uint16_t* sq_table;  // device table for a TABLE-kind scale rounder
+  vq_rounder qr;             // element rounder
+  vq_rounder sq;             // scale rounder
+};
+
+template <typename TIn, int K, int TPB, int UNROLL>
+__global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxArgs a) {
+  extern __shared__ __align__(16) uint16_t smem[];
+  stage_table<K>(a.qr, smem);
+  constexpr bool BF = sizeof(TIn) == 2;
+  constexpr int VEC = 16 / sizeof(TIn);
+  const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t lane = tid % TPB;
+  constexpr uint32_t GPW = 32 / TPB;  // groups (blocks) per warp
+  // The loop bound is warp-uniform so every lane reaches the shuffles.
+  const uint32_t warp_first = (tid / 32) * GPW;
+  const uint32_t my_off = (tid % 32) / TPB;
+  const uint32_t gstride = (gridDim.x * blockDim.x) / TPB;
+
+  for (uint32_t wb = warp_first; wb < a.ngroups; wb += gstride * UNROLL) {
+    const uint32_t gb = wb + my_off;
+    uint4 v[UNROLL];
+    uint32_t row[UNROLL], col[UNROLL];
+    bool ok[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      uint32_t g = gb + u * gstride;
+      uint32_t r = a.nb.div(g);
+      uint32_t blk = g - r * a.nb.d;
+      row[u] = r;
+      col[u] = blk * a.bs + lane * VEC;
+      ok[u] = (g < a.ngroups) && (col[u] < a.C);
+      v[u] = make_uint4(0, 0, 0, 0);
+      if (ok[u]) {
+        const uint4* p = reinterpret_cast<const uint4*>(
+            reinterpret_cast<const TIn*>(a.in) + (uint64_t)r * a.C + col[u]);
+        v[u] = __ldcs(p);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      // block amax on the magnitude bits: non-negative IEEE patterns order
+      // like integers and every NaN sorts above +inf, so this max propagates
+      // NaN exactly like torch.amax.
+      uint32_t m;
+      if (BF) {
+        uint32_t w0 = v[u].x & 0x7FFF7FFFu, w1 = v[u].y & 0x7FFF7FFFu;
+        uint32_t w2 = v[u].z & 0x7FFF7FFFu, w3 = v[u].w & 0x7FFF7FFFu;
+        uint32_t w = __vmaxu2(__vmaxu2(w0, w1), __vmaxu2(w2, w3));
+        m = max(w & 0xFFFFu, w >> 16);
+      } else {
+        m = max(max(v[u].x & 0x7FFFFFFFu, v[u].y & 0x7FFFFFFFu),
+                max(v[u].z & 0x7FFFFFFFu, v[u].w & 0x7FFFFFFFu));
+      }
+#pragma unroll
+      for (int o = TPB / 2; o >= 1; o >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, o, TPB));
+      // block scale
+      float s;
+      uint32_t sbits;
+      if (a.pow2) {
+        sbits = BF ? pow2_scale_bf16(m, a.fl2q) : pow2_scale_f32(m, a.fl2q);
+        s = BF ? bf2f(sbits) : u2f(sbits);
+      } else {
+        float amax = BF ? bf2f(m) : u2f(m);
+        s = div_scale(amax, a.quant_max, BF, a.has_sq ? &a.sq : nullptr, a.sq_table);
+        sbits = BF ? f2bf(s) : f2u(s);
+      }
+      const uint32_t g = gb + u * gstride;
+      if (g < a.ngroups && lane == 0) {
+        if (BF) reinterpret_cast<uint16_t*>(a.scale)[g] = (uint16_t)sbits;
+        else reinterpret_cast<uint32_t*>(a.scale)[g] = sbits;
+      }
+      if (a.codes == nullptr || !ok[u]) continue;
+      uint4 o;
+      if (BF) {
+        uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t lo = f2bf(fdiv_rn(bf2f(w[j] & 0xFFFFu), s));
+          uint32_t hi = f2bf(fdiv_rn(bf2f(w[j] >> 16), s));
+          lo = round_elem<K>(a.qr, lo, smem);
+          hi = round_elem<K>(a.qr, hi, smem);
+          w[j] = lo | (hi << 16);
+        }
+        o = make_uint4(w[0], w[1], w[2], w[3]);
+      } else {
+        uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t idx = f2bf(fdiv_rn(u2f(w[j]), s));
+          w[j] = round_elem<K>(a.qr, idx, smem) << 16;
+        }
+        o = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      uint4* q = reinterpret_cast<uint4*>(reinterpret_cast<TIn*>(a.codes) +
+                                          (uint64_t)row[u] * a.C + col[u]);
+      __stcs(q, o);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// k_qparam: calculate_mx_qparam over one or two blocked axes (generic)
+// ---------------------------------------------------------------------------
+struct QparamArgs {
+  const void* in;
+  void* scale;
+  int32_t is_bf16;
+  int32_t ndim;
+  int64_t nscale;
+  int64_t sshape[VQ_MAX_DIMS];   // scale (blocked) shape
+  int64_t ishape[VQ_MAX_DIMS];   // input shape
+  int64_t istride[VQ_MAX_DIMS];  // input strides (elements)
+  int32_t blocked[VQ_MAX_DIMS];  // 1 if the dim is blocked
+  int64_t bs;
+  float quant_max;
+  int32_t pow2;
+  int32_t fl2q;
+  int32_t has_sq;
+  const uint16_t* sq_table;
+  vq_rounder sq;
+};
+
+__global__ void __launch_bounds__(256) k_qparam(const __grid_constant__ QparamArgs a) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.nscale) return;
+  // coordinates of this block and the element range it covers
+  int64_t rem = i, base = 0;
+  int64_t ext[2] = {1, 1}, str[2] = {0, 0};
+  int nb = 0;
+  for (int d = a.ndim - 1; d >= 0; --d) {
+    int64_t c = rem % a.sshape[d];
+    rem /= a.sshape[d];
+    if (a.blocked[d]) {
+      int64_t lo = c * a.bs;
+      int64_t e = a.ishape[d] - lo;
+      if (e > a.bs) e = a.bs;
+      base += lo * a.istride[d];
+      if (nb < 2) {
+        ext[nb] = e;
+        str[nb] = a.istride[d];
+      }
+      ++nb;
+    } else {
+      base += c * a.istride[d];
+    }
+  }
+  uint32_t m = 0;
+  for (int64_t p = 0; p < ext[0]; ++p) {
+    for (int64_t q = 0; q < ext[1]; ++q) {
+      int64_t off = base + p * str[0] + q * str[1];
+      uint32_t bits = a.is_bf16 ? (uint32_t)((const uint16_t*)a.in)[off] & 0x7FFFu
+                                : ((const uint32_t*)a.in)[off] & 0x7FFFFFFFu;
+      m = max(m, bits);
+    }
+  }
+  uint32_t sbits;
+  if (a.pow2) {
+    sbits = a.is_bf16 ? pow2_scale_bf16(m, a.fl2q) : pow2_scale_f32(m, a.fl2q);
+  } else {
+    float amax = a.is_bf16 ? bf2f(m) : u2f(m);
+    float s = div_scale(amax, a.quant_max, a.is_bf16, a.has_sq ? &a.sq : nullptr, a.sq_table);
+    sbits = a.is_bf16 ? f2bf(s) : f2u(s);
+  }
+  if (a.is_bf16) ((uint16_t*)a.scale)[i] = (uint16_t)sbits;
+  else ((uint32_t*)a.scale)[i] = sbits;
+}
+
+// ---------------------------------------------------------------------------
+// k_elem: quantize / dequantize with broadcast or expand()ed operands
+// ---------------------------------------------------------------------------
+constexpr int kElemDims = 4;
+
+struct OperandMap {  // offset = sum_d (i_d / div_d) * str_d
+  const void* ptr;
+  int32_t is_bf16;
+  int32_t uniform_vec;  // scale constant across one vector
+  FastDiv div[kElemDims];
+  int64_t str[kElemDims];
+};
+
+struct ElemArgs {
+  const void* in;
+  void* out;
+  uint32_t nvec;  // vectors in this launch
+  uint32_t vec;   // elements per vector
+  FastDiv D[kElemDims];  // collapsed output dims (D[3] innermost)
+  OperandMap scale, zp;
+  int32_t has_zp;
+  // rounding of intermediates to bf16 (result dtypes of each binary op)
+  int32_t r1_bf16, r2_bf16;
+  // dequantize only
+  int32_t has_inq, has_outq;
+  const uint16_t* inq_table;
+  const uint16_t* outq_table;
+  vq_rounder inq, outq;
+  vq_rounder qr;  // quantize element rounder
+};
+
+__device__ __forceinline__ int64_t op_offset(const OperandMap& m, const uint32_t* c) {
+  int64_t off = 0;
+#pragma unroll
+  for (int d = 0; d < kElemDims; ++d) off += (int64_t)m.div[d].div(c[d]) * m.str[d];
+  return off;
+}
+
+template <bool DEQ, int K>
+__device__ __forceinline__ uint32_t elem_op(const ElemArgs& a, float x, uint32_t xbits_bf,
+                                            bool x_is_bf, float s, float z,
+                                            const uint16_t* stab, float* outf) {
+  if (!DEQ) {
+    float t = fdiv_rn(x, s);
+    if (a.r1_bf16) t = round_bf(t);
+    if (a.has_zp) {
+      t = fadd_rn(t, z);
+      if (a.r2_bf16) t = round_bf(t);
+    }
+    uint32_t code = round_elem<K>(a.qr, f2bf(t), stab);
+    *outf = bf2f(code);
+    return code;
+  } else {
+    float v = x;
+    if (a.has_inq) {
+      uint32_t idx = x_is_bf ? xbits_bf : f2bf(x);
+      v = bf2f(round_any(a.inq, idx, a.inq_table));
+    }
+    if (a.has_zp) {
+      v = fsub_rn(v, z);
+      if (a.r1_bf16) v = round_bf(v);
+    }
+    v = fmul_rn(v, s);
+    if (a.r2_bf16) v = round_bf(v);
+    if (a.has_outq) v = bf2f(round_any(a.outq, f2bf(v), a.outq_table));
+    *outf = v;
+    return f2bf(v);
+  }
+}
+
+template <typename TIn, typename TOut, bool DEQ, int K, int VEC>
+__global__ void __launch_bounds__(1024) k_elem(const __grid_constant__ ElemArgs a) {
+  extern __shared__ __align__(16) uint16_t smem[];
+  if (!DEQ) stage_table<K>(a.qr, smem);
+  constexpr bool IN_BF = sizeof(TIn) == 2;
+  constexpr bool OUT_BF = sizeof(TOut) == 2;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t v = blockIdx.x * blockDim.x + threadIdx.x; v < a.nvec; v += stride) {
+    // coordinates of the vector's first element
+    uint32_t e = v * VEC;
+    uint32_t c[kElemDims];
+    uint32_t q3 = a.D[3].div(e);
+    c[3] = e - q3 * a.D[3].d;
+    uint32_t q2 = a.D[2].div(q3);
+    c[2] = q3 - q2 * a.D[2].d;
+    uint32_t q1 = a.D[1].div(q2);
+    c[1] = q2 - q1 * a.D[1].d;
+    c[0] = q1;
+    const uint64_t base = (uint64_t)v * VEC;
+    TIn xin[VEC];
+    if (VEC * sizeof(TIn) == 16) {
+      *reinterpret_cast<uint4*>(xin) = __ldcs(reinterpret_cast<const uint4*>(
+          reinterpret_cast<const TIn*>(a.in) + base));
+    } else if (VEC * sizeof(TIn) == 8) {
+      *reinterpret_cast<uint2*>(xin) =
+          *reinterpret_cast<const uint2*>(reinterpret_cast<const TIn*>(a.in) + base);
+    } else {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) xin[j] = reinterpret_cast<const TIn*>(a.in)[base + j];
+    }
+    float s = 0.f, z = 0.f;
+    if (a.scale.uniform_vec) s = ld_f(a.scale.ptr, op_offset(a.scale, c), a.scale.is_bf16);
+    if (a.has_zp && a.zp.uniform_vec) z = ld_f(a.zp.ptr, op_offset(a.zp, c), a.zp.is_bf16);
+    TOut res[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      if (!a.scale.uniform_vec || (a.has_zp && !a.zp.uniform_vec)) {
+        uint32_t cj[kElemDims] = {c[0], c[1], c[2], c[3] + j};
+        if (!a.scale.uniform_vec) s = ld_f(a.scale.ptr, op_offset(a.scale, cj), a.scale.is_bf16);
+        if (a.has_zp && !a.zp.uniform_vec) z = ld_f(a.zp.ptr, op_offset(a.zp, cj), a.zp.is_bf16);
+      }
+      uint32_t xb;
+      float x;
+      if (IN_BF) {
+        xb = (uint32_t)(*reinterpret_cast<const uint16_t*>(&xin[j]));
+        x = bf2f(xb);
+      } else {
+        x = *reinterpret_cast<const float*>(&xin[j]);
+        xb = 0;
+      }
+      float of;
+      uint32_t ob = elem_op<DEQ, K>(a, x, xb, IN_BF, s, z, smem, &of);
+      if (OUT_BF) *reinterpret_cast<uint16_t*>(&res[j]) = (uint16_t)ob;
+      else *reinterpret_cast<float*>(&res[j]) = of;
+    }
+    TOut* op = reinterpret_cast<TOut*>(a.out) + base;
+    if (VEC * sizeof(TOut) == 16) {
+      __stcs(reinterpret_cast<uint4*>(op), *reinterpret_cast<uint4*>(res));
+    } else if (VEC * sizeof(TOut) == 32) {
+      __stcs(reinterpret_cast<uint4*>(op), reinterpret_cast<uint4*>(res)[0]);
+      __stcs(reinterpret_cast<uint4*>(op) + 1, reinterpret_cast<uint4*>(res)[1]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) op[j] = res[j];
+    }
+  }
+}
+
+}  // namespace vq
+
+// ===========================================================================
+// Host side: validation, broadcast plans, launches
+// ===========================================================================
+using namespace vq;
+
+namespace {
+
+bool is_float_dtype(int d) { return d == VQ_BF16 || d == VQ_F32; }
+int64_t numel(const vq_tensor& t) {
+  int64_t n = 1;
+  for (int i = 0; i < t.ndim; ++i) n *= t.shape[i];
+  return n;
+}
+size_t esize(int d) { return d == VQ_BF16 ? 2 : 4; }
+
+// torch's result dtype for a binary op on float operands: a 0-d operand
+// does not promote a dimensioned one.
+int promote(int da, int na, int db, int nb) {
+  if (nb == 0 && na > 0) return da;
+  if (na == 0 && nb > 0) return db;
+  return (da == VQ_F32 || db == VQ_F32) ? VQ_F32 : VQ_BF16;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? VQ_OK : VQ_ERR_CUDA; }
+
+// Rounders whose element form is the shared-memory table.
+int elem_kind(const vq_rounder* r) {
+  if (r == nullptr) return VQ_R_IDENTITY;
+  if (r->kind == VQ_R_IDENTITY || r->kind == VQ_R_MINIFLOAT || r->kind == VQ_R_INT)
+    return r->kind;
+  return VQ_R_TABLE;
+}
+
+int check_rounder(const vq_rounder* r) {
+  if (r == nullptr) return VQ_OK;
+  if (r->kind < VQ_R_IDENTITY || r->kind > VQ_R_TABLE) return VQ_ERR_INVALID;
+  if ((r->kind == VQ_R_TABLE || r->kind == VQ_R_POSIT || r->kind == VQ_R_STEP) &&
+      r->table == nullptr)
+    return VQ_ERR_NULL;
+  if (r->kind == VQ_R_TABLE && !aligned16(r->table)) return VQ_ERR_ALIGNMENT;
+  if (r->kind == VQ_R_STEP && (r->nsteps < 0 || r->nsteps > VQ_STEP_MAX)) return VQ_ERR_INVALID;
+  return VQ_OK;
+}
+
+// Per-dim map of an operand broadcast against an input shape, following
+// expand() (quantized.py:158-171) when block_size > 0.
+struct DimMap {
+  int64_t div, str;
+};
+
+int operand_map(const vq_tensor& x, const vq_tensor& s, int64_t bs, DimMap* out) {
+  const int n = x.ndim;
+  if (s.ndim > n) return VQ_ERR_SHAPE;
+  int64_t sshape[VQ_MAX_DIMS], sstride[VQ_MAX_DIMS];
+  const int pad = n - s.ndim;
+  for (int d = 0; d < n; ++d) sshape[d] = d < pad ? 1 : s.shape[d - pad];
+  int64_t st = 1;
+  for (int d = n - 1; d >= 0; --d) {
+    sstride[d] = st;
+    st *= sshape[d];
+  }
+  for (int d = 0; d < n; ++d) {
+    const int64_t X = x.shape[d], S = sshape[d];
+    if (S == X) {
+      out[d] = {1, S == 1 ? 0 : sstride[d]};
+    } else if (bs > 0) {
+      if (S * bs < X) return VQ_ERR_SHAPE;  // repeat_interleave cannot reach X
+      out[d] = {bs, S == 1 ? 0 : sstride[d]};
+    } else if (S == 1) {
+      out[d] = {1, 0};
+    } else {
+      return VQ_ERR_SHAPE;
+    }
+  }
+  return VQ_OK;
+}
+
+// Collapse an n-d elementwise problem (contiguous output plus up to two
+// mapped operands) to kElemDims dims.
+struct Plan {
+  int nd;
+  int64_t D[VQ_MAX_DIMS];
+  DimMap m[2][VQ_MAX_DIMS];
+};
+
+int make_plan(const vq_tensor& x, const DimMap* m0, const DimMap* m1, Plan* p) {
+  p->nd = 0;
+  for (int d = 0; d < x.ndim; ++d) {
+    if (x.shape[d] == 1) continue;  // size-1 dims index nothing
+    int k = p->nd;
+    p->D[k] = x.shape[d];
+    p->m[0][k] = m0[d];
+    p->m[1][k] = m1 ? m1[d] : DimMap{1, 0};
+    // merge with the previous dim when every operand is contiguous across it
+    if (k > 0) {
+      bool ok = true;
+      for (int o = 0; o < 2; ++o) {
+        const DimMap& a = p->m[o][k - 1];
+        const DimMap& b = p->m[o][k];
+        if (a.div != 1 || b.div != 1) ok = false;
+        else if (!((a.str == 0 && b.str == 0) || a.str == b.str * p->D[k])) ok = false;
+      }
+      if (ok) {
+        p->D[k - 1] *= p->D[k];
+        for (int o = 0; o < 2; ++o) p->m[o][k - 1] = p->m[o][k];
+        continue;
+      }
+    }
+    p->nd++;
+  }
+  if (p->nd == 0) {  // a single element
+    p->nd = 1;
+    p->D[0] = 1;
+    p->m[0][0] = {1, 0};
+    p->m[1][0] = {1, 0};
+  }
+  if (p->nd > kElemDims) return VQ_ERR_UNSUPPORTED;
+  // right-align into kElemDims dims
+  const int sh = kElemDims - p->nd;
+  for (int k = kElemDims - 1; k >= 0; --k) {
+    if (k >= sh) {
+      p->D[k] = p->D[k - sh];
+      p->m[0][k] = p->m[0][k - sh];
+      p->m[1][k] = p->m[1][k - sh];
+    } else {
+      p->D[k] = 1;
+      p->m[0][k] = {1, 0};
+      p->m[1][k] = {1, 0};
+    }
+  }
+  p->nd = kElemDims;
+  return VQ_OK;
+}
+
+template <typename TIn, typename TOut, bool DEQ, int K, int VEC>
+int launch_elem(ElemArgs& a, cudaStream_t st) {
+  auto kern = k_elem<TIn, TOut, DEQ, K, VEC>;
+  int smem = (!DEQ && K == VQ_R_TABLE) ? kTableBytes : 0;
+  int threads = 256;
+  int sms = num_sms();
+  int blocks;
+  if (smem) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return VQ_ERR_CUDA;
+    threads = 1024;  // one resident CTA per SM holds the table
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+    blocks = sms * std::max(per_sm, 1);
+  } else {
+    blocks = sms * 8;
+  }
+  int64_t need = ((int64_t)a.nvec + threads - 1) / threads;
+  if (need < blocks) blocks = (int)std::max<int64_t>(need, 1);
+  kern<<<blocks, threads, smem, st>>>(a);
+  return cuda_status(cudaGetLastError());
+}
+
+template <typename TIn, typename TOut, bool DEQ, int VEC>
+int dispatch_kind(ElemArgs& a, int K, cudaStream_t st) {
+  if (DEQ) return launch_elem<TIn, TOut, DEQ, VQ_R_IDENTITY, VEC>(a, st);
+  switch (K) {
+    case VQ_R_IDENTITY: return launch_elem<TIn, TOut, DEQ, VQ_R_IDENTITY, VEC>(a, st);
+    case VQ_R_MINIFLOAT: return launch_elem<TIn, TOut, DEQ, VQ_R_MINIFLOAT, VEC>(a, st);
+    case VQ_R_INT: return launch_elem<TIn, TOut, DEQ, VQ_R_INT, VEC>(a, st);
+    default: return launch_elem<TIn, TOut, DEQ, VQ_R_TABLE, VEC>(a, st);
+  }
+}
+
+template <bool DEQ>
+int dispatch_types(ElemArgs& a, int in_dt, int out_dt, int K, bool vec_ok, cudaStream_t st) {
+  if (in_dt == VQ_BF16 && out_dt == VQ_BF16)
+    return vec_ok ? dispatch_kind<uint16_t, uint16_t, DEQ, 8>(a, K, st)
+                  : dispatch_kind<uint16_t, uint16_t, DEQ, 1>(a, K, st);
+  if (in_dt == VQ_BF16 && out_dt == VQ_F32)
+    return vec_ok ? dispatch_kind<uint16_t, float, DEQ, 8>(a, K, st)
+                  : dispatch_kind<uint16_t, float, DEQ, 1>(a, K, st);
+  if (in_dt == VQ_F32 && out_dt == VQ_F32)
+    return vec_ok ? dispatch_kind<float, float, DEQ, 4>(a, K, st)
+                  : dispatch_kind<float, float, DEQ, 1>(a, K, st);
+  if (in_dt == VQ_F32 && out_dt == VQ_BF16)  // not produced by promotion
+    return VQ_ERR_UNSUPPORTED;
+  return VQ_ERR_UNSUPPORTED;
+}
+
+void fill_operand(OperandMap& om, const vq_tensor* t, const DimMap* m, int vec) {
+  om.ptr = t ? t->data : nullptr;
+  om.is_bf16 = t ? (t->dtype == VQ_BF16) : 0;
+  for (int d = 0; d < kElemDims; ++d) {
+    om.div[d] = FastDiv::make((uint32_t)m[d].div);
+    om.str[d] = m[d].str;
+  }
+  om.uniform_vec = (m[kElemDims - 1].str == 0) || (m[kElemDims - 1].div % vec == 0);
+}
+
+// Shared driver of quantize (DEQ=false) and dequantize (DEQ=true).
+template <bool DEQ>
+int run_elementwise(const vq_tensor* input, const vq_tensor* scale, const vq_tensor* zp,
+                    int64_t bs, const vq_rounder* qr, const vq_rounder* inq,
+                    const vq_rounder* outq, vq_tensor* out, void* stream) {
+  if (!input || !scale || !out) return VQ_ERR_NULL;
+  if (!is_float_dtype(input->dtype) || !is_float_dtype(scale->dtype)) return VQ_ERR_UNSUPPORTED;
+  if (zp && !is_float_dtype(zp->dtype)) return VQ_ERR_UNSUPPORTED;
+  if (input->ndim > VQ_MAX_DIMS || scale->ndim > VQ_MAX_DIMS || input->ndim < 0)
+    return VQ_ERR_INVALID;
+  int st;
+  if ((st = check_rounder(qr)) || (st = check_rounder(inq)) || (st = check_rounder(outq)))
+    return st;
+  // result dtypes of the chain of binary ops, as eager torch computes them
+  int r1, r2;
+  if (!DEQ) {
+    r1 = promote(input->dtype, input->ndim, scale->dtype, scale->ndim);  // x / s
+    r2 = zp ? promote(r1, input->ndim, zp->dtype, zp->ndim) : r1;       // + zp
+  } else {
+    r1 = zp ? promote(input->dtype, input->ndim, zp->dtype, zp->ndim) : input->dtype;
+    r2 = promote(r1, input->ndim, scale->dtype, scale->ndim);
+  }
+  if (out->dtype != r2) return VQ_ERR_INVALID;
+  if (out->ndim != input->ndim) return VQ_ERR_SHAPE;
+  for (int d = 0; d < input->ndim; ++d)
+    if (out->shape[d] != input->shape[d]) return VQ_ERR_SHAPE;
+  const int64_t n = numel(*input);
+  if (n == 0) return VQ_OK;
+  if (!input->data || !out->data || !scale->data || (zp && !zp->data)) return VQ_ERR_NULL;
+
+  DimMap ms[VQ_MAX_DIMS], mz[VQ_MAX_DIMS];
+  if ((st = operand_map(*input, *scale, bs, ms))) return st;
+  if (zp && (st = operand_map(*input, *zp, bs, mz))) return st;
+  Plan p;
+  if ((st = make_plan(*input, ms, zp ? mz : nullptr, &p))) return st;
+
+  const int in_dt = input->dtype, out_dt = r2;
+  const int vec = in_dt == VQ_BF16 ? 8 : 4;
+  bool vec_ok = (p.D[kElemDims - 1] % vec == 0) && aligned16(input->data) && aligned16(out->data);
+
+  ElemArgs a;
+  memset(&a, 0, sizeof(a));
+  a.in = input->data;
+  a.out = out->data;
+  a.has_zp = zp != nullptr;
+  // dequantize: r1 is the dtype after "- zp", r2 after "* scale";
+  // quantize: r1 after "/ scale", r2 after "+ zp".
+  a.r1_bf16 = r1 == VQ_BF16;
+  a.r2_bf16 = r2 == VQ_BF16;
+  if (qr) a.qr = *qr;
+  a.has_inq = inq != nullptr;
+  a.has_outq = outq != nullptr;
+  if (inq) {
+    a.inq = *inq;
+    a.inq_table = inq->table;
+  }
+  if (outq) {
+    a.outq = *outq;
+    a.outq_table = outq->table;
+  }
+  const int K = elem_kind(qr);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  // Launch in chunks of whole outer rows so 32-bit indexing holds.
+  const int64_t inner = p.D[1] * p.D[2] * p.D[3];
+  const int use_vec = vec_ok ? vec : 1;
+  int64_t rows_per = std::max<int64_t>(1, ((int64_t)1 << 30) / std::max<int64_t>(inner, 1));
+  if (inner > ((int64_t)1 << 30)) return VQ_ERR_UNSUPPORTED;
+  // chunk boundaries must keep the outer-dim block mapping intact
+  const int64_t od0 = std::max(p.m[0][0].div, p.m[1][0].div);
+  rows_per = std::max<int64_t>(od0, rows_per - rows_per % od0);
+  for (int64_t r0 = 0; r0 < p.D[0]; r0 += rows_per) {
+    const int64_t rows = std::min(rows_per, p.D[0] - r0);
+    const int64_t elems = rows * inner;
+    a.in = reinterpret_cast<const char*>(input->data) + r0 * inner * esize(in_dt);
+    a.out = reinterpret_cast<char*>(out->data) + r0 * inner * esize(out_dt);
+    a.nvec = (uint32_t)(elems / use_vec);
+    a.vec = use_vec;
+    a.D[0] = FastDiv::make((uint32_t)rows);
+    for (int d = 1; d < kElemDims; ++d) a.D[d] = FastDiv::make((uint32_t)p.D[d]);
+    // operand maps, shifted to this chunk's first outer row
+    DimMap sm[kElemDims], zm[kElemDims];
+    for (int d = 0; d < kElemDims; ++d) {
+      sm[d] = p.m[0][d];
+      zm[d] = p.m[1][d];
+    }
+    vq_tensor sc = *scale;
+    sc.data = (char*)scale->data + (r0 / sm[0].div) * sm[0].str * esize(scale->dtype);
+    fill_operand(a.scale, &sc, sm, use_vec);
+    if (zp) {
+      vq_tensor zc = *zp;
+      zc.data = (char*)zp->data + (r0 / zm[0].div) * zm[0].str * esize(zp->dtype);
+      fill_operand(a.zp, &zc, zm, use_vec);
+    } else {
+      fill_operand(a.zp, nullptr, zm, use_vec);
+    }
+    if ((st = dispatch_types<DEQ>(a, in_dt, out_dt, K, vec_ok, cs))) return st;
+  }
+  return VQ_OK;
+}
+
+// Normalised blocked axes (sorted, non-negative) or an error.
+int norm_axes(const vq_tensor& x, const int64_t* axes, int naxes, int* out_blocked) {
+  for (int d = 0; d < VQ_MAX_DIMS; ++d) out_blocked[d] = 0;
+  if (naxes <= 0 || !axes) return VQ_ERR_INVALID;
+  for (int i = 0; i < naxes; ++i) {
+    int64_t a = axes[i] < 0 ? axes[i] + x.ndim : axes[i];
+    if (a < 0 || a >= x.ndim) return VQ_ERR_INVALID;
+    out_blocked[a] = 1;
+  }
+  return VQ_OK;
+}
+
+int blocked_shape(const vq_tensor& x, const int* blocked, int64_t bs, vq_tensor* s) {
+  s->ndim = x.ndim;
+  for (int d = 0; d < x.ndim; ++d)
+    s->shape[d] = blocked[d] ? (x.shape[d] + bs - 1) / bs : x.shape[d];
+  return VQ_OK;
+}
+
+int qmx_last_fast_ok(const vq_tensor& x, const int* blocked, int64_t bs) {
+  if (x.ndim < 1) return 0;
+  for (int d = 0; d < x.ndim - 1; ++d)
+    if (blocked[d]) return 0;
+  if (!blocked[x.ndim - 1]) return 0;
+  const int vec = x.dtype == VQ_BF16 ? 8 : 4;
+  const int64_t C = x.shape[x.ndim - 1];
+  if (C % vec || bs % vec) return 0;
+  const int64_t nv = bs / vec;
+  if (nv > 32 || (nv & (nv - 1))) return 0;
+  if (!aligned16(x.data)) return 0;
+  const int64_t rows = numel(x) / std::max<int64_t>(C, 1);
+  const int64_t nb = (C + bs - 1) / bs;
+  if (rows * nb >= ((int64_t)1 << 31) || C >= ((int64_t)1 << 31)) return 0;
+  return (int)nv;
+}
+
+template <typename TIn, int K, int TPB>
+int launch_qmx(QmxArgs& a, cudaStream_t st) {
+  constexpr int UNROLL = 4;
+  auto kern = k_qmx_last<TIn, K, TPB, UNROLL>;
+  int smem = K == VQ_R_TABLE ? kTableBytes : 0;
+  int threads = 256, sms = num_sms(), blocks;
+  if (smem) {
+    threads = 1024;  // one resident CTA per SM holds the table
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return VQ_ERR_CUDA;
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+    blocks = sms * std::max(per_sm, 1);
+  } else {
+    blocks = sms * 8;
+  }
+  int64_t need = ((int64_t)a.ngroups * TPB + threads * UNROLL - 1) / (threads * UNROLL);
+  if (need < blocks) blocks = (int)std::max<int64_t>(need, 1);
+  kern<<<blocks, threads, smem, st>>>(a);
+  return cuda_status(cudaGetLastError());
+}
+
+template <typename TIn, int K>
+int launch_qmx_tpb(QmxArgs& a, int tpb, cudaStream_t st) {
+  switch (tpb) {
+    case 1: return launch_qmx<TIn, K, 1>(a, st);
+    case 2: return launch_qmx<TIn, K, 2>(a, st);
+    case 4: return launch_qmx<TIn, K, 4>(a, st);
+    case 8: return launch_qmx<TIn, K, 8>(a, st);
+    case 16: return launch_qmx<TIn, K, 16>(a, st);
+    default: return launch_qmx<TIn, K, 32>(a, st);
+  }
+}
+
+template <typename TIn>
+int launch_qmx_kind(QmxArgs& a, int K, int tpb, cudaStream_t st) {
+  switch (K) {
+    case VQ_R_IDENTITY: return launch_qmx_tpb<TIn, VQ_R_IDENTITY>(a, tpb, st);
+    case VQ_R_MINIFLOAT: return launch_qmx_tpb<TIn, VQ_R_MINIFLOAT>(a, tpb, st);
+    case VQ_R_INT: return launch_qmx_tpb<TIn, VQ_R_INT>(a, tpb, st);
+    default: return launch_qmx_tpb<TIn, VQ_R_TABLE>(a, tpb, st);
+  }
+}
+
+int run_qparam_generic(const vq_tensor* input, const int* blocked, int64_t bs, float qmax,
+                       int pow2, int fl2q, const vq_rounder* sq, vq_tensor* scale_out,
+                       cudaStream_t st) {
+  QparamArgs a;
+  memset(&a, 0, sizeof(a));
+  int nbl = 0;
+  for (int d = 0; d < input->ndim; ++d) nbl += blocked[d];
+  if (nbl > 2) return VQ_ERR_UNSUPPORTED;
+  a.in = input->data;
+  a.scale = scale_out->data;
+  a.is_bf16 = input->dtype == VQ_BF16;
+  a.ndim = input->ndim;
+  int64_t stride = 1;
+  for (int d = input->ndim - 1; d >= 0; --d) {
+    a.istride[d] = stride;
+    stride *= input->shape[d];
+    a.ishape[d] = input->shape[d];
+    a.sshape[d] = scale_out->shape[d];
+    a.blocked[d] = blocked[d];
+  }
+  a.nscale = numel(*scale_out);
+  a.bs = bs;
+  a.quant_max = qmax;
+  a.pow2 = pow2;
+  a.fl2q = fl2q;
+  a.has_sq = sq != nullptr;
+  if (sq) {
+    a.sq = *sq;
+    a.sq_table = sq->table;
+  }
+  if (a.nscale == 0) return VQ_OK;
+  int64_t blocks = (a.nscale + 255) / 256;
+  if (blocks > INT32_MAX) return VQ_ERR_UNSUPPORTED;
+  k_qparam<<<(unsigned)blocks, 256, 0, st>>>(a);
+  return cuda_status(cudaGetLastError());
+}
+
+int validate_mx(const vq_tensor* input, const int64_t* axes, int naxes, int64_t bs,
+                const vq_rounder* sq, vq_tensor* scale_out, int* blocked) {
+  if (!input || !scale_out) return VQ_ERR_NULL;
+  if (!is_float_dtype(input->dtype)) return VQ_ERR_UNSUPPORTED;
+  if (input->ndim < 1 || input->ndim > VQ_MAX_DIMS) return VQ_ERR_INVALID;
+  if (bs <= 0) return VQ_ERR_INVALID;
+  int st;
+  if ((st = norm_axes(*input, axes, naxes, blocked))) return st;
+  if ((st = check_rounder(sq))) return st;
+  vq_tensor want;
+  blocked_shape(*input, blocked, bs, &want);
+  if (scale_out->dtype != input->dtype) return VQ_ERR_INVALID;
+  if (scale_out->ndim != want.ndim) return VQ_ERR_SHAPE;
+  for (int d = 0; d < want.ndim; ++d)
+    if (scale_out->shape[d] != want.shape[d]) return VQ_ERR_SHAPE;
+  if (numel(*input) > 0 && (!input->data || !scale_out->data)) return VQ_ERR_NULL;
+  return VQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int vq_quantize(const vq_tensor* input, const vq_tensor* scale, const vq_tensor* zero_point,
+                int64_t block_size, const vq_rounder* qmap, vq_tensor* out, void* stream) {
+  if (!qmap) return VQ_ERR_NULL;
+  return run_elementwise<false>(input, scale, zero_point, block_size, qmap, nullptr, nullptr,
+                                out, stream);
+}
+
+int vq_dequantize(const vq_tensor* input, const vq_tensor* scale, const vq_tensor* zero_point,
+                  int64_t block_size, const vq_rounder* input_qmap,
+                  const vq_rounder* output_qmap, vq_tensor* out, void* stream) {
+  return run_elementwise<true>(input, scale, zero_point, block_size, nullptr, input_qmap,
+                               output_qmap, out, stream);
+}
+
+int vq_calculate_mx_qparam(const vq_tensor* input, const int64_t* axes, int32_t naxes,
+                           int64_t block_size, float quant_max, int32_t pow2,
+                           int32_t floor_log2_qmax, const vq_rounder* scale_qmap,
+                           vq_tensor* scale_out, void* stream) {
+  int blocked[VQ_MAX_DIMS];
+  int st = validate_mx(input, axes, naxes, block_size, scale_qmap, scale_out, blocked);
+  if (st) return st;
+  if (numel(*input) == 0) return VQ_OK;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const int nv = qmx_last_fast_ok(*input, blocked, block_size);
+  if (nv && aligned16(scale_out->data)) {
+    QmxArgs a;
+    memset(&a, 0, sizeof(a));
+    const int64_t C = input->shape[input->ndim - 1];
+    const int64_t nb = (C + block_size - 1) / block_size;
+    a.in = input->data;
+    a.codes = nullptr;
+    a.scale = scale_out->data;
+    a.C = (uint32_t)C;
+    a.bs = (uint32_t)block_size;
+    a.nb = FastDiv::make((uint32_t)nb);
+    a.ngroups = (uint32_t)(numel(*input) / C * nb);
+    a.quant_max = quant_max;
+    a.pow2 = pow2;
+    a.fl2q = floor_log2_qmax;
+    a.has_sq = scale_qmap != nullptr;
+    if (scale_qmap) {
+      a.sq = *scale_qmap;
+      a.sq_table = scale_qmap->table;
+    }
+    a.qr.kind = VQ_R_IDENTITY;
+    return input->dtype == VQ_BF16 ? launch_qmx_kind<uint16_t>(a, VQ_R_IDENTITY, nv, cs)
+                                   : launch_qmx_kind<float>(a, VQ_R_IDENTITY, nv, cs);
+  }
+  return run_qparam_generic(input, blocked, block_size, quant_max, pow2, floor_log2_qmax,
+                            scale_qmap, scale_out, cs);
+}
+
+int vq_quantize_mx(const vq_tensor* input, const vq_rounder* qmap, const int64_t* axes,
+                   int32_t naxes, int64_t block_size, float quant_max, int32_t pow2,
+                   int32_t floor_log2_qmax, const vq_rounder* scale_qmap, vq_tensor* scale_out,
+                   vq_tensor* codes_out, void* stream) {
+  if (!qmap || !codes_out) return VQ_ERR_NULL;
+  int blocked[VQ_MAX_DIMS];
+  int st = validate_mx(input, axes, naxes, block_size, scale_qmap, scale_out, blocked);
+  if (st) return st;
+  if ((st = check_rounder(qmap))) return st;
+  if (codes_out->dtype != input->dtype || codes_out->ndim != input->ndim) return VQ_ERR_SHAPE;
+  for (int d = 0; d < input->ndim; ++d)
+    if (codes_out->shape[d] != input->shape[d]) return VQ_ERR_SHAPE;
+  if (numel(*input) == 0) return VQ_OK;
+  if (!codes_out->data) return VQ_ERR_NULL;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const int nv = qmx_last_fast_ok(*input, blocked, block_size);
+  if (nv && aligned16(codes_out->data)) {
+    QmxArgs a;
+    memset(&a, 0, sizeof(a));
+    const int64_t C = input->shape[input->ndim - 1];
+    const int64_t nb = (C + block_size - 1) / block_size;
+    a.in = input->data;
+    a.codes = codes_out->data;
+    a.scale = scale_out->data;
+    a.C = (uint32_t)C;
+    a.bs = (uint32_t)block_size;
+    a.nb = FastDiv::make((uint32_t)nb);
+    a.ngroups = (uint32_t)(numel(*input) / C * nb);
+    a.quant_max = quant_max;
+    a.pow2 = pow2;
+    a.fl2q = floor_log2_qmax;
+    a.has_sq = scale_qmap != nullptr;
+    if (scale_qmap) {
+      a.sq = *scale_qmap;
+      a.sq_table = scale_qmap->table;
+    }
+    a.qr = *qmap;
+    const int K = elem_kind(qmap);
+    return input->dtype == VQ_BF16 ? launch_qmx_kind<uint16_t>(a, K, nv, cs)
+                                   : launch_qmx_kind<float>(a, K, nv, cs);
+  }
+  // generic: scales, then an expand()ed quantize
+  if ((st = run_qparam_generic(input, blocked, block_size, quant_max, pow2, floor_log2_qmax,
+                               scale_qmap, scale_out, cs)))
+    return st;
+  return run_elementwise<false>(input, scale_out, nullptr, block_size, qmap, nullptr, nullptr,
+                                codes_out, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,92 @@
+"""``linear_mx`` / ``matmul_mx`` on CUDA (``src/voyager_compiler/ops/quantized.py:522-648``).
+
+Both operands are read back through their codebook and block scale
+(``_dequantize_mx``, ``quantized.py:455-472``) and multiplied with float32
+accumulation, the result in the operands' dtype.
+
+Paths, chosen per call:
+  * MXFP8 x MXFP8 (E4M3 codes, power-of-two block-32 scales along K on both
+    operands, bf16): the tcgen05 block-scaled GEMM in ``libvoyager_b200``
+    (``voyager_b200.mxgemm``), weights packed once and cached;
+  * everything else: the operands are dequantized by this library's kernels
+    and multiplied by cuBLAS (bf16, float32 accumulate).
+The outlier CSR side-stream (``A_data`` / ``A_indices`` / ``A_indptr``) is not
+provided and raises.
+"""
+
+import threading
+import weakref
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from voyager_b200 import ops as _ops
+
+_lock = threading.Lock()
+_wcache: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+
+
+def dequantize_mx(x: torch.Tensor, scale: Optional[torch.Tensor], code: Optional[torch.Tensor],
+                  block_size: Optional[int]) -> torch.Tensor:
+    """``_dequantize_mx``: decode through ``code``, then scale by the
+    expand()ed block ``scale``; either may be absent."""
+    if code is None and scale is None:
+        return x
+    if code is not None:
+        from voyager_b200.codebook import decode_table
+
+        x = _ops.vmap(x, decode_table(code, x.dtype, x.device))
+    if scale is not None:
+        x = _ops.dequantize(x, scale, None, None, block_size)
+    return x
+
+
+def _weight_dequant(w, scale, code, bs):
+    """Dequantized weights, cached per (tensor, version) of codes and scale."""
+    key = (w._version, None if scale is None else (id(scale), scale._version),
+           None if code is None else (id(code), code._version), bs)
+    with _lock:
+        hit = _wcache.get(w)
+        if hit is not None and hit[0] == key:
+            return hit[1]
+    d = dequantize_mx(w, scale, code, bs)
+    with _lock:
+        _wcache[w] = (key, d)
+    return d
+
+
+def _no_outliers(A_data):
+    if A_data is not None:
+        raise NotImplementedError(
+            "quantized_ops on CUDA: the outlier CSR side-stream (A_data/A_indices/A_indptr) "
+            "is not provided")
+
+
+def linear_mx(input, weight, bias=None, *, input_scale=None, weight_scale=None,
+              block_size=None, input_code=None, weight_code=None, A_data=None,
+              A_indices=None, A_indptr=None, weight_layout="kc"):
+    assert weight_layout in ("kc", "ck"), weight_layout
+    _no_outliers(A_data)
+    from voyager_b200 import mxgemm
+
+    if mxgemm.applies(input, weight, input_scale, weight_scale, block_size, input_code,
+                      weight_code, weight_layout, "linear"):
+        return mxgemm.linear(input, weight, bias, input_scale, weight_scale)
+    a = dequantize_mx(input, input_scale, input_code, block_size)
+    w = _weight_dequant(weight, weight_scale, weight_code, block_size)
+    if weight_layout == "ck":
+        w = w.transpose(-1, -2)
+    return F.linear(a, w, bias)
+
+
+def matmul_mx(self, other, *, input_scale=None, weight_scale=None, block_size=None,
+              input_code=None, weight_code=None, A_data=None, A_indices=None, A_indptr=None,
+              weight_layout="ck"):
+    assert weight_layout in ("kc", "ck"), weight_layout
+    _no_outliers(A_data)
+    a = dequantize_mx(self, input_scale, input_code, block_size)
+    b = dequantize_mx(other, weight_scale, weight_code, block_size)
+    if weight_layout == "kc":
+        b = b.transpose(-1, -2)
+    return torch.matmul(a, b)
