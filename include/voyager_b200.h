@@ -169,6 +169,18 @@ int vq_quantize_mx(const vq_tensor* input, const vq_rounder* qmap, const int64_t
                    int32_t floor_log2_qmax, const vq_rounder* scale_qmap,
                    vq_tensor* scale_out, vq_tensor* codes_out, void* stream);
 
+/* The per-block parameters of quantized_ops::quantize_affine
+ * (quantized.py:884-948): for blocks of `block_size` elements along the one
+ * axis in `axes` (zero-padded when ragged),
+ *   scale = (max - min) / (quant_max - quant_min), 1 where not > 0,
+ *   optionally rounded through scale_qmap (and 1 where not > 0 again),
+ *   zero_point = -min / scale + quant_min, optionally through scale_qmap.
+ * The codes are then vq_quantize(input, scale, zero_point, block_size). */
+int vq_quantize_affine_qparams(const vq_tensor* input, const int64_t* axes, int32_t naxes,
+                               int64_t block_size, float quant_min, float quant_max,
+                               const vq_rounder* scale_qmap, vq_tensor* scale_out,
+                               vq_tensor* zero_point_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

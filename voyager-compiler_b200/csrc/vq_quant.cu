@@ -273,6 +273,76 @@ __global__ void __launch_bounds__(256) k_qparam(const __grid_constant__ QparamAr
 }
 
 // ---------------------------------------------------------------------------
+// k_affine_qparam: quantize_affine's per-block scale and zero point
+// (quantized.py:884-948): min / max of each zero-padded block, then
+//   scale = where(s > 0, s, 1) with s = (max - min) / (qmax - qmin),
+//   optionally through scale_qmap (and where() again),
+//   zero_point = -min / scale + qmin, optionally through scale_qmap,
+// every binary op rounded to the input dtype.
+// ---------------------------------------------------------------------------
+struct AffineArgs {
+  QparamArgs q;  // shapes, blocked dims, scale rounder
+  void* zp;
+  float qmin, qmax;
+};
+
+__device__ __forceinline__ float nan_min(float a, float b) {
+  return (is_nan_f(a) || is_nan_f(b)) ? u2f(0x7FC00000u) : fminf(a, b);
+}
+__device__ __forceinline__ float nan_max(float a, float b) {
+  return (is_nan_f(a) || is_nan_f(b)) ? u2f(0x7FC00000u) : fmaxf(a, b);
+}
+
+__global__ void __launch_bounds__(256) k_affine_qparam(const __grid_constant__ AffineArgs aa) {
+  const QparamArgs& a = aa.q;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.nscale) return;
+  int64_t rem = i, base = 0, ext = 1, str = 0;
+  bool padded = false;
+  for (int d = a.ndim - 1; d >= 0; --d) {
+    int64_t c = rem % a.sshape[d];
+    rem /= a.sshape[d];
+    if (a.blocked[d]) {
+      int64_t lo = c * a.bs;
+      int64_t e = a.ishape[d] - lo;
+      // _reshape_to_blocks pads the ragged tail with zeros
+      if (e < a.bs && a.ishape[d] >= a.bs) padded = true;
+      if (a.ishape[d] % a.bs != 0 && a.ishape[d] < a.bs) padded = true;
+      if (e > a.bs) e = a.bs;
+      base += lo * a.istride[d];
+      ext = e;
+      str = a.istride[d];
+    } else {
+      base += c * a.istride[d];
+    }
+  }
+  const bool bf = a.is_bf16;
+  float lo = padded ? 0.0f : INFINITY, hi = padded ? 0.0f : -INFINITY;
+  for (int64_t p = 0; p < ext; ++p) {
+    float v = ld_f(a.in, base + p * str, bf);
+    lo = nan_min(lo, v);
+    hi = nan_max(hi, v);
+  }
+  auto rnd = [bf](float v) { return bf ? round_bf(v) : v; };
+  float s = rnd(fdiv_rn(rnd(fsub_rn(hi, lo)), fsub_rn(aa.qmax, aa.qmin)));
+  s = (s > 0.0f) ? s : 1.0f;
+  const vq_rounder* sq = a.has_sq ? &a.sq : nullptr;
+  if (sq) {
+    s = bf2f(round_any(*sq, f2bf(s), a.sq_table));
+    s = (s > 0.0f) ? s : 1.0f;
+  }
+  float z = rnd(fadd_rn(rnd(fdiv_rn(-lo, s)), aa.qmin));
+  if (sq) z = bf2f(round_any(*sq, f2bf(z), a.sq_table));
+  if (bf) {
+    ((uint16_t*)a.scale)[i] = (uint16_t)f2bf(s);
+    ((uint16_t*)aa.zp)[i] = (uint16_t)f2bf(z);
+  } else {
+    ((float*)a.scale)[i] = s;
+    ((float*)aa.zp)[i] = z;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // k_elem: quantize / dequantize with broadcast or expand()ed operands
 // ---------------------------------------------------------------------------
 constexpr int kElemDims = 4;
@@ -949,6 +1019,52 @@ int vq_quantize_mx(const vq_tensor* input, const vq_rounder* qmap, const int64_t
     return st;
   return run_elementwise<false>(input, scale_out, nullptr, block_size, qmap, nullptr, nullptr,
                                 codes_out, stream);
+}
+
+int vq_quantize_affine_qparams(const vq_tensor* input, const int64_t* axes, int32_t naxes,
+                               int64_t block_size, float quant_min, float quant_max,
+                               const vq_rounder* scale_qmap, vq_tensor* scale_out,
+                               vq_tensor* zero_point_out, void* stream) {
+  if (naxes != 1) return VQ_ERR_INVALID;
+  if (!zero_point_out) return VQ_ERR_NULL;
+  int blocked[VQ_MAX_DIMS];
+  int st = validate_mx(input, axes, naxes, block_size, scale_qmap, scale_out, blocked);
+  if (st) return st;
+  if (zero_point_out->dtype != scale_out->dtype || zero_point_out->ndim != scale_out->ndim)
+    return VQ_ERR_SHAPE;
+  for (int d = 0; d < scale_out->ndim; ++d)
+    if (zero_point_out->shape[d] != scale_out->shape[d]) return VQ_ERR_SHAPE;
+  if (numel(*input) == 0) return VQ_OK;
+  if (!zero_point_out->data) return VQ_ERR_NULL;
+  AffineArgs aa;
+  memset(&aa, 0, sizeof(aa));
+  QparamArgs& a = aa.q;
+  a.in = input->data;
+  a.scale = scale_out->data;
+  a.is_bf16 = input->dtype == VQ_BF16;
+  a.ndim = input->ndim;
+  int64_t stride = 1;
+  for (int d = input->ndim - 1; d >= 0; --d) {
+    a.istride[d] = stride;
+    stride *= input->shape[d];
+    a.ishape[d] = input->shape[d];
+    a.sshape[d] = scale_out->shape[d];
+    a.blocked[d] = blocked[d];
+  }
+  a.nscale = numel(*scale_out);
+  a.bs = block_size;
+  a.has_sq = scale_qmap != nullptr;
+  if (scale_qmap) {
+    a.sq = *scale_qmap;
+    a.sq_table = scale_qmap->table;
+  }
+  aa.zp = zero_point_out->data;
+  aa.qmin = quant_min;
+  aa.qmax = quant_max;
+  int64_t blocks = (a.nscale + 255) / 256;
+  if (blocks > INT32_MAX) return VQ_ERR_UNSUPPORTED;
+  k_affine_qparam<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(aa);
+  return cuda_status(cudaGetLastError());
 }
 
 }  // extern "C"

@@ -91,6 +91,10 @@ _SIGNATURES = {
     "vq_quantize_mx": (ctypes.c_int, [P(VqTensor), P(VqRounder), P(ctypes.c_int64), ctypes.c_int32,
                                       ctypes.c_int64, ctypes.c_float, ctypes.c_int32, ctypes.c_int32,
                                       P(VqRounder), P(VqTensor), P(VqTensor), ctypes.c_void_p]),
+    "vq_quantize_affine_qparams": (ctypes.c_int, [P(VqTensor), P(ctypes.c_int64), ctypes.c_int32,
+                                                  ctypes.c_int64, ctypes.c_float, ctypes.c_float,
+                                                  P(VqRounder), P(VqTensor), P(VqTensor),
+                                                  ctypes.c_void_p]),
 }
 
 _lib = None

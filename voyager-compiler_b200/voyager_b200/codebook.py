@@ -9,17 +9,14 @@ as every other table.  Region-grid codebooks (``[*counts, k]``) are not
 provided yet and raise.
 """
 
-import threading
-import weakref
-
 import numpy as np
 import torch
 
+from voyager_b200._cache import TensorCache
 from voyager_b200.tables import QMAP_SIZE, _bf16_bits_to_f32, _f32_to_bf16_bits
 
-_lock = threading.Lock()
-_enc: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
-_dec: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+_enc = TensorCache()
+_dec = TensorCache()
 
 
 def _as_f32(t: torch.Tensor) -> np.ndarray:
@@ -37,8 +34,7 @@ def encode_table(codebook: torch.Tensor, bounds, out_dtype: torch.dtype, device)
     index when ``bounds`` are given) of the interval the value falls in."""
     _check_1d(codebook)
     key = (codebook._version, None if bounds is None else id(bounds), out_dtype, str(device))
-    with _lock:
-        hit = _enc.get(codebook, {}).get(key)
+    hit = _enc.get(codebook, key)
     if hit is not None:
         return hit
     cb = _as_f32(codebook)
@@ -55,9 +51,7 @@ def encode_table(codebook: torch.Tensor, bounds, out_dtype: torch.dtype, device)
                 "bfloat16 values are not provided yet")
     table = torch.from_numpy(_f32_to_bf16_bits(picked).view(np.int16).copy()).view(
         torch.bfloat16).to(device)
-    with _lock:
-        _enc.setdefault(codebook, {})[key] = table
-    return table
+    return _enc.put(codebook, key, table)
 
 
 def decode_table(codebook: torch.Tensor, in_dtype: torch.dtype, device) -> torch.Tensor:
@@ -65,8 +59,7 @@ def decode_table(codebook: torch.Tensor, in_dtype: torch.dtype, device) -> torch
     integers 0..k-1 (``decode``, ``quantized.py:312-337``)."""
     _check_1d(codebook)
     key = (codebook._version, in_dtype, str(device))
-    with _lock:
-        hit = _dec.get(codebook, {}).get(key)
+    hit = _dec.get(codebook, key)
     if hit is not None:
         return hit
     cb = _as_f32(codebook)
@@ -82,6 +75,4 @@ def decode_table(codebook: torch.Tensor, in_dtype: torch.dtype, device) -> torch
     ints = _f32_to_bf16_bits(np.arange(cb.size, dtype=np.float32))
     bits[ints] = _f32_to_bf16_bits(cb)
     table = torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16).to(device)
-    with _lock:
-        _dec.setdefault(codebook, {})[key] = table
-    return table
+    return _dec.put(codebook, key, table)

@@ -14,17 +14,15 @@ The outlier CSR side-stream (``A_data`` / ``A_indices`` / ``A_indptr``) is not
 provided and raises.
 """
 
-import threading
-import weakref
 from typing import Optional
 
 import torch
 import torch.nn.functional as F
 
 from voyager_b200 import ops as _ops
+from voyager_b200._cache import TensorCache
 
-_lock = threading.Lock()
-_wcache: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+_wcache = TensorCache()
 
 
 def dequantize_mx(x: torch.Tensor, scale: Optional[torch.Tensor], code: Optional[torch.Tensor],
@@ -46,14 +44,10 @@ def _weight_dequant(w, scale, code, bs):
     """Dequantized weights, cached per (tensor, version) of codes and scale."""
     key = (w._version, None if scale is None else (id(scale), scale._version),
            None if code is None else (id(code), code._version), bs)
-    with _lock:
-        hit = _wcache.get(w)
-        if hit is not None and hit[0] == key:
-            return hit[1]
-    d = dequantize_mx(w, scale, code, bs)
-    with _lock:
-        _wcache[w] = (key, d)
-    return d
+    hit = _wcache.get(w, key)
+    if hit is not None:
+        return hit
+    return _wcache.put(w, key, dequantize_mx(w, scale, code, bs))
 
 
 def _no_outliers(A_data):

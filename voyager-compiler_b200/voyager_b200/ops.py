@@ -219,11 +219,25 @@ def quantize_mx(input: torch.Tensor, qmap: torch.Tensor, axes, block_size: int,
 def quantize_affine(input: torch.Tensor, qmap: torch.Tensor, axes, block_size: int,
                     quant_min: float, quant_max: float,
                     scale_qmap: Optional[torch.Tensor] = None):
-    """``quantized.py:884-948`` (group-wise affine) -- provided by
-    ``voyager_b200.affine`` once built; raises until then."""
-    from voyager_b200.affine import quantize_affine as qa
-
-    return qa(input, qmap, axes, block_size, quant_min, quant_max, scale_qmap)
+    """``quantized.py:884-948`` -> ``(scale, zero_point, codes)``: per-block
+    parameters from each block's min / max, then an affine quantize."""
+    assert block_size > 0
+    _check_cuda(input, "quantize_affine")
+    (axis,) = axes
+    dev = input.device
+    x = input.contiguous()
+    ax = [axis % x.dim()]
+    shape = _blocked_shape(x.shape, ax, block_size)
+    scale = torch.empty(shape, dtype=x.dtype, device=dev)
+    zp = torch.empty(shape, dtype=x.dtype, device=dev)
+    sq = rounder_for(scale_qmap, dev) if scale_qmap is not None else None
+    axes_c = (ctypes.c_int64 * 1)(ax[0])
+    st = lib().vq_quantize_affine_qparams(_ref(_vt(x)), axes_c, 1, int(block_size),
+                                          float(quant_min), float(quant_max),
+                                          sq.ref() if sq else None, _ref(_vt(scale)),
+                                          _ref(_vt(zp)), _stream(dev))
+    _lib.check(st, "quantized_ops::quantize_affine")
+    return scale, zp, quantize(x, scale, zp, ax, block_size, qmap)
 
 
 def linear_mx(input, weight, bias=None, *, input_scale=None, weight_scale=None,

@@ -22,13 +22,13 @@ import functools
 import math
 import re
 import threading
-import weakref
 from typing import NamedTuple, Optional, Tuple
 
 import numpy as np
 import torch
 
 from voyager_b200 import _lib
+from voyager_b200._cache import TensorCache
 
 QMAP_SIZE = 1 << 16
 
@@ -143,7 +143,7 @@ class Rounder:
 
 
 _lock = threading.Lock()
-_cache: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+_cache = TensorCache()
 _content_cache = {}
 
 
@@ -163,10 +163,9 @@ def rounder_for(qmap: torch.Tensor, device: torch.device) -> Rounder:
     if qmap.numel() != QMAP_SIZE or qmap.dim() != 1:
         raise ValueError("a lookup table has 65,536 entries, one per bfloat16 pattern")
     key = (qmap._version, str(device))
-    with _lock:
-        per_tensor = _cache.get(qmap)
-        if per_tensor is not None and key in per_tensor:
-            return per_tensor[key]
+    hit = _cache.get(qmap, key)
+    if hit is not None:
+        return hit
     if qmap.is_cuda and torch.cuda.is_current_stream_capturing():
         raise RuntimeError(
             "quantized_ops: a lookup table seen for the first time during CUDA-graph "
@@ -182,9 +181,7 @@ def rounder_for(qmap: torch.Tensor, device: torch.device) -> Rounder:
         rd = Rounder(c, dev, bits)
         with _lock:
             _content_cache[ck] = rd
-    with _lock:
-        _cache.setdefault(qmap, {})[key] = rd
-    return rd
+    return _cache.put(qmap, key, rd)
 
 
 # ---------------------------------------------------------------------------
