@@ -41,12 +41,14 @@ BYTES_PER_ELEM = {"nf4_g64": 4 + 4 + 4.0 / 64, "posit8_tensor": 8.0, "int8_chann
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", default=None, choices=["c1", "c2", "c3"],
+                    help="profiling aid: run only this workload's kernels, no JSON line")
     return ap.parse_args()
 
 
@@ -165,7 +167,10 @@ class Clocks:
                  "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
                  "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-lms", "20"], stdout=self.f, stderr=subprocess.DEVNULL)
+            t0 = time.time()
+            while time.time() - t0 < 5 and os.path.getsize(self.path) == 0:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
@@ -235,8 +240,10 @@ def run_ours(args):
     idx_tab = index_table(get_quantization_map("lut4")).to(dev)
     posit = get_quantization_map("posit8_1", dev)
     i8 = get_quantization_map("int8", dev)
-    sp = w.abs().amax() / 4096.0
-    si = w.abs().amax(dim=1, keepdim=True) / 127.0
+    # observer scales, divided on the host as the reference's observer does
+    sp = torch.tensor(np.abs(w_host).max() / np.float32(4096.0), dtype=torch.float32).to(dev)
+    si = torch.from_numpy((np.abs(w_host).max(axis=1, keepdims=True)
+                           / np.float32(127.0)).astype(np.float32)).to(dev)
     stream = torch.cuda.current_stream(dev)
 
     def step():
@@ -419,8 +426,51 @@ def run_secondary(dev, hbm_peak, peaks):
     return out
 
 
+def run_only(args):
+    """Run one workload's kernels (for ncu captures of committed code)."""
+    import torch
+
+    import voyager_b200  # noqa: F401
+    from voyager_b200 import synth
+    from voyager_b200.tables import get_quantization_map, index_table
+
+    Q = torch.ops.quantized_ops
+    dev = torch.device("cuda", 0)
+    if args.only == "c1":
+        x = torch.from_numpy(synth.c1_input().view(np.int16)).view(torch.bfloat16).to(dev)
+        e2m1, e4m3 = get_quantization_map("fp4_e2m1", dev), get_quantization_map("fp8_e4m3", dev)
+        for _ in range(args.warmup + args.steps):
+            s, c = Q.quantize_mx(x, e2m1, [-1], 16, 6.0, False, e4m3)
+            Q.dequantize(c, s, None, [-1], 16)
+    elif args.only == "c2":
+        w_host = synth.c2_weight()
+        w = torch.from_numpy(w_host).to(dev)
+        idx_tab = index_table(get_quantization_map("lut4")).to(dev)
+        posit, i8 = get_quantization_map("posit8_1", dev), get_quantization_map("int8", dev)
+        sp = torch.tensor(np.abs(w_host).max() / np.float32(4096.0)).to(dev)
+        si = torch.from_numpy((np.abs(w_host).max(axis=1, keepdims=True)
+                               / np.float32(127.0)).astype(np.float32)).to(dev)
+        for _ in range(args.warmup + args.steps):
+            Q.quantize_mx(w, idx_tab, [-1], 64, 1.0, False)
+            Q.quantize(w, sp, qmap=posit)
+            Q.quantize(w, si, qmap=i8)
+    else:
+        a_np, w_np = synth.c3_operands()
+        e4m3 = get_quantization_map("fp8_e4m3", dev)
+        a = torch.from_numpy(a_np.view(np.int16)).view(torch.bfloat16).to(dev)
+        wq = torch.from_numpy(w_np.view(np.int16)).view(torch.bfloat16).to(dev)
+        sa, ca = Q.quantize_mx(a, e4m3, [-1], 32, 448.0, True)
+        sw, cw = Q.quantize_mx(wq, e4m3, [-1], 32, 448.0, True)
+        for _ in range(args.warmup + args.steps):
+            Q.linear_mx(ca, cw, None, input_scale=sa, weight_scale=sw, block_size=32)
+    torch.cuda.synchronize()
+
+
 def main():
     args = parse()
+    if args.only:
+        run_only(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

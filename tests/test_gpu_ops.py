@@ -219,7 +219,9 @@ def test_full_c2_weights():
     sp = wd.abs().amax() / 4096.0
     assert sha(to_np(sp)) == S["c2_posit8_scale"]
     assert sha(to_np(Q.quantize(wd, sp, qmap=to_dev(quantization_map("posit8_1"))))) == S["c2_posit8_codes"]
-    si = wd.abs().amax(dim=1, keepdim=True) / 127.0
+    # the observer's per-channel scale, divided as the reference does on the
+    # host (torch's CUDA scalar division multiplies by a reciprocal instead)
+    si = to_dev((np.abs(w).max(axis=1, keepdims=True) / np.float32(127.0)).astype(np.float32))
     assert sha(to_np(si)) == S["c2_int8_scale"]
     assert sha(to_np(Q.quantize(wd, si, qmap=to_dev(quantization_map("int8"))))) == S["c2_int8_codes"]
 
