@@ -115,30 +115,34 @@ VQ_HD float rint_f(float x) {
 // tables: clamp to +-max_norm (abs first when unsigned), scale by the private
 // exponent max(floor(log2|x|), min_exp), round the mantissa half-to-even,
 // scale back (dtypes/fp8.py:69-133 via fake_quantize.py:70-83).
+//
+// Worked on the bf16 pattern: the magnitude is clamped as an integer
+// (non-negative bf16 patterns order like their values), the rounding is one
+// multiply by an exact power of two, rint, and the inverse multiply; the
+// result has at most mbits+1 <= 8 significant bits, so it is exactly a bf16
+// and its pattern is the top half of the float32.  A -0 input gives +0 and a
+// negative input that rounds to zero gives -0, as the table has it.
 VQ_HD uint32_t round_minifloat(const vq_rounder& r, uint32_t b) {
-  float x = bf2f(b);
-  if (is_nan_f(x)) return r.nan_bits;
-  if (!r.is_signed) x = u2f(f2u(x) & 0x7FFFFFFFu);
-  const float mx = r.max_norm;
-  if (x > mx) x = mx;
-  if (x < -mx) x = -mx;
-  uint32_t ux = f2u(x);
-  bool neg = (ux >> 31) && (ux & 0x7FFFFFFFu);  // -0 rounds like +0
-  float ax = u2f(ux & 0x7FFFFFFFu);
-  int e = (int)((f2u(ax) >> 23) & 0xFF) - 127;
-  if (e < r.min_exp) e = r.min_exp;
-  float v = rint_f(fmul_rn(ax, pow2i(r.mbits - e)));
-  float y = fmul_rn(v, pow2i(e - r.mbits));
-  if (y > mx) y = mx;
-  if (neg) y = -y;
-  return f2bf(y);
+  uint32_t mag = b & 0x7FFFu;
+  if (mag > 0x7F80u) return r.nan_bits;
+  const uint32_t sign = r.is_signed ? (b & 0x8000u) : 0u;
+  const uint32_t maxb = f2u(r.max_norm) >> 16;
+  if (mag > maxb) mag = maxb;
+  int E = (int)(mag >> 7);                 // biased exponent of |x|
+  const int Emin = r.min_exp + 127;
+  if (E < Emin) E = Emin;
+  // |x| * 2^(mbits - e) with e = E - 127, rounded to an integer, scaled back
+  const float up = u2f((uint32_t)(254 + r.mbits - E) << 23);
+  const float dn = u2f((uint32_t)(E - r.mbits) << 23);
+  const float v = rint_f(fmul_rn(u2f(mag << 16), up));
+  const uint32_t y = f2u(fmul_rn(v, dn)) >> 16;
+  return y | ((mag != 0) ? sign : 0u);
 }
 
 // clamp(round_half_even(x), qmin, qmax); a -0 result survives the clamp.
 VQ_HD uint32_t round_int(const vq_rounder& r, uint32_t b) {
-  float x = bf2f(b);
-  if (is_nan_f(x)) return r.nan_bits;
-  float y = round_bf(rint_f(x));
+  if ((b & 0x7FFFu) > 0x7F80u) return r.nan_bits;
+  float y = rint_f(bf2f(b));  // exact in bf16: |x| < 256 rounds to <= 8 bits
   if (y < r.qmin) y = r.qmin;
   if (y > r.qmax) y = r.qmax;
   return f2bf(y);
@@ -235,6 +239,39 @@ VQ_HD uint32_t round_any(const vq_rounder& r, uint32_t b, const uint16_t* tbl) {
     case VQ_R_STEP: return round_step_arrays(r.step_keys, r.step_vals, r.nsteps, b);
     default: return tbl[b & 0xFFFFu];
   }
+}
+
+// ---------------------------------------------------------------------------
+// Division whose result is rounded to bfloat16 next
+// ---------------------------------------------------------------------------
+// quantize's index is bf16(fl32(x / s)).  With r = fl32(1/s) a normal number,
+// q = fl32(x * r) lies within 3 float32 patterns of fl32(x / s) (relative
+// error <= 2^-23 + 2^-48 in the normal range, <= 1 subnormal ulp below it),
+// so both round to the same bf16 unless q's low 16 bits sit within 4 of the
+// round-to-nearest-even tie at 0x8000.  Those few quotients take the IEEE
+// division.  Overflow of x * r only happens where bf16(x / s) is infinite
+// anyway.  The result is NOT fl32(x / s) in general: callers round it to bf16
+// (or take its bf16 pattern) immediately.
+struct Divisor {
+  float s, r;
+  int fast;
+};
+
+VQ_HD Divisor make_divisor(float s) {
+  Divisor d;
+  d.s = s;
+  const uint32_t e = (f2u(s) >> 23) & 0xFF;  // |s| in [2^-126, 2^126)
+  d.fast = (e >= 1u && e <= 252u) ? 1 : 0;    // 1/s then normal too
+  d.r = d.fast ? fdiv_rn(1.0f, s) : 0.0f;
+  return d;
+}
+
+VQ_HD float div_to_bf16_domain(float x, const Divisor& d) {
+  if (d.fast) {
+    const float q = fmul_rn(x, d.r);
+    if (((f2u(q) & 0xFFFFu) - 0x7FFCu) > 8u) return q;
+  }
+  return fdiv_rn(x, d.s);
 }
 
 // ---------------------------------------------------------------------------

@@ -15,6 +15,7 @@
 // minifloat and integer tables, a shared-memory copy of the 65,536-entry bf16
 // table otherwise.  Every launch validates its arguments on the host first,
 // returns a status and never traps on the device.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -79,6 +80,15 @@ __device__ __forceinline__ uint32_t round_elem(const vq_rounder& r, uint32_t b,
   return stab[b & 0xFFFFu];
 }
 
+// bf16 pattern of a float32 (nearest-even).  The analytic rounders map every
+// NaN pattern alike, so they take the hardware conversion; a table needs the
+// exact pattern the reference indexes with (0xFFFF for NaN).
+template <int K>
+__device__ __forceinline__ uint32_t to_bf16_index(float q) {
+  if (K == VQ_R_TABLE) return f2bf(q);
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(q));
+}
+
 // Copy the 128 KB table into shared memory (TABLE kind only).
 template <int K>
 __device__ __forceinline__ void stage_table(const vq_rounder& r, uint16_t* stab) {
@@ -109,38 +119,43 @@ struct QmxArgs {
   vq_rounder sq;             // scale rounder
 };
 
-template <typename TIn, int K, int TPB, int UNROLL>
+// One block of bs = TPB * VPT * VEC elements per TPB threads; lane l holds
+// vectors l, l + TPB, ... so each warp load instruction is contiguous within
+// a block.  UNROLL blocks per thread are loaded before any is processed.
+template <typename TIn, int K, int TPB, int VPT, int UNROLL>
 __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxArgs a) {
   extern __shared__ __align__(16) uint16_t smem[];
   stage_table<K>(a.qr, smem);
   constexpr bool BF = sizeof(TIn) == 2;
   constexpr int VEC = 16 / sizeof(TIn);
+  constexpr uint32_t GPW = 32 / TPB;  // blocks per warp
   const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t lane = tid % TPB;
-  constexpr uint32_t GPW = 32 / TPB;  // groups (blocks) per warp
-  // The loop bound is warp-uniform so every lane reaches the shuffles.
+  // the loop bound is warp-uniform so every lane reaches the shuffles
   const uint32_t warp_first = (tid / 32) * GPW;
   const uint32_t my_off = (tid % 32) / TPB;
   const uint32_t gstride = (gridDim.x * blockDim.x) / TPB;
 
   for (uint32_t wb = warp_first; wb < a.ngroups; wb += gstride * UNROLL) {
-    const uint32_t gb = wb + my_off;
-    uint4 v[UNROLL];
-    uint32_t row[UNROLL], col[UNROLL];
-    bool ok[UNROLL];
+    uint4 v[UNROLL][VPT];
+    uint64_t base[UNROLL];
+    uint32_t cb[UNROLL];
+    bool live[UNROLL];
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
-      uint32_t g = gb + u * gstride;
-      uint32_t r = a.nb.div(g);
-      uint32_t blk = g - r * a.nb.d;
-      row[u] = r;
-      col[u] = blk * a.bs + lane * VEC;
-      ok[u] = (g < a.ngroups) && (col[u] < a.C);
-      v[u] = make_uint4(0, 0, 0, 0);
-      if (ok[u]) {
-        const uint4* p = reinterpret_cast<const uint4*>(
-            reinterpret_cast<const TIn*>(a.in) + (uint64_t)r * a.C + col[u]);
-        v[u] = __ldcs(p);
+      const uint32_t g = wb + my_off + u * gstride;
+      const uint32_t r = a.nb.div(g);
+      const uint32_t blk = g - r * a.nb.d;
+      cb[u] = blk * a.bs;
+      base[u] = (uint64_t)r * a.C + cb[u];
+      live[u] = g < a.ngroups;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const uint32_t col = blk * a.bs + (j * TPB + lane) * VEC;
+        v[u][j] = make_uint4(0, 0, 0, 0);
+        if (live[u] && col < a.C)
+          v[u][j] = __ldcs(reinterpret_cast<const uint4*>(
+              reinterpret_cast<const TIn*>(a.in) + base[u] + (j * TPB + lane) * VEC));
       }
     }
 #pragma unroll
@@ -148,15 +163,17 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
       // block amax on the magnitude bits: non-negative IEEE patterns order
       // like integers and every NaN sorts above +inf, so this max propagates
       // NaN exactly like torch.amax.
-      uint32_t m;
-      if (BF) {
-        uint32_t w0 = v[u].x & 0x7FFF7FFFu, w1 = v[u].y & 0x7FFF7FFFu;
-        uint32_t w2 = v[u].z & 0x7FFF7FFFu, w3 = v[u].w & 0x7FFF7FFFu;
-        uint32_t w = __vmaxu2(__vmaxu2(w0, w1), __vmaxu2(w2, w3));
-        m = max(w & 0xFFFFu, w >> 16);
-      } else {
-        m = max(max(v[u].x & 0x7FFFFFFFu, v[u].y & 0x7FFFFFFFu),
-                max(v[u].z & 0x7FFFFFFFu, v[u].w & 0x7FFFFFFFu));
+      uint32_t m = 0;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        if (BF) {
+          uint32_t w = __vmaxu2(__vmaxu2(v[u][j].x & 0x7FFF7FFFu, v[u][j].y & 0x7FFF7FFFu),
+                                __vmaxu2(v[u][j].z & 0x7FFF7FFFu, v[u][j].w & 0x7FFF7FFFu));
+          m = max(m, max(w & 0xFFFFu, w >> 16));
+        } else {
+          m = max(m, max(max(v[u][j].x & 0x7FFFFFFFu, v[u][j].y & 0x7FFFFFFFu),
+                         max(v[u][j].z & 0x7FFFFFFFu, v[u][j].w & 0x7FFFFFFFu)));
+        }
       }
 #pragma unroll
       for (int o = TPB / 2; o >= 1; o >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, o, TPB));
@@ -171,36 +188,37 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
         s = div_scale(amax, a.quant_max, BF, a.has_sq ? &a.sq : nullptr, a.sq_table);
         sbits = BF ? f2bf(s) : f2u(s);
       }
-      const uint32_t g = gb + u * gstride;
-      if (g < a.ngroups && lane == 0) {
+      const uint32_t g = wb + my_off + u * gstride;
+      if (live[u] && lane == 0) {
         if (BF) reinterpret_cast<uint16_t*>(a.scale)[g] = (uint16_t)sbits;
         else reinterpret_cast<uint32_t*>(a.scale)[g] = sbits;
       }
-      if (a.codes == nullptr || !ok[u]) continue;
-      uint4 o;
-      if (BF) {
-        uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      if (a.codes == nullptr || !live[u]) continue;
+      const Divisor dv = make_divisor(s);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t lo = f2bf(fdiv_rn(bf2f(w[j] & 0xFFFFu), s));
-          uint32_t hi = f2bf(fdiv_rn(bf2f(w[j] >> 16), s));
-          lo = round_elem<K>(a.qr, lo, smem);
-          hi = round_elem<K>(a.qr, hi, smem);
-          w[j] = lo | (hi << 16);
-        }
-        o = make_uint4(w[0], w[1], w[2], w[3]);
-      } else {
-        uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      for (int j = 0; j < VPT; ++j) {
+        const uint32_t off = (j * TPB + lane) * VEC;
+        if (cb[u] + off >= a.C) continue;
+        uint32_t w[4] = {v[u][j].x, v[u][j].y, v[u][j].z, v[u][j].w};
+        if (BF) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t idx = f2bf(fdiv_rn(u2f(w[j]), s));
-          w[j] = round_elem<K>(a.qr, idx, smem) << 16;
+          for (int k = 0; k < 4; ++k) {
+            const float q0 = div_to_bf16_domain(bf2f(w[k] & 0xFFFFu), dv);
+            const float q1 = div_to_bf16_domain(bf2f(w[k] >> 16), dv);
+            const uint32_t lo = round_elem<K>(a.qr, to_bf16_index<K>(q0), smem);
+            const uint32_t hi = round_elem<K>(a.qr, to_bf16_index<K>(q1), smem);
+            w[k] = lo | (hi << 16);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float q = div_to_bf16_domain(u2f(w[k]), dv);
+            w[k] = round_elem<K>(a.qr, to_bf16_index<K>(q), smem) << 16;
+          }
         }
-        o = make_uint4(w[0], w[1], w[2], w[3]);
+        __stcs(reinterpret_cast<uint4*>(reinterpret_cast<TIn*>(a.codes) + base[u] + off),
+               make_uint4(w[0], w[1], w[2], w[3]));
       }
-      uint4* q = reinterpret_cast<uint4*>(reinterpret_cast<TIn*>(a.codes) +
-                                          (uint64_t)row[u] * a.C + col[u]);
-      __stcs(q, o);
     }
   }
 }
@@ -339,6 +357,163 @@ __global__ void __launch_bounds__(256) k_affine_qparam(const __grid_constant__ A
   } else {
     ((float*)a.scale)[i] = s;
     ((float*)aa.zp)[i] = z;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// k_elem2d: quantize / dequantize on a [R, C] view (the common layouts)
+// ---------------------------------------------------------------------------
+// The operand offset is (row / div_r) * str_r + (col / div_c) * str_c, with
+// the layout known at compile time:
+//   SL_SCALAR  one value (per-tensor scale),
+//   SL_ROW     constant along a row (per-channel scale, [R, 1]),
+//   SL_2D      anything else on the 2-D view (block scales along C, ...).
+// Quantize divides by a cached Divisor (one reciprocal per distinct scale);
+// the zero point, when present, is read per element through its own map.
+enum { SL_SCALAR = 0, SL_ROW = 1, SL_2D = 2 };
+
+struct Map2D {
+  const void* ptr;
+  int32_t is_bf16;
+  int32_t uniform_vec;
+  FastDiv div_r, div_c;
+  int64_t str_r, str_c;
+};
+
+struct Elem2DArgs {
+  const void* in;
+  void* out;
+  uint32_t nvec;
+  FastDiv C;
+  Map2D scale, zp;
+  int32_t has_zp;
+  int32_t r1_bf16, r2_bf16;
+  int32_t exact_div;  // x / s feeds an fp32 add: needs the IEEE quotient
+  int32_t has_inq, has_outq;
+  const uint16_t* inq_table;
+  const uint16_t* outq_table;
+  vq_rounder inq, outq;
+  vq_rounder qr;
+};
+
+__device__ __forceinline__ int64_t map_off(const Map2D& m, uint32_t row, uint32_t col) {
+  return (int64_t)m.div_r.div(row) * m.str_r + (int64_t)m.div_c.div(col) * m.str_c;
+}
+
+template <typename TIn, typename TOut, bool DEQ, int K, int VEC, int SL, int UNROLL>
+__global__ void __launch_bounds__(1024) k_elem2d(const __grid_constant__ Elem2DArgs a) {
+  extern __shared__ __align__(16) uint16_t smem[];
+  if (!DEQ) stage_table<K>(a.qr, smem);
+  constexpr bool IN_BF = sizeof(TIn) == 2;
+  constexpr bool OUT_BF = sizeof(TOut) == 2;
+  constexpr int IN_B = VEC * sizeof(TIn), OUT_B = VEC * sizeof(TOut);
+  const uint32_t stride = gridDim.x * blockDim.x;
+  int64_t cached = -1;
+  float s = 0.f;
+  Divisor dv;
+  dv.s = 1.f;
+  dv.r = 1.f;
+  dv.fast = 1;
+  if (SL == SL_SCALAR) {
+    s = ld_f(a.scale.ptr, 0, a.scale.is_bf16);
+    if (!DEQ) dv = make_divisor(s);
+  }
+  for (uint32_t v0 = blockIdx.x * blockDim.x + threadIdx.x; v0 < a.nvec; v0 += stride * UNROLL) {
+    TIn xin[UNROLL][VEC];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const uint32_t v = v0 + u * stride;
+      if (v >= a.nvec) continue;
+      const TIn* src = reinterpret_cast<const TIn*>(a.in) + (uint64_t)v * VEC;
+      if (IN_B == 16) {
+        *reinterpret_cast<uint4*>(xin[u]) = __ldcs(reinterpret_cast<const uint4*>(src));
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) xin[u][j] = src[j];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const uint32_t v = v0 + u * stride;
+      if (v >= a.nvec) continue;
+      const uint32_t e = v * VEC;
+      uint32_t row = 0, col = 0;
+      if (SL != SL_SCALAR || a.has_zp) {
+        row = a.C.div(e);
+        col = e - row * a.C.d;
+      }
+      const bool uni = SL != SL_2D || a.scale.uniform_vec;
+      if (SL != SL_SCALAR && uni) {
+        const int64_t off = map_off(a.scale, row, col);
+        if (off != cached) {
+          cached = off;
+          s = ld_f(a.scale.ptr, off, a.scale.is_bf16);
+          if (!DEQ) dv = make_divisor(s);
+        }
+      }
+      TOut res[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        if (!uni) {
+          s = ld_f(a.scale.ptr, map_off(a.scale, row, col + j), a.scale.is_bf16);
+          if (!DEQ) dv = make_divisor(s);
+        }
+        float z = 0.f;
+        if (a.has_zp) z = ld_f(a.zp.ptr, map_off(a.zp, row, col + j), a.zp.is_bf16);
+        float x;
+        uint32_t xb = 0;
+        if (IN_BF) {
+          xb = (uint32_t)(*reinterpret_cast<const uint16_t*>(&xin[u][j]));
+          x = bf2f(xb);
+        } else {
+          x = *reinterpret_cast<const float*>(&xin[u][j]);
+        }
+        uint32_t ob;
+        float of;
+        if (!DEQ) {
+          float t;
+          if (a.exact_div) {
+            t = fdiv_rn(x, s);
+            if (a.r1_bf16) t = round_bf(t);
+            t = fadd_rn(t, z);
+            if (a.r2_bf16) t = round_bf(t);
+            ob = round_elem<K>(a.qr, f2bf(t), smem);
+          } else {
+            t = div_to_bf16_domain(x, dv);
+            if (a.has_zp) {  // r1 is bf16 here: round, add, round per r2
+              t = fadd_rn(round_bf(t), z);
+              if (a.r2_bf16) t = round_bf(t);
+            }
+            ob = round_elem<K>(a.qr, to_bf16_index<K>(t), smem);
+          }
+          of = bf2f(ob);
+        } else {
+          float w = x;
+          if (a.has_inq) w = bf2f(round_any(a.inq, IN_BF ? xb : f2bf(x), a.inq_table));
+          if (a.has_zp) {
+            w = fsub_rn(w, z);
+            if (a.r1_bf16) w = round_bf(w);
+          }
+          w = fmul_rn(w, s);
+          if (a.r2_bf16) w = round_bf(w);
+          if (a.has_outq) w = bf2f(round_any(a.outq, f2bf(w), a.outq_table));
+          of = w;
+          ob = f2bf(w);
+        }
+        if (OUT_BF) *reinterpret_cast<uint16_t*>(&res[j]) = (uint16_t)ob;
+        else *reinterpret_cast<float*>(&res[j]) = of;
+      }
+      TOut* dst = reinterpret_cast<TOut*>(a.out) + (uint64_t)v * VEC;
+      if (OUT_B == 16) {
+        __stcs(reinterpret_cast<uint4*>(dst), *reinterpret_cast<uint4*>(res));
+      } else if (OUT_B == 32) {
+        __stcs(reinterpret_cast<uint4*>(dst), reinterpret_cast<uint4*>(res)[0]);
+        __stcs(reinterpret_cast<uint4*>(dst) + 1, reinterpret_cast<uint4*>(res)[1]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) dst[j] = res[j];
+      }
+    }
   }
 }
 
@@ -669,6 +844,75 @@ int dispatch_types(ElemArgs& a, int in_dt, int out_dt, int K, bool vec_ok, cudaS
   return VQ_ERR_UNSUPPORTED;
 }
 
+template <typename TIn, typename TOut, bool DEQ, int K, int VEC, int SL>
+int launch_2d(Elem2DArgs& a, cudaStream_t st) {
+  constexpr int UNROLL = 2;
+  auto kern = k_elem2d<TIn, TOut, DEQ, K, VEC, SL, UNROLL>;
+  const int smem = (!DEQ && K == VQ_R_TABLE) ? kTableBytes : 0;
+  int threads = 256, sms = num_sms(), blocks;
+  if (smem) {
+    threads = 1024;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return VQ_ERR_CUDA;
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+    blocks = sms * std::max(per_sm, 1);
+  } else {
+    blocks = sms * 8;
+  }
+  int64_t need = ((int64_t)a.nvec + (int64_t)threads * UNROLL - 1) / ((int64_t)threads * UNROLL);
+  if (need < blocks) blocks = (int)std::max<int64_t>(need, 1);
+  kern<<<blocks, threads, smem, st>>>(a);
+  return cuda_status(cudaGetLastError());
+}
+
+template <typename TIn, typename TOut, bool DEQ, int VEC, int SL>
+int dispatch_2d_kind(Elem2DArgs& a, int K, cudaStream_t st) {
+  if (DEQ) return launch_2d<TIn, TOut, DEQ, VQ_R_IDENTITY, VEC, SL>(a, st);
+  switch (K) {
+    case VQ_R_IDENTITY: return launch_2d<TIn, TOut, DEQ, VQ_R_IDENTITY, VEC, SL>(a, st);
+    case VQ_R_MINIFLOAT: return launch_2d<TIn, TOut, DEQ, VQ_R_MINIFLOAT, VEC, SL>(a, st);
+    case VQ_R_INT: return launch_2d<TIn, TOut, DEQ, VQ_R_INT, VEC, SL>(a, st);
+    default: return launch_2d<TIn, TOut, DEQ, VQ_R_TABLE, VEC, SL>(a, st);
+  }
+}
+
+template <typename TIn, typename TOut, bool DEQ, int VEC>
+int dispatch_2d_layout(Elem2DArgs& a, int K, int SL, cudaStream_t st) {
+  switch (SL) {
+    case SL_SCALAR: return dispatch_2d_kind<TIn, TOut, DEQ, VEC, SL_SCALAR>(a, K, st);
+    case SL_ROW: return dispatch_2d_kind<TIn, TOut, DEQ, VEC, SL_ROW>(a, K, st);
+    default: return dispatch_2d_kind<TIn, TOut, DEQ, VEC, SL_2D>(a, K, st);
+  }
+}
+
+template <bool DEQ>
+int dispatch_2d(Elem2DArgs& a, int in_dt, int out_dt, int K, int SL, bool vec_ok,
+                cudaStream_t st) {
+  if (in_dt == VQ_BF16 && out_dt == VQ_BF16)
+    return vec_ok ? dispatch_2d_layout<uint16_t, uint16_t, DEQ, 8>(a, K, SL, st)
+                  : dispatch_2d_layout<uint16_t, uint16_t, DEQ, 1>(a, K, SL, st);
+  if (in_dt == VQ_BF16 && out_dt == VQ_F32)
+    return vec_ok ? dispatch_2d_layout<uint16_t, float, DEQ, 8>(a, K, SL, st)
+                  : dispatch_2d_layout<uint16_t, float, DEQ, 1>(a, K, SL, st);
+  if (in_dt == VQ_F32 && out_dt == VQ_F32)
+    return vec_ok ? dispatch_2d_layout<float, float, DEQ, 4>(a, K, SL, st)
+                  : dispatch_2d_layout<float, float, DEQ, 1>(a, K, SL, st);
+  return VQ_ERR_UNSUPPORTED;
+}
+
+void fill_map2d(Map2D& m, const void* ptr, int dtype, const DimMap& r, const DimMap& c,
+                int vec) {
+  m.ptr = ptr;
+  m.is_bf16 = dtype == VQ_BF16;
+  m.div_r = FastDiv::make((uint32_t)r.div);
+  m.div_c = FastDiv::make((uint32_t)c.div);
+  m.str_r = r.str;
+  m.str_c = c.str;
+  m.uniform_vec = (c.str == 0) || (c.div % vec == 0);
+}
+
 void fill_operand(OperandMap& om, const vq_tensor* t, const DimMap* m, int vec) {
   om.ptr = t ? t->data : nullptr;
   om.is_bf16 = t ? (t->dtype == VQ_BF16) : 0;
@@ -718,6 +962,51 @@ int run_elementwise(const vq_tensor* input, const vq_tensor* scale, const vq_ten
   const int in_dt = input->dtype, out_dt = r2;
   const int vec = in_dt == VQ_BF16 ? 8 : 4;
   bool vec_ok = (p.D[kElemDims - 1] % vec == 0) && aligned16(input->data) && aligned16(out->data);
+
+  if (p.D[0] == 1 && p.D[1] == 1) {
+    // [R, C] view: the specialised kernel
+    const int64_t R = p.D[2], C = p.D[3];
+    const DimMap &sr = p.m[0][2], &sc = p.m[0][3], &zr = p.m[1][2], &zc = p.m[1][3];
+    const int SL = (sr.str == 0 && sc.str == 0) ? SL_SCALAR : (sc.str == 0 ? SL_ROW : SL_2D);
+    const int use_vec = vec_ok ? vec : 1;
+    Elem2DArgs b;
+    memset(&b, 0, sizeof(b));
+    b.has_zp = zp != nullptr;
+    b.r1_bf16 = r1 == VQ_BF16;
+    b.r2_bf16 = r2 == VQ_BF16;
+    b.exact_div = !DEQ && zp != nullptr && r1 != VQ_BF16;
+    if (qr) b.qr = *qr;
+    b.has_inq = inq != nullptr;
+    b.has_outq = outq != nullptr;
+    if (inq) {
+      b.inq = *inq;
+      b.inq_table = inq->table;
+    }
+    if (outq) {
+      b.outq = *outq;
+      b.outq_table = outq->table;
+    }
+    const int Kq = elem_kind(qr);
+    cudaStream_t cs2 = reinterpret_cast<cudaStream_t>(stream);
+    if (C > ((int64_t)1 << 30)) return VQ_ERR_UNSUPPORTED;
+    int64_t rows_per = std::max<int64_t>(1, ((int64_t)1 << 30) / C);
+    const int64_t od = std::max(sr.div, zr.div);
+    rows_per = std::max<int64_t>(od, rows_per - rows_per % od);
+    for (int64_t r0 = 0; r0 < R; r0 += rows_per) {
+      const int64_t rows = std::min(rows_per, R - r0);
+      b.in = reinterpret_cast<const char*>(input->data) + r0 * C * esize(in_dt);
+      b.out = reinterpret_cast<char*>(out->data) + r0 * C * esize(out_dt);
+      b.nvec = (uint32_t)(rows * C / use_vec);
+      b.C = FastDiv::make((uint32_t)C);
+      fill_map2d(b.scale, (const char*)scale->data + (r0 / sr.div) * sr.str * esize(scale->dtype),
+                 scale->dtype, sr, sc, use_vec);
+      if (zp)
+        fill_map2d(b.zp, (const char*)zp->data + (r0 / zr.div) * zr.str * esize(zp->dtype),
+                   zp->dtype, zr, zc, use_vec);
+      if ((st = dispatch_2d<DEQ>(b, in_dt, out_dt, Kq, SL, vec_ok, cs2))) return st;
+    }
+    return VQ_OK;
+  }
 
   ElemArgs a;
   memset(&a, 0, sizeof(a));
@@ -815,10 +1104,10 @@ int qmx_last_fast_ok(const vq_tensor& x, const int* blocked, int64_t bs) {
   return (int)nv;
 }
 
-template <typename TIn, int K, int TPB>
+template <typename TIn, int K, int TPB, int VPT>
 int launch_qmx(QmxArgs& a, cudaStream_t st) {
-  constexpr int UNROLL = 4;
-  auto kern = k_qmx_last<TIn, K, TPB, UNROLL>;
+  constexpr int UNROLL = 2;
+  auto kern = k_qmx_last<TIn, K, TPB, VPT, UNROLL>;
   int smem = K == VQ_R_TABLE ? kTableBytes : 0;
   int threads = 256, sms = num_sms(), blocks;
   if (smem) {
@@ -838,25 +1127,27 @@ int launch_qmx(QmxArgs& a, cudaStream_t st) {
   return cuda_status(cudaGetLastError());
 }
 
+// nv = vectors per block: one thread per block up to two vectors, then two
+// vectors per thread across nv/2 threads.
 template <typename TIn, int K>
-int launch_qmx_tpb(QmxArgs& a, int tpb, cudaStream_t st) {
-  switch (tpb) {
-    case 1: return launch_qmx<TIn, K, 1>(a, st);
-    case 2: return launch_qmx<TIn, K, 2>(a, st);
-    case 4: return launch_qmx<TIn, K, 4>(a, st);
-    case 8: return launch_qmx<TIn, K, 8>(a, st);
-    case 16: return launch_qmx<TIn, K, 16>(a, st);
-    default: return launch_qmx<TIn, K, 32>(a, st);
+int launch_qmx_tpb(QmxArgs& a, int nv, cudaStream_t st) {
+  switch (nv) {
+    case 1: return launch_qmx<TIn, K, 1, 1>(a, st);
+    case 2: return launch_qmx<TIn, K, 1, 2>(a, st);
+    case 4: return launch_qmx<TIn, K, 2, 2>(a, st);
+    case 8: return launch_qmx<TIn, K, 4, 2>(a, st);
+    case 16: return launch_qmx<TIn, K, 8, 2>(a, st);
+    default: return launch_qmx<TIn, K, 16, 2>(a, st);
   }
 }
 
 template <typename TIn>
-int launch_qmx_kind(QmxArgs& a, int K, int tpb, cudaStream_t st) {
+int launch_qmx_kind(QmxArgs& a, int K, int nv, cudaStream_t st) {
   switch (K) {
-    case VQ_R_IDENTITY: return launch_qmx_tpb<TIn, VQ_R_IDENTITY>(a, tpb, st);
-    case VQ_R_MINIFLOAT: return launch_qmx_tpb<TIn, VQ_R_MINIFLOAT>(a, tpb, st);
-    case VQ_R_INT: return launch_qmx_tpb<TIn, VQ_R_INT>(a, tpb, st);
-    default: return launch_qmx_tpb<TIn, VQ_R_TABLE>(a, tpb, st);
+    case VQ_R_IDENTITY: return launch_qmx_tpb<TIn, VQ_R_IDENTITY>(a, nv, st);
+    case VQ_R_MINIFLOAT: return launch_qmx_tpb<TIn, VQ_R_MINIFLOAT>(a, nv, st);
+    case VQ_R_INT: return launch_qmx_tpb<TIn, VQ_R_INT>(a, nv, st);
+    default: return launch_qmx_tpb<TIn, VQ_R_TABLE>(a, nv, st);
   }
 }
 
