@@ -266,12 +266,20 @@ VQ_HD Divisor make_divisor(float s) {
   return d;
 }
 
+// The IEEE division, kept out of line on the device so the rare slow path is
+// a real branch rather than predicated into every element.
+#if defined(__CUDACC__)
+__host__ __device__ __noinline__ float div_slow(float x, float s);
+#else
+inline float div_slow(float x, float s) { return fdiv_rn(x, s); }
+#endif
+
 VQ_HD float div_to_bf16_domain(float x, const Divisor& d) {
   if (d.fast) {
     const float q = fmul_rn(x, d.r);
     if (((f2u(q) & 0xFFFFu) - 0x7FFCu) > 8u) return q;
   }
-  return fdiv_rn(x, d.s);
+  return div_slow(x, d.s);
 }
 
 // ---------------------------------------------------------------------------

@@ -26,6 +26,27 @@
 
 namespace vq {
 
+__host__ __device__ __noinline__ float div_slow(float x, float s) { return fdiv_rn(x, s); }
+
+// Any rounder, dispatched at run time, out of line (scale rounding once per
+// block, qmaps of dequantize): keeps the switch out of the hot loops' code.
+__device__ __noinline__ uint32_t round_any_dev(const vq_rounder& r, uint32_t b,
+                                               const uint16_t* tbl) {
+  return round_any(r, b, tbl);
+}
+
+// Block scale by division (see div_scale) with the scale rounder's kind known
+// at compile time: SK 0 = none, 1 = minifloat (inline), 2 = any (out of line).
+template <int SK>
+__device__ __forceinline__ float div_scale_k(float amax, float qmax, bool is_bf16,
+                                             const vq_rounder& sq, const uint16_t* sq_table) {
+  float s = fdiv_rn(amax, qmax);
+  if (is_bf16) s = round_bf(s);
+  if (SK == 1) s = bf2f(round_minifloat(sq, f2bf(s)));
+  if (SK == 2) s = bf2f(round_any_dev(sq, f2bf(s), sq_table));
+  return (s > 0.0f) ? s : 1.0f;
+}
+
 // ---------------------------------------------------------------------------
 // Small helpers
 // ---------------------------------------------------------------------------
@@ -122,7 +143,7 @@ struct QmxArgs {
 // One block of bs = TPB * VPT * VEC elements per TPB threads; lane l holds
 // vectors l, l + TPB, ... so each warp load instruction is contiguous within
 // a block.  UNROLL blocks per thread are loaded before any is processed.
-template <typename TIn, int K, int TPB, int VPT, int UNROLL>
+template <typename TIn, int K, int SK, int TPB, int VPT, int UNROLL>
 __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxArgs a) {
   extern __shared__ __align__(16) uint16_t smem[];
   stage_table<K>(a.qr, smem);
@@ -185,7 +206,7 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
         s = BF ? bf2f(sbits) : u2f(sbits);
       } else {
         float amax = BF ? bf2f(m) : u2f(m);
-        s = div_scale(amax, a.quant_max, BF, a.has_sq ? &a.sq : nullptr, a.sq_table);
+        s = div_scale_k<SK>(amax, a.quant_max, BF, a.sq, a.sq_table);
         sbits = BF ? f2bf(s) : f2u(s);
       }
       const uint32_t g = wb + my_off + u * gstride;
@@ -346,11 +367,11 @@ __global__ void __launch_bounds__(256) k_affine_qparam(const __grid_constant__ A
   s = (s > 0.0f) ? s : 1.0f;
   const vq_rounder* sq = a.has_sq ? &a.sq : nullptr;
   if (sq) {
-    s = bf2f(round_any(*sq, f2bf(s), a.sq_table));
+    s = bf2f(round_any_dev(*sq, f2bf(s), a.sq_table));
     s = (s > 0.0f) ? s : 1.0f;
   }
   float z = rnd(fadd_rn(rnd(fdiv_rn(-lo, s)), aa.qmin));
-  if (sq) z = bf2f(round_any(*sq, f2bf(z), a.sq_table));
+  if (sq) z = bf2f(round_any_dev(*sq, f2bf(z), a.sq_table));
   if (bf) {
     ((uint16_t*)a.scale)[i] = (uint16_t)f2bf(s);
     ((uint16_t*)aa.zp)[i] = (uint16_t)f2bf(z);
@@ -400,7 +421,7 @@ __device__ __forceinline__ int64_t map_off(const Map2D& m, uint32_t row, uint32_
   return (int64_t)m.div_r.div(row) * m.str_r + (int64_t)m.div_c.div(col) * m.str_c;
 }
 
-template <typename TIn, typename TOut, bool DEQ, int K, int VEC, int SL, int UNROLL>
+template <typename TIn, typename TOut, bool DEQ, int K, int VEC, int SL, bool QM, int UNROLL>
 __global__ void __launch_bounds__(1024) k_elem2d(const __grid_constant__ Elem2DArgs a) {
   extern __shared__ __align__(16) uint16_t smem[];
   if (!DEQ) stage_table<K>(a.qr, smem);
@@ -489,14 +510,14 @@ __global__ void __launch_bounds__(1024) k_elem2d(const __grid_constant__ Elem2DA
           of = bf2f(ob);
         } else {
           float w = x;
-          if (a.has_inq) w = bf2f(round_any(a.inq, IN_BF ? xb : f2bf(x), a.inq_table));
+          if (QM && a.has_inq) w = bf2f(round_any_dev(a.inq, IN_BF ? xb : f2bf(x), a.inq_table));
           if (a.has_zp) {
             w = fsub_rn(w, z);
             if (a.r1_bf16) w = round_bf(w);
           }
           w = fmul_rn(w, s);
           if (a.r2_bf16) w = round_bf(w);
-          if (a.has_outq) w = bf2f(round_any(a.outq, f2bf(w), a.outq_table));
+          if (QM && a.has_outq) w = bf2f(round_any_dev(a.outq, f2bf(w), a.outq_table));
           of = w;
           ob = f2bf(w);
         }
@@ -573,7 +594,7 @@ __device__ __forceinline__ uint32_t elem_op(const ElemArgs& a, float x, uint32_t
     float v = x;
     if (a.has_inq) {
       uint32_t idx = x_is_bf ? xbits_bf : f2bf(x);
-      v = bf2f(round_any(a.inq, idx, a.inq_table));
+      v = bf2f(round_any_dev(a.inq, idx, a.inq_table));
     }
     if (a.has_zp) {
       v = fsub_rn(v, z);
@@ -581,7 +602,7 @@ __device__ __forceinline__ uint32_t elem_op(const ElemArgs& a, float x, uint32_t
     }
     v = fmul_rn(v, s);
     if (a.r2_bf16) v = round_bf(v);
-    if (a.has_outq) v = bf2f(round_any(a.outq, f2bf(v), a.outq_table));
+    if (a.has_outq) v = bf2f(round_any_dev(a.outq, f2bf(v), a.outq_table));
     *outf = v;
     return f2bf(v);
   }
@@ -844,10 +865,10 @@ int dispatch_types(ElemArgs& a, int in_dt, int out_dt, int K, bool vec_ok, cudaS
   return VQ_ERR_UNSUPPORTED;
 }
 
-template <typename TIn, typename TOut, bool DEQ, int K, int VEC, int SL>
+template <typename TIn, typename TOut, bool DEQ, int K, int VEC, int SL, bool QM>
 int launch_2d(Elem2DArgs& a, cudaStream_t st) {
   constexpr int UNROLL = 2;
-  auto kern = k_elem2d<TIn, TOut, DEQ, K, VEC, SL, UNROLL>;
+  auto kern = k_elem2d<TIn, TOut, DEQ, K, VEC, SL, QM, UNROLL>;
   const int smem = (!DEQ && K == VQ_R_TABLE) ? kTableBytes : 0;
   int threads = 256, sms = num_sms(), blocks;
   if (smem) {
@@ -869,12 +890,15 @@ int launch_2d(Elem2DArgs& a, cudaStream_t st) {
 
 template <typename TIn, typename TOut, bool DEQ, int VEC, int SL>
 int dispatch_2d_kind(Elem2DArgs& a, int K, cudaStream_t st) {
-  if (DEQ) return launch_2d<TIn, TOut, DEQ, VQ_R_IDENTITY, VEC, SL>(a, st);
+  if (DEQ) {
+    if (a.has_inq || a.has_outq) return launch_2d<TIn, TOut, DEQ, VQ_R_IDENTITY, VEC, SL, true>(a, st);
+    return launch_2d<TIn, TOut, DEQ, VQ_R_IDENTITY, VEC, SL, false>(a, st);
+  }
   switch (K) {
-    case VQ_R_IDENTITY: return launch_2d<TIn, TOut, DEQ, VQ_R_IDENTITY, VEC, SL>(a, st);
-    case VQ_R_MINIFLOAT: return launch_2d<TIn, TOut, DEQ, VQ_R_MINIFLOAT, VEC, SL>(a, st);
-    case VQ_R_INT: return launch_2d<TIn, TOut, DEQ, VQ_R_INT, VEC, SL>(a, st);
-    default: return launch_2d<TIn, TOut, DEQ, VQ_R_TABLE, VEC, SL>(a, st);
+    case VQ_R_IDENTITY: return launch_2d<TIn, TOut, DEQ, VQ_R_IDENTITY, VEC, SL, false>(a, st);
+    case VQ_R_MINIFLOAT: return launch_2d<TIn, TOut, DEQ, VQ_R_MINIFLOAT, VEC, SL, false>(a, st);
+    case VQ_R_INT: return launch_2d<TIn, TOut, DEQ, VQ_R_INT, VEC, SL, false>(a, st);
+    default: return launch_2d<TIn, TOut, DEQ, VQ_R_TABLE, VEC, SL, false>(a, st);
   }
 }
 
@@ -1104,10 +1128,10 @@ int qmx_last_fast_ok(const vq_tensor& x, const int* blocked, int64_t bs) {
   return (int)nv;
 }
 
-template <typename TIn, int K, int TPB, int VPT>
+template <typename TIn, int K, int SK, int TPB, int VPT>
 int launch_qmx(QmxArgs& a, cudaStream_t st) {
   constexpr int UNROLL = 2;
-  auto kern = k_qmx_last<TIn, K, TPB, VPT, UNROLL>;
+  auto kern = k_qmx_last<TIn, K, SK, TPB, VPT, UNROLL>;
   int smem = K == VQ_R_TABLE ? kTableBytes : 0;
   int threads = 256, sms = num_sms(), blocks;
   if (smem) {
@@ -1129,25 +1153,36 @@ int launch_qmx(QmxArgs& a, cudaStream_t st) {
 
 // nv = vectors per block: one thread per block up to two vectors, then two
 // vectors per thread across nv/2 threads.
-template <typename TIn, int K>
+template <typename TIn, int K, int SK>
 int launch_qmx_tpb(QmxArgs& a, int nv, cudaStream_t st) {
   switch (nv) {
-    case 1: return launch_qmx<TIn, K, 1, 1>(a, st);
-    case 2: return launch_qmx<TIn, K, 1, 2>(a, st);
-    case 4: return launch_qmx<TIn, K, 2, 2>(a, st);
-    case 8: return launch_qmx<TIn, K, 4, 2>(a, st);
-    case 16: return launch_qmx<TIn, K, 8, 2>(a, st);
-    default: return launch_qmx<TIn, K, 16, 2>(a, st);
+    case 1: return launch_qmx<TIn, K, SK, 1, 1>(a, st);
+    case 2: return launch_qmx<TIn, K, SK, 1, 2>(a, st);
+    case 4: return launch_qmx<TIn, K, SK, 2, 2>(a, st);
+    case 8: return launch_qmx<TIn, K, SK, 4, 2>(a, st);
+    case 16: return launch_qmx<TIn, K, SK, 8, 2>(a, st);
+    default: return launch_qmx<TIn, K, SK, 16, 2>(a, st);
+  }
+}
+
+template <typename TIn, int K>
+int launch_qmx_sk(QmxArgs& a, int nv, cudaStream_t st) {
+  // the power-of-two path never rounds through scale_qmap
+  const int SK = (a.pow2 || !a.has_sq) ? 0 : (a.sq.kind == VQ_R_MINIFLOAT ? 1 : 2);
+  switch (SK) {
+    case 0: return launch_qmx_tpb<TIn, K, 0>(a, nv, st);
+    case 1: return launch_qmx_tpb<TIn, K, 1>(a, nv, st);
+    default: return launch_qmx_tpb<TIn, K, 2>(a, nv, st);
   }
 }
 
 template <typename TIn>
 int launch_qmx_kind(QmxArgs& a, int K, int nv, cudaStream_t st) {
   switch (K) {
-    case VQ_R_IDENTITY: return launch_qmx_tpb<TIn, VQ_R_IDENTITY>(a, nv, st);
-    case VQ_R_MINIFLOAT: return launch_qmx_tpb<TIn, VQ_R_MINIFLOAT>(a, nv, st);
-    case VQ_R_INT: return launch_qmx_tpb<TIn, VQ_R_INT>(a, nv, st);
-    default: return launch_qmx_tpb<TIn, VQ_R_TABLE>(a, nv, st);
+    case VQ_R_IDENTITY: return launch_qmx_sk<TIn, VQ_R_IDENTITY>(a, nv, st);
+    case VQ_R_MINIFLOAT: return launch_qmx_sk<TIn, VQ_R_MINIFLOAT>(a, nv, st);
+    case VQ_R_INT: return launch_qmx_sk<TIn, VQ_R_INT>(a, nv, st);
+    default: return launch_qmx_sk<TIn, VQ_R_TABLE>(a, nv, st);
   }
 }
 
