@@ -106,7 +106,15 @@ typedef struct vq_rounder {
   uint16_t pad_;
   /* TABLE: device pointer to 65,536 bf16 entries (caller-owned). */
   const uint16_t* table;
+  /* MINIFLOAT only: a hardware conversion that reproduces this rounder
+   * (VQ_HW_*), set by vq_rounder_from_table() as a candidate and kept only
+   * after vq_rounder_check_hw() has compared it with the table on the
+   * device; 0 = evaluate analytically. */
+  int32_t hw;
+  int32_t pad2_;
 } vq_rounder;
+
+enum { VQ_HW_NONE = 0, VQ_HW_E4M3 = 1, VQ_HW_E5M2 = 2, VQ_HW_E2M1 = 3 };
 
 /* Name of a status code (static string). */
 const char* vq_status_string(int status);
@@ -168,6 +176,12 @@ int vq_quantize_mx(const vq_tensor* input, const vq_rounder* qmap, const int64_t
                    int32_t naxes, int64_t block_size, float quant_max, int32_t pow2,
                    int32_t floor_log2_qmax, const vq_rounder* scale_qmap,
                    vq_tensor* scale_out, vq_tensor* codes_out, void* stream);
+
+/* Count, on the device, the bf16 patterns whose hardware-conversion rounding
+ * (r->hw) differs from r->table (65,536 entries, device).  Writes the count
+ * to *d_mismatches (device int32, zeroed by the call).  Used once per table
+ * before r->hw is trusted. */
+int vq_rounder_check_hw(const vq_rounder* r, int32_t* d_mismatches, void* stream);
 
 /* The per-block parameters of quantized_ops::quantize_affine
  * (quantized.py:884-948): for blocks of `block_size` elements along the one

@@ -283,3 +283,13 @@ def test_codebook_quantize_and_decode():
     want_i = oracle.quantize(x, s, qmap=cb, output_code=mid)
     got_i = to_np(Q.quantize(to_dev(x), to_dev(s), qmap=to_dev(cb), output_code=to_dev(mid)))
     assert len(G.bit_mismatches(got_i, want_i)) == 0
+
+
+def test_hardware_rounders_verified():
+    """The tensor-core formats take the hardware conversion path, kept only
+    after matching all 65,536 table entries on this device."""
+    from voyager_b200.tables import rounder_for
+
+    for name, hw in (("fp8_e4m3", 1), ("fp8_e5m2", 2), ("fp4_e2m1", 3)):
+        rd = rounder_for(to_dev(G.tables()[name]), torch.device("cuda", 0))
+        assert rd.c.hw == hw, (name, rd.c.describe())

@@ -53,6 +53,11 @@ bool try_minifloat(const uint16_t* t, vq_rounder* out) {
           r.nan_bits = t[0xFFFF];
           if ((double)r.max_norm != mx) continue;
           if (matches(r, t)) {
+            // formats the tensor cores' conversion instructions produce
+            // (round-to-nearest-even, saturating to the largest finite)
+            if (sgn && ebits == 4 && mbits == 3 && mx == 448.0) r.hw = VQ_HW_E4M3;
+            if (sgn && ebits == 5 && mbits == 2 && mx == 57344.0) r.hw = VQ_HW_E5M2;
+            if (sgn && ebits == 2 && mbits == 1 && mx == 6.0) r.hw = VQ_HW_E2M1;
             *out = r;
             return true;
           }

@@ -120,6 +120,67 @@ __device__ __forceinline__ void stage_table(const vq_rounder& r, uint16_t* stab)
   __syncthreads();
 }
 
+// Element kinds beyond vq_rounder_kind: a MINIFLOAT rounder that the
+// hardware conversions reproduce (vq_rounder.hw, verified on the device).
+constexpr int K_HW_E4M3 = 10, K_HW_E5M2 = 11, K_HW_E2M1 = 12;
+
+// Two bf16 indices (lo | hi << 16) through a hardware minifloat conversion
+// (round-to-nearest-even, saturating) and back: every value of these formats
+// is exactly a bf16, so the result is the table entry except for the two
+// cases the table treats specially: a -0 index gives +0, a NaN index gives
+// nan_bits.
+template <int K>
+__device__ __forceinline__ uint32_t hw_pair(uint32_t idx2, uint32_t nan_bits) {
+  const float lo = __uint_as_float(idx2 << 16);
+  const float hi = __uint_as_float(idx2 & 0xFFFF0000u);
+  uint32_t h2;
+  if (K == K_HW_E4M3) {
+    asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e4m3x2.f32 t, %1, %2;\n\t"
+        "cvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(h2) : "f"(hi), "f"(lo));
+  } else if (K == K_HW_E5M2) {
+    asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e5m2x2.f32 t, %1, %2;\n\t"
+        "cvt.rn.f16x2.e5m2x2 %0, t;\n\t}" : "=r"(h2) : "f"(hi), "f"(lo));
+  } else {
+    asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h2) : "f"(hi), "f"(lo));
+  }
+  const float flo = __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+  const float fhi = __half2float(__ushort_as_half((unsigned short)(h2 >> 16)));
+  uint32_t out = (__float_as_uint(flo) >> 16) | (__float_as_uint(fhi) & 0xFFFF0000u);
+  const uint32_t mag = idx2 & 0x7FFF7FFFu;
+  out &= __vcmpne2(mag, 0u) | 0x7FFF7FFFu;          // -0 -> +0
+  const uint32_t nan = __vcmpgtu2(mag, 0x7F807F80u);  // NaN -> nan_bits
+  return (out & ~nan) | ((nan_bits * 0x10001u) & nan);
+}
+
+// bf16 indices of two quotients, packed: the exact patterns for a table
+// (NaN -> 0xFFFF), the hardware pair conversion otherwise.
+template <int K>
+__device__ __forceinline__ uint32_t pair_index(float q0, float q1) {
+  if (K == VQ_R_TABLE) return f2bf(q0) | (f2bf(q1) << 16);
+  __nv_bfloat162 b = __floats2bfloat162_rn(q0, q1);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+template <int K>
+__device__ __forceinline__ uint32_t round_pair(const vq_rounder& r, uint32_t idx2,
+                                               const uint16_t* stab) {
+  if (K >= K_HW_E4M3) return hw_pair<K>(idx2, r.nan_bits);
+  return round_elem<K>(r, idx2 & 0xFFFFu, stab) | (round_elem<K>(r, idx2 >> 16, stab) << 16);
+}
+
+__global__ void k_check_hw(const __grid_constant__ vq_rounder r, int32_t* mism) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;  // pair 0..32767
+  if (i >= 32768) return;
+  const uint32_t idx2 = (2 * i) | ((2 * i + 1) << 16);
+  uint32_t o;
+  if (r.hw == VQ_HW_E4M3) o = hw_pair<K_HW_E4M3>(idx2, r.nan_bits);
+  else if (r.hw == VQ_HW_E5M2) o = hw_pair<K_HW_E5M2>(idx2, r.nan_bits);
+  else o = hw_pair<K_HW_E2M1>(idx2, r.nan_bits);
+  const int bad = ((o & 0xFFFFu) != r.table[2 * i]) + ((o >> 16) != r.table[2 * i + 1]);
+  if (bad) atomicAdd(mism, bad);
+}
+
 // ---------------------------------------------------------------------------
 // k_qmx_last: fused block scale + quantize, blocks along the last dim
 // ---------------------------------------------------------------------------
@@ -226,15 +287,16 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
           for (int k = 0; k < 4; ++k) {
             const float q0 = div_to_bf16_domain(bf2f(w[k] & 0xFFFFu), dv);
             const float q1 = div_to_bf16_domain(bf2f(w[k] >> 16), dv);
-            const uint32_t lo = round_elem<K>(a.qr, to_bf16_index<K>(q0), smem);
-            const uint32_t hi = round_elem<K>(a.qr, to_bf16_index<K>(q1), smem);
-            w[k] = lo | (hi << 16);
+            w[k] = round_pair<K>(a.qr, pair_index<K>(q0, q1), smem);
           }
         } else {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float q = div_to_bf16_domain(u2f(w[k]), dv);
-            w[k] = round_elem<K>(a.qr, to_bf16_index<K>(q), smem) << 16;
+          for (int k = 0; k < 4; k += 2) {
+            const float q0 = div_to_bf16_domain(u2f(w[k]), dv);
+            const float q1 = div_to_bf16_domain(u2f(w[k + 1]), dv);
+            const uint32_t c2 = round_pair<K>(a.qr, pair_index<K>(q0, q1), smem);
+            w[k] = c2 << 16;
+            w[k + 1] = c2 & 0xFFFF0000u;
           }
         }
         __stcs(reinterpret_cast<uint4*>(reinterpret_cast<TIn*>(a.codes) + base[u] + off),
@@ -421,6 +483,66 @@ __device__ __forceinline__ int64_t map_off(const Map2D& m, uint32_t row, uint32_
   return (int64_t)m.div_r.div(row) * m.str_r + (int64_t)m.div_c.div(col) * m.str_c;
 }
 
+// Quantize one vector's quotients (x / s, rounded to bf16 when the index is
+// taken) into codes, in pairs.
+template <typename TIn, int K, int VEC>
+__device__ __forceinline__ void quant_vec(const Elem2DArgs& a, const TIn* xin, const float* s,
+                                          const float* z, bool zp, uint32_t* codes,
+                                          const uint16_t* stab) {
+  constexpr bool IN_BF = sizeof(TIn) == 2;
+  float t[VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) {
+    const float x = IN_BF ? bf2f(*reinterpret_cast<const uint16_t*>(&xin[j]))
+                          : *reinterpret_cast<const float*>(&xin[j]);
+    if (!zp) {
+      t[j] = div_slow(x, s[j]);
+    } else if (a.exact_div) {  // r1 float32: the add needs the IEEE quotient
+      float q = fdiv_rn(x, s[j]);
+      q = fadd_rn(q, z[j]);
+      t[j] = a.r2_bf16 ? round_bf(q) : q;
+    } else {  // r1 bf16: round the quotient, add, round per r2
+      float q = fadd_rn(round_bf(fdiv_rn(x, s[j])), z[j]);
+      t[j] = a.r2_bf16 ? round_bf(q) : q;
+    }
+  }
+  if (VEC == 1) {
+    codes[0] = round_elem<K < K_HW_E4M3 ? K : VQ_R_MINIFLOAT>(a.qr, f2bf(t[0]), stab);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < VEC; j += 2) {
+    const uint32_t c2 = round_pair<K>(a.qr, pair_index<K>(t[j], t[j + 1]), stab);
+    codes[j] = c2 & 0xFFFFu;
+    codes[j + 1] = c2 >> 16;
+  }
+}
+
+// Same for a uniform scale with a Divisor (reciprocal multiply, exact).
+template <typename TIn, int K, int VEC>
+__device__ __forceinline__ void quant_vec_fast(const Elem2DArgs& a, const TIn* xin,
+                                               const Divisor& dv, uint32_t* codes,
+                                               const uint16_t* stab) {
+  constexpr bool IN_BF = sizeof(TIn) == 2;
+  float t[VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) {
+    const float x = IN_BF ? bf2f(*reinterpret_cast<const uint16_t*>(&xin[j]))
+                          : *reinterpret_cast<const float*>(&xin[j]);
+    t[j] = div_to_bf16_domain(x, dv);
+  }
+  if (VEC == 1) {
+    codes[0] = round_elem<K < K_HW_E4M3 ? K : VQ_R_MINIFLOAT>(a.qr, f2bf(t[0]), stab);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < VEC; j += 2) {
+    const uint32_t c2 = round_pair<K>(a.qr, pair_index<K>(t[j], t[j + 1]), stab);
+    codes[j] = c2 & 0xFFFFu;
+    codes[j + 1] = c2 >> 16;
+  }
+}
+
 template <typename TIn, typename TOut, bool DEQ, int K, int VEC, int SL, bool QM, int UNROLL>
 __global__ void __launch_bounds__(1024) k_elem2d(const __grid_constant__ Elem2DArgs a) {
   extern __shared__ __align__(16) uint16_t smem[];
@@ -429,12 +551,10 @@ __global__ void __launch_bounds__(1024) k_elem2d(const __grid_constant__ Elem2DA
   constexpr bool OUT_BF = sizeof(TOut) == 2;
   constexpr int IN_B = VEC * sizeof(TIn), OUT_B = VEC * sizeof(TOut);
   const uint32_t stride = gridDim.x * blockDim.x;
+  const bool zp = a.has_zp;
   int64_t cached = -1;
-  float s = 0.f;
-  Divisor dv;
-  dv.s = 1.f;
-  dv.r = 1.f;
-  dv.fast = 1;
+  float s = 1.f;
+  Divisor dv = make_divisor(1.f);
   if (SL == SL_SCALAR) {
     s = ld_f(a.scale.ptr, 0, a.scale.is_bf16);
     if (!DEQ) dv = make_divisor(s);
@@ -459,7 +579,7 @@ __global__ void __launch_bounds__(1024) k_elem2d(const __grid_constant__ Elem2DA
       if (v >= a.nvec) continue;
       const uint32_t e = v * VEC;
       uint32_t row = 0, col = 0;
-      if (SL != SL_SCALAR || a.has_zp) {
+      if (SL != SL_SCALAR || zp) {
         row = a.C.div(e);
         col = e - row * a.C.d;
       }
@@ -472,57 +592,48 @@ __global__ void __launch_bounds__(1024) k_elem2d(const __grid_constant__ Elem2DA
           if (!DEQ) dv = make_divisor(s);
         }
       }
+      uint32_t ob[VEC];
+      float of[VEC];
+      if (!DEQ && uni && !zp) {
+        // the hot path: one scale per vector, reciprocal multiply
+        quant_vec_fast<TIn, K, VEC>(a, xin[u], dv, ob, smem);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) of[j] = bf2f(ob[j]);
+      } else {
+        float sv[VEC], zv[VEC];
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          sv[j] = uni ? s : ld_f(a.scale.ptr, map_off(a.scale, row, col + j), a.scale.is_bf16);
+          zv[j] = zp ? ld_f(a.zp.ptr, map_off(a.zp, row, col + j), a.zp.is_bf16) : 0.f;
+        }
+        if (!DEQ) {
+          quant_vec<TIn, K, VEC>(a, xin[u], sv, zv, zp, ob, smem);
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) of[j] = bf2f(ob[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            const uint32_t xb = IN_BF ? (uint32_t)(*reinterpret_cast<const uint16_t*>(&xin[u][j])) : 0u;
+            float w = IN_BF ? bf2f(xb) : *reinterpret_cast<const float*>(&xin[u][j]);
+            if (QM && a.has_inq)
+              w = bf2f(round_any_dev(a.inq, IN_BF ? xb : f2bf(w), a.inq_table));
+            if (zp) {
+              w = fsub_rn(w, zv[j]);
+              if (a.r1_bf16) w = round_bf(w);
+            }
+            w = fmul_rn(w, sv[j]);
+            if (a.r2_bf16) w = round_bf(w);
+            if (QM && a.has_outq) w = bf2f(round_any_dev(a.outq, f2bf(w), a.outq_table));
+            of[j] = w;
+            ob[j] = f2bf(w);
+          }
+        }
+      }
       TOut res[VEC];
 #pragma unroll
       for (int j = 0; j < VEC; ++j) {
-        if (!uni) {
-          s = ld_f(a.scale.ptr, map_off(a.scale, row, col + j), a.scale.is_bf16);
-          if (!DEQ) dv = make_divisor(s);
-        }
-        float z = 0.f;
-        if (a.has_zp) z = ld_f(a.zp.ptr, map_off(a.zp, row, col + j), a.zp.is_bf16);
-        float x;
-        uint32_t xb = 0;
-        if (IN_BF) {
-          xb = (uint32_t)(*reinterpret_cast<const uint16_t*>(&xin[u][j]));
-          x = bf2f(xb);
-        } else {
-          x = *reinterpret_cast<const float*>(&xin[u][j]);
-        }
-        uint32_t ob;
-        float of;
-        if (!DEQ) {
-          float t;
-          if (a.exact_div) {
-            t = fdiv_rn(x, s);
-            if (a.r1_bf16) t = round_bf(t);
-            t = fadd_rn(t, z);
-            if (a.r2_bf16) t = round_bf(t);
-            ob = round_elem<K>(a.qr, f2bf(t), smem);
-          } else {
-            t = div_to_bf16_domain(x, dv);
-            if (a.has_zp) {  // r1 is bf16 here: round, add, round per r2
-              t = fadd_rn(round_bf(t), z);
-              if (a.r2_bf16) t = round_bf(t);
-            }
-            ob = round_elem<K>(a.qr, to_bf16_index<K>(t), smem);
-          }
-          of = bf2f(ob);
-        } else {
-          float w = x;
-          if (QM && a.has_inq) w = bf2f(round_any_dev(a.inq, IN_BF ? xb : f2bf(x), a.inq_table));
-          if (a.has_zp) {
-            w = fsub_rn(w, z);
-            if (a.r1_bf16) w = round_bf(w);
-          }
-          w = fmul_rn(w, s);
-          if (a.r2_bf16) w = round_bf(w);
-          if (QM && a.has_outq) w = bf2f(round_any_dev(a.outq, f2bf(w), a.outq_table));
-          of = w;
-          ob = f2bf(w);
-        }
-        if (OUT_BF) *reinterpret_cast<uint16_t*>(&res[j]) = (uint16_t)ob;
-        else *reinterpret_cast<float*>(&res[j]) = of;
+        if (OUT_BF) *reinterpret_cast<uint16_t*>(&res[j]) = (uint16_t)ob[j];
+        else *reinterpret_cast<float*>(&res[j]) = of[j];
       }
       TOut* dst = reinterpret_cast<TOut*>(a.out) + (uint64_t)v * VEC;
       if (OUT_B == 16) {
@@ -708,6 +819,9 @@ int cuda_status(cudaError_t e) { return e == cudaSuccess ? VQ_OK : VQ_ERR_CUDA; 
 // Rounders whose element form is the shared-memory table.
 int elem_kind(const vq_rounder* r) {
   if (r == nullptr) return VQ_R_IDENTITY;
+  if (r->kind == VQ_R_MINIFLOAT && r->hw == VQ_HW_E4M3) return K_HW_E4M3;
+  if (r->kind == VQ_R_MINIFLOAT && r->hw == VQ_HW_E5M2) return K_HW_E5M2;
+  if (r->kind == VQ_R_MINIFLOAT && r->hw == VQ_HW_E2M1) return K_HW_E2M1;
   if (r->kind == VQ_R_IDENTITY || r->kind == VQ_R_MINIFLOAT || r->kind == VQ_R_INT)
     return r->kind;
   return VQ_R_TABLE;
@@ -898,6 +1012,9 @@ int dispatch_2d_kind(Elem2DArgs& a, int K, cudaStream_t st) {
     case VQ_R_IDENTITY: return launch_2d<TIn, TOut, DEQ, VQ_R_IDENTITY, VEC, SL, false>(a, st);
     case VQ_R_MINIFLOAT: return launch_2d<TIn, TOut, DEQ, VQ_R_MINIFLOAT, VEC, SL, false>(a, st);
     case VQ_R_INT: return launch_2d<TIn, TOut, DEQ, VQ_R_INT, VEC, SL, false>(a, st);
+    case K_HW_E4M3: return launch_2d<TIn, TOut, DEQ, K_HW_E4M3, VEC, SL, false>(a, st);
+    case K_HW_E5M2: return launch_2d<TIn, TOut, DEQ, K_HW_E5M2, VEC, SL, false>(a, st);
+    case K_HW_E2M1: return launch_2d<TIn, TOut, DEQ, K_HW_E2M1, VEC, SL, false>(a, st);
     default: return launch_2d<TIn, TOut, DEQ, VQ_R_TABLE, VEC, SL, false>(a, st);
   }
 }
@@ -1168,12 +1285,9 @@ int launch_qmx_tpb(QmxArgs& a, int nv, cudaStream_t st) {
 template <typename TIn, int K>
 int launch_qmx_sk(QmxArgs& a, int nv, cudaStream_t st) {
   // the power-of-two path never rounds through scale_qmap
-  const int SK = (a.pow2 || !a.has_sq) ? 0 : (a.sq.kind == VQ_R_MINIFLOAT ? 1 : 2);
-  switch (SK) {
-    case 0: return launch_qmx_tpb<TIn, K, 0>(a, nv, st);
-    case 1: return launch_qmx_tpb<TIn, K, 1>(a, nv, st);
-    default: return launch_qmx_tpb<TIn, K, 2>(a, nv, st);
-  }
+  if (a.pow2 || !a.has_sq) return launch_qmx_tpb<TIn, K, 0>(a, nv, st);
+  if (a.sq.kind == VQ_R_MINIFLOAT) return launch_qmx_tpb<TIn, K, 1>(a, nv, st);
+  return launch_qmx_tpb<TIn, K, 2>(a, nv, st);
 }
 
 template <typename TIn>
@@ -1182,6 +1296,9 @@ int launch_qmx_kind(QmxArgs& a, int K, int nv, cudaStream_t st) {
     case VQ_R_IDENTITY: return launch_qmx_sk<TIn, VQ_R_IDENTITY>(a, nv, st);
     case VQ_R_MINIFLOAT: return launch_qmx_sk<TIn, VQ_R_MINIFLOAT>(a, nv, st);
     case VQ_R_INT: return launch_qmx_sk<TIn, VQ_R_INT>(a, nv, st);
+    case K_HW_E4M3: return launch_qmx_sk<TIn, K_HW_E4M3>(a, nv, st);
+    case K_HW_E5M2: return launch_qmx_sk<TIn, K_HW_E5M2>(a, nv, st);
+    case K_HW_E2M1: return launch_qmx_sk<TIn, K_HW_E2M1>(a, nv, st);
     default: return launch_qmx_sk<TIn, VQ_R_TABLE>(a, nv, st);
   }
 }
@@ -1345,6 +1462,15 @@ int vq_quantize_mx(const vq_tensor* input, const vq_rounder* qmap, const int64_t
     return st;
   return run_elementwise<false>(input, scale_out, nullptr, block_size, qmap, nullptr, nullptr,
                                 codes_out, stream);
+}
+
+int vq_rounder_check_hw(const vq_rounder* r, int32_t* d_mismatches, void* stream) {
+  if (!r || !d_mismatches || !r->table) return VQ_ERR_NULL;
+  if (r->kind != VQ_R_MINIFLOAT || r->hw < VQ_HW_E4M3 || r->hw > VQ_HW_E2M1) return VQ_ERR_INVALID;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(d_mismatches, 0, sizeof(int32_t), cs) != cudaSuccess) return VQ_ERR_CUDA;
+  k_check_hw<<<128, 256, 0, cs>>>(*r, d_mismatches);
+  return cuda_status(cudaGetLastError());
 }
 
 int vq_quantize_affine_qparams(const vq_tensor* input, const int64_t* axes, int32_t naxes,

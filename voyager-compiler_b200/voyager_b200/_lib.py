@@ -57,13 +57,16 @@ class VqRounder(ctypes.Structure):
         ("step_vals", ctypes.c_uint16 * (VQ_STEP_MAX + 1)),
         ("pad_", ctypes.c_uint16),
         ("table", ctypes.c_void_p),
+        ("hw", ctypes.c_int32),
+        ("pad2_", ctypes.c_int32),
     ]
 
     def describe(self) -> str:
         k = KIND_NAMES.get(self.kind, "?")
         if self.kind == VQ_R_MINIFLOAT:
+            hw = {1: ", hw e4m3", 2: ", hw e5m2", 3: ", hw e2m1"}.get(self.hw, "")
             return (f"minifloat(e{self.ebits}m{self.mbits}, "
-                    f"{'signed' if self.is_signed else 'unsigned'}, max={self.max_norm:g})")
+                    f"{'signed' if self.is_signed else 'unsigned'}, max={self.max_norm:g}{hw})")
         if self.kind == VQ_R_INT:
             return f"int[{self.qmin:g},{self.qmax:g}]"
         if self.kind == VQ_R_POSIT:
@@ -91,6 +94,7 @@ _SIGNATURES = {
     "vq_quantize_mx": (ctypes.c_int, [P(VqTensor), P(VqRounder), P(ctypes.c_int64), ctypes.c_int32,
                                       ctypes.c_int64, ctypes.c_float, ctypes.c_int32, ctypes.c_int32,
                                       P(VqRounder), P(VqTensor), P(VqTensor), ctypes.c_void_p]),
+    "vq_rounder_check_hw": (ctypes.c_int, [P(VqRounder), ctypes.c_void_p, ctypes.c_void_p]),
     "vq_quantize_affine_qparams": (ctypes.c_int, [P(VqTensor), P(ctypes.c_int64), ctypes.c_int32,
                                                   ctypes.c_int64, ctypes.c_float, ctypes.c_float,
                                                   P(VqRounder), P(VqTensor), P(VqTensor),

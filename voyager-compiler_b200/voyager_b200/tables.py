@@ -156,6 +156,17 @@ def classify_host_table(bits: np.ndarray) -> "_lib.VqRounder":
     return r
 
 
+def _verify_hw(c: "_lib.VqRounder", device) -> None:
+    """Keep the hardware-conversion form of a minifloat rounder only if it
+    reproduces all 65,536 table entries on this device (one launch, one
+    synchronisation, once per table)."""
+    mism = torch.zeros(1, dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    st = _lib.load().vq_rounder_check_hw(ctypes.byref(c), mism.data_ptr(), stream)
+    if st != 0 or int(mism.item()) != 0:
+        c.hw = 0
+
+
 def rounder_for(qmap: torch.Tensor, device: torch.device) -> Rounder:
     """The rounder of a 65,536-entry table, with its bf16 device copy on
     ``device``.  Cached per tensor object (and its version counter) and per
@@ -178,6 +189,8 @@ def rounder_for(qmap: torch.Tensor, device: torch.device) -> Rounder:
         c = classify_host_table(bits)
         dev = torch.from_numpy(bits.view(np.int16).copy()).to(device).view(torch.bfloat16)
         c.table = dev.data_ptr()
+        if c.hw and torch.device(device).type == "cuda":
+            _verify_hw(c, device)
         rd = Rounder(c, dev, bits)
         with _lock:
             _content_cache[ck] = rd
