@@ -183,6 +183,34 @@ int vq_quantize_mx(const vq_tensor* input, const vq_rounder* qmap, const int64_t
  * before r->hw is trusted. */
 int vq_rounder_check_hw(const vq_rounder* r, int32_t* d_mismatches, void* stream);
 
+/* ---- MXFP8 block-scaled GEMM (tcgen05) -------------------------------------
+ * linear_mx / matmul_mx (src/voyager_compiler/ops/quantized.py:455-472,
+ * 522-648) for E4M3 codes with power-of-two block-32 scales along K on both
+ * operands: out = (A codes x 2^sA) @ (B codes x 2^sB)^T (+ bias), fp32
+ * accumulation, bf16 out.  Operands are packed first. */
+
+/* Bytes of a packed operand of `rows` x `k` codes: E4M3 bytes [rows padded to
+ * row_multiple (128 for A, 256 for B)][k padded to 128] and UE8M0 scale atoms
+ * [k/128][rows/128][512]. */
+int vq_mx_pack_sizes(int64_t rows, int64_t k, int32_t row_multiple, int64_t* codes_bytes,
+                     int64_t* sf_bytes, int64_t* ld_bytes);
+
+/* Pack bf16 codes [R, K] and bf16 scales [R, ceil(K/32)] (block_size 32).
+ * *d_inexact (device, may be NULL) counts codes that are not E4M3 values and
+ * scales that are not normal powers of two; a caller that cannot vouch for
+ * its operands checks it is 0 before using the GEMM. */
+int vq_mx_pack(const vq_tensor* codes, const vq_tensor* scale, int64_t block_size,
+               int32_t row_multiple, void* packed_codes, void* packed_sf, int32_t* d_inexact,
+               void* stream);
+
+/* out[M, N] (bf16, row stride ldo) = A[M, K] . B[N, K]^T (+ bias[N], bf16),
+ * from packed operands (A with row_multiple 128, B with 256).  N and ldo must
+ * be multiples of 8.  *d_err (device) is zeroed, and set non-zero if a
+ * bounded wait in the kernel gave up. */
+int vq_gemm_mxf8(const void* a, const void* a_sf, const void* b, const void* b_sf, int64_t M,
+                 int64_t N, int64_t K, const void* bias, void* out, int64_t ldo, int32_t* d_err,
+                 void* stream);
+
 /* The per-block parameters of quantized_ops::quantize_affine
  * (quantized.py:884-948): for blocks of `block_size` elements along the one
  * axis in `axes` (zero-padded when ragged),

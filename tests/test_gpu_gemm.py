@@ -1,0 +1,110 @@
+"""tcgen05 MXFP8 linear_mx against the oracle's dequantize-then-matmul.
+
+Tolerance: rel-L2 <= 1e-3 against the oracle GEMM rounded to the output
+dtype (bf16), as the reference's bf16 linear rounds it; the only difference
+is the float32 summation order."""
+
+import numpy as np
+import pytest
+import torch
+
+import _golden as G
+import oracle
+from _tt import to_dev, to_np
+from oracle.numerics import quantization_map
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _setup():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA GPU")
+    import voyager_b200  # noqa: F401
+
+    yield
+
+
+def _operands(m, k, n, seed):
+    from voyager_b200.synth import f32_to_bf16_bits
+
+    rng = np.random.Generator(np.random.PCG64(seed))
+    a = f32_to_bf16_bits(rng.standard_normal((m, k)).astype(np.float32))
+    w = f32_to_bf16_bits((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    qm = quantization_map("fp8_e4m3")
+    sa, ca = oracle.quantize_mx(a, qm, [-1], 32, 448.0, True)
+    sw, cw = oracle.quantize_mx(w, qm, [-1], 32, 448.0, True)
+    return ca, sa, cw, sw
+
+
+def _run(ca, sa, cw, sw, bias=None):
+    from voyager_b200 import mxgemm
+
+    dca, dsa, dcw, dsw = to_dev(ca), to_dev(sa), to_dev(cw), to_dev(sw)
+    assert mxgemm.applies(dca, dcw, dsa, dsw, 32, None, None, "kc", "linear")
+    out = mxgemm.linear(dca, dcw, None if bias is None else to_dev(bias), dsa, dsw)
+    assert out is not None, "operands were not accepted as exact MXFP8"
+    torch.cuda.synchronize()
+    return to_np(out)
+
+
+SHAPES = [(128, 128, 256), (1, 128, 8), (130, 256, 264), (256, 512, 512), (96, 96, 40),
+          (300, 4096, 11008), (1024, 4096, 4096)]
+
+
+@pytest.mark.parametrize("m,k,n", SHAPES)
+def test_mxf8_linear(m, k, n):
+    ca, sa, cw, sw = _operands(m, k, n, seed=m * 7 + k + n)
+    got = _run(ca, sa, cw, sw)
+    want = oracle.linear_mx(ca, cw, None, input_scale=sa, weight_scale=sw, block_size=32)
+    assert got.shape == want.shape and got.dtype == want.dtype
+    assert G.rel_l2(got, want) < 1e-3, G.rel_l2(got, want)
+
+
+def test_mxf8_linear_bias_and_op():
+    from voyager_b200.synth import f32_to_bf16_bits
+
+    ca, sa, cw, sw = _operands(200, 384, 136, seed=5)
+    bias = f32_to_bf16_bits(np.random.default_rng(1).standard_normal(136).astype(np.float32))
+    got = _run(ca, sa, cw, sw, bias)
+    want = oracle.linear_mx(ca, cw, bias, input_scale=sa, weight_scale=sw, block_size=32)
+    assert G.rel_l2(got, want) < 1e-3
+    # through the op (dispatches to the same kernel)
+    Q = torch.ops.quantized_ops
+    got2 = to_np(Q.linear_mx(to_dev(ca), to_dev(cw), to_dev(bias), input_scale=to_dev(sa),
+                             weight_scale=to_dev(sw), block_size=32))
+    assert G.rel_l2(got2, want) < 1e-3
+
+
+def test_mxf8_rejects_non_e4m3_codes():
+    """Codes that are not E4M3 values are detected by the pack check and the
+    op falls back to dequantize + matmul (still matching the oracle)."""
+    from voyager_b200 import mxgemm
+
+    ca, sa, cw, sw = _operands(64, 128, 64, seed=9)
+    cw = cw.copy()
+    cw[0, 0] = 0x3F81  # 1.0078125: not an E4M3 value
+    out = mxgemm.linear(to_dev(ca), to_dev(cw), None, to_dev(sa), to_dev(sw))
+    assert out is None
+    want = oracle.linear_mx(ca, cw, None, input_scale=sa, weight_scale=sw, block_size=32)
+    got = to_np(torch.ops.quantized_ops.linear_mx(to_dev(ca), to_dev(cw), None,
+                                                   input_scale=to_dev(sa),
+                                                   weight_scale=to_dev(sw), block_size=32))
+    assert G.rel_l2(got, want) < 1e-3
+
+
+def test_c3_full_size_rows_sample():
+    """C3 at full size (M=8192, K=4096, N=11008) through quantize_mx and
+    linear_mx; checked on a 256-row sample against the oracle."""
+    from voyager_b200 import synth
+
+    a, w = synth.c3_operands()
+    Q = torch.ops.quantized_ops
+    e4m3 = to_dev(quantization_map("fp8_e4m3"))
+    sa, ca = Q.quantize_mx(to_dev(a), e4m3, [-1], 32, 448.0, True)
+    sw, cw = Q.quantize_mx(to_dev(w), e4m3, [-1], 32, 448.0, True)
+    out = Q.linear_mx(ca, cw, None, input_scale=sa, weight_scale=sw, block_size=32)
+    rows = np.arange(0, 8192, 32)
+    want = oracle.linear_mx(to_np(ca)[rows], to_np(cw), None, input_scale=to_np(sa)[rows],
+                            weight_scale=to_np(sw), block_size=32)
+    assert G.rel_l2(to_np(out)[rows], want) < 1e-3

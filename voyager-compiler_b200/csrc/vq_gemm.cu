@@ -1,0 +1,554 @@
+// MXFP8 block-scaled GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// Replaces the dequantize-then-matmul of quantized_ops::linear_mx /
+// matmul_mx (src/voyager_compiler/ops/quantized.py:455-472, 522-648) when
+// both operands are E4M3 codes with power-of-two block-32 scales along K:
+//
+//   out[m, n] = sum_k (A[m,k] * sA[m,k/32]) * (B[n,k] * sB[n,k/32]) (+ bias[n])
+//
+// Operands are first packed (vq_mx_pack): codes to E4M3 bytes, row-major
+// [rows, Kp] with Kp = K rounded up to 128 (zero filled), and scales to UE8M0
+// bytes in the tensor cores' scale-factor layout: for each 128-element K tile
+// and each 128-row chunk a 512-byte atom, byte (r % 32) * 16 + (r / 32 % 4) * 4
+// + j for row r and K block j (0..3) of the tile; atoms ordered
+// [k_tile][row_chunk].
+//
+// Kernel: persistent, one CTA (6 warps) per SM.
+//   warp 0  TMA producer: A tile 128x128 B, B tile 256x128 B (SWIZZLE_128B),
+//           scale atoms by bulk copy, 4-stage mbarrier pipeline;
+//   warp 1  TMEM owner and MMA issuer: per K tile, tcgen05.cp of the scale
+//           atoms into TMEM, then 4 x tcgen05.mma.kind::mxf8f6f4.block_scale
+//           (M=128, N=256, K=32) accumulating in TMEM (fp32, 256 columns);
+//   warps 2-5 epilogue: tcgen05.ld of the accumulator, + bias, round to bf16,
+//           store.  One accumulator buffer: the MMA warp waits for the
+//           epilogue to drain it before the next tile.
+// Every wait is bounded; a wait that gives up sets *err and the kernel ends.
+// No TMA multicast is used.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "vq_numerics.cuh"
+
+namespace vq {
+namespace mx {
+
+constexpr int BM = 128, BN = 256, BK = 128;  // BK in fp8 bytes = elements
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK;             // 16 KB
+constexpr int B_BYTES = BN * BK;             // 32 KB
+constexpr int SFA_BYTES = 512;               // one 128-row atom
+constexpr int SFB_BYTES = 1024;              // two 128-row atoms
+constexpr int TX_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;  // per stage
+constexpr int STAGE_BYTES = (TX_BYTES + 1023) / 1024 * 1024;  // stages stay 1024-aligned
+constexpr int TMEM_COLS = 512;
+constexpr int ACC_COL = 0;    // 256 fp32 columns
+constexpr int SFA_COL = 256;  // 4 columns
+constexpr int SFB_COL = 260;  // 8 columns
+constexpr int THREADS = 192;
+constexpr uint64_t WAIT_NS = 2000000000ull;  // a wait gives up after 2 s
+
+enum { ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_TIMEOUT_ACC = 3 };
+
+struct SmemLayout {
+  // stages first (1024-byte aligned for SWIZZLE_128B), then barriers
+  static constexpr int kStages = 0;
+  static constexpr int kBars = STAGES * STAGE_BYTES;
+  static constexpr int kTotal = kBars + 256;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: false (and *err set) if the phase has not completed within
+// WAIT_NS of wall-clock time.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > WAIT_NS) break;
+  }
+  atomicCAS(err, 0, code);
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// K-major SWIZZLE_128B shared-memory matrix descriptor (tcgen05 format,
+// version 1): start >> 4, LBO 1 (unused for swizzled K-major), SBO = 1024 B
+// between 8-row groups, layout type 2.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;  // version
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+// Descriptor of a 32-row x 16-byte scale atom for tcgen05.cp.32x128b:
+// no swizzle, 8-row core matrices 128 B apart.
+__device__ __forceinline__ uint64_t sf_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(128 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  return d;
+}
+
+// Instruction descriptor, kind::mxf8f6f4 block-scaled: E4M3 x E4M3, UE8M0
+// scales, K-major A and B, M = 128, N = 256, scale-factor byte j.
+__device__ __forceinline__ uint32_t idesc_mxf8(uint32_t j) {
+  return (j << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) | (1u << 23) |
+         ((uint32_t)(BM >> 4) << 24) | (j << 29);
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+struct GemmArgs {
+  const uint8_t* sfa;  // [KT][MT][512]
+  const uint8_t* sfb;  // [KT][NT128][512]
+  const uint16_t* bias;  // bf16 [N] or null
+  uint16_t* out;         // bf16 [M, ldo]
+  int64_t ldo;
+  int M, N, KT;          // KT = Kp / 128
+  int MT, NT128, NTILE_N, ntiles;
+  int* err;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+    k_gemm_mxf8(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                const __grid_constant__ GemmArgs g) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // align the stage area to 1024 bytes (SWIZZLE_128B atoms)
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::kBars);
+  // bars[0..S) full, [S..2S) empty, [2S] acc_full, [2S+1] acc_empty, [2S+2] tmem slot
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+  const uint32_t acc_full = smem_u32(bars + 2 * STAGES), acc_empty = smem_u32(bars + 2 * STAGES + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 128);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_b)) : "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < g.ntiles && ok; t += gridDim.x) {
+        const int tm = t / g.NTILE_N, tn = t % g.NTILE_N;
+        for (int kt = 0; kt < g.KT; ++kt) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, g.err, ERR_TIMEOUT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sbase = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t fb = full0 + 8 * stage;
+          mbar_expect_tx(fb, TX_BYTES);
+          tma_load_2d(sbase, &tma_a, kt * BK, tm * BM, fb);
+          tma_load_2d(sbase + A_BYTES, &tma_b, kt * BK, tn * BN, fb);
+          bulk_load(sbase + A_BYTES + B_BYTES, g.sfa + ((size_t)kt * g.MT + tm) * 512, SFA_BYTES, fb);
+          bulk_load(sbase + A_BYTES + B_BYTES + SFA_BYTES,
+                    g.sfb + ((size_t)kt * g.NT128 + 2 * tn) * 512, SFB_BYTES, fb);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < g.ntiles && ok; t += gridDim.x) {
+        // the epilogue has drained the accumulator of the previous tile
+        if (!mbar_wait(acc_empty, acc_phase ^ 1, g.err, ERR_TIMEOUT_ACC)) break;
+        acc_phase ^= 1;
+        tc_fence_after();
+        for (int kt = 0; kt < g.KT; ++kt) {
+          if (!mbar_wait(full0 + 8 * stage, phase, g.err, ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sbase = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sa = sbase, sb = sbase + A_BYTES;
+          const uint32_t ssfa = sbase + A_BYTES + B_BYTES, ssfb = ssfa + SFA_BYTES;
+          // scale atoms -> TMEM (ordered before the MMAs that read them)
+          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem + SFA_COL),
+                       "l"(sf_desc(ssfa)));
+          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem + SFB_COL),
+                       "l"(sf_desc(ssfb)));
+          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem + SFB_COL + 4),
+                       "l"(sf_desc(ssfb + 512)));
+#pragma unroll
+          for (uint32_t j = 0; j < 4; ++j) {
+            const uint64_t da = sw128_desc(sa + j * 32);
+            const uint64_t db = sw128_desc(sb + j * 32);
+            const uint32_t accum = (kt > 0 || j > 0) ? 1u : 0u;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], "
+                "p;\n\t}" ::"r"(tmem + ACC_COL),
+                "l"(da), "l"(db), "r"(idesc_mxf8(j)), "r"(accum), "r"(tmem + SFA_COL + (j << 30)),
+                "r"(tmem + SFB_COL + (j << 30)));
+          }
+          // frees the stage once these MMAs (and copies) have read it
+          asm volatile(
+              "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                  empty0 + 8 * stage)
+              : "memory");
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        asm volatile(
+            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                acc_full)
+            : "memory");
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < g.ntiles; t += gridDim.x) {
+      const int tm = t / g.NTILE_N, tn = t % g.NTILE_N;
+      if (!mbar_wait(acc_full, acc_phase, g.err, ERR_TIMEOUT_ACC)) break;
+      acc_phase ^= 1;
+      tc_fence_after();
+      const int row = tm * BM + row_in_tile;
+      uint16_t* orow = g.out + (int64_t)row * g.ldo;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + ACC_COL + c0;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+            "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+              "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+              "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+              "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+              "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+              "=r"(r[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        const int col0 = tn * BN + c0;
+        if (row < g.M && col0 < g.N) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float v0 = __uint_as_float(r[2 * i]), v1 = __uint_as_float(r[2 * i + 1]);
+            if (g.bias) {
+              v0 += bf2f(g.bias[min(col0 + 2 * i, g.N - 1)]);
+              v1 += bf2f(g.bias[min(col0 + 2 * i + 1, g.N - 1)]);
+            }
+            __nv_bfloat162 b = __floats2bfloat162_rn(v0, v1);
+            packed[i] = *reinterpret_cast<uint32_t*>(&b);
+          }
+          if (col0 + 32 <= g.N) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + col0);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+          } else {
+            for (int i = 0; i < 32 && col0 + i < g.N; ++i)
+              orow[col0 + i] = (uint16_t)((packed[i / 2] >> (16 * (i & 1))) & 0xFFFFu);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Packing: bf16 E4M3 codes -> bytes, bf16 power-of-two scales -> UE8M0 atoms
+// ---------------------------------------------------------------------------
+struct PackArgs {
+  const uint16_t* codes;  // bf16 [R, K]
+  const uint16_t* scale;  // bf16 [R, nkb]
+  uint8_t* out;           // [R_pad, Kp]
+  uint8_t* sf;            // [KT][RT][512]
+  int R, K, Kp, nkb, RT, KT;
+  int* inexact;           // count of codes / scales not representable (may be null)
+};
+
+// One thread: 16 codes of a row (16 bytes out).
+__global__ void k_pack_codes(const __grid_constant__ PackArgs p) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_row = p.Kp / 16;
+  const int64_t total = (int64_t)p.RT * 128 * per_row;
+  if (i >= total) return;
+  const int r = (int)(i / per_row), c0 = (int)(i % per_row) * 16;
+  uint32_t w[4] = {0, 0, 0, 0};
+  int bad = 0;
+  if (r < p.R) {
+#pragma unroll
+    for (int k = 0; k < 16; k += 2) {
+      const int c = c0 + k;
+      float f0 = 0.f, f1 = 0.f;
+      if (c < p.K) f0 = bf2f(p.codes[(int64_t)r * p.K + c]);
+      if (c + 1 < p.K) f1 = bf2f(p.codes[(int64_t)r * p.K + c + 1]);
+      uint16_t b;
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(b) : "f"(f1), "f"(f0));
+      // exact round trip check
+      uint32_t h2;
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(b));
+      const float g0 = __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFF)));
+      const float g1 = __half2float(__ushort_as_half((unsigned short)(h2 >> 16)));
+      bad += (__float_as_uint(g0) != __float_as_uint(f0) && !(g0 == 0.f && f0 == 0.f));
+      bad += (__float_as_uint(g1) != __float_as_uint(f1) && !(g1 == 0.f && f1 == 0.f));
+      w[k / 4] |= (uint32_t)b << (16 * ((k / 2) & 1));
+    }
+  }
+  *reinterpret_cast<uint4*>(p.out + (int64_t)r * p.Kp + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+  if (bad && p.inexact) atomicAdd(p.inexact, bad);
+}
+
+// One thread per (row, K block of 32): the UE8M0 byte in its atom.
+__global__ void k_pack_scales(const __grid_constant__ PackArgs p) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int kb_all = p.KT * 4;
+  const int64_t total = (int64_t)p.RT * 128 * kb_all;
+  if (i >= total) return;
+  const int r = (int)(i / kb_all), kb = (int)(i % kb_all);
+  uint8_t e = 127;  // 1.0 for padding rows / blocks
+  int bad = 0;
+  if (r < p.R && kb < p.nkb) {
+    const uint32_t s = p.scale[(int64_t)r * p.nkb + kb];
+    const uint32_t ex = (s >> 7) & 0xFF;
+    // a positive normal power of two; UE8M0 holds 2^-127 .. 2^127
+    bad = (s & 0x807Fu) != 0 || ex == 0 || ex == 0xFF;
+    e = (uint8_t)(ex == 0 ? 0 : (ex == 0xFF ? 0xFE : ex));
+  }
+  const int kt = kb / 4, j = kb % 4, rt = r / 128, rr = r % 128;
+  p.sf[((int64_t)kt * p.RT + rt) * 512 + (rr % 32) * 16 + (rr / 32) * 4 + j] = e;
+  if (bad && p.inexact) atomicAdd(p.inexact, 1);
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols_bytes,
+              uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols_bytes, rows};
+  cuuint64_t strides[1] = {cols_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+}  // namespace mx
+}  // namespace vq
+
+using namespace vq::mx;
+
+extern "C" {
+
+int vq_mx_pack_sizes(int64_t rows, int64_t k, int32_t row_multiple, int64_t* codes_bytes,
+                     int64_t* sf_bytes, int64_t* ld_bytes) {
+  if (rows < 0 || k <= 0 || !codes_bytes || !sf_bytes || !ld_bytes) return VQ_ERR_INVALID;
+  if (row_multiple != 128 && row_multiple != 256) return VQ_ERR_INVALID;
+  const int64_t RT = (rows + row_multiple - 1) / row_multiple * (row_multiple / 128);
+  const int64_t KT = (k + 127) / 128;
+  *ld_bytes = KT * 128;
+  *codes_bytes = RT * 128 * KT * 128;
+  *sf_bytes = KT * RT * 512;
+  return VQ_OK;
+}
+
+int vq_mx_pack(const vq_tensor* codes, const vq_tensor* scale, int64_t block_size,
+               int32_t row_multiple, void* packed_codes, void* packed_sf, int32_t* d_inexact,
+               void* stream) {
+  if (!codes || !scale || !packed_codes || !packed_sf) return VQ_ERR_NULL;
+  if (codes->dtype != VQ_BF16 || scale->dtype != VQ_BF16) return VQ_ERR_UNSUPPORTED;
+  if (block_size != 32) return VQ_ERR_UNSUPPORTED;
+  if (codes->ndim != 2 || scale->ndim != 2) return VQ_ERR_SHAPE;
+  const int64_t R = codes->shape[0], K = codes->shape[1];
+  if (scale->shape[0] != R || scale->shape[1] != (K + 31) / 32) return VQ_ERR_SHAPE;
+  if (R <= 0 || K <= 0) return VQ_ERR_INVALID;
+  if (row_multiple != 128 && row_multiple != 256) return VQ_ERR_INVALID;
+  if (R >= (1ll << 31) / 4 || K >= (1 << 24)) return VQ_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(packed_codes) & 15) || (reinterpret_cast<uintptr_t>(packed_sf) & 15))
+    return VQ_ERR_ALIGNMENT;
+  PackArgs p;
+  p.codes = (const uint16_t*)codes->data;
+  p.scale = (const uint16_t*)scale->data;
+  p.out = (uint8_t*)packed_codes;
+  p.sf = (uint8_t*)packed_sf;
+  p.R = (int)R;
+  p.K = (int)K;
+  p.RT = (int)((R + row_multiple - 1) / row_multiple * (row_multiple / 128));
+  p.KT = (int)((K + 127) / 128);
+  p.Kp = p.KT * 128;
+  p.nkb = (int)((K + 31) / 32);
+  p.inexact = d_inexact;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (d_inexact && cudaMemsetAsync(d_inexact, 0, sizeof(int32_t), st) != cudaSuccess)
+    return VQ_ERR_CUDA;
+  const int64_t n1 = (int64_t)p.RT * 128 * (p.Kp / 16);
+  k_pack_codes<<<(unsigned)((n1 + 255) / 256), 256, 0, st>>>(p);
+  const int64_t n2 = (int64_t)p.RT * 128 * p.KT * 4;
+  k_pack_scales<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
+}
+
+int vq_gemm_mxf8(const void* a, const void* a_sf, const void* b, const void* b_sf, int64_t M,
+                 int64_t N, int64_t K, const void* bias, void* out, int64_t ldo, int32_t* d_err,
+                 void* stream) {
+  if (!a || !a_sf || !b || !b_sf || !out || !d_err) return VQ_ERR_NULL;
+  if (M <= 0 || N <= 0 || K <= 0) return VQ_ERR_INVALID;
+  if (N % 8 != 0 || ldo < N || ldo % 8 != 0) return VQ_ERR_UNSUPPORTED;
+  if (M > (1 << 30) || N > (1 << 30)) return VQ_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(a) & 15) ||
+      (reinterpret_cast<uintptr_t>(b) & 15) || (reinterpret_cast<uintptr_t>(a_sf) & 15) ||
+      (reinterpret_cast<uintptr_t>(b_sf) & 15))
+    return VQ_ERR_ALIGNMENT;
+  const int64_t KT = (K + 127) / 128, Kp = KT * 128;
+  const int64_t MT = (M + 127) / 128;
+  // B is packed over 128-row chunks; a 256-wide tile reads two chunks, so
+  // the packed B must hold an even number of chunks (the caller pads).
+  const int64_t NTILE_N = (N + BN - 1) / BN;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, a, MT * 128, Kp, BM) || !make_map(&mb, b, NTILE_N * 2 * 128, Kp, BN))
+    return VQ_ERR_CUDA;
+  GemmArgs g;
+  g.sfa = (const uint8_t*)a_sf;
+  g.sfb = (const uint8_t*)b_sf;
+  g.bias = (const uint16_t*)bias;
+  g.out = (uint16_t*)out;
+  g.ldo = ldo;
+  g.M = (int)M;
+  g.N = (int)N;
+  g.KT = (int)KT;
+  g.MT = (int)MT;
+  g.NT128 = (int)(NTILE_N * 2);
+  g.NTILE_N = (int)NTILE_N;
+  g.ntiles = (int)(MT * NTILE_N);
+  g.err = d_err;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int smem = SmemLayout::kTotal + 1024;
+  if (cudaFuncSetAttribute(k_gemm_mxf8, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
+    return VQ_ERR_CUDA;
+  if (cudaMemsetAsync(d_err, 0, sizeof(int32_t), st) != cudaSuccess) return VQ_ERR_CUDA;
+  const int grid = (int)std::min<int64_t>(g.ntiles, sm_count());
+  k_gemm_mxf8<<<grid, THREADS, smem, st>>>(ma, mb, g);
+  return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -94,6 +94,14 @@ _SIGNATURES = {
     "vq_quantize_mx": (ctypes.c_int, [P(VqTensor), P(VqRounder), P(ctypes.c_int64), ctypes.c_int32,
                                       ctypes.c_int64, ctypes.c_float, ctypes.c_int32, ctypes.c_int32,
                                       P(VqRounder), P(VqTensor), P(VqTensor), ctypes.c_void_p]),
+    "vq_mx_pack_sizes": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                        P(ctypes.c_int64), P(ctypes.c_int64), P(ctypes.c_int64)]),
+    "vq_mx_pack": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_int64, ctypes.c_int32,
+                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_gemm_mxf8": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                    ctypes.c_void_p, ctypes.c_void_p]),
     "vq_rounder_check_hw": (ctypes.c_int, [P(VqRounder), ctypes.c_void_p, ctypes.c_void_p]),
     "vq_quantize_affine_qparams": (ctypes.c_int, [P(VqTensor), P(ctypes.c_int64), ctypes.c_int32,
                                                   ctypes.c_int64, ctypes.c_float, ctypes.c_float,

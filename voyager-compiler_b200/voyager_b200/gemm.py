@@ -66,7 +66,9 @@ def linear_mx(input, weight, bias=None, *, input_scale=None, weight_scale=None,
 
     if mxgemm.applies(input, weight, input_scale, weight_scale, block_size, input_code,
                       weight_code, weight_layout, "linear"):
-        return mxgemm.linear(input, weight, bias, input_scale, weight_scale)
+        out = mxgemm.linear(input, weight, bias, input_scale, weight_scale)
+        if out is not None:
+            return out
     a = dequantize_mx(input, input_scale, input_code, block_size)
     w = _weight_dequant(weight, weight_scale, weight_code, block_size)
     if weight_layout == "ck":

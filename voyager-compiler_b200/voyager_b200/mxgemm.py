@@ -1,5 +1,131 @@
-"""tcgen05 block-scaled MXFP8 GEMM (placeholder until the kernel lands)."""
+"""MXFP8 ``linear_mx`` on the tcgen05 block-scaled tensor cores.
+
+Applies when both operands are E4M3 codes (bf16 values) with power-of-two
+block-32 scales along K, blocks along the last dim of both ``input`` [.., K]
+and ``weight`` [N, K] (``weight_layout="kc"``), no codebooks, bf16 everywhere
+(SURVEY config C3: ``fp8_e4m3,qs=microscaling,bs=32`` with
+``--force_scale_power_of_two``).  The product equals the reference's
+dequantize-then-matmul (``quantized.py:455-586``) up to the float32
+summation order: E4M3 x 2^e values are exact in bf16, and the tensor cores
+multiply them exactly and accumulate in float32.
+
+Operands are packed to E4M3 bytes + UE8M0 scale atoms (``vq_mx_pack``).
+Weights are packed once and cached per (tensor, version).  An operand whose
+provenance is unknown is packed with an exactness count that is checked on
+the host (one synchronisation); activations produced by this package's
+``quantize_mx`` with an E4M3 table and power-of-two scales are vouched for
+and skip it.
+"""
+
+import ctypes
+import os
+
+import torch
+
+from voyager_b200 import _lib
+from voyager_b200._cache import TensorCache
+
+# codes tensors produced by quantize_mx with (E4M3 table, pow2 scales, block
+# 32, last-dim blocks): (version, scale tensor id)
+_vouched = TensorCache()
+_wcache = TensorCache()
+
+CHECK_ERRORS = os.environ.get("VQ_CHECK_ERRORS", "0") == "1"
 
 
-def applies(*args, **kwargs) -> bool:
-    return False
+def vouch(codes: torch.Tensor, scale: torch.Tensor):
+    _vouched.put(codes, "mxfp8", (codes._version, id(scale), scale._version))
+
+
+def _is_vouched(codes, scale) -> bool:
+    v = _vouched.get(codes, "mxfp8")
+    return v is not None and v == (codes._version, id(scale), scale._version)
+
+
+def applies(input, weight, input_scale, weight_scale, block_size, input_code, weight_code,
+            weight_layout, op) -> bool:
+    if op != "linear" or weight_layout != "kc" or block_size != 32:
+        return False
+    if input_code is not None or weight_code is not None:
+        return False
+    if input_scale is None or weight_scale is None:
+        return False
+    ts = (input, weight, input_scale, weight_scale)
+    if any(t.dtype != torch.bfloat16 or not t.is_cuda for t in ts):
+        return False
+    if weight.dim() != 2 or input.dim() < 1 or input.shape[-1] != weight.shape[1]:
+        return False
+    K, N = weight.shape[1], weight.shape[0]
+    nkb = (K + 31) // 32
+    if tuple(weight_scale.shape) != (N, nkb):
+        return False
+    if tuple(input_scale.shape) != tuple(input.shape[:-1]) + (nkb,):
+        return False
+    if N % 8 != 0 or input.numel() == 0:
+        return False
+    return True
+
+
+def _pack(codes2d: torch.Tensor, scale2d: torch.Tensor, row_multiple: int, check: bool):
+    lib = _lib.load()
+    R, K = codes2d.shape
+    cb, sb, ld = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+    _lib.check(lib.vq_mx_pack_sizes(R, K, row_multiple, ctypes.byref(cb), ctypes.byref(sb),
+                                    ctypes.byref(ld)), "mx pack sizes")
+    dev = codes2d.device
+    pc = torch.empty(cb.value, dtype=torch.uint8, device=dev)
+    ps = torch.empty(sb.value, dtype=torch.uint8, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
+    from voyager_b200.ops import _ref, _stream, _vt
+
+    st = lib.vq_mx_pack(_ref(_vt(codes2d)), _ref(_vt(scale2d)), 32, row_multiple,
+                        pc.data_ptr(), ps.data_ptr(), bad.data_ptr() if check else None,
+                        _stream(dev))
+    _lib.check(st, "quantized_ops::linear_mx (pack)")
+    ok = True
+    if check:
+        ok = int(bad.item()) == 0
+    return pc, ps, ok
+
+
+def packed_weight(weight, weight_scale):
+    key = (weight._version, id(weight_scale), weight_scale._version)
+    hit = _wcache.get(weight, key)
+    if hit is not None:
+        return hit
+    pc, ps, ok = _pack(weight.contiguous(), weight_scale.contiguous(), 256, True)
+    return _wcache.put(weight, key, (pc, ps, ok))
+
+
+def linear(input, weight, bias, input_scale, weight_scale):
+    """MXFP8 linear; returns None when an operand turns out not to be exact
+    E4M3 / power-of-two (the caller then takes the dequantize path)."""
+    if bias is not None and (bias.dtype != torch.bfloat16 or bias.dim() != 1
+                             or bias.shape[0] != weight.shape[0] or not bias.is_cuda):
+        return None
+    pw, pws, wok = packed_weight(weight, weight_scale)
+    if not wok:
+        return None
+    K, N = weight.shape[1], weight.shape[0]
+    a2 = input.reshape(-1, K).contiguous()
+    s2 = input_scale.reshape(-1, input_scale.shape[-1]).contiguous()
+    M = a2.shape[0]
+    pa, pas, aok = _pack(a2, s2, 128, not _is_vouched(input, input_scale))
+    if not aok:
+        return None
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=input.device)
+    err = torch.empty(1, dtype=torch.int32, device=input.device)
+    b = bias.contiguous() if bias is not None else None
+    from voyager_b200.ops import _stream
+
+    st = _lib.load().vq_gemm_mxf8(pa.data_ptr(), pas.data_ptr(), pw.data_ptr(), pws.data_ptr(),
+                                  M, N, K, b.data_ptr() if b is not None else None,
+                                  out.data_ptr(), N, err.data_ptr(), _stream(input.device))
+    _lib.check(st, "quantized_ops::linear_mx (tcgen05 MXFP8)")
+    if CHECK_ERRORS and int(err.item()) != 0:
+        raise _lib.VqError(f"linear_mx: device wait timed out (code {int(err.item())})")
+    return out.reshape(tuple(input.shape[:-1]) + (N,))
+
+
+def last_error(err: torch.Tensor) -> int:
+    return int(err.item())

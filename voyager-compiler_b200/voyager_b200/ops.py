@@ -213,6 +213,14 @@ def quantize_mx(input: torch.Tensor, qmap: torch.Tensor, axes, block_size: int,
                               sq.ref() if sq else None, _ref(_vt(scale)), _ref(_vt(codes)),
                               _stream(dev))
     _lib.check(st, "quantized_ops::quantize_mx")
+    if (block_size == 32 and ax == [x.dim() - 1] and force_scale_power_of_two
+            and x.dtype == torch.bfloat16 and rd.c.kind == _lib.VQ_R_MINIFLOAT
+            and rd.c.ebits == 4 and rd.c.mbits == 3 and rd.c.is_signed and rd.c.max_norm == 448.0):
+        # E4M3 codes with power-of-two scales: the MXFP8 GEMM may take them
+        # without re-checking
+        from voyager_b200 import mxgemm
+
+        mxgemm.vouch(codes, scale)
     return scale, codes
 
 
