@@ -40,7 +40,8 @@ typedef enum vq_status {
   VQ_ERR_CUDA = 4,         /* a CUDA runtime call failed                   */
   VQ_ERR_SHAPE = 5,        /* shapes do not broadcast as the op requires   */
   VQ_ERR_NULL = 6,         /* required pointer is NULL                     */
-  VQ_ERR_TIMEOUT = 7       /* a bounded device wait gave up                */
+  VQ_ERR_TIMEOUT = 7,      /* a bounded device wait gave up                */
+  VQ_ERR_TOO_LARGE = 8     /* problem exceeds a fixed-size scratch area    */
 } vq_status;
 
 typedef enum vq_dtype {
@@ -210,6 +211,31 @@ int vq_mx_pack(const vq_tensor* codes, const vq_tensor* scale, int64_t block_siz
 int vq_gemm_mxf8(const void* a, const void* a_sf, const void* b, const void* b_sf, int64_t M,
                  int64_t N, int64_t K, const void* bias, void* out, int64_t ldo, int32_t* d_err,
                  void* stream);
+
+/* MXFP8 linear that allocates nothing: for callers that cannot call
+ * cudaMalloc -- an allocator-free runtime, code running under a caller-owned
+ * memory budget, or a library hook invoked where allocating is not allowed.
+ * This entry point has no counterpart in the reference; it is the
+ * vq_mx_pack + vq_gemm_mxf8 pair with the packed activations and the
+ * kernel's error word kept in a fixed device array inside the library
+ * (VQ_NOALLOC_SCRATCH_BYTES per GPU, held from first use until exit).
+ *   a_codes  bf16 [M, K] E4M3 codes, a_scale bf16 [M, ceil(K/32)] powers of two
+ *   w_packed / w_sf_packed  the weight as vq_mx_pack wrote it (row_multiple
+ *            256) into caller memory; N its rows
+ *   out      bf16 [M, ldo], caller memory
+ * Rejects with VQ_ERR_TOO_LARGE, before launching anything, when the packed
+ * activations do not fit: with Mp = round_up(M, 128) and Kp = round_up(K, 128),
+ * 256 + round_up(Mp * Kp, 256) + (Mp / 128) * (Kp / 128) * 512 bytes must be
+ * at most VQ_NOALLOC_SCRATCH_BYTES (16 MiB: e.g. M = 2048 rows at K = 4096,
+ * or M = 8192 at K = 1920).  The operand
+ * exactness check of vq_mx_pack is not run: the codes must be E4M3 values
+ * and the scales normal powers of two.  The first call on a device looks up
+ * the array's device address (make it before any stream capture).  Every
+ * call reuses the one array: calls that overlap on the GPU race. */
+#define VQ_NOALLOC_SCRATCH_BYTES (16u << 20)
+int vq_linear_mxf8_noalloc(const vq_tensor* a_codes, const vq_tensor* a_scale,
+                           const void* w_packed, const void* w_sf_packed, int64_t N,
+                           const void* bias, void* out, int64_t ldo, void* stream);
 
 /* The per-block parameters of quantized_ops::quantize_affine
  * (quantized.py:884-948): for blocks of `block_size` elements along the one

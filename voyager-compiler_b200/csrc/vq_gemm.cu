@@ -30,6 +30,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "vq_numerics.cuh"
 
@@ -452,6 +453,38 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
+// ---------------------------------------------------------------------------
+// Scratch for vq_linear_mxf8_noalloc: a file-scope device array, one copy per
+// GPU that loads the library, held until the process exits.  Layout: the
+// kernel's error word (first 256 bytes), then the packed activation codes,
+// then their scale atoms.  Every call reuses it, so calls that overlap on
+// the GPU (different streams, or graph replays in flight together) race.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_noalloc_scratch[VQ_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch, looked up once per device with that
+// device current (host code may not use the symbol itself as an address).
+uint8_t* noalloc_scratch_ptr(int* status) {
+  static std::mutex mu;
+  static uint8_t* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = VQ_ERR_CUDA;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+      *status = VQ_ERR_CUDA;
+      return nullptr;
+    }
+    ptrs[dev] = static_cast<uint8_t*>(p);
+  }
+  *status = VQ_OK;
+  return ptrs[dev];
+}
+
 }  // namespace mx
 }  // namespace vq
 
@@ -549,6 +582,30 @@ int vq_gemm_mxf8(const void* a, const void* a_sf, const void* b, const void* b_s
   const int grid = (int)std::min<int64_t>(g.ntiles, sm_count());
   k_gemm_mxf8<<<grid, THREADS, smem, st>>>(ma, mb, g);
   return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
+}
+
+int vq_linear_mxf8_noalloc(const vq_tensor* a_codes, const vq_tensor* a_scale,
+                           const void* w_packed, const void* w_sf_packed, int64_t N,
+                           const void* bias, void* out, int64_t ldo, void* stream) {
+  if (!a_codes || !a_scale || !w_packed || !w_sf_packed || !out) return VQ_ERR_NULL;
+  if (a_codes->dtype != VQ_BF16 || a_scale->dtype != VQ_BF16) return VQ_ERR_UNSUPPORTED;
+  if (a_codes->ndim != 2) return VQ_ERR_SHAPE;
+  const int64_t M = a_codes->shape[0], K = a_codes->shape[1];
+  if (M <= 0 || K <= 0 || N <= 0) return VQ_ERR_INVALID;
+  int64_t cb = 0, sb = 0, ld = 0;
+  int st = vq_mx_pack_sizes(M, K, 128, &cb, &sb, &ld);
+  if (st) return st;
+  // error word, packed codes, scale atoms; each region 256-byte aligned
+  const int64_t codes_off = 256, sf_off = codes_off + (cb + 255) / 256 * 256;
+  if (sf_off + sb > (int64_t)VQ_NOALLOC_SCRATCH_BYTES) return VQ_ERR_TOO_LARGE;
+  uint8_t* base = noalloc_scratch_ptr(&st);
+  if (!base) return st;
+  int32_t* err = reinterpret_cast<int32_t*>(base);
+  if ((st = vq_mx_pack(a_codes, a_scale, 32, 128, base + codes_off, base + sf_off, nullptr,
+                       stream)))
+    return st;
+  return vq_gemm_mxf8(base + codes_off, base + sf_off, w_packed, w_sf_packed, M, N, K, bias, out,
+                      ldo, err, stream);
 }
 
 }  // extern "C"

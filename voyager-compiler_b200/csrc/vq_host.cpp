@@ -145,6 +145,7 @@ const char* vq_status_string(int status) {
     case VQ_ERR_SHAPE: return "shapes do not broadcast";
     case VQ_ERR_NULL: return "required pointer is NULL";
     case VQ_ERR_TIMEOUT: return "bounded device wait timed out";
+    case VQ_ERR_TOO_LARGE: return "problem exceeds the fixed scratch area";
     default: return "unknown status";
   }
 }

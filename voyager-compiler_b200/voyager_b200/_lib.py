@@ -26,8 +26,10 @@ STATUS = {
     0: "ok", 1: "invalid argument", 2: "unsupported dtype or layout",
     3: "alignment requirement not met", 4: "CUDA runtime error",
     5: "shapes do not broadcast", 6: "required pointer is NULL",
-    7: "bounded device wait timed out",
+    7: "bounded device wait timed out", 8: "problem exceeds the fixed scratch area",
 }
+
+VQ_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 
 class VqTensor(ctypes.Structure):
@@ -102,6 +104,9 @@ _SIGNATURES = {
                                     ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                     ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_linear_mxf8_noalloc": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p,
+                                              ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                              ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
     "vq_rounder_check_hw": (ctypes.c_int, [P(VqRounder), ctypes.c_void_p, ctypes.c_void_p]),
     "vq_quantize_affine_qparams": (ctypes.c_int, [P(VqTensor), P(ctypes.c_int64), ctypes.c_int32,
                                                   ctypes.c_int64, ctypes.c_float, ctypes.c_float,
@@ -145,5 +150,5 @@ class VqError(RuntimeError):
 def check(status: int, what: str):
     if status != 0:
         msg = STATUS.get(status, f"status {status}")
-        exc = ValueError if status in (1, 2, 3, 5, 6) else VqError
+        exc = ValueError if status in (1, 2, 3, 5, 6, 8) else VqError
         raise exc(f"{what}: {msg}")
