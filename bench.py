@@ -335,6 +335,10 @@ def run_ours(args):
     secondary = {}
     if not args.no_secondary and rank == 0:
         secondary = run_secondary(dev, hbm_peak, peaks)
+    if not args.no_secondary and world > 1:
+        tp = run_tp_linear(dev, pg, world)
+        if rank == 0:
+            secondary["c3_tp_linear"] = tp
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -383,6 +387,42 @@ def _time_ms(fn, stream, reps=10, warm=3):
     b.record(stream)
     torch.cuda.synchronize()
     return a.elapsed_time(b) / reps
+
+
+def run_tp_linear(dev, pg, world):
+    """C3 MXFP8 linear, tensor parallel over N (weight shard per rank, NCCL
+    all-gather of the output columns): strong scaling of one [8192, 11008]
+    product.  All ranks take part; max time over ranks."""
+    import torch
+
+    from voyager_b200 import parallel, synth
+    from voyager_b200.tables import get_quantization_map
+
+    Q = torch.ops.quantized_ops
+    a_np, w_np = synth.c3_operands()
+    e4m3 = get_quantization_map("fp8_e4m3", dev)
+    a = torch.from_numpy(a_np.view(np.int16)).view(torch.bfloat16).to(dev)
+    w = torch.from_numpy(w_np.view(np.int16)).view(torch.bfloat16).to(dev)
+    sa, ca = Q.quantize_mx(a, e4m3, [-1], 32, 448.0, True)
+    sw, cw = Q.quantize_mx(w, e4m3, [-1], 32, 448.0, True)
+    lin = parallel.NShardedLinear(cw, sw)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        lin(ca, sa)
+    torch.cuda.synchronize()
+    pg.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    e0.record(stream)
+    for _ in range(reps):
+        lin(ca, sa)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"ms": round(ms, 3), "TFLOPs": round(2 * 8192 * 4096 * 11008 / (ms / 1e3) / 1e12, 1),
+            "gpus": world, "note": "weight N-sharded, output all-gathered (NCCL)"}
 
 
 def run_secondary(dev, hbm_peak, peaks):
