@@ -140,11 +140,15 @@ VQ_HD uint32_t round_minifloat(const vq_rounder& r, uint32_t b) {
 }
 
 // clamp(round_half_even(x), qmin, qmax); a -0 result survives the clamp.
+// Integers of magnitude <= 256 are exactly bf16 values, so for the usual
+// ranges the result's pattern is the top half of the float32; wider ranges
+// (int16 and up) round the clamp bound to bf16 as the table does.
 VQ_HD uint32_t round_int(const vq_rounder& r, uint32_t b) {
   if ((b & 0x7FFFu) > 0x7F80u) return r.nan_bits;
   float y = rint_f(bf2f(b));  // exact in bf16: |x| < 256 rounds to <= 8 bits
   if (y < r.qmin) y = r.qmin;
   if (y > r.qmax) y = r.qmax;
+  if (r.qmax <= 256.0f && r.qmin >= -256.0f) return f2u(y) >> 16;
   return f2bf(y);
 }
 

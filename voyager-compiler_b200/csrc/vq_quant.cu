@@ -650,6 +650,115 @@ __global__ void __launch_bounds__(1024) k_elem2d(const __grid_constant__ Elem2DA
 }
 
 // ---------------------------------------------------------------------------
+// k_rows: quantize / dequantize row by row (the hot layouts)
+// ---------------------------------------------------------------------------
+// A persistent grid walks the rows of the [R, C] view; the CTA's threads
+// stride over one row's vectors.  The scale is per tensor (SL_SCALAR), per
+// row (SL_ROW) or per block of 2^shift columns along the row (SL_2D with
+// str_c = 1 and a power-of-two block), so an element's scale needs no
+// division: row offset + (col >> shift).  Quantize divides by the row's (or
+// block's) Divisor: one reciprocal per distinct scale per thread.
+struct RowsArgs {
+  const void* in;
+  void* out;
+  const void* scale;
+  int32_t scale_bf16;
+  int32_t nrows;
+  int32_t vpr;      // vectors per row (C / VEC)
+  int64_t C;
+  int64_t str_r;    // scale offset per row (0 for SL_SCALAR)
+  int32_t shift;    // SL_2D: log2(block size)
+  vq_rounder qr;
+};
+
+template <typename TIn, typename TOut, bool DEQ, int K, int SL>
+__global__ void __launch_bounds__(1024) k_rows(const __grid_constant__ RowsArgs a) {
+  extern __shared__ __align__(16) uint16_t smem[];
+  if (!DEQ) stage_table<K>(a.qr, smem);
+  constexpr bool IN_BF = sizeof(TIn) == 2;
+  constexpr bool OUT_BF = sizeof(TOut) == 2;
+  constexpr int VEC = 16 / sizeof(TIn);
+  float s = 1.f;
+  Divisor dv = make_divisor(1.f);
+  if (SL == SL_SCALAR) {
+    s = ld_f(a.scale, 0, a.scale_bf16);
+    if (!DEQ) dv = make_divisor(s);
+  }
+  int64_t cached = -1;
+  for (int row = blockIdx.x; row < a.nrows; row += gridDim.x) {
+    if (SL == SL_ROW) {
+      s = ld_f(a.scale, (int64_t)row * a.str_r, a.scale_bf16);
+      if (!DEQ) dv = make_divisor(s);
+    }
+    const TIn* src = reinterpret_cast<const TIn*>(a.in) + (int64_t)row * a.C;
+    TOut* dst = reinterpret_cast<TOut*>(a.out) + (int64_t)row * a.C;
+    for (int v = threadIdx.x; v < a.vpr; v += blockDim.x) {
+      const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(src) + v);
+      if (SL == SL_2D) {
+        const int64_t off = (int64_t)row * a.str_r + (((int64_t)v * VEC) >> a.shift);
+        if (off != cached) {
+          cached = off;
+          s = ld_f(a.scale, off, a.scale_bf16);
+          if (!DEQ) dv = make_divisor(s);
+        }
+      }
+      const TIn* x = reinterpret_cast<const TIn*>(&raw);
+      uint32_t ob[VEC];
+      float of[VEC];
+      if (!DEQ) {
+        float t[VEC];
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float xf = IN_BF ? bf2f(*reinterpret_cast<const uint16_t*>(&x[j]))
+                                 : *reinterpret_cast<const float*>(&x[j]);
+          t[j] = div_to_bf16_domain(xf, dv);
+        }
+#pragma unroll
+        for (int j = 0; j < VEC; j += 2) {
+          const uint32_t c2 = round_pair<K>(a.qr, pair_index<K>(t[j], t[j + 1]), smem);
+          ob[j] = c2 & 0xFFFFu;
+          ob[j + 1] = c2 >> 16;
+          of[j] = __uint_as_float(c2 << 16);
+          of[j + 1] = __uint_as_float(c2 & 0xFFFF0000u);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float xf = IN_BF ? bf2f(*reinterpret_cast<const uint16_t*>(&x[j]))
+                                 : *reinterpret_cast<const float*>(&x[j]);
+          float w = fmul_rn(xf, s);
+          if (OUT_BF) {
+            ob[j] = f2bf(w);
+          } else {
+            of[j] = w;
+          }
+        }
+      }
+      if (OUT_BF) {
+        uint4 o;
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int j = 0; j < VEC / 2; ++j) ow[j] = ob[2 * j] | (ob[2 * j + 1] << 16);
+        if (VEC == 8) {
+          __stcs(reinterpret_cast<uint4*>(dst) + v, o);
+        } else {  // fp32 in, bf16 out does not arise (promotion)
+          *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(dst) + (int64_t)v * VEC) =
+              make_uint2(ow[0], ow[1]);
+        }
+      } else {
+        TOut* d = dst + (int64_t)v * VEC;
+        if (VEC == 4) {
+          __stcs(reinterpret_cast<float4*>(d), make_float4(of[0], of[1], of[2], of[3]));
+        } else {
+          __stcs(reinterpret_cast<float4*>(d), make_float4(of[0], of[1], of[2], of[3]));
+          __stcs(reinterpret_cast<float4*>(d) + 1, make_float4(of[4], of[5], of[6], of[7]));
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // k_elem: quantize / dequantize with broadcast or expand()ed operands
 // ---------------------------------------------------------------------------
 constexpr int kElemDims = 4;
@@ -1054,6 +1163,53 @@ void fill_map2d(Map2D& m, const void* ptr, int dtype, const DimMap& r, const Dim
   m.uniform_vec = (c.str == 0) || (c.div % vec == 0);
 }
 
+template <typename TIn, typename TOut, bool DEQ, int K, int SL>
+int launch_rows(RowsArgs& a, cudaStream_t st) {
+  auto kern = k_rows<TIn, TOut, DEQ, K, SL>;
+  const int smem = (!DEQ && K == VQ_R_TABLE) ? kTableBytes : 0;
+  const int sms = num_sms();
+  int threads, blocks;
+  if (smem) {
+    threads = 1024;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return VQ_ERR_CUDA;
+    blocks = sms;
+  } else {
+    threads = 256;
+    blocks = sms * 8;
+  }
+  if (a.vpr < threads) threads = std::max(32, (a.vpr + 31) / 32 * 32);
+  if (blocks > a.nrows) blocks = std::max(a.nrows, 1);
+  kern<<<blocks, threads, smem, st>>>(a);
+  return cuda_status(cudaGetLastError());
+}
+
+template <typename TIn, typename TOut, bool DEQ, int SL>
+int dispatch_rows_kind(RowsArgs& a, int K, cudaStream_t st) {
+  if (DEQ) return launch_rows<TIn, TOut, DEQ, VQ_R_IDENTITY, SL>(a, st);
+  switch (K) {
+    case VQ_R_IDENTITY: return launch_rows<TIn, TOut, DEQ, VQ_R_IDENTITY, SL>(a, st);
+    case VQ_R_MINIFLOAT: return launch_rows<TIn, TOut, DEQ, VQ_R_MINIFLOAT, SL>(a, st);
+    case VQ_R_INT: return launch_rows<TIn, TOut, DEQ, VQ_R_INT, SL>(a, st);
+    case K_HW_E4M3: return launch_rows<TIn, TOut, DEQ, K_HW_E4M3, SL>(a, st);
+    case K_HW_E5M2: return launch_rows<TIn, TOut, DEQ, K_HW_E5M2, SL>(a, st);
+    case K_HW_E2M1: return launch_rows<TIn, TOut, DEQ, K_HW_E2M1, SL>(a, st);
+    default: return launch_rows<TIn, TOut, DEQ, VQ_R_TABLE, SL>(a, st);
+  }
+}
+
+template <bool DEQ, int SL>
+int dispatch_rows(RowsArgs& a, int in_dt, int out_dt, int K, cudaStream_t st) {
+  if (in_dt == VQ_BF16 && out_dt == VQ_BF16)
+    return dispatch_rows_kind<uint16_t, uint16_t, DEQ, SL>(a, K, st);
+  if (in_dt == VQ_BF16 && out_dt == VQ_F32)
+    return dispatch_rows_kind<uint16_t, float, DEQ, SL>(a, K, st);
+  if (in_dt == VQ_F32 && out_dt == VQ_F32)
+    return dispatch_rows_kind<float, float, DEQ, SL>(a, K, st);
+  return VQ_ERR_UNSUPPORTED;
+}
+
 void fill_operand(OperandMap& om, const vq_tensor* t, const DimMap* m, int vec) {
   om.ptr = t ? t->data : nullptr;
   om.is_bf16 = t ? (t->dtype == VQ_BF16) : 0;
@@ -1129,6 +1285,29 @@ int run_elementwise(const vq_tensor* input, const vq_tensor* scale, const vq_ten
     }
     const int Kq = elem_kind(qr);
     cudaStream_t cs2 = reinterpret_cast<cudaStream_t>(stream);
+    // the row kernel: no zero point, no qmaps, 16-byte vectors, scale per
+    // tensor / per row / per power-of-two block along the row
+    const bool pow2_blk = SL == SL_2D && sc.str == 1 && sc.div >= vec && (sc.div & (sc.div - 1)) == 0;
+    if (!zp && !inq && !outq && vec_ok && R < (1ll << 31) && C / vec < (1ll << 31) &&
+        (SL == SL_SCALAR || SL == SL_ROW || pow2_blk) && sr.div == 1) {
+      RowsArgs ra;
+      memset(&ra, 0, sizeof(ra));
+      ra.in = input->data;
+      ra.out = out->data;
+      ra.scale = scale->data;
+      ra.scale_bf16 = scale->dtype == VQ_BF16;
+      ra.nrows = (int32_t)R;
+      ra.vpr = (int32_t)(C / vec);
+      ra.C = C;
+      ra.str_r = sr.str;
+      int sh = 0;
+      while ((1ll << sh) < sc.div) ++sh;
+      ra.shift = sh;
+      if (qr) ra.qr = *qr;
+      if (SL == SL_SCALAR) return dispatch_rows<DEQ, SL_SCALAR>(ra, in_dt, out_dt, Kq, cs2);
+      if (SL == SL_ROW) return dispatch_rows<DEQ, SL_ROW>(ra, in_dt, out_dt, Kq, cs2);
+      return dispatch_rows<DEQ, SL_2D>(ra, in_dt, out_dt, Kq, cs2);
+    }
     if (C > ((int64_t)1 << 30)) return VQ_ERR_UNSUPPORTED;
     int64_t rows_per = std::max<int64_t>(1, ((int64_t)1 << 30) / C);
     const int64_t od = std::max(sr.div, zr.div);
