@@ -665,6 +665,7 @@ struct RowsArgs {
   int32_t scale_bf16;
   int32_t nrows;
   int32_t vpr;      // vectors per row (C / VEC)
+  int64_t nvec;     // vectors in the whole tensor (a scalar scale's last row may be short)
   int64_t C;
   int64_t str_r;    // scale offset per row (0 for SL_SCALAR)
   int32_t shift;    // SL_2D: log2(block size)
@@ -692,7 +693,8 @@ __global__ void __launch_bounds__(1024) k_rows(const __grid_constant__ RowsArgs 
     }
     const TIn* src = reinterpret_cast<const TIn*>(a.in) + (int64_t)row * a.C;
     TOut* dst = reinterpret_cast<TOut*>(a.out) + (int64_t)row * a.C;
-    for (int v = threadIdx.x; v < a.vpr; v += blockDim.x) {
+    const int vend = (int)min((int64_t)a.vpr, a.nvec - (int64_t)row * a.vpr);
+    for (int v = threadIdx.x; v < vend; v += blockDim.x) {
       const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(src) + v);
       if (SL == SL_2D) {
         const int64_t off = (int64_t)row * a.str_r + (((int64_t)v * VEC) >> a.shift);
@@ -1288,8 +1290,8 @@ int run_elementwise(const vq_tensor* input, const vq_tensor* scale, const vq_ten
     // the row kernel: no zero point, no qmaps, 16-byte vectors, scale per
     // tensor / per row / per power-of-two block along the row
     const bool pow2_blk = SL == SL_2D && sc.str == 1 && sc.div >= vec && (sc.div & (sc.div - 1)) == 0;
-    if (!zp && !inq && !outq && vec_ok && R < (1ll << 31) && C / vec < (1ll << 31) &&
-        (SL == SL_SCALAR || SL == SL_ROW || pow2_blk) && sr.div == 1) {
+    if (!zp && !inq && !outq && vec_ok && R * (C / vec) < (1ll << 40) && C / vec < (1ll << 31) &&
+        (SL == SL_SCALAR || ((SL == SL_ROW || pow2_blk) && R >= 4 * num_sms())) && sr.div == 1) {
       RowsArgs ra;
       memset(&ra, 0, sizeof(ra));
       ra.in = input->data;
@@ -1298,7 +1300,16 @@ int run_elementwise(const vq_tensor* input, const vq_tensor* scale, const vq_ten
       ra.scale_bf16 = scale->dtype == VQ_BF16;
       ra.nrows = (int32_t)R;
       ra.vpr = (int32_t)(C / vec);
+      ra.nvec = R * (C / vec);
       ra.C = C;
+      if (SL == SL_SCALAR) {
+        // rows carry no meaning for a per-tensor scale: cut the tensor into
+        // rows of 1024 vectors so every SM gets work
+        const int64_t nv = R * (C / vec);
+        ra.vpr = (int32_t)std::min<int64_t>(nv, 1024);
+        ra.nrows = (int32_t)((nv + ra.vpr - 1) / ra.vpr);
+        ra.C = (int64_t)ra.vpr * vec;
+      }
       ra.str_r = sr.str;
       int sh = 0;
       while ((1ll << sh) < sc.div) ++sh;
