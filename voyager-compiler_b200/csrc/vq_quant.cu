@@ -694,66 +694,75 @@ __global__ void __launch_bounds__(1024) k_rows(const __grid_constant__ RowsArgs 
     const TIn* src = reinterpret_cast<const TIn*>(a.in) + (int64_t)row * a.C;
     TOut* dst = reinterpret_cast<TOut*>(a.out) + (int64_t)row * a.C;
     const int vend = (int)min((int64_t)a.vpr, a.nvec - (int64_t)row * a.vpr);
-    for (int v = threadIdx.x; v < vend; v += blockDim.x) {
-      const uint4 raw = __ldcs(reinterpret_cast<const uint4*>(src) + v);
-      if (SL == SL_2D) {
-        const int64_t off = (int64_t)row * a.str_r + (((int64_t)v * VEC) >> a.shift);
-        if (off != cached) {
-          cached = off;
-          s = ld_f(a.scale, off, a.scale_bf16);
-          if (!DEQ) dv = make_divisor(s);
-        }
-      }
-      const TIn* x = reinterpret_cast<const TIn*>(&raw);
-      uint32_t ob[VEC];
-      float of[VEC];
-      if (!DEQ) {
-        float t[VEC];
+    for (int v0 = threadIdx.x; v0 < vend; v0 += 2 * blockDim.x) {
+      uint4 raws[2];
+      const int vv[2] = {v0, v0 + (int)blockDim.x};
+      raws[0] = __ldcs(reinterpret_cast<const uint4*>(src) + vv[0]);
+      if (vv[1] < vend) raws[1] = __ldcs(reinterpret_cast<const uint4*>(src) + vv[1]);
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-          const float xf = IN_BF ? bf2f(*reinterpret_cast<const uint16_t*>(&x[j]))
-                                 : *reinterpret_cast<const float*>(&x[j]);
-          t[j] = div_to_bf16_domain(xf, dv);
-        }
-#pragma unroll
-        for (int j = 0; j < VEC; j += 2) {
-          const uint32_t c2 = round_pair<K>(a.qr, pair_index<K>(t[j], t[j + 1]), smem);
-          ob[j] = c2 & 0xFFFFu;
-          ob[j + 1] = c2 >> 16;
-          of[j] = __uint_as_float(c2 << 16);
-          of[j + 1] = __uint_as_float(c2 & 0xFFFF0000u);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-          const float xf = IN_BF ? bf2f(*reinterpret_cast<const uint16_t*>(&x[j]))
-                                 : *reinterpret_cast<const float*>(&x[j]);
-          float w = fmul_rn(xf, s);
-          if (OUT_BF) {
-            ob[j] = f2bf(w);
-          } else {
-            of[j] = w;
+      for (int u = 0; u < 2; ++u) {
+        const int v = vv[u];
+        if (v >= vend) break;
+        const uint4 raw = raws[u];
+        if (SL == SL_2D) {
+          const int64_t off = (int64_t)row * a.str_r + (((int64_t)v * VEC) >> a.shift);
+          if (off != cached) {
+            cached = off;
+            s = ld_f(a.scale, off, a.scale_bf16);
+            if (!DEQ) dv = make_divisor(s);
           }
         }
-      }
-      if (OUT_BF) {
-        uint4 o;
-        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+        const TIn* x = reinterpret_cast<const TIn*>(&raw);
+        uint32_t ob[VEC];
+        float of[VEC];
+        if (!DEQ) {
+          float t[VEC];
 #pragma unroll
-        for (int j = 0; j < VEC / 2; ++j) ow[j] = ob[2 * j] | (ob[2 * j + 1] << 16);
-        if (VEC == 8) {
-          __stcs(reinterpret_cast<uint4*>(dst) + v, o);
-        } else {  // fp32 in, bf16 out does not arise (promotion)
-          *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(dst) + (int64_t)v * VEC) =
-              make_uint2(ow[0], ow[1]);
-        }
-      } else {
-        TOut* d = dst + (int64_t)v * VEC;
-        if (VEC == 4) {
-          __stcs(reinterpret_cast<float4*>(d), make_float4(of[0], of[1], of[2], of[3]));
+          for (int j = 0; j < VEC; ++j) {
+            const float xf = IN_BF ? bf2f(*reinterpret_cast<const uint16_t*>(&x[j]))
+                                   : *reinterpret_cast<const float*>(&x[j]);
+            t[j] = div_to_bf16_domain(xf, dv);
+          }
+#pragma unroll
+          for (int j = 0; j < VEC; j += 2) {
+            const uint32_t c2 = round_pair<K>(a.qr, pair_index<K>(t[j], t[j + 1]), smem);
+            ob[j] = c2 & 0xFFFFu;
+            ob[j + 1] = c2 >> 16;
+            of[j] = __uint_as_float(c2 << 16);
+            of[j + 1] = __uint_as_float(c2 & 0xFFFF0000u);
+          }
         } else {
-          __stcs(reinterpret_cast<float4*>(d), make_float4(of[0], of[1], of[2], of[3]));
-          __stcs(reinterpret_cast<float4*>(d) + 1, make_float4(of[4], of[5], of[6], of[7]));
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            const float xf = IN_BF ? bf2f(*reinterpret_cast<const uint16_t*>(&x[j]))
+                                   : *reinterpret_cast<const float*>(&x[j]);
+            float w = fmul_rn(xf, s);
+            if (OUT_BF) {
+              ob[j] = f2bf(w);
+            } else {
+              of[j] = w;
+            }
+          }
+        }
+        if (OUT_BF) {
+          uint4 o;
+          uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int j = 0; j < VEC / 2; ++j) ow[j] = ob[2 * j] | (ob[2 * j + 1] << 16);
+          if (VEC == 8) {
+            __stcs(reinterpret_cast<uint4*>(dst) + v, o);
+          } else {  // fp32 in, bf16 out does not arise (promotion)
+            *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(dst) + (int64_t)v * VEC) =
+                make_uint2(ow[0], ow[1]);
+          }
+        } else {
+          TOut* d = dst + (int64_t)v * VEC;
+          if (VEC == 4) {
+            __stcs(reinterpret_cast<float4*>(d), make_float4(of[0], of[1], of[2], of[3]));
+          } else {
+            __stcs(reinterpret_cast<float4*>(d), make_float4(of[0], of[1], of[2], of[3]));
+            __stcs(reinterpret_cast<float4*>(d) + 1, make_float4(of[4], of[5], of[6], of[7]));
+          }
         }
       }
     }
@@ -1304,9 +1313,9 @@ int run_elementwise(const vq_tensor* input, const vq_tensor* scale, const vq_ten
       ra.C = C;
       if (SL == SL_SCALAR) {
         // rows carry no meaning for a per-tensor scale: cut the tensor into
-        // rows of 1024 vectors so every SM gets work
+        // rows of 2048 vectors so every SM gets work
         const int64_t nv = R * (C / vec);
-        ra.vpr = (int32_t)std::min<int64_t>(nv, 1024);
+        ra.vpr = (int32_t)std::min<int64_t>(nv, 2048);
         ra.nrows = (int32_t)((nv + ra.vpr - 1) / ra.vpr);
         ra.C = (int64_t)ra.vpr * vec;
       }
