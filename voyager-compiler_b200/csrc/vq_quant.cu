@@ -672,7 +672,7 @@ struct RowsArgs {
   vq_rounder qr;
 };
 
-template <typename TIn, typename TOut, bool DEQ, int K, int SL>
+template <typename TIn, typename TOut, bool DEQ, int K, int SL, int U>
 __global__ void __launch_bounds__(1024) k_rows(const __grid_constant__ RowsArgs a) {
   extern __shared__ __align__(16) uint16_t smem[];
   if (!DEQ) stage_table<K>(a.qr, smem);
@@ -694,13 +694,16 @@ __global__ void __launch_bounds__(1024) k_rows(const __grid_constant__ RowsArgs 
     const TIn* src = reinterpret_cast<const TIn*>(a.in) + (int64_t)row * a.C;
     TOut* dst = reinterpret_cast<TOut*>(a.out) + (int64_t)row * a.C;
     const int vend = (int)min((int64_t)a.vpr, a.nvec - (int64_t)row * a.vpr);
-    for (int v0 = threadIdx.x; v0 < vend; v0 += 2 * blockDim.x) {
-      uint4 raws[2];
-      const int vv[2] = {v0, v0 + (int)blockDim.x};
-      raws[0] = __ldcs(reinterpret_cast<const uint4*>(src) + vv[0]);
-      if (vv[1] < vend) raws[1] = __ldcs(reinterpret_cast<const uint4*>(src) + vv[1]);
+    for (int v0 = threadIdx.x; v0 < vend; v0 += U * blockDim.x) {
+      uint4 raws[U];
+      int vv[U];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
+      for (int u = 0; u < U; ++u) {
+        vv[u] = v0 + u * (int)blockDim.x;
+        if (vv[u] < vend) raws[u] = __ldcs(reinterpret_cast<const uint4*>(src) + vv[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
         const int v = vv[u];
         if (v >= vend) break;
         const uint4 raw = raws[u];
@@ -1176,7 +1179,10 @@ void fill_map2d(Map2D& m, const void* ptr, int dtype, const DimMap& r, const Dim
 
 template <typename TIn, typename TOut, bool DEQ, int K, int SL>
 int launch_rows(RowsArgs& a, cudaStream_t st) {
-  auto kern = k_rows<TIn, TOut, DEQ, K, SL>;
+  // the table kinds run one CTA per SM and need the second load in flight;
+  // the analytic kinds keep eight CTAs per SM and do better without it
+  constexpr int U = (!DEQ && K == VQ_R_TABLE) ? 2 : 1;
+  auto kern = k_rows<TIn, TOut, DEQ, K, SL, U>;
   const int smem = (!DEQ && K == VQ_R_TABLE) ? kTableBytes : 0;
   const int sms = num_sms();
   int threads, blocks;
