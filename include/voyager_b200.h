@@ -204,6 +204,15 @@ int vq_mx_pack(const vq_tensor* codes, const vq_tensor* scale, int64_t block_siz
                int32_t row_multiple, void* packed_codes, void* packed_sf, int32_t* d_inexact,
                void* stream);
 
+/* quantize_mx for MXFP8 activations (E4M3 table, power-of-two scales,
+ * block 32 along the last dim of a bf16 [R, C] input, C a multiple of 128)
+ * that also writes the GEMM operand in the same pass: E4M3 bytes [R, C]
+ * (rows beyond R of a 128-row tile are not written; the GEMM discards
+ * their products) and UE8M0 scale atoms as vq_mx_pack lays them out. */
+int vq_quantize_mx_packed(const vq_tensor* input, const vq_rounder* qmap, int32_t floor_log2_qmax,
+                          vq_tensor* scale_out, vq_tensor* codes_out, void* packed_codes,
+                          void* packed_sf, void* stream);
+
 /* out[M, N] (bf16, row stride ldo) = A[M, K] . B[N, K]^T (+ bias[N], bf16),
  * from packed operands (A with row_multiple 128, B with 256).  N and ldo must
  * be multiples of 8.  *d_err (device) is zeroed, and set non-zero if a

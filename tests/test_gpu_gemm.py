@@ -108,3 +108,25 @@ def test_c3_full_size_rows_sample():
     want = oracle.linear_mx(to_np(ca)[rows], to_np(cw), None, input_scale=to_np(sa)[rows],
                             weight_scale=to_np(sw), block_size=32)
     assert G.rel_l2(to_np(out)[rows], want) < 1e-3
+
+
+def test_fused_pack_matches_separate_pack():
+    """quantize_mx writes the GEMM operand in the same pass for MXFP8
+    activations; the product must equal the one from a separate pack."""
+    from voyager_b200 import mxgemm
+
+    g = torch.Generator().manual_seed(11)
+    a = torch.randn(300, 512, generator=g).bfloat16().cuda()
+    w = (torch.randn(264, 512, generator=g) * 0.02).bfloat16().cuda()
+    Q = torch.ops.quantized_ops
+    e4m3 = to_dev(quantization_map("fp8_e4m3"))
+    sa, ca = Q.quantize_mx(a, e4m3, [-1], 32, 448.0, True)
+    sw, cw = Q.quantize_mx(w, e4m3, [-1], 32, 448.0, True)
+    assert mxgemm._vouched_entry(ca, sa)[1] is not None  # fused operand present
+    fused = mxgemm.linear(ca, cw, None, sa, sw)
+    sep = mxgemm.linear(ca.clone(), cw, None, sa, sw)  # clone: no provenance -> pack + check
+    torch.cuda.synchronize()
+    assert sep is not None and torch.equal(fused, sep)
+    want = oracle.linear_mx(to_np(ca), to_np(cw), None, input_scale=to_np(sa),
+                            weight_scale=to_np(sw), block_size=32)
+    assert G.rel_l2(to_np(fused), want) < 1e-3

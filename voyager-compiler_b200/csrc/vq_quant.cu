@@ -199,6 +199,12 @@ struct QmxArgs {
   const uint16_t* sq_table;  // device table for a TABLE-kind scale rounder
   vq_rounder qr;             // element rounder
   vq_rounder sq;             // scale rounder
+  // optional MXFP8 GEMM operand written in the same pass (E4M3 codes with
+  // power-of-two block-32 scales): E4M3 bytes [rows, C] and UE8M0 scale
+  // atoms [C/128][ceil(rows/128)][512] (see vq_gemm.cu)
+  uint8_t* packed;
+  uint8_t* packed_sf;
+  int32_t packed_rt;
 };
 
 // One block of bs = TPB * VPT * VEC elements per TPB threads; lane l holds
@@ -274,6 +280,14 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
       if (live[u] && lane == 0) {
         if (BF) reinterpret_cast<uint16_t*>(a.scale)[g] = (uint16_t)sbits;
         else reinterpret_cast<uint32_t*>(a.scale)[g] = sbits;
+        if (K == K_HW_E4M3 && BF && a.packed_sf) {
+          // UE8M0 = the bf16 exponent field; a subnormal scale (block amax
+          // below 2^-118) is stored as 2^-127
+          const uint32_t row = (uint32_t)(base[u] / a.C), col = cb[u];
+          const uint32_t kt = col / 128, j = (col / 32) % 4, rt = row / 128, rr = row % 128;
+          a.packed_sf[((size_t)kt * a.packed_rt + rt) * 512 + (rr % 32) * 16 + (rr / 32) * 4 + j] =
+              (uint8_t)((sbits >> 7) & 0xFF);
+        }
       }
       if (a.codes == nullptr || !live[u]) continue;
       const Divisor dv = make_divisor(s);
@@ -288,6 +302,21 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
             const float q0 = div_to_bf16_domain(bf2f(w[k] & 0xFFFFu), dv);
             const float q1 = div_to_bf16_domain(bf2f(w[k] >> 16), dv);
             w[k] = round_pair<K>(a.qr, pair_index<K>(q0, q1), smem);
+          }
+          if (K == K_HW_E4M3 && a.packed) {
+            // the codes are E4M3 values: their bytes for the GEMM
+            uint32_t pb[2];
+#pragma unroll
+            for (int k = 0; k < 4; k += 2) {
+              uint16_t b0, b1;
+              const float c0 = __uint_as_float(w[k] << 16), c1 = __uint_as_float(w[k] & 0xFFFF0000u);
+              const float c2 = __uint_as_float(w[k + 1] << 16),
+                          c3 = __uint_as_float(w[k + 1] & 0xFFFF0000u);
+              asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(b0) : "f"(c1), "f"(c0));
+              asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(b1) : "f"(c3), "f"(c2));
+              pb[k / 2] = (uint32_t)b0 | ((uint32_t)b1 << 16);
+            }
+            *reinterpret_cast<uint2*>(a.packed + base[u] + off) = make_uint2(pb[0], pb[1]);
           }
         } else {
 #pragma unroll
@@ -1667,6 +1696,44 @@ int vq_quantize_mx(const vq_tensor* input, const vq_rounder* qmap, const int64_t
     return st;
   return run_elementwise<false>(input, scale_out, nullptr, block_size, qmap, nullptr, nullptr,
                                 codes_out, stream);
+}
+
+int vq_quantize_mx_packed(const vq_tensor* input, const vq_rounder* qmap, int32_t floor_log2_qmax,
+                          vq_tensor* scale_out, vq_tensor* codes_out, void* packed_codes,
+                          void* packed_sf, void* stream) {
+  if (!input || !qmap || !scale_out || !codes_out || !packed_codes || !packed_sf)
+    return VQ_ERR_NULL;
+  if (input->dtype != VQ_BF16 || input->ndim != 2) return VQ_ERR_UNSUPPORTED;
+  if (elem_kind(qmap) != K_HW_E4M3) return VQ_ERR_UNSUPPORTED;
+  const int64_t R = input->shape[0], C = input->shape[1];
+  if (C % 128 != 0 || R <= 0) return VQ_ERR_UNSUPPORTED;
+  const int64_t axes[1] = {-1};
+  int blocked[VQ_MAX_DIMS];
+  int st = validate_mx(input, axes, 1, 32, nullptr, scale_out, blocked);
+  if (st) return st;
+  if (codes_out->dtype != VQ_BF16 || codes_out->ndim != 2 || codes_out->shape[0] != R ||
+      codes_out->shape[1] != C)
+    return VQ_ERR_SHAPE;
+  const int nv = qmx_last_fast_ok(*input, blocked, 32);
+  if (!nv || !aligned16(codes_out->data) || !aligned16(packed_codes) || !aligned16(packed_sf))
+    return VQ_ERR_ALIGNMENT;
+  QmxArgs a;
+  memset(&a, 0, sizeof(a));
+  a.in = input->data;
+  a.codes = codes_out->data;
+  a.scale = scale_out->data;
+  a.C = (uint32_t)C;
+  a.bs = 32;
+  a.nb = FastDiv::make((uint32_t)(C / 32));
+  a.ngroups = (uint32_t)(R * (C / 32));
+  a.quant_max = 448.0f;
+  a.pow2 = 1;
+  a.fl2q = floor_log2_qmax;
+  a.qr = *qmap;
+  a.packed = (uint8_t*)packed_codes;
+  a.packed_sf = (uint8_t*)packed_sf;
+  a.packed_rt = (int32_t)((R + 127) / 128);
+  return launch_qmx_kind<uint16_t>(a, K_HW_E4M3, nv, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int vq_rounder_check_hw(const vq_rounder* r, int32_t* d_mismatches, void* stream) {

@@ -33,13 +33,22 @@ _wcache = TensorCache()
 CHECK_ERRORS = os.environ.get("VQ_CHECK_ERRORS", "0") == "1"
 
 
-def vouch(codes: torch.Tensor, scale: torch.Tensor):
-    _vouched.put(codes, "mxfp8", (codes._version, id(scale), scale._version))
+def vouch(codes: torch.Tensor, scale: torch.Tensor, packed=None):
+    """Record that ``codes`` / ``scale`` are exact MXFP8 (quantize_mx wrote
+    them); ``packed`` = the (E4M3 bytes, scale atoms) written in the same
+    pass, if any."""
+    _vouched.put(codes, "mxfp8", ((codes._version, id(scale), scale._version), packed))
+
+
+def _vouched_entry(codes, scale):
+    v = _vouched.get(codes, "mxfp8")
+    if v is None or v[0] != (codes._version, id(scale), scale._version):
+        return None
+    return v
 
 
 def _is_vouched(codes, scale) -> bool:
-    v = _vouched.get(codes, "mxfp8")
-    return v is not None and v == (codes._version, id(scale), scale._version)
+    return _vouched_entry(codes, scale) is not None
 
 
 def applies(input, weight, input_scale, weight_scale, block_size, input_code, weight_code,
@@ -107,12 +116,16 @@ def linear(input, weight, bias, input_scale, weight_scale):
     if not wok:
         return None
     K, N = weight.shape[1], weight.shape[0]
-    a2 = input.reshape(-1, K).contiguous()
-    s2 = input_scale.reshape(-1, input_scale.shape[-1]).contiguous()
-    M = a2.shape[0]
-    pa, pas, aok = _pack(a2, s2, 128, not _is_vouched(input, input_scale))
-    if not aok:
-        return None
+    M = input.numel() // K
+    entry = _vouched_entry(input, input_scale)
+    if entry is not None and entry[1] is not None:
+        pa, pas = entry[1]  # packed by quantize_mx in the same pass
+    else:
+        a2 = input.reshape(-1, K).contiguous()
+        s2 = input_scale.reshape(-1, input_scale.shape[-1]).contiguous()
+        pa, pas, aok = _pack(a2, s2, 128, entry is None)
+        if not aok:
+            return None
     out = torch.empty((M, N), dtype=torch.bfloat16, device=input.device)
     err = torch.empty(1, dtype=torch.int32, device=input.device)
     b = bias.contiguous() if bias is not None else None

@@ -206,16 +206,33 @@ def quantize_mx(input: torch.Tensor, qmap: torch.Tensor, axes, block_size: int,
     codes = torch.empty_like(x)
     rd = rounder_for(qmap, dev)
     sq = rounder_for(scale_qmap, dev) if scale_qmap is not None else None
-    axes_c = (ctypes.c_int64 * len(ax))(*ax)
     fl2q = floor_log2(quant_max) if force_scale_power_of_two else 0
+    mxfp8 = (block_size == 32 and ax == [x.dim() - 1] and force_scale_power_of_two
+             and scale_qmap is None and x.dtype == torch.bfloat16 and x.dim() >= 1
+             and rd.c.kind == _lib.VQ_R_MINIFLOAT and rd.c.hw == 1)
+    if mxfp8 and x.shape[-1] % 128 == 0 and x.numel() > 0:
+        # MXFP8 activations: also write the tcgen05 GEMM operand in this pass
+        from voyager_b200 import mxgemm
+
+        C = x.shape[-1]
+        R = x.numel() // C
+        rt = (R + 127) // 128
+        packed = torch.empty(rt * 128 * C, dtype=torch.uint8, device=dev)
+        packed_sf = torch.empty((C // 128) * rt * 512, dtype=torch.uint8, device=dev)
+        st = lib().vq_quantize_mx_packed(_ref(_vt(x.view(R, C))), rd.ref(), fl2q,
+                                         _ref(_vt(scale.view(R, C // 32))),
+                                         _ref(_vt(codes.view(R, C))), packed.data_ptr(),
+                                         packed_sf.data_ptr(), _stream(dev))
+        _lib.check(st, "quantized_ops::quantize_mx")
+        mxgemm.vouch(codes, scale, (packed, packed_sf))
+        return scale, codes
+    axes_c = (ctypes.c_int64 * len(ax))(*ax)
     st = lib().vq_quantize_mx(_ref(_vt(x)), rd.ref(), axes_c, len(ax), int(block_size),
                               float(quant_max), int(bool(force_scale_power_of_two)), fl2q,
                               sq.ref() if sq else None, _ref(_vt(scale)), _ref(_vt(codes)),
                               _stream(dev))
     _lib.check(st, "quantized_ops::quantize_mx")
-    if (block_size == 32 and ax == [x.dim() - 1] and force_scale_power_of_two
-            and x.dtype == torch.bfloat16 and rd.c.kind == _lib.VQ_R_MINIFLOAT
-            and rd.c.ebits == 4 and rd.c.mbits == 3 and rd.c.is_signed and rd.c.max_norm == 448.0):
+    if mxfp8:
         # E4M3 codes with power-of-two scales: the MXFP8 GEMM may take them
         # without re-checking
         from voyager_b200 import mxgemm
