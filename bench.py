@@ -47,7 +47,7 @@ def parse():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", default=None, choices=["c1", "c2", "c3"],
+    ap.add_argument("--only", default=None, choices=["c1", "c2", "c3", "c4"],
                     help="profiling aid: run only this workload's kernels, no JSON line")
     return ap.parse_args()
 
@@ -463,7 +463,59 @@ def run_secondary(dev, hbm_peak, peaks):
             ca, cw, sa, sw, 32, None, None, "kc", "linear") else "dequant + cuBLAS bf16"
     except Exception as e:  # report, do not hide
         out["c3_error"] = repr(e)[:200]
+    try:
+        out["c4_w4a8_sweep"] = run_c4_sweep(dev, hbm_peak)
+    except Exception as e:
+        out["c4_error"] = repr(e)[:200]
     return out
+
+
+def c4_operands(dev, m, k, n, seed):
+    """C4 inputs on the device: A ~ N(0,1) [M,K] MXFP8, W ~ N(0,0.02) [N,K] NVFP4."""
+    import torch
+
+    from voyager_b200.tables import get_quantization_map
+
+    Q = torch.ops.quantized_ops
+    g = torch.Generator(device=dev).manual_seed(seed)
+    a = torch.randn((m, k), generator=g, device=dev, dtype=torch.float32).bfloat16()
+    w = (torch.randn((n, k), generator=g, device=dev, dtype=torch.float32) * 0.02).bfloat16()
+    e4m3 = get_quantization_map("fp8_e4m3", dev)
+    sa, ca = Q.quantize_mx(a, e4m3, [-1], 32, 448.0, True)
+    sw, cw = Q.quantize_mx(w, get_quantization_map("fp4_e2m1", dev), [-1], 16, 6.0, False, e4m3)
+    del a, w
+    return ca, sa, cw, sw
+
+
+def run_c4_sweep(dev, hbm_peak):
+    """C4: W4A8 linear over M x (K, N); TFLOP/s per point, and packed-byte
+    GB/s (fraction of HBM) for the weight-streaming points M <= 16."""
+    import torch
+
+    from voyager_b200 import w4a8
+
+    stream = torch.cuda.current_stream(dev)
+    res = []
+    for (k, n) in [(4096, 4096), (4096, 14336), (14336, 4096)]:
+        ca0, sa0, cw, sw = c4_operands(dev, 16384, k, n, seed=k + n)
+        for m in (1, 16, 128, 1024, 16384):
+            ca, sa = ca0[:m].contiguous(), sa0[:m].contiguous()
+            if m == 16384:
+                ca, sa = ca0, sa0
+            reps = 20 if m <= 1024 else 5
+            ms = _time_ms(lambda: w4a8.linear(ca, sa, cw, sw), stream, reps=reps)
+            fl = 2.0 * m * n * k
+            pt = {"M": m, "K": k, "N": n, "ms": round(ms, 4),
+                  "TFLOPs": round(fl / (ms / 1e3) / 1e12, 2),
+                  "path": "packed-weight mma" if w4a8.applies_small(ca, cw) else "dequant + cuBLAS bf16"}
+            if m <= 16:
+                byts = n * k * (0.5 + 1 / 16) + m * k * (1 + 1 / 32) + 2 * m * n
+                pt["GBps"] = round(byts / (ms / 1e3) / 1e9, 1)
+                pt["frac_hbm"] = round(pt["GBps"] / hbm_peak, 3)
+            res.append(pt)
+        del ca0, sa0, cw, sw
+        torch.cuda.empty_cache()
+    return res
 
 
 def run_only(args):
@@ -494,6 +546,12 @@ def run_only(args):
             Q.quantize_mx(w, idx_tab, [-1], 64, 1.0, False)
             Q.quantize(w, sp, qmap=posit)
             Q.quantize(w, si, qmap=i8)
+    elif args.only == "c4":
+        from voyager_b200 import w4a8
+
+        ca, sa, cw, sw = c4_operands(dev, 16, 4096, 14336, seed=1)
+        for _ in range(args.warmup + args.steps):
+            w4a8.linear(ca, sa, cw, sw)
     else:
         a_np, w_np = synth.c3_operands()
         e4m3 = get_quantization_map("fp8_e4m3", dev)

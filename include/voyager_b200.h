@@ -246,6 +246,27 @@ int vq_linear_mxf8_noalloc(const vq_tensor* a_codes, const vq_tensor* a_scale,
                            const void* w_packed, const void* w_sf_packed, int64_t N,
                            const void* bias, void* out, int64_t ldo, void* stream);
 
+/* ---- W4A8 (NVFP4 weights x MXFP8 activations) for few tokens --------------
+ * The reference has no single op for this pair; its result is aten.linear of
+ * the operands dequantized with their own block sizes
+ * (src/voyager_compiler/ops/quantized.py:455-472, 522-586). */
+
+/* Pack bf16 E2M1 codes [N, K] (K % 64 == 0) to nibbles [N, K/2] (even k in
+ * the low nibble) and bf16 E4M3 scales [N, K/16] to bytes.  *d_inexact
+ * (device, may be NULL) counts entries that are not such values. */
+int vq_w4_pack_weights(const vq_tensor* codes, const vq_tensor* scales, void* wq, void* ws,
+                       int32_t* d_inexact, void* stream);
+
+/* Pack bf16 E4M3 codes [M, K] to bytes and bf16 scales [M, K/32] to float. */
+int vq_a8_pack(const vq_tensor* codes, const vq_tensor* scales, void* aq, float* as,
+               int32_t* d_inexact, void* stream);
+
+/* out[M, N] bf16 = A . W^T (+ bias) for M <= 16, from the packed operands;
+ * `workspace` is float32 [M, N] scratch (zeroed by the call). */
+int vq_w4a8_linear_small(const void* aq, const float* as, const void* wq, const void* ws,
+                         int64_t M, int64_t N, int64_t K, const void* bias, float* workspace,
+                         void* out, void* stream);
+
 /* The per-block parameters of quantized_ops::quantize_affine
  * (quantized.py:884-948): for blocks of `block_size` elements along the one
  * axis in `axes` (zero-padded when ragged),

@@ -110,6 +110,14 @@ _SIGNATURES = {
     "vq_quantize_mx_packed": (ctypes.c_int, [P(VqTensor), P(VqRounder), ctypes.c_int32,
                                              P(VqTensor), P(VqTensor), ctypes.c_void_p,
                                              ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_w4_pack_weights": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_a8_pack": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p, ctypes.c_void_p,
+                                  ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_w4a8_linear_small": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                                            ctypes.c_void_p, ctypes.c_void_p]),
     "vq_rounder_check_hw": (ctypes.c_int, [P(VqRounder), ctypes.c_void_p, ctypes.c_void_p]),
     "vq_quantize_affine_qparams": (ctypes.c_int, [P(VqTensor), P(ctypes.c_int64), ctypes.c_int32,
                                                   ctypes.c_int64, ctypes.c_float, ctypes.c_float,
