@@ -425,6 +425,31 @@ def run_tp_linear(dev, pg, world):
             "gpus": world, "note": "weight N-sharded, output all-gathered (NCCL)"}
 
 
+def _time_graph_ms(fn, stream, reps=20, warm=3):
+    """Device time of fn replayed from a CUDA graph (for µs-scale calls whose
+    eager time is the host's launch cost, as in a graph-captured decode)."""
+    import torch
+
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = torch.cuda.current_stream()
+    a.record(st)
+    for _ in range(reps):
+        g.replay()
+    b.record(st)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    del g
+    return ms
+
+
 def run_secondary(dev, hbm_peak, peaks):
     import torch
 
@@ -503,7 +528,8 @@ def run_c4_sweep(dev, hbm_peak):
             if m == 16384:
                 ca, sa = ca0, sa0
             reps = 20 if m <= 1024 else 5
-            ms = _time_ms(lambda: w4a8.linear(ca, sa, cw, sw), stream, reps=reps)
+            # graph replay: the small-M calls take microseconds on the device
+            ms = _time_graph_ms(lambda: w4a8.linear(ca, sa, cw, sw), stream, reps=reps)
             fl = 2.0 * m * n * k
             pt = {"M": m, "K": k, "N": n, "ms": round(ms, 4),
                   "TFLOPs": round(fl / (ms / 1e3) / 1e12, 2),
