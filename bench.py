@@ -11,8 +11,9 @@ metric = algorithmic GB/s over the three (8.0625 + 8 + 8 bytes per element),
 whole job (all ranks).  Multi-GPU: every rank quantizes its own weight matrix
 (weak scaling, no collective on the data path).
 
-Secondary results in the same line ("secondary"): C1 NVFP4 round trip GB/s
-and C3 MXFP8 quantized-linear TFLOP/s on one GPU.
+Secondary results in the same line ("secondary"): C1 NVFP4 round trip GB/s,
+C3 MXFP8 quantized-linear TFLOP/s, the C4 W4A8 sweep on one GPU, and the C5
+4-layer decoder forward (tensor parallel over the ranks when N > 1).
 
 --impl reference times the reference algorithm's CPU restatement (the oracle
 port under oracle/) on this host's cores, on a bounded row sample of the
@@ -47,7 +48,7 @@ def parse():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", default=None, choices=["c1", "c2", "c3", "c4"],
+    ap.add_argument("--only", default=None, choices=["c1", "c2", "c3", "c4", "c5"],
                     help="profiling aid: run only this workload's kernels, no JSON line")
     return ap.parse_args()
 
@@ -339,6 +340,13 @@ def run_ours(args):
         tp = run_tp_linear(dev, pg, world)
         if rank == 0:
             secondary["c3_tp_linear"] = tp
+    if not args.no_secondary:
+        try:
+            c5 = run_c5(dev, pg, world, peaks.get("bf16_tflops", 1590.0))
+        except Exception as e:  # report, do not hide
+            c5 = {"error": repr(e)[:200]}
+        if rank == 0:
+            secondary["c5_decoder"] = c5
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -423,6 +431,52 @@ def run_tp_linear(dev, pg, world):
     ms = float(t.item())
     return {"ms": round(ms, 3), "TFLOPs": round(2 * 8192 * 4096 * 11008 / (ms / 1e3) / 1e12, 1),
             "gpus": world, "note": "weight N-sharded, output all-gathered (NCCL)"}
+
+
+def run_c5(dev, pg, world, bf16_peak, reps=3, warm=2):
+    """C5: the 4-layer LLaMA-style decoder forward (hidden 4096, 32 heads,
+    ffn 11008, B=8, S=2048) through the MXFP8 quantized graph; tensor
+    parallel over the ranks when world > 1 (strong scaling of one forward).
+    Random-init weights N(0, 0.02) and N(0, 1) hidden states, made on the
+    device from fixed seeds."""
+    import torch
+
+    from voyager_b200.decoder import Decoder, DecoderConfig, init_weights
+
+    cfg, B, S = DecoderConfig(), 8, 2048
+    dec = Decoder(cfg, init_weights(cfg, 0, dev), group=None)
+    torch.cuda.empty_cache()
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn((B * S, cfg.hidden), generator=g, device=dev).bfloat16()
+    xs = x[dec.tp.split(B * S, "tokens")].contiguous()
+    del x
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(warm):
+        dec.forward_shard(xs, B)
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        dec.forward_shard(xs, B)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    if pg:
+        t = torch.tensor([ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    tf = cfg.flops(B, S) / (ms / 1e3) / 1e12
+    peak = 2 * bf16_peak
+    del dec
+    torch.cuda.empty_cache()
+    return {"ms": round(ms, 2), "TFLOPs": round(tf, 1), "gpus": world,
+            "frac_fp8_dense": round(tf / peak, 3),
+            "fp8_dense_peak_TFLOPs": peak,
+            "flop_per_forward": cfg.flops(B, S),
+            "parallelism": f"tp{world} (Megatron, sequence-parallel norms)" if world > 1
+            else "1 GPU"}
 
 
 def _time_graph_ms(fn, stream, reps=20, warm=3):
@@ -572,6 +626,14 @@ def run_only(args):
             Q.quantize_mx(w, idx_tab, [-1], 64, 1.0, False)
             Q.quantize(w, sp, qmap=posit)
             Q.quantize(w, si, qmap=i8)
+    elif args.only == "c5":
+        from voyager_b200.decoder import Decoder, DecoderConfig, init_weights
+
+        cfg = DecoderConfig()
+        dec = Decoder(cfg, init_weights(cfg, 0, dev))
+        x = torch.randn((8 * 2048, cfg.hidden), device=dev).bfloat16()
+        for _ in range(args.warmup + args.steps):
+            dec.forward_shard(x, 8)
     elif args.only == "c4":
         from voyager_b200 import w4a8
 

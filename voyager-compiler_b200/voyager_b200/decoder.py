@@ -1,0 +1,286 @@
+"""LLaMA-style decoder stack over the quantized ops (benchmark config C5).
+
+This is the forward that a PT2E-converted LLaMA graph runs when every linear
+and both attention matmuls are MXFP8 (``fp8_e4m3,qs=microscaling,bs=32`` with
+``force_scale_power_of_two``): ``convert_pt2e`` quantizes each weight once
+(``src/voyager_compiler/quantize_pt2e.py:739-766``), inserts a
+``quantize_mx`` before every activation operand (``:779-808``) with blocks
+along the operand's contraction axis (``:136-161``: -1 for a matmul's first
+operand, -2 for its second), and retargets ``linear`` / ``matmul`` to
+``linear_mx`` / ``matmul_mx`` (``:851-938``).  Everything between those ops
+(RMSNorm, RoPE, softmax, SwiGLU, residual adds) stays in bf16 torch ops, as
+in the exported eager graph of HF LLaMA.
+
+Two rewrites that leave every value unchanged:
+  * q/k/v and gate/up share their input codes, so each group is one
+    ``linear_mx`` over the concatenated weight rows (every output element is
+    the same dot product over the same K blocks);
+  * the second operand of ``q @ k^T`` is quantized as ``k`` along its last
+    axis and passed transposed (a block of 32 along -2 of ``k^T`` is the same
+    32 values as a block along -1 of ``k``); likewise ``v``'s blocks along the
+    token axis are computed on ``v^T`` along -1.
+
+Tensor parallel (Megatron with sequence-parallel norms) when a process group
+of g > 1 ranks is given: the residual stream is split by tokens; q/k/v and
+gate/up are column-parallel (output rows / heads split g ways), o_proj and
+down row-parallel (K split g ways at multiples of 32, so every quantization
+block of the single-device graph stays whole on one rank).  Per layer: the
+normalised activations are quantized on their token shard and all-gathered
+(codes + scales, bit-identical to quantizing the full tensor), and the
+row-parallel partial products are reduce-scattered back to token shards.
+
+Weights are random-init N(0, 0.02) (no checkpoint); ``init_weights`` makes
+them from a seed so every rank (and a CPU check) builds the same model.
+"""
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import torch
+import torch.distributed as dist
+
+W_NAMES = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+@dataclass
+class DecoderConfig:
+    layers: int = 4
+    hidden: int = 4096
+    heads: int = 32
+    ffn: int = 11008
+    eps: float = 1e-5
+    rope_theta: float = 10000.0
+    block_size: int = 32
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden // self.heads
+
+    def flops(self, batch: int, seq: int) -> float:
+        """Forward FLOPs of the matmuls as the eager graph computes them
+        (full S x S attention products)."""
+        t = batch * seq
+        lin = 2 * t * self.hidden * (4 * self.hidden + 3 * self.ffn)
+        att = 2 * 2 * batch * self.heads * seq * seq * self.head_dim
+        return float(self.layers * (lin + att))
+
+
+def init_weights(cfg: DecoderConfig, seed: int, device) -> List[Dict[str, torch.Tensor]]:
+    """bf16 weights ~ N(0, 0.02) per layer ([out, in] like nn.Linear), the
+    RMSNorm weights ones; drawn in a fixed order from one generator."""
+    device = torch.device(device)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    h, f = cfg.hidden, cfg.ffn
+    shapes = {"q": (h, h), "k": (h, h), "v": (h, h), "o": (h, h),
+              "gate": (f, h), "up": (f, h), "down": (h, f)}
+    layers = []
+    for _ in range(cfg.layers):
+        w = {n: (torch.randn(shapes[n], generator=gen, device=device) * 0.02).bfloat16()
+             for n in W_NAMES}
+        w["ln1"] = torch.ones(h, dtype=torch.bfloat16, device=device)
+        w["ln2"] = torch.ones(h, dtype=torch.bfloat16, device=device)
+        layers.append(w)
+    return layers
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """LLaMA RMSNorm: float32 statistics, cast back to the input dtype, times
+    the weight."""
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return w * y.to(x.dtype)
+
+
+def rope_tables(seq: int, dim: int, theta: float, device, dtype):
+    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.int64, device=device).float() / dim))
+    t = torch.arange(seq, device=device, dtype=torch.float32)
+    f = torch.outer(t, inv)
+    emb = torch.cat([f, f], dim=-1)
+    return emb.cos().to(dtype), emb.sin().to(dtype)
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x: [B, heads, S, D]; the rotate-half convention of HF LLaMA."""
+    d = x.shape[-1] // 2
+    rot = torch.cat([-x[..., d:], x[..., :d]], dim=-1)
+    return x * cos + rot * sin
+
+
+class TensorParallel:
+    """The process group a decoder is split over (world 1: no collectives)."""
+
+    def __init__(self, group=None):
+        on = dist.is_available() and dist.is_initialized()
+        self.group = group
+        self.world = dist.get_world_size(group) if on else 1
+        self.rank = dist.get_rank(group) if on else 0
+
+    def split(self, n: int, what: str) -> slice:
+        if n % self.world:
+            raise ValueError(f"{what}: {n} does not split into {self.world} equal shards")
+        step = n // self.world
+        return slice(self.rank * step, (self.rank + 1) * step)
+
+    def all_gather_rows(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return t
+        t = t.contiguous()
+        out = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype,
+                          device=t.device)
+        dist.all_gather_into_tensor(out, t, group=self.group)
+        return out
+
+    def reduce_scatter_rows(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return t
+        t = t.contiguous()
+        out = torch.empty((t.shape[0] // self.world,) + tuple(t.shape[1:]), dtype=t.dtype,
+                          device=t.device)
+        dist.reduce_scatter_tensor(out, t, group=self.group)
+        return out
+
+
+class DecoderLayer:
+    def __init__(self, cfg: DecoderConfig, w: Dict[str, torch.Tensor], table: torch.Tensor,
+                 ops, tp: TensorParallel):
+        self.cfg, self.table, self.ops, self.tp = cfg, table, ops, tp
+        h, f = cfg.hidden, cfg.ffn
+        if cfg.heads % tp.world:
+            raise ValueError(f"{cfg.heads} heads do not split over {tp.world} ranks")
+        hs = tp.split(h, "hidden")
+        fs = tp.split(f, "ffn")
+        for n, k in ((h // tp.world, "hidden shard"), (f // tp.world, "ffn shard")):
+            if n % cfg.block_size or n % 8:
+                raise ValueError(f"{k} {n} is not a multiple of the block size and of 8")
+        self.ln1, self.ln2 = w["ln1"], w["ln2"]
+        # column-parallel: this rank's output rows; row-parallel: its K columns
+        qkv = torch.cat([w["q"][hs], w["k"][hs], w["v"][hs]], 0)
+        gu = torch.cat([w["gate"][fs], w["up"][fs]], 0)
+        self.qkv = self._quant_weight(qkv)
+        self.gu = self._quant_weight(gu)
+        self.o = self._quant_weight(w["o"][:, hs])
+        self.down = self._quant_weight(w["down"][:, fs])
+
+    def _qmx(self, x: torch.Tensor):
+        """quantize_mx along the last axis (MXFP8, power-of-two scales)."""
+        return self.ops.quantize_mx(x, self.table, [-1], self.cfg.block_size, 448.0, True)
+
+    def _quant_weight(self, w: torch.Tensor):
+        scale, codes = self._qmx(w.contiguous())
+        return codes, scale
+
+    def _linear(self, codes, scale, w):
+        return self.ops.linear_mx(codes, w[0], None, input_scale=scale, weight_scale=w[1],
+                                  block_size=self.cfg.block_size)
+
+    def _gathered_qmx(self, x: torch.Tensor):
+        """quantize_mx of the token shard, then all-gather codes and scales."""
+        scale, codes = self._qmx(x)
+        codes = self.tp.all_gather_rows(codes)
+        scale = self.tp.all_gather_rows(scale)
+        mark = getattr(self.ops, "mark_exact", None)
+        if mark is not None and self.tp.world > 1:
+            mark(codes, scale)
+        return codes, scale
+
+    def __call__(self, x: torch.Tensor, batch: int, cos, sin, mask) -> torch.Tensor:
+        """x: this rank's token shard [T/g, H] of the [batch * S, H] residual
+        stream -> the same shard after the layer."""
+        cfg, tp, ops = self.cfg, self.tp, self.ops
+        bs = cfg.block_size
+        T = x.shape[0] * tp.world
+        S = T // batch
+        nh, hd = cfg.heads // tp.world, cfg.head_dim
+        hl = nh * hd
+        # --- attention ---------------------------------------------------
+        codes, scale = self._gathered_qmx(rms_norm(x, self.ln1, cfg.eps))
+        qkv = self._linear(codes, scale, self.qkv)                    # [T, 3 hl]
+        q, k, v = (t.reshape(batch, S, nh, hd).transpose(1, 2) for t in qkv.split(hl, -1))
+        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+        sq, cq = self._qmx(q.contiguous())
+        sk, ck = self._qmx(k.contiguous())
+        scores = ops.matmul_mx(cq, ck.transpose(-1, -2), input_scale=sq,
+                               weight_scale=sk.transpose(-1, -2), block_size=bs)
+        scores = scores * (1.0 / math.sqrt(hd)) + mask
+        probs = torch.softmax(scores, dim=-1, dtype=torch.float32).to(x.dtype)
+        sp, cp = self._qmx(probs)
+        sv, cv = self._qmx(v.transpose(-1, -2).contiguous())
+        o = ops.matmul_mx(cp, cv.transpose(-1, -2), input_scale=sp,
+                          weight_scale=sv.transpose(-1, -2), block_size=bs)
+        o = o.transpose(1, 2).reshape(T, hl)
+        so, co = self._qmx(o)
+        x = x + tp.reduce_scatter_rows(self._linear(co, so, self.o))
+        # --- SwiGLU MLP ----------------------------------------------------
+        codes, scale = self._gathered_qmx(rms_norm(x, self.ln2, cfg.eps))
+        g, u = self._linear(codes, scale, self.gu).chunk(2, -1)
+        sa, ca = self._qmx(torch.nn.functional.silu(g) * u)
+        return x + tp.reduce_scatter_rows(self._linear(ca, sa, self.down))
+
+
+class Decoder:
+    """``cfg.layers`` decoder layers; ``ops`` defaults to
+    ``torch.ops.quantized_ops`` (this library's CUDA kernels)."""
+
+    def __init__(self, cfg: DecoderConfig, weights: List[Dict[str, torch.Tensor]], *,
+                 table: Optional[torch.Tensor] = None, ops=None, group=None):
+        self.cfg = cfg
+        self.tp = TensorParallel(group)
+        self.ops = ops if ops is not None else _CudaOps()
+        dev = weights[0]["q"].device
+        if table is None:
+            from voyager_b200.tables import get_quantization_map
+
+            table = get_quantization_map("fp8_e4m3", dev)
+        self.layers = [DecoderLayer(cfg, w, table, self.ops, self.tp) for w in weights]
+        self._tabs = {}
+
+    def _tables(self, seq: int, device, dtype):
+        key = (seq, device, dtype)
+        if key not in self._tabs:
+            cos, sin = rope_tables(seq, self.cfg.head_dim, self.cfg.rope_theta, device, dtype)
+            mask = torch.full((seq, seq), torch.finfo(dtype).min, dtype=dtype,
+                              device=device).triu(1)
+            self._tabs[key] = (cos, sin, mask)
+        return self._tabs[key]
+
+    @torch.no_grad()
+    def forward_shard(self, x: torch.Tensor, batch: int) -> torch.Tensor:
+        """x: this rank's token shard [batch * S / g, H] -> the shard after
+        all layers."""
+        S = x.shape[0] * self.tp.world // batch
+        cos, sin, mask = self._tables(S, x.device, x.dtype)
+        for layer in self.layers:
+            x = layer(x, batch, cos, sin, mask)
+        return x
+
+    @torch.no_grad()
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """x: the full hidden states [B, S, H] (the same on every rank) ->
+        [B, S, H]; with g > 1 ranks the output is all-gathered."""
+        B, S, H = x.shape
+        flat = x.reshape(B * S, H)
+        lo = self.tp.split(B * S, "tokens")
+        y = self.forward_shard(flat[lo].contiguous(), B)
+        return self.tp.all_gather_rows(y).reshape(B, S, H)
+
+    __call__ = forward
+
+
+class _CudaOps:
+    """``torch.ops.quantized_ops`` plus ``mark_exact``: codes and scales that
+    were gathered from this library's ``quantize_mx`` outputs are E4M3 values
+    and powers of two by construction, so ``linear_mx`` may skip its
+    operand check on them."""
+
+    def __init__(self):
+        self._q = torch.ops.quantized_ops
+        self.quantize_mx = self._q.quantize_mx
+        self.linear_mx = self._q.linear_mx
+        self.matmul_mx = self._q.matmul_mx
+
+    @staticmethod
+    def mark_exact(codes, scale):
+        from voyager_b200 import mxgemm
+
+        mxgemm.vouch(codes, scale)
