@@ -246,6 +246,30 @@ int vq_linear_mxf8_noalloc(const vq_tensor* a_codes, const vq_tensor* a_scale,
                            const void* w_packed, const void* w_sf_packed, int64_t N,
                            const void* bias, void* out, int64_t ldo, void* stream);
 
+/* ---- Fused MXFP8 attention (tcgen05) ---------------------------------------
+ * quantized_ops::sdpa_mx (src/voyager_compiler/ops/quantized.py:651-784)
+ * without residual operands, for E4M3 codes with power-of-two block-32
+ * scales (query / key along head_dim, value along the keys) and the
+ * probabilities quantized to E4M3 with power-of-two block-32 scales along
+ * the keys (probs_qmap = E4M3, force_scale_power_of_two):
+ *   out[b,h,i,:] = bf16( sum_j P[i,j] V[j,:] ),
+ *   P = dequantized quantize_mx(bf16(softmax(bf16(bf16(Q K^T) * scale)
+ *       masked)), E4M3, [-1], 32, 2^floor_log2_qmax .. )
+ * Operands packed as vq_mx_pack (row_multiple 128) lays them out:
+ *   q  [batch*heads*sq, 128] codes, k [batch*kv_heads*skv, 128] codes,
+ *   vt [batch*kv_heads*128, skv] codes (the value transposed: keys
+ *   contiguous) with their scale atoms.  head_dim must be 128, sq and skv
+ *   multiples of 128, heads a multiple of kv_heads (grouped-query heads).
+ * causal: keys past the query's position (top-left aligned) are masked.
+ * out: bf16 [b, h, i, d] at element strides (out_stride_b, _h, _s), d
+ * contiguous; strides multiples of 8.  *d_err (device) is zeroed and set
+ * non-zero if a bounded wait in the kernel gave up. */
+int vq_attn_mxf8(const void* q, const void* q_sf, const void* k, const void* k_sf, const void* vt,
+                 const void* vt_sf, int64_t batch, int64_t heads, int64_t kv_heads, int64_t sq,
+                 int64_t skv, int64_t head_dim, float scale, int32_t causal,
+                 int32_t floor_log2_qmax, void* out, int64_t out_stride_b, int64_t out_stride_h,
+                 int64_t out_stride_s, int32_t* d_err, void* stream);
+
 /* ---- W4A8 (NVFP4 weights x MXFP8 activations) for few tokens --------------
  * The reference has no single op for this pair; its result is aten.linear of
  * the operands dequantized with their own block sizes

@@ -11,6 +11,7 @@ bfloat16 (NaN -> ``0xFFFF``) before the gather and casts table entries to
 bfloat16 before widening back.
 """
 
+import math
 from concurrent.futures import ThreadPoolExecutor
 from typing import List, Optional, Sequence
 
@@ -348,3 +349,76 @@ def matmul_mx(x, other, *, input_scale=None, weight_scale=None,
         return out
     dt = BF16 if (dtype_of(xa) == BF16 and dtype_of(ba) == BF16) else F32
     return round_to(out, dt)
+
+
+def _softmax_last(x_f32: np.ndarray) -> np.ndarray:
+    """float32 softmax along the last axis: exp(x - max) / sum, every step in
+    float32 (a row of -inf only gives NaN, as in torch)."""
+    m = np.max(x_f32, axis=-1, keepdims=True)
+    with np.errstate(invalid="ignore", over="ignore"):
+        e = np.exp((x_f32 - m).astype(np.float32)).astype(np.float32)
+        s = np.sum(e, axis=-1, keepdims=True, dtype=np.float32)
+        return (e / s).astype(np.float32)
+
+
+def _masked(scores: np.ndarray, mask) -> np.ndarray:
+    """``quantized.py:772-780``: a bool mask keeps where true (-inf
+    elsewhere), a float mask adds; scores are bf16 bits."""
+    if mask is None:
+        return scores
+    mask = np.asarray(mask)
+    if mask.dtype == np.bool_:
+        neg = np.uint16(0xFF80) if scores.dtype == np.uint16 else np.float32(-np.inf)
+        return np.where(mask, scores, neg).astype(scores.dtype)
+    return _binary(scores, mask, np.add)
+
+
+def sdpa_mx(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False,
+            query_residual=None, key_residual=None, value_residual=None,
+            residual_mask=None, *, scale=None, enable_gqa=False, query_scale=None,
+            key_scale=None, value_scale=None, block_size=None, input_code=None,
+            weight_code=None, probs_qmap=None, probs_quant_max=None,
+            probs_scale_qmap=None, probs_code=None, force_scale_power_of_two=False):
+    """``quantized.py:663-769``: dequantize the three operands, scores =
+    bf16(bf16(q k^T) * scale) under the mask, softmax (float32 inside, bf16
+    out), probabilities through ``quantize_mx`` along the keys and back,
+    then ``probs @ v`` (float32 accumulation, bf16 out)."""
+    if is_causal and attn_mask is not None:
+        raise ValueError("is_causal excludes an explicit attn_mask")
+    q = dequantize_mx(query, query_scale, input_code, block_size)
+    k = dequantize_mx(key, key_scale, weight_code, block_size)
+    v = dequantize_mx(value, value_scale, weight_code, block_size)
+    d = dtype_of(q)
+    residual = key_residual is not None
+    if enable_gqa:
+        g = q.shape[-3] // k.shape[-3]
+        k, v = np.repeat(k, g, axis=-3), np.repeat(v, g, axis=-3)
+        if residual:
+            key_residual = np.repeat(key_residual, g, axis=-3)
+            value_residual = np.repeat(value_residual, g, axis=-3)
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    sc = np.float32(scale)
+    raw = np.matmul(to_f32(q), np.swapaxes(to_f32(k), -1, -2)).astype(np.float32)
+    scores = round_to(to_f32(round_to(raw, d)) * sc, d)
+    if is_causal:
+        attn_mask = np.tril(np.ones(scores.shape[-2:], dtype=np.bool_))
+    scores = _masked(scores, attn_mask)
+    keys = scores.shape[-1]
+    if residual:
+        rraw = np.matmul(to_f32(query_residual),
+                         np.swapaxes(to_f32(key_residual), -1, -2)).astype(np.float32)
+        rs = round_to(to_f32(round_to(rraw, d)) * sc, d)
+        scores = np.concatenate([scores, _masked(rs, residual_mask)], axis=-1)
+    probs = round_to(_softmax_last(to_f32(scores)), d)
+    probs, rprobs = probs[..., :keys], probs[..., keys:]
+    if probs_qmap is not None:
+        ps, pc = quantize_mx(np.ascontiguousarray(probs), probs_qmap, [-1], block_size,
+                             probs_quant_max, force_scale_power_of_two, probs_scale_qmap,
+                             probs_code)
+        probs = dequantize_mx(pc, ps, input_code, block_size)
+    out = round_to(np.matmul(to_f32(probs), to_f32(v)).astype(np.float32), d)
+    if residual:
+        ro = round_to(np.matmul(to_f32(rprobs), to_f32(value_residual)).astype(np.float32), d)
+        out = _binary(out, ro, np.add)
+    return out

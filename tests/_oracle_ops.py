@@ -44,6 +44,18 @@ class OracleOps:
                              weight_scale=_np(weight_scale), block_size=block_size)
         return _t(y)
 
+    def sdpa_mx(self, q, k, v, attn_mask=None, dropout_p=0.0, is_causal=False, *, scale=None,
+                enable_gqa=False, query_scale=None, key_scale=None, value_scale=None,
+                block_size=None, probs_qmap=None, probs_quant_max=None,
+                force_scale_power_of_two=False):
+        y = oracle.sdpa_mx(to_np(q), to_np(k), to_np(v), _np(attn_mask), dropout_p, is_causal,
+                           scale=scale, enable_gqa=enable_gqa, query_scale=_np(query_scale),
+                           key_scale=_np(key_scale), value_scale=_np(value_scale),
+                           block_size=block_size, probs_qmap=self.qmap,
+                           probs_quant_max=probs_quant_max,
+                           force_scale_power_of_two=force_scale_power_of_two)
+        return _t(y)
+
 
 def rel_l2(got: torch.Tensor, want: torch.Tensor) -> float:
     g, w = got.double().cpu(), want.double().cpu()

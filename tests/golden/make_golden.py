@@ -28,6 +28,7 @@ Outputs (all under ``tests/golden/``):
 
 import argparse
 import hashlib
+import importlib.util
 import json
 import os
 import sys
@@ -38,9 +39,12 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-sys.path.insert(0, os.path.join(ROOT, "voyager-compiler_b200"))
-
-from voyager_b200 import synth  # noqa: E402
+# the input generators only (importing the voyager_b200 package would
+# register its own quantized_ops namespace before the reference's)
+_spec = importlib.util.spec_from_file_location(
+    "voyager_b200_synth", os.path.join(ROOT, "voyager-compiler_b200", "voyager_b200", "synth.py"))
+synth = importlib.util.module_from_spec(_spec)
+_spec.loader.exec_module(synth)
 
 TABLE_DTYPES = [
     None, "fp4_e2m1", "fp6_e2m3", "fp6_e3m2", "fp8_e4m3", "fp8_e5m2",
@@ -327,6 +331,26 @@ def main():
     swt = np.ascontiguousarray(to_np(sw).T)
     run("matmul_mxfp8_ck", "matmul_mx", [to_np(ca), cwt],
         input_scale=to_np(sa), weight_scale=swt, block_size=32)
+
+    # fused-attention op (sdpa_mx): MXFP8 q / k (blocks along head_dim),
+    # v (blocks along the keys), probabilities quantized to MXFP8
+    def mx_operand(shape, axis, sd=1.0):
+        x = synth.f32_to_bf16_bits((rng.standard_normal(shape) * sd).astype(np.float32))
+        s, c = Q.quantize_mx(to_t(x), gqm("fp8_e4m3"), [axis], 32, 448.0, True)
+        return to_np(c), to_np(s)
+
+    for name, (B, H, HKV, S, causal) in {
+        "sdpa_mxfp8_causal": (1, 2, 2, 256, True),
+        "sdpa_mxfp8_full": (1, 2, 2, 128, False),
+        "sdpa_mxfp8_gqa_causal": (1, 4, 2, 128, True),
+    }.items():
+        cq, sq_ = mx_operand((B, H, S, 128), -1, 2.0)
+        ck, sk = mx_operand((B, HKV, S, 128), -1, 2.0)
+        cv, sv = mx_operand((B, HKV, S, 128), -2)
+        run(name, "sdpa_mx", [cq, ck, cv], is_causal=causal, enable_gqa=HKV != H,
+            query_scale=sq_, key_scale=sk, value_scale=sv, block_size=32,
+            probs_qmap="table:fp8_e4m3", probs_quant_max=448.0,
+            force_scale_power_of_two=True)
 
     np.savez_compressed(os.path.join(HERE, "ops_small.npz"), **arrays)
     with open(os.path.join(HERE, "ops_small.json"), "w") as f:

@@ -74,3 +74,17 @@ def test_linears_take_the_tcgen05_path(monkeypatch):
     w = init_weights(cfg, 5, "cuda")
     Decoder(cfg, w)(torch.randn((1, 128, 256), device="cuda").bfloat16())
     assert calls["n"] == 4 * cfg.layers
+
+
+def test_eager_and_sdpa_graphs_agree():
+    """The eager attention graph (matmul_mx / softmax / quantize_mx /
+    matmul_mx) and the converted sdpa_mx graph compute the same values; the
+    fused kernel and cuBLAS sum in different orders."""
+    from voyager_b200.decoder import Decoder, DecoderConfig, init_weights
+
+    cfg = DecoderConfig(layers=2, hidden=512, heads=4, ffn=1024)
+    w = init_weights(cfg, 7, "cuda")
+    x = torch.randn((2, 256, cfg.hidden), device="cuda").bfloat16()
+    a = Decoder(cfg, w, attn="sdpa")(x)
+    b = Decoder(cfg, w, attn="eager")(x)
+    assert rel_l2(a, b) < 1e-2, rel_l2(a, b)

@@ -62,8 +62,9 @@ def test_small_case(case):
     assert len(got) == len(outs)
     for g, w in zip(got, outs):
         assert g.shape == w.shape and g.dtype == w.dtype
-        if case["op"] in ("linear_mx", "matmul_mx"):
-            # The reference's CPU bf16 GEMM sums in its own order.
+        if case["op"] in ("linear_mx", "matmul_mx", "sdpa_mx"):
+            # The reference's CPU bf16 GEMM (and softmax) sums in its own
+            # order (sdpa_mx: 0-1 differing elements per case, rel-L2 < 2e-5).
             assert G.rel_l2(g, w) < 1e-3
         else:
             assert len(G.bit_mismatches(g, w)) == 0

@@ -33,6 +33,7 @@
 #include <mutex>
 
 #include "vq_numerics.cuh"
+#include "vq_tc.cuh"
 
 namespace vq {
 namespace mx {
@@ -50,7 +51,6 @@ constexpr int ACC_COL = 0;    // 256 fp32 columns
 constexpr int SFA_COL = 256;  // 4 columns
 constexpr int SFB_COL = 260;  // 8 columns
 constexpr int THREADS = 192;
-constexpr uint64_t WAIT_NS = 2000000000ull;  // a wait gives up after 2 s
 
 enum { ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_TIMEOUT_ACC = 3 };
 
@@ -61,102 +61,10 @@ struct SmemLayout {
   static constexpr int kTotal = kBars + 256;
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
+using namespace vq::tc;
 
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-// Bounded wait: false (and *err set) if the phase has not completed within
-// WAIT_NS of wall-clock time.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > WAIT_NS) break;
-  }
-  atomicCAS(err, 0, code);
-  return false;
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
-                                            uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
-      "%3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
-                                          uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          dst),
-      "l"(src), "r"(bytes), "r"(bar)
-      : "memory");
-}
-
-// K-major SWIZZLE_128B shared-memory matrix descriptor (tcgen05 format,
-// version 1): start >> 4, LBO 1 (unused for swizzled K-major), SBO = 1024 B
-// between 8-row groups, layout type 2.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)1 << 16;
-  d |= (uint64_t)(1024 >> 4) << 32;
-  d |= (uint64_t)1 << 46;  // version
-  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
-  return d;
-}
-// Descriptor of a 32-row x 16-byte scale atom for tcgen05.cp.32x128b:
-// no swizzle, 8-row core matrices 128 B apart.
-__device__ __forceinline__ uint64_t sf_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)1 << 16;
-  d |= (uint64_t)(128 >> 4) << 32;
-  d |= (uint64_t)1 << 46;
-  return d;
-}
-
-// Instruction descriptor, kind::mxf8f6f4 block-scaled: E4M3 x E4M3, UE8M0
-// scales, K-major A and B, M = 128, N = 256, scale-factor byte j.
-__device__ __forceinline__ uint32_t idesc_mxf8(uint32_t j) {
-  return (j << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) | (1u << 23) |
-         ((uint32_t)(BM >> 4) << 24) | (j << 29);
-}
-
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
+// Instruction descriptor of this kernel's MMA (M = 128, N = 256).
+__device__ __forceinline__ uint32_t idesc_mxf8(uint32_t j) { return tc::idesc_mxf8(j, BM, BN); }
 
 struct GemmArgs {
   const uint8_t* sfa;  // [KT][MT][512]
@@ -296,7 +204,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < g.ntiles; t += gridDim.x) {
       const int tm = t / g.NTILE_N, tn = t % g.NTILE_N;
-      if (!mbar_wait(acc_full, acc_phase, g.err, ERR_TIMEOUT_ACC)) break;
+      if (!mbar_wait_warp(acc_full, acc_phase, g.err, ERR_TIMEOUT_ACC)) break;
       acc_phase ^= 1;
       tc_fence_after();
       const int row = tm * BM + row_in_tile;

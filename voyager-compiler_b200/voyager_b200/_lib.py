@@ -110,6 +110,9 @@ _SIGNATURES = {
     "vq_quantize_mx_packed": (ctypes.c_int, [P(VqTensor), P(VqRounder), ctypes.c_int32,
                                              P(VqTensor), P(VqTensor), ctypes.c_void_p,
                                              ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_attn_mxf8": (ctypes.c_int, [ctypes.c_void_p] * 6 + [ctypes.c_int64] * 6
+                     + [ctypes.c_float, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]
+                     + [ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_void_p]),
     "vq_w4_pack_weights": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p,
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "vq_a8_pack": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p, ctypes.c_void_p,

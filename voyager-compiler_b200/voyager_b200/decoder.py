@@ -19,6 +19,11 @@ Two rewrites that leave every value unchanged:
     axis and passed transposed (a block of 32 along -2 of ``k^T`` is the same
     32 values as a block along -1 of ``k``); likewise ``v``'s blocks along the
     token axis are computed on ``v^T`` along -1.
+The attention itself is either ``sdpa_mx`` (a model exported with
+scaled-dot-product attention; ``quantize_pt2e`` converts it to this op) or
+the eager matmul / softmax graph; they differ only in where the masked
+scores are set to -inf (``masked_fill`` vs. adding the dtype's minimum), and
+both give the masked keys a probability of exactly 0.
 
 Tensor parallel (Megatron with sequence-parallel norms) when a process group
 of g > 1 ranks is given: the residual stream is split by tokens; q/k/v and
@@ -143,8 +148,10 @@ class TensorParallel:
 
 class DecoderLayer:
     def __init__(self, cfg: DecoderConfig, w: Dict[str, torch.Tensor], table: torch.Tensor,
-                 ops, tp: TensorParallel):
-        self.cfg, self.table, self.ops, self.tp = cfg, table, ops, tp
+                 ops, tp: TensorParallel, attn: str = "sdpa"):
+        if attn not in ("sdpa", "eager"):
+            raise ValueError(f"attn must be 'sdpa' or 'eager', not {attn!r}")
+        self.cfg, self.table, self.ops, self.tp, self.attn = cfg, table, ops, tp, attn
         h, f = cfg.hidden, cfg.ffn
         if cfg.heads % tp.world:
             raise ValueError(f"{cfg.heads} heads do not split over {tp.world} ranks")
@@ -200,14 +207,22 @@ class DecoderLayer:
         q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
         sq, cq = self._qmx(q.contiguous())
         sk, ck = self._qmx(k.contiguous())
-        scores = ops.matmul_mx(cq, ck.transpose(-1, -2), input_scale=sq,
-                               weight_scale=sk.transpose(-1, -2), block_size=bs)
-        scores = scores * (1.0 / math.sqrt(hd)) + mask
-        probs = torch.softmax(scores, dim=-1, dtype=torch.float32).to(x.dtype)
-        sp, cp = self._qmx(probs)
         sv, cv = self._qmx(v.transpose(-1, -2).contiguous())
-        o = ops.matmul_mx(cp, cv.transpose(-1, -2), input_scale=sp,
-                          weight_scale=sv.transpose(-1, -2), block_size=bs)
+        if self.attn == "sdpa":
+            # scaled_dot_product_attention(is_causal=True), converted
+            o = ops.sdpa_mx(cq, ck, cv.transpose(-1, -2), is_causal=True, query_scale=sq,
+                            key_scale=sk, value_scale=sv.transpose(-1, -2), block_size=bs,
+                            probs_qmap=self.table, probs_quant_max=448.0,
+                            force_scale_power_of_two=True)
+        else:
+            # eager attention: matmul, scale, additive mask, float32 softmax
+            scores = ops.matmul_mx(cq, ck.transpose(-1, -2), input_scale=sq,
+                                   weight_scale=sk.transpose(-1, -2), block_size=bs)
+            scores = scores * (1.0 / math.sqrt(hd)) + mask
+            probs = torch.softmax(scores, dim=-1, dtype=torch.float32).to(x.dtype)
+            sp, cp = self._qmx(probs)
+            o = ops.matmul_mx(cp, cv.transpose(-1, -2), input_scale=sp,
+                              weight_scale=sv.transpose(-1, -2), block_size=bs)
         o = o.transpose(1, 2).reshape(T, hl)
         so, co = self._qmx(o)
         x = x + tp.reduce_scatter_rows(self._linear(co, so, self.o))
@@ -220,10 +235,16 @@ class DecoderLayer:
 
 class Decoder:
     """``cfg.layers`` decoder layers; ``ops`` defaults to
-    ``torch.ops.quantized_ops`` (this library's CUDA kernels)."""
+    ``torch.ops.quantized_ops`` (this library's CUDA kernels).  ``attn``:
+    "sdpa" -- the graph of a model exported with scaled-dot-product attention,
+    converted to ``sdpa_mx`` (one fused kernel); "eager" -- the eager
+    attention graph (``matmul_mx``, scale, additive causal mask, float32
+    softmax, ``quantize_mx`` of the probabilities, ``matmul_mx``).  Both
+    compute the same values."""
 
     def __init__(self, cfg: DecoderConfig, weights: List[Dict[str, torch.Tensor]], *,
-                 table: Optional[torch.Tensor] = None, ops=None, group=None):
+                 table: Optional[torch.Tensor] = None, ops=None, group=None,
+                 attn: str = "sdpa"):
         self.cfg = cfg
         self.tp = TensorParallel(group)
         self.ops = ops if ops is not None else _CudaOps()
@@ -232,7 +253,7 @@ class Decoder:
             from voyager_b200.tables import get_quantization_map
 
             table = get_quantization_map("fp8_e4m3", dev)
-        self.layers = [DecoderLayer(cfg, w, table, self.ops, self.tp) for w in weights]
+        self.layers = [DecoderLayer(cfg, w, table, self.ops, self.tp, attn) for w in weights]
         self._tabs = {}
 
     def _tables(self, seq: int, device, dtype):
@@ -278,6 +299,7 @@ class _CudaOps:
         self.quantize_mx = self._q.quantize_mx
         self.linear_mx = self._q.linear_mx
         self.matmul_mx = self._q.matmul_mx
+        self.sdpa_mx = self._q.sdpa_mx
 
     @staticmethod
     def mark_exact(codes, scale):

@@ -289,6 +289,24 @@ def matmul_mx(self, other, *, input_scale=None, weight_scale=None, block_size=No
                 weight_layout=weight_layout)
 
 
+def sdpa_mx(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False,
+            query_residual=None, key_residual=None, value_residual=None, residual_mask=None,
+            *, scale=None, enable_gqa=False, query_scale=None, key_scale=None, value_scale=None,
+            block_size=None, input_code=None, weight_code=None, probs_qmap=None,
+            probs_quant_max=None, probs_scale_qmap=None, probs_code=None,
+            force_scale_power_of_two=False):
+    """``quantized.py:651-784``."""
+    from voyager_b200.attention import sdpa_mx as impl
+
+    return impl(query, key, value, attn_mask, dropout_p, is_causal, query_residual,
+                key_residual, value_residual, residual_mask, scale=scale, enable_gqa=enable_gqa,
+                query_scale=query_scale, key_scale=key_scale, value_scale=value_scale,
+                block_size=block_size, input_code=input_code, weight_code=weight_code,
+                probs_qmap=probs_qmap, probs_quant_max=probs_quant_max,
+                probs_scale_qmap=probs_scale_qmap, probs_code=probs_code,
+                force_scale_power_of_two=force_scale_power_of_two)
+
+
 # ---------------------------------------------------------------------------
 # registration
 # ---------------------------------------------------------------------------
@@ -313,6 +331,16 @@ SCHEMAS = {
         "Tensor? weight_scale=None, int? block_size=None, Tensor? input_code=None, "
         "Tensor? weight_code=None, Tensor? A_data=None, Tensor? A_indices=None, "
         'Tensor? A_indptr=None, str weight_layout="ck") -> Tensor'),
+    "sdpa_mx": (
+        "sdpa_mx(Tensor query, Tensor key, Tensor value, Tensor? attn_mask=None, "
+        "float dropout_p=0., bool is_causal=False, Tensor? query_residual=None, "
+        "Tensor? key_residual=None, Tensor? value_residual=None, "
+        "Tensor? residual_mask=None, *, float? scale=None, "
+        "bool enable_gqa=False, Tensor? query_scale=None, Tensor? key_scale=None, "
+        "Tensor? value_scale=None, int? block_size=None, Tensor? input_code=None, "
+        "Tensor? weight_code=None, Tensor? probs_qmap=None, "
+        "float? probs_quant_max=None, Tensor? probs_scale_qmap=None, "
+        "Tensor? probs_code=None, bool force_scale_power_of_two=False) -> Tensor"),
     "calculate_mx_qparam": (
         "calculate_mx_qparam(Tensor self, SymInt[] axes, int block_size, "
         "float quant_max, bool force_scale_power_of_two=False, "
@@ -336,6 +364,7 @@ CUDA_IMPLS = {
     "quantize_affine": quantize_affine,
     "linear_mx": linear_mx,
     "matmul_mx": matmul_mx,
+    "sdpa_mx": sdpa_mx,
 }
 
 
@@ -381,8 +410,12 @@ def _meta_impls():
             other = other.transpose(-1, -2)
         return torch.matmul(self, other)
 
+    def sdpa(query, key, value, *a, **kw):
+        return query.new_empty(list(query.shape[:-1]) + [value.shape[-1]])
+
     return {"quantize": q, "dequantize": dq, "vmap": vm, "calculate_mx_qparam": mxq,
-            "quantize_mx": qmx, "quantize_affine": qaff, "linear_mx": lin, "matmul_mx": mm}
+            "quantize_mx": qmx, "quantize_affine": qaff, "linear_mx": lin, "matmul_mx": mm,
+            "sdpa_mx": sdpa}
 
 
 _LIBS = []
