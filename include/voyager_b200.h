@@ -270,6 +270,45 @@ int vq_attn_mxf8(const void* q, const void* q_sf, const void* k, const void* k_s
                  int32_t floor_log2_qmax, void* out, int64_t out_stride_b, int64_t out_stride_h,
                  int64_t out_stride_s, int32_t* d_err, void* stream);
 
+/* ---- Decoder-graph fusions feeding quantize_mx -------------------------------
+ * In a converted LLaMA layer, the bf16 graph ops in front of each MXFP8
+ * quantize_mx (quantized.py:854-881 with an E4M3 qmap, block 32 along the
+ * last dim, force_scale_power_of_two) computed and quantized in one pass.
+ * Each writes quantize_mx's two outputs (bf16 codes, bf16 scales) and the
+ * tcgen05 operand as vq_mx_pack lays it out (row_multiple 128; rows past the
+ * last are not written), and accepts only an E4M3 rounder with hw set.
+ * These entry points have no single counterpart in the reference: each
+ * replaces a chain of its graph's aten ops and one quantize_mx.
+ *
+ * RMSNorm (x * rsqrt(mean(x^2) + eps) in float32, to bf16, times weight)
+ * of x [rows, cols]; cols a multiple of 32.  Output [rows, cols]. */
+int vq_rmsnorm_quantize_mx(const void* x, const void* weight, int64_t rows, int64_t cols, float eps,
+                           const vq_rounder* qmap, int32_t floor_log2_qmax, void* codes,
+                           void* scale, void* packed, void* packed_sf, void* stream);
+/* Rotate-half RoPE (x * cos + cat(-x2, x1) * sin, each op rounded to bf16)
+ * of the q and k heads of a fused projection qkv [batch*seq, ld] (q heads of
+ * 128 at column q_off, k heads at k_off), cos / sin bf16 [seq, 128];
+ * outputs head-major [batch, heads, seq, 128] (blocks along head_dim). */
+int vq_rope_quantize_qk(const void* qkv, int64_t ld, int64_t q_off, int64_t k_off,
+                        const void* cos, const void* sin, int64_t batch, int64_t seq,
+                        int64_t heads, const vq_rounder* qmap, int32_t floor_log2_qmax,
+                        void* q_codes, void* q_scale, void* q_packed, void* q_sf, void* k_codes,
+                        void* k_scale, void* k_packed, void* k_sf, void* stream);
+/* The v heads of qkv (column v_off) quantized along the tokens (blocks of
+ * 32 tokens, seq a multiple of 128), written transposed: codes
+ * [batch, heads, 128, seq], scales [batch, heads, 128, seq / 32]: the
+ * value operand vq_attn_mxf8 takes. */
+int vq_quantize_vt(const void* qkv, int64_t ld, int64_t v_off, int64_t batch, int64_t seq,
+                   int64_t heads, const vq_rounder* qmap, int32_t floor_log2_qmax, void* codes,
+                   void* scale, void* packed, void* packed_sf, void* stream);
+/* bf16(silu(gate)) * up of gate_up [rows, ld] (gate at columns [0, cols),
+ * up at [up_off, up_off + cols)); silu = g / (1 + expf(-g)).  Output
+ * [rows, cols], cols a multiple of 32; the packed operand pads cols to 128
+ * with zero codes. */
+int vq_swiglu_quantize_mx(const void* gate_up, int64_t ld, int64_t up_off, int64_t rows,
+                          int64_t cols, const vq_rounder* qmap, int32_t floor_log2_qmax,
+                          void* codes, void* scale, void* packed, void* packed_sf, void* stream);
+
 /* ---- W4A8 (NVFP4 weights x MXFP8 activations) for few tokens --------------
  * The reference has no single op for this pair; its result is aten.linear of
  * the operands dequantized with their own block sizes

@@ -23,6 +23,7 @@
 #include <mutex>
 
 #include "vq_numerics.cuh"
+#include "vq_hw.cuh"
 
 namespace vq {
 
@@ -118,48 +119,6 @@ __device__ __forceinline__ void stage_table(const vq_rounder& r, uint16_t* stab)
   uint4* dst = reinterpret_cast<uint4*>(stab);
   for (int i = threadIdx.x; i < kTableBytes / 16; i += blockDim.x) dst[i] = __ldg(src + i);
   __syncthreads();
-}
-
-// Element kinds beyond vq_rounder_kind: a MINIFLOAT rounder that the
-// hardware conversions reproduce (vq_rounder.hw, verified on the device).
-constexpr int K_HW_E4M3 = 10, K_HW_E5M2 = 11, K_HW_E2M1 = 12;
-
-// Two bf16 indices (lo | hi << 16) through a hardware minifloat conversion
-// (round-to-nearest-even, saturating) and back: every value of these formats
-// is exactly a bf16, so the result is the table entry except for the two
-// cases the table treats specially: a -0 index gives +0, a NaN index gives
-// nan_bits.
-template <int K>
-__device__ __forceinline__ uint32_t hw_pair(uint32_t idx2, uint32_t nan_bits) {
-  const float lo = __uint_as_float(idx2 << 16);
-  const float hi = __uint_as_float(idx2 & 0xFFFF0000u);
-  uint32_t h2;
-  if (K == K_HW_E4M3) {
-    asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e4m3x2.f32 t, %1, %2;\n\t"
-        "cvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(h2) : "f"(hi), "f"(lo));
-  } else if (K == K_HW_E5M2) {
-    asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e5m2x2.f32 t, %1, %2;\n\t"
-        "cvt.rn.f16x2.e5m2x2 %0, t;\n\t}" : "=r"(h2) : "f"(hi), "f"(lo));
-  } else {
-    asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\t"
-        "cvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h2) : "f"(hi), "f"(lo));
-  }
-  const float flo = __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
-  const float fhi = __half2float(__ushort_as_half((unsigned short)(h2 >> 16)));
-  uint32_t out = (__float_as_uint(flo) >> 16) | (__float_as_uint(fhi) & 0xFFFF0000u);
-  const uint32_t mag = idx2 & 0x7FFF7FFFu;
-  out &= __vcmpne2(mag, 0u) | 0x7FFF7FFFu;          // -0 -> +0
-  const uint32_t nan = __vcmpgtu2(mag, 0x7F807F80u);  // NaN -> nan_bits
-  return (out & ~nan) | ((nan_bits * 0x10001u) & nan);
-}
-
-// bf16 indices of two quotients, packed: the exact patterns for a table
-// (NaN -> 0xFFFF), the hardware pair conversion otherwise.
-template <int K>
-__device__ __forceinline__ uint32_t pair_index(float q0, float q1) {
-  if (K == VQ_R_TABLE) return f2bf(q0) | (f2bf(q1) << 16);
-  __nv_bfloat162 b = __floats2bfloat162_rn(q0, q1);
-  return *reinterpret_cast<uint32_t*>(&b);
 }
 
 template <int K>

@@ -113,6 +113,16 @@ _SIGNATURES = {
     "vq_attn_mxf8": (ctypes.c_int, [ctypes.c_void_p] * 6 + [ctypes.c_int64] * 6
                      + [ctypes.c_float, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]
                      + [ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_rmsnorm_quantize_mx": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                              ctypes.c_int64, ctypes.c_float, P(VqRounder),
+                                              ctypes.c_int32] + [ctypes.c_void_p] * 5),
+    "vq_rope_quantize_qk": (ctypes.c_int, [ctypes.c_void_p] + [ctypes.c_int64] * 3
+                            + [ctypes.c_void_p] * 2 + [ctypes.c_int64] * 3
+                            + [P(VqRounder), ctypes.c_int32] + [ctypes.c_void_p] * 9),
+    "vq_quantize_vt": (ctypes.c_int, [ctypes.c_void_p] + [ctypes.c_int64] * 5
+                       + [P(VqRounder), ctypes.c_int32] + [ctypes.c_void_p] * 5),
+    "vq_swiglu_quantize_mx": (ctypes.c_int, [ctypes.c_void_p] + [ctypes.c_int64] * 4
+                              + [P(VqRounder), ctypes.c_int32] + [ctypes.c_void_p] * 5),
     "vq_w4_pack_weights": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p,
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "vq_a8_pack": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p, ctypes.c_void_p,

@@ -148,10 +148,11 @@ class TensorParallel:
 
 class DecoderLayer:
     def __init__(self, cfg: DecoderConfig, w: Dict[str, torch.Tensor], table: torch.Tensor,
-                 ops, tp: TensorParallel, attn: str = "sdpa"):
+                 ops, tp: TensorParallel, attn: str = "sdpa", fused: bool = False):
         if attn not in ("sdpa", "eager"):
             raise ValueError(f"attn must be 'sdpa' or 'eager', not {attn!r}")
         self.cfg, self.table, self.ops, self.tp, self.attn = cfg, table, ops, tp, attn
+        self.fused = fused
         h, f = cfg.hidden, cfg.ffn
         if cfg.heads % tp.world:
             raise ValueError(f"{cfg.heads} heads do not split over {tp.world} ranks")
@@ -181,9 +182,17 @@ class DecoderLayer:
         return self.ops.linear_mx(codes, w[0], None, input_scale=scale, weight_scale=w[1],
                                   block_size=self.cfg.block_size)
 
-    def _gathered_qmx(self, x: torch.Tensor):
-        """quantize_mx of the token shard, then all-gather codes and scales."""
-        scale, codes = self._qmx(x)
+    def _gathered_qmx(self, x: torch.Tensor, norm_w: Optional[torch.Tensor] = None):
+        """quantize_mx of the token shard (RMSNorm'd first when ``norm_w`` is
+        given), then all-gather codes and scales."""
+        if norm_w is None:
+            scale, codes = self._qmx(x)
+        elif self.fused:
+            from voyager_b200 import fused
+
+            scale, codes = fused.rmsnorm_quantize_mx(x, norm_w, self.cfg.eps, self.table)
+        else:
+            scale, codes = self._qmx(rms_norm(x, norm_w, self.cfg.eps))
         codes = self.tp.all_gather_rows(codes)
         scale = self.tp.all_gather_rows(scale)
         mark = getattr(self.ops, "mark_exact", None)
@@ -201,13 +210,20 @@ class DecoderLayer:
         nh, hd = cfg.heads // tp.world, cfg.head_dim
         hl = nh * hd
         # --- attention ---------------------------------------------------
-        codes, scale = self._gathered_qmx(rms_norm(x, self.ln1, cfg.eps))
+        codes, scale = self._gathered_qmx(x, self.ln1)
         qkv = self._linear(codes, scale, self.qkv)                    # [T, 3 hl]
-        q, k, v = (t.reshape(batch, S, nh, hd).transpose(1, 2) for t in qkv.split(hl, -1))
-        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
-        sq, cq = self._qmx(q.contiguous())
-        sk, ck = self._qmx(k.contiguous())
-        sv, cv = self._qmx(v.transpose(-1, -2).contiguous())
+        if self.fused and S % 128 == 0:
+            from voyager_b200 import fused
+
+            (sq, cq), (sk, ck) = fused.rope_quantize_qk(qkv, 0, hl, cos, sin, batch, S, nh,
+                                                        self.table)
+            sv, cv = fused.quantize_vt(qkv, 2 * hl, batch, S, nh, self.table)
+        else:
+            q, k, v = (t.reshape(batch, S, nh, hd).transpose(1, 2) for t in qkv.split(hl, -1))
+            q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+            sq, cq = self._qmx(q.contiguous())
+            sk, ck = self._qmx(k.contiguous())
+            sv, cv = self._qmx(v.transpose(-1, -2).contiguous())
         if self.attn == "sdpa":
             # scaled_dot_product_attention(is_causal=True), converted
             o = ops.sdpa_mx(cq, ck, cv.transpose(-1, -2), is_causal=True, query_scale=sq,
@@ -227,9 +243,15 @@ class DecoderLayer:
         so, co = self._qmx(o)
         x = x + tp.reduce_scatter_rows(self._linear(co, so, self.o))
         # --- SwiGLU MLP ----------------------------------------------------
-        codes, scale = self._gathered_qmx(rms_norm(x, self.ln2, cfg.eps))
-        g, u = self._linear(codes, scale, self.gu).chunk(2, -1)
-        sa, ca = self._qmx(torch.nn.functional.silu(g) * u)
+        codes, scale = self._gathered_qmx(x, self.ln2)
+        gu = self._linear(codes, scale, self.gu)
+        if self.fused:
+            from voyager_b200 import fused
+
+            sa, ca = fused.swiglu_quantize_mx(gu, gu.shape[-1] // 2, self.table)
+        else:
+            g, u = gu.chunk(2, -1)
+            sa, ca = self._qmx(torch.nn.functional.silu(g) * u)
         return x + tp.reduce_scatter_rows(self._linear(ca, sa, self.down))
 
 
@@ -240,11 +262,13 @@ class Decoder:
     converted to ``sdpa_mx`` (one fused kernel); "eager" -- the eager
     attention graph (``matmul_mx``, scale, additive causal mask, float32
     softmax, ``quantize_mx`` of the probabilities, ``matmul_mx``).  Both
-    compute the same values."""
+    compute the same values.  ``fused`` (default: with the CUDA ops) runs
+    RMSNorm, RoPE, the v transpose and SwiGLU inside the quantize_mx that
+    follows each of them (``voyager_b200.fused``)."""
 
     def __init__(self, cfg: DecoderConfig, weights: List[Dict[str, torch.Tensor]], *,
                  table: Optional[torch.Tensor] = None, ops=None, group=None,
-                 attn: str = "sdpa"):
+                 attn: str = "sdpa", fused: Optional[bool] = None):
         self.cfg = cfg
         self.tp = TensorParallel(group)
         self.ops = ops if ops is not None else _CudaOps()
@@ -253,7 +277,10 @@ class Decoder:
             from voyager_b200.tables import get_quantization_map
 
             table = get_quantization_map("fp8_e4m3", dev)
-        self.layers = [DecoderLayer(cfg, w, table, self.ops, self.tp, attn) for w in weights]
+        if fused is None:
+            fused = isinstance(self.ops, _CudaOps)
+        self.layers = [DecoderLayer(cfg, w, table, self.ops, self.tp, attn, fused)
+                       for w in weights]
         self._tabs = {}
 
     def _tables(self, seq: int, device, dtype):
