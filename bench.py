@@ -48,7 +48,7 @@ def parse():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", default=None, choices=["c1", "c2", "c3", "c4", "c5"],
+    ap.add_argument("--only", default=None, choices=["c1", "c2", "c3", "c4", "c5", "attn"],
                     help="profiling aid: run only this workload's kernels, no JSON line")
     return ap.parse_args()
 
@@ -634,6 +634,18 @@ def run_only(args):
         x = torch.randn((8 * 2048, cfg.hidden), device=dev).bfloat16()
         for _ in range(args.warmup + args.steps):
             dec.forward_shard(x, 8)
+    elif args.only == "attn":
+        # the C5 attention at batch 2: causal sdpa_mx, 32 heads, S 2048
+        B, H, S = 2, 32, 2048
+        e4m3 = get_quantization_map("fp8_e4m3", dev)
+        q, k, v = (torch.randn((B, H, S, 128), device=dev).bfloat16() for _ in range(3))
+        sq, cq = Q.quantize_mx(q, e4m3, [-1], 32, 448.0, True)
+        sk, ck = Q.quantize_mx(k, e4m3, [-1], 32, 448.0, True)
+        sv, cv = Q.quantize_mx(v.transpose(-1, -2).contiguous(), e4m3, [-1], 32, 448.0, True)
+        for _ in range(args.warmup + args.steps):
+            Q.sdpa_mx(cq, ck, cv.transpose(-1, -2), is_causal=True, query_scale=sq, key_scale=sk,
+                      value_scale=sv.transpose(-1, -2), block_size=32, probs_qmap=e4m3,
+                      probs_quant_max=448.0, force_scale_power_of_two=True)
     elif args.only == "c4":
         from voyager_b200 import w4a8
 

@@ -29,8 +29,9 @@
 // Since P is final after pass 1, O needs no rescaling.
 //
 // Warps: 0 TMA producer (Q double-buffered, K / V^T tiles through a 6-slot
-// ring), 1 TMEM owner + single-thread MMA issuer, 2-9 softmax (two warps per
-// TMEM lane quarter, each on 64 of the 128 columns).  Every wait is bounded
+// ring), 1 TMEM owner + single-thread MMA issuer, 2-17 softmax (four warps
+// per TMEM lane quarter, each on 32 of the 128 columns: one block of 32
+// probabilities per thread and tile).  Every wait is bounded
 // and sets *err when it gives up; no TMA multicast.
 //
 // exp is evaluated as ex2.approx((s - m) * log2 e); probabilities of a
@@ -56,7 +57,8 @@ constexpr int TILE_BYTES = 128 * 128;  // one E4M3 tile (128 rows x 128 bytes)
 constexpr int SF_BYTES = 512;          // one UE8M0 scale atom (128 rows x 4 blocks)
 constexpr int SLOT = 17408;            // tile + atom, 1024-aligned
 constexpr int RING = 6;
-constexpr int SM_WARPS = 8;            // softmax warps
+constexpr int SM_WARPS = 16;           // softmax warps
+constexpr int NG = SM_WARPS / 4;       // column groups of 32 per TMEM lane quarter
 constexpr int SMT = 32 * SM_WARPS;     // softmax threads
 constexpr int THREADS = 64 + SMT;
 
@@ -64,8 +66,8 @@ constexpr int OFF_Q = 0;                         // 2 slots
 constexpr int OFF_RING = 2 * SLOT;               // RING slots
 constexpr int OFF_P = (2 + RING) * SLOT;         // 2 slots
 constexpr int OFF_BAR = (4 + RING) * SLOT;
-constexpr int OFF_STATS = OFF_BAR + 256;         // float2 [2 items][2 groups][128 rows]
-constexpr int SMEM_TOTAL = OFF_STATS + 2 * 2 * 128 * 8;
+constexpr int OFF_STATS = OFF_BAR + 256;         // float2 [2 items][NG groups][128 rows]
+constexpr int SMEM_TOTAL = OFF_STATS + 2 * NG * 128 * 8;
 
 // barrier indices
 constexpr int B_RFULL = 0, B_REMPTY = RING, B_QFULL = 2 * RING, B_QEMPTY = B_QFULL + 2,
@@ -116,12 +118,12 @@ __device__ __forceinline__ float ex2(float x) {
 }
 constexpr float L2E = 1.4426950408889634f;
 
-// 64 score columns of one row -> 32 packed bf16 pairs of
+// 32 score columns of one row -> 16 packed bf16 pairs of
 // bf16(bf16(acc) * scale), -inf where the key lies past the query.
-__device__ __forceinline__ void scores_bf16(const uint32_t (&v)[64], float scale, int key0,
-                                            int q_idx, bool diag, uint32_t (&tb)[32]) {
+__device__ __forceinline__ void scores_bf16(const uint32_t (&v)[32], float scale, int key0,
+                                            int q_idx, bool diag, uint32_t (&tb)[16]) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
+  for (int i = 0; i < 16; ++i) {
     const uint32_t s2 = bf2_rn(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
     uint32_t t2 = bf2_rn(bf_lo(s2) * scale, bf_hi(s2) * scale);
     if (diag) {
@@ -323,9 +325,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // ---------------- softmax + P quantization + O epilogue ----------------
     const int wq = warp & 3;           // TMEM lane quarter
-    const int grp = (warp - 2) >> 2;   // column half
+    const int grp = (warp - 2) >> 2;   // column group: columns grp * 32 .. + 31
     const int r = wq * 32 + lane;      // row in the tile
-    const int cb = grp * 64;           // first column of this thread
+    const int cb = grp * 32;
     const uint32_t tq = tmem + ((uint32_t)(wq * 32) << 16);
     int sb = 0, pb = 0, it = 0;
     uint32_t sph = 0, pph = 0, oph = 0;
@@ -334,13 +336,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       int bh, qt, nkv;
       item_coords(a, t, bh, qt, nkv);
       const int q_idx = qt * 128 + r;
-      auto load_s = [&](uint32_t (&v)[64]) -> bool {
+      auto load_s = [&](uint32_t (&v)[32]) -> bool {
         if (!mbar_wait_warp(bar(B_SFULL + sb), sph, a.err, ERR_S)) return false;
         tc_fence_after();
-        uint32_t(&v0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[0]);
-        uint32_t(&v1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&v[32]);
-        tmem_ld32(tq + COL_S + sb * 128 + cb, v0);
-        tmem_ld32(tq + COL_S + sb * 128 + cb + 32, v1);
+        tmem_ld32(tq + COL_S + sb * 128 + cb, v);
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(bar(B_SEMPTY + sb));
@@ -350,88 +349,90 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         return true;
       };
-      // ---- pass 1: row max and sum of exp over this thread's columns ----
+      // ---- pass 1: row max and sum of exp over this thread's 32 columns ----
       float m = -INFINITY, l = 0.f;
       for (int kt = 0; kt < nkv; ++kt) {
-        uint32_t v[64], tb[32];
+        uint32_t v[32], tb[16];
         if (!(ok = load_s(v))) break;
         scores_bf16(v, a.scale, kt * 128 + cb, q_idx, a.causal && kt == qt, tb);
         __nv_bfloat162 mx2 = *reinterpret_cast<__nv_bfloat162*>(&tb[0]);
 #pragma unroll
-        for (int i = 1; i < 32; ++i) mx2 = __hmax2(mx2, *reinterpret_cast<__nv_bfloat162*>(&tb[i]));
-        const float tmax = fmaxf(__low2float(mx2), __high2float(mx2));
-        const float mn = fmaxf(m, tmax);
-        if (mn == -INFINITY) continue;  // every key of this tile is masked for this row
-        float sum = 0.f;
+        for (int i = 1; i < 16; ++i) mx2 = __hmax2(mx2, *reinterpret_cast<__nv_bfloat162*>(&tb[i]));
+        const float mn = fmaxf(m, fmaxf(__low2float(mx2), __high2float(mx2)));
+        if (mn == -INFINITY) continue;  // every key of this group is masked for this row
+        const float nml = -mn * L2E;
+        float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          sum += ex2((bf_lo(tb[i]) - mn) * L2E) + ex2((bf_hi(tb[i]) - mn) * L2E);
-        l = l * ex2((m - mn) * L2E) + sum;
+        for (int i = 0; i < 16; ++i) {
+          s0 += ex2(fmaf(bf_lo(tb[i]), L2E, nml));
+          s1 += ex2(fmaf(bf_hi(tb[i]), L2E, nml));
+        }
+        l = l * ex2((m - mn) * L2E) + (s0 + s1);
         m = mn;
       }
       if (!ok) break;
-      // ---- combine the two column halves of each row ----
-      float2* slot = stats + (it & 1) * 256;
+      // ---- combine the column groups of each row (same order everywhere) ----
+      float2* slot = stats + (it & 1) * (NG * 128);
       slot[grp * 128 + r] = make_float2(m, l);
       mbar_arrive(bar(B_STATS + (it & 1)));
       if (!(ok = mbar_wait_warp(bar(B_STATS + (it & 1)), (it >> 1) & 1, a.err, ERR_STATS))) break;
-      const float2 s0 = slot[r], s1 = slot[128 + r];
-      const float M = fmaxf(s0.x, s1.x);
-      const float L = (s0.x == -INFINITY ? 0.f : s0.y * ex2((s0.x - M) * L2E)) +
-                      (s1.x == -INFINITY ? 0.f : s1.y * ex2((s1.x - M) * L2E));
+      float2 st[NG];
+#pragma unroll
+      for (int g = 0; g < NG; ++g) st[g] = slot[g * 128 + r];
+      float M = st[0].x;
+#pragma unroll
+      for (int g = 1; g < NG; ++g) M = fmaxf(M, st[g].x);
+      float L = 0.f;
+#pragma unroll
+      for (int g = 0; g < NG; ++g)
+        L += st[g].x == -INFINITY ? 0.f : st[g].y * ex2((st[g].x - M) * L2E);
       const float rinv = __frcp_rn(L);
+      const float nml = -M * L2E;
       // ---- pass 2: P = bf16(exp(s - M) / L) as MXFP8 into shared memory ----
       for (int kt = 0; kt < nkv; ++kt) {
-        uint32_t v[64], tb[32];
+        uint32_t v[32], tb[16];
         if (!(ok = load_s(v))) break;
         scores_bf16(v, a.scale, kt * 128 + cb, q_idx, a.causal && kt == qt, tb);
+        uint32_t p2[16];
+        uint32_t am = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float e0 = ex2(fmaf(bf_lo(tb[i]), L2E, nml));
+          const float e1 = ex2(fmaf(bf_hi(tb[i]), L2E, nml));
+          p2[i] = bf2_rn(e0 * rinv, e1 * rinv);
+          am = __vmaxu2(am, p2[i]);
+        }
+        const uint32_t sbits = pow2_scale_bf16(max(am & 0xFFFFu, am >> 16), a.fl2q);
+        const uint32_t ue = (sbits >> 7) & 0xFFu;
+        uint32_t c[8];
+        if (ue == 0) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) c[i] = 0;
+        } else {
+          // 1 / scale = 2^(127 - ue), exact
+          const float inv = __uint_as_float((254u - min(ue, 253u)) << 23);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            uint16_t b0, b1;
+            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;"
+                : "=h"(b0)
+                : "f"(bf_hi(p2[2 * i]) * inv), "f"(bf_lo(p2[2 * i]) * inv));
+            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;"
+                : "=h"(b1)
+                : "f"(bf_hi(p2[2 * i + 1]) * inv), "f"(bf_lo(p2[2 * i + 1]) * inv));
+            c[i] = (uint32_t)b0 | ((uint32_t)b1 << 16);
+          }
+        }
         if (!(ok = mbar_wait_warp(bar(B_PEMPTY + pb), pph ^ 1, a.err, ERR_P))) break;
         uint8_t* sp = smem + OFF_P + pb * SLOT;
-        uint32_t ue2 = 0;
-#pragma unroll
-        for (int blk = 0; blk < 2; ++blk) {
-          uint32_t p2[16];
-          uint32_t am = 0;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const uint32_t w = tb[blk * 16 + i];
-            const float e0 = ex2((bf_lo(w) - M) * L2E), e1 = ex2((bf_hi(w) - M) * L2E);
-            p2[i] = bf2_rn(e0 * rinv, e1 * rinv);
-            am = __vmaxu2(am, p2[i]);
-          }
-          const uint32_t amax = max(am & 0xFFFFu, am >> 16);
-          const uint32_t sbits = pow2_scale_bf16(amax, a.fl2q);
-          uint32_t ue = (sbits >> 7) & 0xFFu;
-          uint32_t c[8];
-          if (ue == 0) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) c[i] = 0;
-          } else {
-            // 1 / scale = 2^(127 - ue), exact
-            const float inv = __uint_as_float((254u - min(ue, 253u)) << 23);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              uint16_t b0, b1;
-              asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;"
-                  : "=h"(b0)
-                  : "f"(bf_hi(p2[2 * i]) * inv), "f"(bf_lo(p2[2 * i]) * inv));
-              asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;"
-                  : "=h"(b1)
-                  : "f"(bf_hi(p2[2 * i + 1]) * inv), "f"(bf_lo(p2[2 * i + 1]) * inv));
-              c[i] = (uint32_t)b0 | ((uint32_t)b1 << 16);
-            }
-          }
-          ue2 |= ue << (8 * blk);
-          // 32 codes = logical 16-byte chunks ch, ch + 1 of row r (SWIZZLE_128B)
-          const int ch = (cb + blk * 32) / 16;
-          *reinterpret_cast<uint4*>(sp + r * 128 + ((ch ^ (r & 7)) * 16)) =
-              make_uint4(c[0], c[1], c[2], c[3]);
-          *reinterpret_cast<uint4*>(sp + r * 128 + (((ch + 1) ^ (r & 7)) * 16)) =
-              make_uint4(c[4], c[5], c[6], c[7]);
-        }
-        // scale bytes j = 2 * grp, 2 * grp + 1 of row r in the atom
-        *reinterpret_cast<uint16_t*>(sp + TILE_BYTES + (r % 32) * 16 + (r / 32) * 4 + grp * 2) =
-            (uint16_t)ue2;
+        // 32 codes = logical 16-byte chunks 2 grp, 2 grp + 1 of row r (SWIZZLE_128B)
+        const int ch = 2 * grp;
+        *reinterpret_cast<uint4*>(sp + r * 128 + ((ch ^ (r & 7)) * 16)) =
+            make_uint4(c[0], c[1], c[2], c[3]);
+        *reinterpret_cast<uint4*>(sp + r * 128 + (((ch + 1) ^ (r & 7)) * 16)) =
+            make_uint4(c[4], c[5], c[6], c[7]);
+        // scale byte j = grp of row r in the atom
+        sp[TILE_BYTES + (r % 32) * 16 + (r / 32) * 4 + grp] = (uint8_t)ue;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive(bar(B_PFULL + pb));
         if (++pb == 2) {
@@ -440,13 +441,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       if (!ok) break;
-      // ---- O epilogue ----
+      // ---- O epilogue: this thread's 32 of the 128 head dims ----
       if (!(ok = mbar_wait_warp(bar(B_OFULL), oph, a.err, ERR_O))) break;
       oph ^= 1;
       tc_fence_after();
-      uint32_t o0[32], o1[32];
+      uint32_t o0[32];
       tmem_ld32(tq + COL_O + cb, o0);
-      tmem_ld32(tq + COL_O + cb + 32, o1);
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(bar(B_OEMPTY));
@@ -459,13 +459,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                             bf2_rn(__uint_as_float(o0[8 * i + 2]), __uint_as_float(o0[8 * i + 3])),
                             bf2_rn(__uint_as_float(o0[8 * i + 4]), __uint_as_float(o0[8 * i + 5])),
                             bf2_rn(__uint_as_float(o0[8 * i + 6]), __uint_as_float(o0[8 * i + 7])));
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        dst[4 + i] =
-            make_uint4(bf2_rn(__uint_as_float(o1[8 * i]), __uint_as_float(o1[8 * i + 1])),
-                       bf2_rn(__uint_as_float(o1[8 * i + 2]), __uint_as_float(o1[8 * i + 3])),
-                       bf2_rn(__uint_as_float(o1[8 * i + 4]), __uint_as_float(o1[8 * i + 5])),
-                       bf2_rn(__uint_as_float(o1[8 * i + 6]), __uint_as_float(o1[8 * i + 7])));
     }
   }
   __syncthreads();

@@ -19,9 +19,10 @@
 //   warp 1  TMEM owner and MMA issuer: per K tile, tcgen05.cp of the scale
 //           atoms into TMEM, then 4 x tcgen05.mma.kind::mxf8f6f4.block_scale
 //           (M=128, N=256, K=32) accumulating in TMEM (fp32, 256 columns);
-//   warps 2-5 epilogue: tcgen05.ld of the accumulator, + bias, round to bf16,
-//           store.  One accumulator buffer: the MMA warp waits for the
-//           epilogue to drain it before the next tile.
+//   warps 2-9 epilogue: tcgen05.ld of the accumulator (two warps per lane
+//           quarter, 128 columns each), + bias, round to bf16; the
+//           accumulator is released before the global stores, so the MMA
+//           warp waits only for the TMEM reads.
 // Every wait is bounded; a wait that gives up sets *err and the kernel ends.
 // No TMA multicast is used.
 #include <cuda.h>
@@ -50,7 +51,7 @@ constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;    // 256 fp32 columns
 constexpr int SFA_COL = 256;  // 4 columns
 constexpr int SFB_COL = 260;  // 8 columns
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;
 
 enum { ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_TIMEOUT_ACC = 3 };
 
@@ -97,7 +98,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(empty0 + 8 * s, 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 128);
+    mbar_init(acc_empty, 256);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -198,8 +199,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // ---------------- epilogue (warps 2..9) ----------------
+    // Two warps per TMEM lane quarter, each on half of the 256 columns.  The
+    // accumulator is read into registers (as bf16) and released before the
+    // stores, so the next tile's MMAs overlap them.
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;       // columns half * 128 .. + 127
     const int row_in_tile = q * 32 + lane;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < g.ntiles; t += gridDim.x) {
@@ -208,48 +213,43 @@ __global__ void __launch_bounds__(THREADS, 1)
       acc_phase ^= 1;
       tc_fence_after();
       const int row = tm * BM + row_in_tile;
-      uint16_t* orow = g.out + (int64_t)row * g.ldo;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + ACC_COL + c0;
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-            "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-              "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-              "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-              "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-              "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-              "=r"(r[31])
-            : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        const int col0 = tn * BN + c0;
-        if (row < g.M && col0 < g.N) {
-          uint32_t packed[16];
+      const int colh = tn * BN + half * 128;
+      uint32_t packed[64];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float v0 = __uint_as_float(r[2 * i]), v1 = __uint_as_float(r[2 * i + 1]);
-            if (g.bias) {
-              v0 += bf2f(g.bias[min(col0 + 2 * i, g.N - 1)]);
-              v1 += bf2f(g.bias[min(col0 + 2 * i + 1, g.N - 1)]);
-            }
-            __nv_bfloat162 b = __floats2bfloat162_rn(v0, v1);
-            packed[i] = *reinterpret_cast<uint32_t*>(&b);
-          }
-          if (col0 + 32 <= g.N) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + col0);
+      for (int c2 = 0; c2 < 2; ++c2) {
+        uint32_t r0[32], r1[32];
+        const uint32_t taddr =
+            tmem + ((uint32_t)(q * 32) << 16) + ACC_COL + half * 128 + c2 * 64;
+        tmem_ld32(taddr, r0);
+        tmem_ld32(taddr + 32, r1);
+        tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
-          } else {
-            for (int i = 0; i < 32 && col0 + i < g.N; ++i)
-              orow[col0 + i] = (uint16_t)((packed[i / 2] >> (16 * (i & 1))) & 0xFFFFu);
+        for (int i = 0; i < 16; ++i) {
+          float v0 = __uint_as_float(r0[2 * i]), v1 = __uint_as_float(r0[2 * i + 1]);
+          float w0 = __uint_as_float(r1[2 * i]), w1 = __uint_as_float(r1[2 * i + 1]);
+          if (g.bias) {
+            const int c = colh + c2 * 64 + 2 * i;
+            v0 += bf2f(g.bias[min(c, g.N - 1)]);
+            v1 += bf2f(g.bias[min(c + 1, g.N - 1)]);
+            w0 += bf2f(g.bias[min(c + 32, g.N - 1)]);
+            w1 += bf2f(g.bias[min(c + 33, g.N - 1)]);
           }
+          __nv_bfloat162 b0 = __floats2bfloat162_rn(v0, v1), b1 = __floats2bfloat162_rn(w0, w1);
+          packed[c2 * 32 + i] = *reinterpret_cast<uint32_t*>(&b0);
+          packed[c2 * 32 + 16 + i] = *reinterpret_cast<uint32_t*>(&b1);
         }
       }
       tc_fence_before();
       mbar_arrive(acc_empty);
+      if (row < g.M && colh < g.N) {
+        uint16_t* orow = g.out + (int64_t)row * g.ldo;
+        // N is a multiple of 8: whole 16-byte groups up to the last column
+        uint4* dst = reinterpret_cast<uint4*>(orow + colh);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (colh + 8 * i < g.N)
+            dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+      }
     }
   }
   __syncthreads();
