@@ -433,7 +433,7 @@ def run_tp_linear(dev, pg, world):
             "gpus": world, "note": "weight N-sharded, output all-gathered (NCCL)"}
 
 
-def run_c5(dev, pg, world, bf16_peak, reps=3, warm=2):
+def run_c5(dev, pg, world, bf16_peak, reps=8, warm=2):
     """C5: the 4-layer LLaMA-style decoder forward (hidden 4096, 32 heads,
     ffn 11008, B=8, S=2048) through the MXFP8 quantized graph; tensor
     parallel over the ranks when world > 1 (strong scaling of one forward).

@@ -34,10 +34,11 @@
 // probabilities per thread and tile).  Every wait is bounded
 // and sets *err when it gives up; no TMA multicast.
 //
-// exp is evaluated as ex2.approx((s - m) * log2 e); probabilities of a
-// block of 32 keys whose largest value is below 2^-118 (a subnormal block
-// scale) are given code 0: their share of an output row is below 2^-100 of
-// the row's largest probability.
+// exp is evaluated as ex2.approx.ftz(s * log2 e - m * log2 e); a block of 32
+// probabilities whose largest value is below 2^-108 is given code 0 (the
+// flush-to-zero exp and the subnormal block scales live there): its share
+// of an output row is below 2^-90 of the row's largest probability, which
+// is at least 1 / keys.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -111,9 +112,10 @@ __device__ __forceinline__ uint32_t bf2_rn(float lo, float hi) {
   __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&b);
 }
+// 2^x, one MUFU op; results below 2^-126 flush to zero
 __device__ __forceinline__ float ex2(float x) {
   float y;
-  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 constexpr float L2E = 1.4426950408889634f;
@@ -402,10 +404,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           p2[i] = bf2_rn(e0 * rinv, e1 * rinv);
           am = __vmaxu2(am, p2[i]);
         }
-        const uint32_t sbits = pow2_scale_bf16(max(am & 0xFFFFu, am >> 16), a.fl2q);
+        const uint32_t amax = max(am & 0xFFFFu, am >> 16);
+        const uint32_t sbits = pow2_scale_bf16(amax, a.fl2q);
         const uint32_t ue = (sbits >> 7) & 0xFFu;
         uint32_t c[8];
-        if (ue == 0) {
+        if ((amax >> 7) < 19u) {  // block max below 2^-108: codes 0
 #pragma unroll
           for (int i = 0; i < 8; ++i) c[i] = 0;
         } else {

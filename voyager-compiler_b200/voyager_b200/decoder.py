@@ -115,8 +115,8 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
 class TensorParallel:
     """The process group a decoder is split over (world 1: no collectives)."""
 
-    def __init__(self, group=None):
-        on = dist.is_available() and dist.is_initialized()
+    def __init__(self, group=None, enabled: bool = True):
+        on = enabled and dist.is_available() and dist.is_initialized()
         self.group = group
         self.world = dist.get_world_size(group) if on else 1
         self.rank = dist.get_rank(group) if on else 0
@@ -256,7 +256,9 @@ class DecoderLayer:
 
 
 class Decoder:
-    """``cfg.layers`` decoder layers; ``ops`` defaults to
+    """``cfg.layers`` decoder layers, tensor parallel over ``group`` (the
+    default process group when one is initialised; ``parallel=False`` keeps
+    the whole model on this rank); ``ops`` defaults to
     ``torch.ops.quantized_ops`` (this library's CUDA kernels).  ``attn``:
     "sdpa" -- the graph of a model exported with scaled-dot-product attention,
     converted to ``sdpa_mx`` (one fused kernel); "eager" -- the eager
@@ -268,9 +270,9 @@ class Decoder:
 
     def __init__(self, cfg: DecoderConfig, weights: List[Dict[str, torch.Tensor]], *,
                  table: Optional[torch.Tensor] = None, ops=None, group=None,
-                 attn: str = "sdpa", fused: Optional[bool] = None):
+                 attn: str = "sdpa", fused: Optional[bool] = None, parallel: bool = True):
         self.cfg = cfg
-        self.tp = TensorParallel(group)
+        self.tp = TensorParallel(group, parallel)
         self.ops = ops if ops is not None else _CudaOps()
         dev = weights[0]["q"].device
         if table is None:
