@@ -445,10 +445,11 @@ def run_c5(dev, pg, world, bf16_peak, reps=8, warm=2):
 
     cfg, B, S = DecoderConfig(), 8, 2048
     dec = Decoder(cfg, init_weights(cfg, 0, dev), group=None)
+    columns = dec.columns
     torch.cuda.empty_cache()
     g = torch.Generator(device=dev).manual_seed(1)
     x = torch.randn((B * S, cfg.hidden), generator=g, device=dev).bfloat16()
-    xs = x[dec.tp.split(B * S, "tokens")].contiguous()
+    xs = dec.shard(x)
     del x
     stream = torch.cuda.current_stream(dev)
     for _ in range(warm):
@@ -469,14 +470,17 @@ def run_c5(dev, pg, world, bf16_peak, reps=8, warm=2):
         ms = float(t.item())
     tf = cfg.flops(B, S) / (ms / 1e3) / 1e12
     peak = 2 * bf16_peak
-    del dec
+    dec.check_errors()
+    del dec, xs
     torch.cuda.empty_cache()
     return {"ms": round(ms, 2), "TFLOPs": round(tf, 1), "gpus": world,
             "frac_fp8_dense": round(tf / peak, 3),
             "fp8_dense_peak_TFLOPs": peak,
             "flop_per_forward": cfg.flops(B, S),
-            "parallelism": f"tp{world} (Megatron, sequence-parallel norms)" if world > 1
-            else "1 GPU"}
+            "parallelism": ("1 GPU" if world == 1 else
+                            f"tp{world}, column-parallel linears, operands all-gathered by "
+                            "NVLS multicast stores" if columns else
+                            f"tp{world} (Megatron, sequence-parallel norms, NCCL)")}
 
 
 def _time_graph_ms(fn, stream, reps=20, warm=3):

@@ -221,6 +221,14 @@ int vq_gemm_mxf8(const void* a, const void* a_sf, const void* b, const void* b_s
                  int64_t N, int64_t K, const void* bias, void* out, int64_t ldo, int32_t* d_err,
                  void* stream);
 
+/* vq_gemm_mxf8 followed by the graph's residual add:
+ * out = bf16(bf16(A . B^T (+ bias)) + residual), residual bf16 [M, ldr]
+ * (ldr >= N, a multiple of 8); out may be the residual buffer itself
+ * (each element is read before it is written, by the same thread). */
+int vq_gemm_mxf8_ex(const void* a, const void* a_sf, const void* b, const void* b_sf, int64_t M,
+                    int64_t N, int64_t K, const void* bias, const void* residual, int64_t ldr,
+                    void* out, int64_t ldo, int32_t* d_err, void* stream);
+
 /* MXFP8 linear that allocates nothing: for callers that cannot call
  * cudaMalloc -- an allocator-free runtime, code running under a caller-owned
  * memory budget, or a library hook invoked where allocating is not allowed.
@@ -308,6 +316,45 @@ int vq_quantize_vt(const void* qkv, int64_t ld, int64_t v_off, int64_t batch, in
 int vq_swiglu_quantize_mx(const void* gate_up, int64_t ld, int64_t up_off, int64_t rows,
                           int64_t cols, const vq_rounder* qmap, int32_t floor_log2_qmax,
                           void* codes, void* scale, void* packed, void* packed_sf, void* stream);
+
+/* ---- Tensor-parallel decoder collectives (NVLink / NVSwitch) ---------------
+ * No reference counterpart: the reference runs on one device.  These serve
+ * the column-parallel decoder (every linear split by output features, the
+ * residual stream split by hidden columns): a rank quantizes its column
+ * shard and writes the MXFP8 operand (E4M3 bytes at packed + row * ld +
+ * col_off, UE8M0 words in the [K/128][row_tiles][512] atom layout) through
+ * a multicast address, so every rank's copy of the full-width operand is
+ * filled by one store.  *_mc pointers are NVLS multicast addresses of
+ * symmetric buffers; col_off and the shard width are multiples of 128.
+ *
+ * Barrier over the ranks: thread j stores `epoch` into rank j's flag
+ * array at [rank] (peer_flag_ptrs: device array of the ranks' flag array
+ * addresses) and waits until my_flags[j] >= epoch; a wait longer than 2 s
+ * sets *d_err = 100 + j and returns. */
+int vq_tp_barrier(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int32_t world,
+                  uint32_t epoch, int32_t* d_err, void* stream);
+/* stats_mc[rank][row] = sum of squares of this rank's columns of x [rows, cols]. */
+int vq_tp_sumsq(const void* x, int64_t rows, int64_t cols, void* stats_mc, int32_t rank,
+                void* stream);
+/* RMSNorm of this rank's columns (statistic: the ranks' partial sums added in
+ * rank order, divided by full_cols) times its weight slice, quantized to
+ * MXFP8 (quantize_mx with an E4M3 table, power-of-two scales, block 32). */
+int vq_tp_norm_quantize(const void* x, int64_t rows, int64_t cols, const void* stats,
+                        int32_t world, int64_t full_cols, const void* weight, float eps,
+                        const vq_rounder* qmap, int32_t floor_log2_qmax, void* packed_mc,
+                        void* atoms_mc, int64_t ld, int64_t col_off, int64_t row_tiles,
+                        void* stream);
+/* MXFP8 quantization of bf16 x [rows, cols] (row stride ldx). */
+int vq_tp_quantize(const void* x, int64_t ldx, int64_t rows, int64_t cols, const vq_rounder* qmap,
+                   int32_t floor_log2_qmax, void* packed_mc, void* atoms_mc, int64_t ld,
+                   int64_t col_off, int64_t row_tiles, void* stream);
+/* bf16(silu(gate)) * up (gate at columns [0, cols), up at [up_off,
+ * up_off + cols) of gate_up) quantized to MXFP8; the shard's operand width is
+ * cols rounded up to 128, the extra columns zero codes with scale 1. */
+int vq_tp_swiglu_quantize(const void* gate_up, int64_t ld_in, int64_t up_off, int64_t rows,
+                          int64_t cols, const vq_rounder* qmap, int32_t floor_log2_qmax,
+                          void* packed_mc, void* atoms_mc, int64_t ld, int64_t col_off,
+                          int64_t row_tiles, void* stream);
 
 /* ---- W4A8 (NVFP4 weights x MXFP8 activations) for few tokens --------------
  * The reference has no single op for this pair; its result is aten.linear of

@@ -120,3 +120,18 @@ def test_tensor_parallel_2_ranks_matches_single():
     assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))  # gathered output
     want = _single()
     assert rel_l2(y0, want) < 1e-2, rel_l2(y0, want)
+
+
+def test_pad_k_chunks_layout():
+    """The column-parallel down projection's K layout: per-rank chunks of the
+    ffn padded to 128 with zeros, products unchanged."""
+    from voyager_b200.tp import pad_k_chunks
+
+    w = torch.arange(3 * 1376 * 2, dtype=torch.float32).reshape(3, 2 * 1376)
+    p = pad_k_chunks(w, 2)
+    assert p.shape == (3, 2 * 1408)
+    assert torch.equal(p[:, :1376], w[:, :1376]) and torch.equal(p[:, 1408:2784], w[:, 1376:])
+    assert not p[:, 1376:1408].any() and not p[:, 2784:].any()
+    a = torch.randn(5, 2 * 1376)
+    ap = pad_k_chunks(a, 2)
+    assert torch.allclose(a @ w.T, ap @ p.T)

@@ -71,7 +71,9 @@ struct GemmArgs {
   const uint8_t* sfa;  // [KT][MT][512]
   const uint8_t* sfb;  // [KT][NT128][512]
   const uint16_t* bias;  // bf16 [N] or null
-  uint16_t* out;         // bf16 [M, ldo]
+  const uint16_t* residual;  // bf16 [M, ldr] added after the bf16 rounding, or null
+  int64_t ldr;
+  uint16_t* out;         // bf16 [M, ldo] (may be the residual itself)
   int64_t ldo;
   int M, N, KT;          // KT = Kp / 128
   int MT, NT128, NTILE_N, ntiles;
@@ -243,6 +245,25 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_arrive(acc_empty);
       if (row < g.M && colh < g.N) {
         uint16_t* orow = g.out + (int64_t)row * g.ldo;
+        if (g.residual) {
+          // out = bf16(bf16(acc) + residual): the residual add that follows
+          // the linear in the graph, one rounding per op
+          const uint4* rrow = reinterpret_cast<const uint4*>(g.residual + (int64_t)row * g.ldr + colh);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (colh + 8 * i >= g.N) break;
+            const uint4 rv = rrow[i];
+            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t pw = packed[4 * i + k];
+              __nv_bfloat162 b = __floats2bfloat162_rn(
+                  __uint_as_float(pw << 16) + __uint_as_float(rw[k] << 16),
+                  __uint_as_float(pw & 0xFFFF0000u) + __uint_as_float(rw[k] & 0xFFFF0000u));
+              packed[4 * i + k] = *reinterpret_cast<uint32_t*>(&b);
+            }
+          }
+        }
         // N is a multiple of 8: whole 16-byte groups up to the last column
         uint4* dst = reinterpret_cast<uint4*>(orow + colh);
 #pragma unroll
@@ -451,7 +472,15 @@ int vq_mx_pack(const vq_tensor* codes, const vq_tensor* scale, int64_t block_siz
 int vq_gemm_mxf8(const void* a, const void* a_sf, const void* b, const void* b_sf, int64_t M,
                  int64_t N, int64_t K, const void* bias, void* out, int64_t ldo, int32_t* d_err,
                  void* stream) {
+  return vq_gemm_mxf8_ex(a, a_sf, b, b_sf, M, N, K, bias, nullptr, 0, out, ldo, d_err, stream);
+}
+
+int vq_gemm_mxf8_ex(const void* a, const void* a_sf, const void* b, const void* b_sf, int64_t M,
+                    int64_t N, int64_t K, const void* bias, const void* residual, int64_t ldr,
+                    void* out, int64_t ldo, int32_t* d_err, void* stream) {
   if (!a || !a_sf || !b || !b_sf || !out || !d_err) return VQ_ERR_NULL;
+  if (residual && (ldr < N || ldr % 8 || (reinterpret_cast<uintptr_t>(residual) & 15)))
+    return VQ_ERR_UNSUPPORTED;
   if (M <= 0 || N <= 0 || K <= 0) return VQ_ERR_INVALID;
   if (N % 8 != 0 || ldo < N || ldo % 8 != 0) return VQ_ERR_UNSUPPORTED;
   if (M > (1 << 30) || N > (1 << 30)) return VQ_ERR_UNSUPPORTED;
@@ -471,6 +500,8 @@ int vq_gemm_mxf8(const void* a, const void* a_sf, const void* b, const void* b_s
   g.sfa = (const uint8_t*)a_sf;
   g.sfb = (const uint8_t*)b_sf;
   g.bias = (const uint16_t*)bias;
+  g.residual = (const uint16_t*)residual;
+  g.ldr = ldr;
   g.out = (uint16_t*)out;
   g.ldo = ldo;
   g.M = (int)M;

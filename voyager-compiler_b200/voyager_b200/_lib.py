@@ -123,6 +123,29 @@ _SIGNATURES = {
                        + [P(VqRounder), ctypes.c_int32] + [ctypes.c_void_p] * 5),
     "vq_swiglu_quantize_mx": (ctypes.c_int, [ctypes.c_void_p] + [ctypes.c_int64] * 4
                               + [P(VqRounder), ctypes.c_int32] + [ctypes.c_void_p] * 5),
+    "vq_gemm_mxf8_ex": (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3
+                        + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                           ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_tp_barrier": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                     ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p,
+                                     ctypes.c_void_p]),
+    "vq_tp_sumsq": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                   ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]),
+    "vq_tp_norm_quantize": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
+                                           ctypes.c_void_p, ctypes.c_float, P(VqRounder),
+                                           ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                           ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_void_p]),
+    "vq_tp_quantize": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                      ctypes.c_int64, P(VqRounder), ctypes.c_int32,
+                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                      ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]),
+    "vq_tp_swiglu_quantize": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                             ctypes.c_int64, ctypes.c_int64, P(VqRounder),
+                                             ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                             ctypes.c_void_p]),
     "vq_w4_pack_weights": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p,
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     "vq_a8_pack": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p, ctypes.c_void_p,

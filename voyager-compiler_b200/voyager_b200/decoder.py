@@ -255,6 +255,134 @@ class DecoderLayer:
         return x + tp.reduce_scatter_rows(self._linear(ca, sa, self.down))
 
 
+class ColumnParallelLayer:
+    """A decoder layer with every linear split by output features over the
+    group (column parallel) and the residual stream split by hidden columns:
+    rank r holds x[:, r*H/g:(r+1)*H/g] for all tokens, the q/k/v rows of its
+    H/g / 128 heads, o_proj's and down's output rows of its hidden columns
+    and gate/up's rows of its ffn columns.  Every GEMM sums over its full K,
+    so each output value is the one-GPU value; the only cross-rank arithmetic
+    is RMSNorm's row statistic, summed from the ranks' partial sums in rank
+    order.  Each linear's input -- the normalised activations (twice), the
+    attention output and the SwiGLU activation -- is quantized by the rank
+    that owns its columns and written straight into every rank's copy of the
+    full-width MXFP8 operand through NVLS multicast (``voyager_b200.tp``);
+    one barrier follows each such write, six per layer."""
+
+    def __init__(self, cfg: DecoderConfig, w: Dict[str, torch.Tensor], table: torch.Tensor,
+                 tp: TensorParallel):
+        from voyager_b200.tp import pad_k_chunks
+
+        g, r = tp.world, tp.rank
+        h, f = cfg.hidden, cfg.ffn
+        if cfg.heads % g or h % g or f % g:
+            raise ValueError(f"heads / hidden / ffn do not split over {g} ranks")
+        self.hs, self.fs = h // g, f // g
+        if self.hs % 128 or self.fs % 32:
+            raise ValueError(f"hidden shard {self.hs} (multiple of 128) or ffn shard {self.fs} "
+                             "(multiple of 32) does not fit the MXFP8 operand tiles")
+        self.fs_p = (self.fs + 127) // 128 * 128
+        self.cfg, self.table, self.tp = cfg, table, tp
+        hsl, fsl = slice(r * self.hs, (r + 1) * self.hs), slice(r * self.fs, (r + 1) * self.fs)
+        self.ln1 = w["ln1"][hsl].contiguous()
+        self.ln2 = w["ln2"][hsl].contiguous()
+        q = torch.ops.quantized_ops
+
+        def quant(wt):
+            s_, c_ = q.quantize_mx(wt.contiguous(), table, [-1], cfg.block_size, 448.0, True)
+            return c_, s_
+
+        self.qkv = quant(torch.cat([w["q"][hsl], w["k"][hsl], w["v"][hsl]], 0))
+        self.o = quant(w["o"][hsl])
+        self.gu = quant(torch.cat([w["gate"][fsl], w["up"][fsl]], 0))
+        self.down = quant(pad_k_chunks(w["down"][hsl], g))
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.ln1.device)
+
+    def operands(self) -> Dict[str, int]:
+        h = self.cfg.hidden
+        return {"h1": h, "o": h, "h2": h, "act": self.tp.world * self.fs_p}
+
+    def _gemm(self, ws, name, wq, out, residual=None):
+        from voyager_b200 import mxgemm
+        from voyager_b200.ops import _stream
+
+        K, a_p, a_s, _, _ = ws.operand(name)
+        pw, pws, ok = mxgemm.packed_weight(wq[0], wq[1])
+        if not ok:
+            raise RuntimeError("column-parallel decoder: weight operand is not exact MXFP8")
+        N = wq[0].shape[0]
+        st = _lib().vq_gemm_mxf8_ex(
+            a_p, a_s, pw.data_ptr(), pws.data_ptr(), ws.T, N, K, None,
+            None if residual is None else residual.data_ptr(), N, out.data_ptr(), N,
+            self.err.data_ptr(), _stream(out.device))
+        _check(st, "column-parallel decoder GEMM")
+
+    def _norm(self, ws, x, weight, name, rd, fl2q, stream):
+        lib = _lib()
+        _check(lib.vq_tp_sumsq(x.data_ptr(), ws.T, self.hs, ws.stats_mc(), ws.rank, stream),
+               "tp sumsq")
+        ws.barrier(stream)
+        _, _, _, p_mc, a_mc = ws.operand(name)
+        _check(lib.vq_tp_norm_quantize(x.data_ptr(), ws.T, self.hs, ws.stats_local(), ws.world,
+                                       self.cfg.hidden, weight.data_ptr(), float(self.cfg.eps),
+                                       rd.ref(), fl2q, p_mc, a_mc, self.cfg.hidden,
+                                       ws.rank * self.hs, ws.RT, stream), "tp norm quantize")
+        ws.barrier(stream)
+
+    def __call__(self, x: torch.Tensor, ws, batch: int, cos, sin) -> torch.Tensor:
+        """x: [T, H/g], this rank's hidden columns (updated in place)."""
+        from voyager_b200 import fused
+        from voyager_b200.ops import _stream, floor_log2
+        from voyager_b200.tables import rounder_for
+
+        cfg, g = self.cfg, self.tp.world
+        T, dev = x.shape[0], x.device
+        S, nh, hs = T // batch, cfg.heads // g, self.hs
+        stream = _stream(dev)
+        rd = rounder_for(self.table, dev)
+        fl2q = floor_log2(448.0)
+        lib = _lib()
+        # attention block
+        self._norm(ws, x, self.ln1, "h1", rd, fl2q, stream)
+        qkv = torch.empty((T, 3 * hs), dtype=torch.bfloat16, device=dev)
+        self._gemm(ws, "h1", self.qkv, qkv)
+        (sq, cq), (sk, ck) = fused.rope_quantize_qk(qkv, 0, hs, cos, sin, batch, S, nh, self.table)
+        sv, cv = fused.quantize_vt(qkv, 2 * hs, batch, S, nh, self.table)
+        o = torch.ops.quantized_ops.sdpa_mx(
+            cq, ck, cv.transpose(-1, -2), is_causal=True, query_scale=sq, key_scale=sk,
+            value_scale=sv.transpose(-1, -2), block_size=cfg.block_size, probs_qmap=self.table,
+            probs_quant_max=448.0, force_scale_power_of_two=True)
+        o = o.transpose(1, 2).reshape(T, hs)
+        _, _, _, p_mc, a_mc = ws.operand("o")
+        _check(lib.vq_tp_quantize(o.data_ptr(), hs, T, hs, rd.ref(), fl2q, p_mc, a_mc,
+                                  cfg.hidden, ws.rank * hs, ws.RT, stream), "tp quantize")
+        ws.barrier(stream)
+        self._gemm(ws, "o", self.o, x, residual=x)
+        # MLP block
+        self._norm(ws, x, self.ln2, "h2", rd, fl2q, stream)
+        gu = torch.empty((T, 2 * self.fs), dtype=torch.bfloat16, device=dev)
+        self._gemm(ws, "h2", self.gu, gu)
+        K, _, _, p_mc, a_mc = ws.operand("act")
+        _check(lib.vq_tp_swiglu_quantize(gu.data_ptr(), 2 * self.fs, self.fs, T, self.fs,
+                                         rd.ref(), fl2q, p_mc, a_mc, K, ws.rank * self.fs_p,
+                                         ws.RT, stream), "tp swiglu quantize")
+        ws.barrier(stream)
+        self._gemm(ws, "act", self.down, x, residual=x)
+        return x
+
+
+def _lib():
+    from voyager_b200 import _lib as L
+
+    return L.load()
+
+
+def _check(st, what):
+    from voyager_b200 import _lib as L
+
+    L.check(st, what)
+
+
 class Decoder:
     """``cfg.layers`` decoder layers, tensor parallel over ``group`` (the
     default process group when one is initialised; ``parallel=False`` keeps
@@ -270,7 +398,8 @@ class Decoder:
 
     def __init__(self, cfg: DecoderConfig, weights: List[Dict[str, torch.Tensor]], *,
                  table: Optional[torch.Tensor] = None, ops=None, group=None,
-                 attn: str = "sdpa", fused: Optional[bool] = None, parallel: bool = True):
+                 attn: str = "sdpa", fused: Optional[bool] = None, parallel: bool = True,
+                 tp_mode: str = "auto"):
         self.cfg = cfg
         self.tp = TensorParallel(group, parallel)
         self.ops = ops if ops is not None else _CudaOps()
@@ -281,9 +410,22 @@ class Decoder:
             table = get_quantization_map("fp8_e4m3", dev)
         if fused is None:
             fused = isinstance(self.ops, _CudaOps)
-        self.layers = [DecoderLayer(cfg, w, table, self.ops, self.tp, attn, fused)
-                       for w in weights]
+        if tp_mode not in ("auto", "columns", "megatron"):
+            raise ValueError(f"tp_mode must be auto, columns or megatron, not {tp_mode!r}")
+        self.columns = False
+        if self.tp.world > 1 and tp_mode != "megatron" and isinstance(self.ops, _CudaOps):
+            from voyager_b200.tp import multicast_available
+
+            self.columns = tp_mode == "columns" or (
+                multicast_available(group) and attn == "sdpa" and fused
+                and (cfg.hidden // self.tp.world) % 128 == 0)
+        if self.columns:
+            self.layers = [ColumnParallelLayer(cfg, w, table, self.tp) for w in weights]
+        else:
+            self.layers = [DecoderLayer(cfg, w, table, self.ops, self.tp, attn, fused)
+                           for w in weights]
         self._tabs = {}
+        self._ws = None
 
     def _tables(self, seq: int, device, dtype):
         key = (seq, device, dtype)
@@ -294,25 +436,64 @@ class Decoder:
             self._tabs[key] = (cos, sin, mask)
         return self._tabs[key]
 
+    def shard(self, flat: torch.Tensor) -> torch.Tensor:
+        """The part of the [T, H] hidden states this rank's forward_shard
+        takes: its token rows (Megatron split) or its hidden columns (column
+        split)."""
+        if self.columns:
+            return flat[:, self.tp.split(flat.shape[1], "hidden")].contiguous()
+        return flat[self.tp.split(flat.shape[0], "tokens")].contiguous()
+
+    def unshard(self, y: torch.Tensor) -> torch.Tensor:
+        """The full [T, H] from every rank's shard (an all-gather)."""
+        if not self.columns:
+            return self.tp.all_gather_rows(y)
+        g = self.tp.world
+        parts = self.tp.all_gather_rows(y)  # [g * T, H/g]
+        T = y.shape[0]
+        return parts.view(g, T, -1).permute(1, 0, 2).reshape(T, -1)
+
+    def _workspace(self, tokens: int, device):
+        from voyager_b200.tp import Workspace
+
+        if self._ws is None or self._ws.T != tokens:
+            self._ws = None
+            self._ws = Workspace(self.tp.group, tokens, self.layers[0].operands(), device)
+        return self._ws
+
     @torch.no_grad()
     def forward_shard(self, x: torch.Tensor, batch: int) -> torch.Tensor:
-        """x: this rank's token shard [batch * S / g, H] -> the shard after
-        all layers."""
+        """x: this rank's shard (``shard``) -> the shard after all layers."""
+        if self.columns:
+            T = x.shape[0]
+            cos, sin, _ = self._tables(T // batch, x.device, x.dtype)
+            ws = self._workspace(T, x.device)
+            x = x.clone()
+            for layer in self.layers:
+                x = layer(x, ws, batch, cos, sin)
+            return x
         S = x.shape[0] * self.tp.world // batch
         cos, sin, mask = self._tables(S, x.device, x.dtype)
         for layer in self.layers:
             x = layer(x, batch, cos, sin, mask)
         return x
 
+    def check_errors(self):
+        """Raise if a bounded device wait gave up since the workspace was made."""
+        if self._ws is not None:
+            self._ws.check()
+        for layer in self.layers:
+            err = getattr(layer, "err", None)
+            if err is not None and int(err.item()):
+                raise RuntimeError(f"decoder GEMM: device wait timed out ({int(err.item())})")
+
     @torch.no_grad()
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """x: the full hidden states [B, S, H] (the same on every rank) ->
         [B, S, H]; with g > 1 ranks the output is all-gathered."""
         B, S, H = x.shape
-        flat = x.reshape(B * S, H)
-        lo = self.tp.split(B * S, "tokens")
-        y = self.forward_shard(flat[lo].contiguous(), B)
-        return self.tp.all_gather_rows(y).reshape(B, S, H)
+        y = self.forward_shard(self.shard(x.reshape(B * S, H)), B)
+        return self.unshard(y).reshape(B, S, H)
 
     __call__ = forward
 
