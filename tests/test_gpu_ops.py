@@ -54,6 +54,10 @@ def test_golden_case(case):
         if case["op"] in ("linear_mx", "matmul_mx"):
             want = getattr(oracle, case["op"])(*ins, **kw)
             assert G.rel_l2(g, want) < 1e-3
+        elif case["op"] == "sdpa_mx":
+            # float32 sums in another order and a hardware exp: the same
+            # bound as tests/test_gpu_attention.py, against the reference
+            assert G.rel_l2(g, w) < 2e-3
         else:
             bad = G.bit_mismatches(g, w)
             assert len(bad) == 0, f"{len(bad)} mismatches, first at {bad[:5]}"
