@@ -429,8 +429,10 @@ def run_tp_linear(dev, pg, world):
     t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
     pg.all_reduce(t, op=pg.ReduceOp.MAX)
     ms = float(t.item())
+    mode = ("output columns copied into every rank through an NVLS multicast address"
+            if lin.multicast else "output all-gathered (NCCL)")
     return {"ms": round(ms, 3), "TFLOPs": round(2 * 8192 * 4096 * 11008 / (ms / 1e3) / 1e12, 1),
-            "gpus": world, "note": "weight N-sharded, output all-gathered (NCCL)"}
+            "gpus": world, "note": f"weight N-sharded, {mode}"}
 
 
 def run_c5(dev, pg, world, bf16_peak, reps=8, warm=2):
@@ -483,6 +485,27 @@ def run_c5(dev, pg, world, bf16_peak, reps=8, warm=2):
                             f"tp{world} (Megatron, sequence-parallel norms, NCCL)")}
 
 
+def _time_cold_ms(fn, stream, dev, reps=20, warm=3):
+    """Mean device time of fn with the L2 flushed before each launch (a
+    256 MB buffer written between launches, outside the timed events)."""
+    import torch
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(warm):
+        fn()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(reps)]
+    for a, b in ev:
+        flush.zero_()
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / reps
+    del flush
+    return ms
+
+
 def _time_graph_ms(fn, stream, reps=20, warm=3):
     """Device time of fn replayed from a CUDA graph (for µs-scale calls whose
     eager time is the host's launch cost, as in a graph-captured decode)."""
@@ -529,6 +552,12 @@ def run_secondary(dev, hbm_peak, peaks):
     out["c1_dequantize_GBps"] = round(n * 4.125 / (td / 1e3) / 1e9, 1)
     out["c1_quantize_mx_frac_hbm"] = round(out["c1_quantize_mx_GBps"] / hbm_peak, 3)
     out["c1_note"] = "16.8M elems, 69 MB per launch (fits L2: warm-L2 figure)"
+    tqc = _time_cold_ms(lambda: Q.quantize_mx(x, e2m1, [-1], 16, 6.0, False, e4m3), stream, dev)
+    tdc = _time_cold_ms(lambda: Q.dequantize(c, s, None, [-1], 16), stream, dev)
+    out["c1_cold"] = {"quantize_mx_GBps": round(n * 4.125 / (tqc / 1e3) / 1e9, 1),
+                      "dequantize_GBps": round(n * 4.125 / (tdc / 1e3) / 1e9, 1),
+                      "quantize_mx_frac_hbm": round(n * 4.125 / (tqc / 1e3) / 1e9 / hbm_peak, 3),
+                      "note": "L2 flushed (256 MB written) before every timed launch"}
     # C3 MXFP8 linear
     try:
         a_np, w_np = synth.c3_operands()

@@ -221,13 +221,18 @@ int vq_gemm_mxf8(const void* a, const void* a_sf, const void* b, const void* b_s
                  int64_t N, int64_t K, const void* bias, void* out, int64_t ldo, int32_t* d_err,
                  void* stream);
 
-/* vq_gemm_mxf8 followed by the graph's residual add:
- * out = bf16(bf16(A . B^T (+ bias)) + residual), residual bf16 [M, ldr]
- * (ldr >= N, a multiple of 8); out may be the residual buffer itself
- * (each element is read before it is written, by the same thread). */
+/* vq_gemm_mxf8 with two epilogue options.
+ * residual (or NULL): the graph's residual add after the linear,
+ *   out = bf16(bf16(A . B^T (+ bias)) + residual), residual bf16 [M, ldr]
+ *   (ldr >= N, a multiple of 8); out may be the residual buffer itself (each
+ *   element is read before it is written, by the same thread).
+ * out_multicast: `out` is an NVLS multicast address of a symmetric buffer
+ *   (tensor parallel over N: every rank's copy of the full output receives
+ *   this rank's columns from one store); not with a residual. */
 int vq_gemm_mxf8_ex(const void* a, const void* a_sf, const void* b, const void* b_sf, int64_t M,
                     int64_t N, int64_t K, const void* bias, const void* residual, int64_t ldr,
-                    void* out, int64_t ldo, int32_t* d_err, void* stream);
+                    void* out, int64_t ldo, int32_t out_multicast, int32_t* d_err,
+                    void* stream);
 
 /* MXFP8 linear that allocates nothing: for callers that cannot call
  * cudaMalloc -- an allocator-free runtime, code running under a caller-owned
@@ -333,6 +338,11 @@ int vq_swiglu_quantize_mx(const void* gate_up, int64_t ld, int64_t up_off, int64
  * sets *d_err = 100 + j and returns. */
 int vq_tp_barrier(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int32_t world,
                   uint32_t epoch, int32_t* d_err, void* stream);
+/* rows x row_bytes from src (row stride src_ld bytes) into every rank's copy
+ * of a symmetric buffer through its multicast address (row stride dst_ld
+ * bytes); all sizes and addresses 16-byte aligned. */
+int vq_tp_copy_multicast(const void* src, int64_t src_ld, int64_t rows, int64_t row_bytes,
+                         void* dst_mc, int64_t dst_ld, void* stream);
 /* stats_mc[rank][row] = sum of squares of this rank's columns of x [rows, cols]. */
 int vq_tp_sumsq(const void* x, int64_t rows, int64_t cols, void* stats_mc, int32_t rank,
                 void* stream);
@@ -367,15 +377,16 @@ int vq_tp_swiglu_quantize(const void* gate_up, int64_t ld_in, int64_t up_off, in
 int vq_w4_pack_weights(const vq_tensor* codes, const vq_tensor* scales, void* wq, void* ws,
                        int32_t* d_inexact, void* stream);
 
-/* Pack bf16 E4M3 codes [M, K] to bytes and bf16 scales [M, K/32] to float. */
-int vq_a8_pack(const vq_tensor* codes, const vq_tensor* scales, void* aq, float* as,
-               int32_t* d_inexact, void* stream);
+/* Dequantize the tokens as _dequantize_mx does (bf16(code x scale)): bf16
+ * codes [M, K] and scales [M, K/32] -> bf16 [16, K] (rows M..15 zero),
+ * M <= 16, K % 128 == 0. */
+int vq_a8_dequant(const vq_tensor* codes, const vq_tensor* scales, void* out16, void* stream);
 
-/* out[M, N] bf16 = A . W^T (+ bias) for M <= 16, from the packed operands;
+/* out[M, N] bf16 = A . W^T (+ bias) for M <= 16 from the dequantized tokens
+ * a16 (bf16 [16, K], vq_a8_dequant) and the packed weights; K % 128 == 0;
  * `workspace` is float32 [M, N] scratch (zeroed by the call). */
-int vq_w4a8_linear_small(const void* aq, const float* as, const void* wq, const void* ws,
-                         int64_t M, int64_t N, int64_t K, const void* bias, float* workspace,
-                         void* out, void* stream);
+int vq_w4a8_linear_small(const void* a16, const void* wq, const void* ws, int64_t M, int64_t N,
+                         int64_t K, const void* bias, float* workspace, void* out, void* stream);
 
 /* The per-block parameters of quantized_ops::quantize_affine
  * (quantized.py:884-948): for blocks of `block_size` elements along the one

@@ -54,10 +54,17 @@ def _worker(rank, world, port, q):
         sa, ca = Q.quantize_mx(a, e4m3, [-1], 32, 448.0, True)
         sw, cw = Q.quantize_mx(w, e4m3, [-1], 32, 448.0, True)
         full = Q.linear_mx(ca, cw, None, input_scale=sa, weight_scale=sw, block_size=32)
-        lin = parallel.NShardedLinear(cw, sw)
-        y = lin(ca, sa)
-        torch.cuda.synchronize()
-        q.put((rank, bool(torch.equal(y, full)), tuple(y.shape)))
+        same, shape = True, None
+        for mc in (False, True):  # NCCL all-gather, then the multicast epilogue
+            lin = parallel.NShardedLinear(cw, sw, multicast=mc)
+            for _ in range(2):  # the second call reuses the symmetric buffer
+                y = lin(ca, sa)
+                torch.cuda.synchronize()
+                same = same and bool(torch.equal(y, full))
+                shape = tuple(y.shape)
+            if mc:
+                lin._ws.check()
+        q.put((rank, same, shape))
     finally:
         dist.destroy_process_group()
 

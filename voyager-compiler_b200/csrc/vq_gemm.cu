@@ -75,6 +75,7 @@ struct GemmArgs {
   int64_t ldr;
   uint16_t* out;         // bf16 [M, ldo] (may be the residual itself)
   int64_t ldo;
+  int out_mc;            // out is an NVLS multicast address: multimem stores
   int M, N, KT;          // KT = Kp / 128
   int MT, NT128, NTILE_N, ntiles;
   int* err;
@@ -266,10 +267,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         // N is a multiple of 8: whole 16-byte groups up to the last column
         uint4* dst = reinterpret_cast<uint4*>(orow + colh);
+        if (g.out_mc) {
+          // one store reaches every rank's copy of the output
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (colh + 8 * i < g.N)
-            dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+          for (int i = 0; i < 16; ++i)
+            if (colh + 8 * i < g.N)
+              asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                               dst + i),
+                           "f"(__uint_as_float(packed[4 * i])), "f"(__uint_as_float(packed[4 * i + 1])),
+                           "f"(__uint_as_float(packed[4 * i + 2])),
+                           "f"(__uint_as_float(packed[4 * i + 3]))
+                           : "memory");
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (colh + 8 * i < g.N)
+              dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+        }
       }
     }
   }
@@ -472,12 +486,15 @@ int vq_mx_pack(const vq_tensor* codes, const vq_tensor* scale, int64_t block_siz
 int vq_gemm_mxf8(const void* a, const void* a_sf, const void* b, const void* b_sf, int64_t M,
                  int64_t N, int64_t K, const void* bias, void* out, int64_t ldo, int32_t* d_err,
                  void* stream) {
-  return vq_gemm_mxf8_ex(a, a_sf, b, b_sf, M, N, K, bias, nullptr, 0, out, ldo, d_err, stream);
+  return vq_gemm_mxf8_ex(a, a_sf, b, b_sf, M, N, K, bias, nullptr, 0, out, ldo, 0, d_err,
+                         stream);
 }
 
 int vq_gemm_mxf8_ex(const void* a, const void* a_sf, const void* b, const void* b_sf, int64_t M,
                     int64_t N, int64_t K, const void* bias, const void* residual, int64_t ldr,
-                    void* out, int64_t ldo, int32_t* d_err, void* stream) {
+                    void* out, int64_t ldo, int32_t out_multicast, int32_t* d_err,
+                    void* stream) {
+  if (out_multicast && residual) return VQ_ERR_UNSUPPORTED;
   if (!a || !a_sf || !b || !b_sf || !out || !d_err) return VQ_ERR_NULL;
   if (residual && (ldr < N || ldr % 8 || (reinterpret_cast<uintptr_t>(residual) & 15)))
     return VQ_ERR_UNSUPPORTED;
@@ -504,6 +521,7 @@ int vq_gemm_mxf8_ex(const void* a, const void* a_sf, const void* b, const void* 
   g.ldr = ldr;
   g.out = (uint16_t*)out;
   g.ldo = ldo;
+  g.out_mc = out_multicast ? 1 : 0;
   g.M = (int)M;
   g.N = (int)N;
   g.KT = (int)KT;

@@ -276,6 +276,22 @@ __global__ void __launch_bounds__(256) k_tp_swiglu_qmx(const __grid_constant__ S
   quant16_store(v, row, c16, a.d, a.fl2q, a.nan_bits);
 }
 
+// ---------------------------------------------------------------------------
+// A [rows, bytes] block copied into every rank's copy of a symmetric buffer:
+// consecutive threads take consecutive 16-byte pieces of a row, so each warp
+// store is 512 contiguous bytes through the multicast address.
+__global__ void __launch_bounds__(256) k_tp_copy_mc(const uint8_t* src, int64_t lds, uint8_t* dst,
+                                                    int64_t ldd, int64_t rows, int64_t bytes) {
+  const int64_t per_row = bytes / 16;
+  const int64_t total = rows * per_row;
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * 256) {
+    const int64_t r = i / per_row, c = (i % per_row) * 16;
+    const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src + r * lds + c));
+    mc_st_v4(dst + r * ldd + c, v.x, v.y, v.z, v.w);
+  }
+}
+
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 int check_dest(const Dest& d, int C) {
@@ -304,6 +320,20 @@ int vq_tp_barrier(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int3
   if (world < 1 || world > 64 || rank < 0 || rank >= world) return VQ_ERR_INVALID;
   k_tp_barrier<<<1, 64, 0, (cudaStream_t)stream>>>((const uint64_t*)peer_flag_ptrs,
                                                    (uint32_t*)my_flags, rank, world, epoch, d_err);
+  return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
+}
+
+int vq_tp_copy_multicast(const void* src, int64_t src_ld, int64_t rows, int64_t row_bytes,
+                         void* dst_mc, int64_t dst_ld, void* stream) {
+  if (!src || !dst_mc) return VQ_ERR_NULL;
+  if (rows <= 0 || row_bytes <= 0 || row_bytes % 16 || src_ld % 16 || dst_ld % 16 ||
+      src_ld < row_bytes || dst_ld < row_bytes)
+    return VQ_ERR_INVALID;
+  if (!al16(src) || !al16(dst_mc)) return VQ_ERR_ALIGNMENT;
+  const int64_t total = rows * (row_bytes / 16);
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
+  k_tp_copy_mc<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      (const uint8_t*)src, src_ld, (uint8_t*)dst_mc, dst_ld, rows, row_bytes);
   return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
 }
 

@@ -125,10 +125,13 @@ _SIGNATURES = {
                               + [P(VqRounder), ctypes.c_int32] + [ctypes.c_void_p] * 5),
     "vq_gemm_mxf8_ex": (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3
                         + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
-                           ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
+                           ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
     "vq_tp_barrier": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                      ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p,
                                      ctypes.c_void_p]),
+    "vq_tp_copy_multicast": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+                                            ctypes.c_void_p]),
     "vq_tp_sumsq": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                    ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]),
     "vq_tp_norm_quantize": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
@@ -148,12 +151,12 @@ _SIGNATURES = {
                                              ctypes.c_void_p]),
     "vq_w4_pack_weights": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p,
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
-    "vq_a8_pack": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p, ctypes.c_void_p,
-                                  ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_a8_dequant": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p,
+                                     ctypes.c_void_p]),
     "vq_w4a8_linear_small": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
-                                            ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
-                                            ctypes.c_void_p, ctypes.c_void_p]),
+                                            ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                            ctypes.c_void_p]),
     "vq_rounder_check_hw": (ctypes.c_int, [P(VqRounder), ctypes.c_void_p, ctypes.c_void_p]),
     "vq_quantize_affine_qparams": (ctypes.c_int, [P(VqTensor), P(ctypes.c_int64), ctypes.c_int32,
                                                   ctypes.c_int64, ctypes.c_float, ctypes.c_float,

@@ -313,7 +313,7 @@ class ColumnParallelLayer:
         N = wq[0].shape[0]
         st = _lib().vq_gemm_mxf8_ex(
             a_p, a_s, pw.data_ptr(), pws.data_ptr(), ws.T, N, K, None,
-            None if residual is None else residual.data_ptr(), N, out.data_ptr(), N,
+            None if residual is None else residual.data_ptr(), N, out.data_ptr(), N, 0,
             self.err.data_ptr(), _stream(out.device))
         _check(st, "column-parallel decoder GEMM")
 

@@ -10,6 +10,7 @@ Layout (byte offsets, each region 256-byte aligned):
   flags     uint32 [64]      this rank's barrier flags (one per peer)
   stats     float  [world, T]
   operands  named regions: E4M3 bytes [T, K] + UE8M0 atoms [K/128][T/128][512]
+  raw       named byte regions (e.g. a GEMM output every rank fills)
 """
 
 import os
@@ -47,7 +48,8 @@ class Workspace:
     """The symmetric buffer of one group for T tokens and the named operand
     widths ``operands = {name: K}``."""
 
-    def __init__(self, group, tokens: int, operands: Dict[str, int], device):
+    def __init__(self, group, tokens: int, operands: Dict[str, int], device,
+                 raw: Dict[str, int] = None):
         import torch.distributed._symmetric_memory as symm_mem
 
         group = group if group is not None else dist.group.WORLD
@@ -70,6 +72,10 @@ class Workspace:
             a_off = off
             off += _up((K // 128) * self.RT * 512)
             self.regions[name] = (K, p_off, a_off)
+        self.raw: Dict[str, int] = {}
+        for name, nbytes in (raw or {}).items():
+            self.raw[name] = off
+            off += _up(nbytes)
         self.nbytes = off
         self.buf = symm_mem.empty(off, dtype=torch.uint8, device=device)
         self.buf[: _up(64 * 4)].zero_()
@@ -101,6 +107,20 @@ class Workspace:
         """(K, local bytes, local atoms, multicast bytes, multicast atoms)."""
         K, p, a = self.regions[name]
         return K, self.base + p, self.base + a, self.mc + p, self.mc + a
+
+    def raw_region(self, name: str):
+        """(local address, multicast address) of a raw region."""
+        off = self.raw[name]
+        return self.base + off, self.mc + off
+
+    def raw_tensor(self, name: str, shape, dtype) -> torch.Tensor:
+        """The local copy of a raw region as a tensor (a view of the buffer)."""
+        off = self.raw[name]
+        n = 1
+        for d in shape:
+            n *= d
+        nbytes = n * torch.empty((), dtype=dtype).element_size()
+        return self.buf[off:off + nbytes].view(dtype).view(*shape)
 
     # synchronisation -----------------------------------------------------
     def barrier(self, stream: int):

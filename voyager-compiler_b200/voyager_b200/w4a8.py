@@ -60,7 +60,7 @@ def _dequant_weight(w_codes, w_scale):
 def applies_small(a_codes, w_codes) -> bool:
     K = w_codes.shape[1]
     M = a_codes.numel() // K
-    return 0 < M <= SMALL_M and K % 64 == 0
+    return 0 < M <= SMALL_M and K % 128 == 0
 
 
 def linear(a_codes: torch.Tensor, a_scale: torch.Tensor, w_codes: torch.Tensor,
@@ -80,20 +80,18 @@ def linear(a_codes: torch.Tensor, a_scale: torch.Tensor, w_codes: torch.Tensor,
         if wok:
             a2 = a_codes.reshape(M, K).contiguous()
             s2 = a_scale.reshape(M, K // 32).contiguous()
-            aq = torch.empty(M * K, dtype=torch.uint8, device=dev)
-            asf = torch.empty(M * (K // 32), dtype=torch.float32, device=dev)
+            a16 = torch.empty((16, K), dtype=torch.bfloat16, device=dev)
             lib = _lib.load()
-            _lib.check(lib.vq_a8_pack(_ops._ref(_ops._vt(a2)), _ops._ref(_ops._vt(s2)),
-                                      aq.data_ptr(), ctypes.c_void_p(asf.data_ptr()), None,
-                                      _ops._stream(dev)), "w4a8 activation pack")
+            _lib.check(lib.vq_a8_dequant(_ops._ref(_ops._vt(a2)), _ops._ref(_ops._vt(s2)),
+                                         a16.data_ptr(), _ops._stream(dev)),
+                       "w4a8 activation dequantize")
             ws_acc = torch.empty(M * N, dtype=torch.float32, device=dev)
             out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
             b = bias.contiguous() if bias is not None else None
             _lib.check(lib.vq_w4a8_linear_small(
-                aq.data_ptr(), ctypes.c_void_p(asf.data_ptr()), wq.data_ptr(), ws.data_ptr(),
-                M, N, K, b.data_ptr() if b is not None else None,
-                ctypes.c_void_p(ws_acc.data_ptr()), out.data_ptr(), _ops._stream(dev)),
-                "w4a8 linear")
+                a16.data_ptr(), wq.data_ptr(), ws.data_ptr(), M, N, K,
+                b.data_ptr() if b is not None else None, ctypes.c_void_p(ws_acc.data_ptr()),
+                out.data_ptr(), _ops._stream(dev)), "w4a8 linear")
             return out.reshape(tuple(lead) + (N,))
     a = _ops.dequantize(a_codes, a_scale, None, None, 32)
     w = _dequant_weight(w_codes, w_scale)
