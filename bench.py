@@ -582,8 +582,9 @@ def run_secondary(dev, hbm_peak, peaks):
     return out
 
 
-def c4_operands(dev, m, k, n, seed):
-    """C4 inputs on the device: A ~ N(0,1) [M,K] MXFP8, W ~ N(0,0.02) [N,K] NVFP4."""
+def c4_operands(dev, m, k, n, seed, keep_input=False):
+    """C4 inputs on the device: A ~ N(0,1) [M,K] MXFP8, W ~ N(0,0.02) [N,K] NVFP4
+    (and the bf16 activations themselves with keep_input)."""
     import torch
 
     from voyager_b200.tables import get_quantization_map
@@ -595,7 +596,9 @@ def c4_operands(dev, m, k, n, seed):
     e4m3 = get_quantization_map("fp8_e4m3", dev)
     sa, ca = Q.quantize_mx(a, e4m3, [-1], 32, 448.0, True)
     sw, cw = Q.quantize_mx(w, get_quantization_map("fp4_e2m1", dev), [-1], 16, 6.0, False, e4m3)
-    del a, w
+    del w
+    if keep_input:
+        return ca, sa, cw, sw, a
     return ca, sa, cw, sw
 
 
@@ -605,13 +608,18 @@ def run_c4_sweep(dev, hbm_peak):
     import torch
 
     from voyager_b200 import w4a8
+    from voyager_b200.tables import get_quantization_map
 
     stream = torch.cuda.current_stream(dev)
     res = []
     for (k, n) in [(4096, 4096), (4096, 14336), (14336, 4096)]:
-        ca0, sa0, cw, sw = c4_operands(dev, 16384, k, n, seed=k + n)
+        ca0, sa0, cw, sw, a0 = c4_operands(dev, 16384, k, n, seed=k + n, keep_input=True)
+        e4m3 = get_quantization_map("fp8_e4m3", dev)
         for m in (1, 16, 128, 1024, 16384):
-            ca, sa = ca0[:m].contiguous(), sa0[:m].contiguous()
+            # the first m tokens quantized as a batch of m (the same codes as
+            # the rows of the full batch: blocks run along K)
+            sa, ca = torch.ops.quantized_ops.quantize_mx(a0[:m].contiguous(), e4m3, [-1], 32,
+                                                         448.0, True)
             if m == 16384:
                 ca, sa = ca0, sa0
             reps = 20 if m <= 1024 else 5
@@ -626,7 +634,7 @@ def run_c4_sweep(dev, hbm_peak):
                 pt["GBps"] = round(byts / (ms / 1e3) / 1e9, 1)
                 pt["frac_hbm"] = round(pt["GBps"] / hbm_peak, 3)
             res.append(pt)
-        del ca0, sa0, cw, sw
+        del ca0, sa0, cw, sw, a0
         torch.cuda.empty_cache()
     return res
 

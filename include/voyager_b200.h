@@ -371,22 +371,24 @@ int vq_tp_swiglu_quantize(const void* gate_up, int64_t ld_in, int64_t up_off, in
  * the operands dequantized with their own block sizes
  * (src/voyager_compiler/ops/quantized.py:455-472, 522-586). */
 
-/* Pack bf16 E2M1 codes [N, K] (K % 64 == 0) to nibbles [N, K/2] (even k in
- * the low nibble) and bf16 E4M3 scales [N, K/16] to bytes.  *d_inexact
- * (device, may be NULL) counts entries that are not such values. */
+/* Pack bf16 E2M1 codes [N, K] (K % 128 == 0) to nibbles [N, K/2] (even k in
+ * the low nibble; within each 64-byte chunk of a row, byte 16b + 4i + t
+ * stored at 16t + 4b + i: the order vq_w4a8_linear_small reads) and bf16
+ * E4M3 scales [N, K/16] to bytes.  *d_inexact (device, may be NULL) counts
+ * entries that are not such values. */
 int vq_w4_pack_weights(const vq_tensor* codes, const vq_tensor* scales, void* wq, void* ws,
                        int32_t* d_inexact, void* stream);
 
-/* Dequantize the tokens as _dequantize_mx does (bf16(code x scale)): bf16
- * codes [M, K] and scales [M, K/32] -> bf16 [16, K] (rows M..15 zero),
- * M <= 16, K % 128 == 0. */
-int vq_a8_dequant(const vq_tensor* codes, const vq_tensor* scales, void* out16, void* stream);
-
-/* out[M, N] bf16 = A . W^T (+ bias) for M <= 16 from the dequantized tokens
- * a16 (bf16 [16, K], vq_a8_dequant) and the packed weights; K % 128 == 0;
- * `workspace` is float32 [M, N] scratch (zeroed by the call). */
-int vq_w4a8_linear_small(const void* a16, const void* wq, const void* ws, int64_t M, int64_t N,
-                         int64_t K, const void* bias, float* workspace, void* out, void* stream);
+/* out[M, N] bf16 = A . W^T (+ bias) for M <= 16 tokens in one launch from
+ * MXFP8 tokens (bf16 E4M3 codes [M, K], bf16 power-of-two scales [M, K/32],
+ * K % 128 == 0) and the packed weights, streamed once.
+ * `workspace` (float32, >= M * N) and `counters` (int32, >= ceil(N / 256))
+ * must be zero before the first call; every call leaves them zero, so a
+ * caller keeps one pair per weight (calls that overlap on the GPU with the
+ * same pair race). */
+int vq_w4a8_linear_small(const vq_tensor* a_codes, const vq_tensor* a_scales, const void* wq,
+                         const void* ws, int64_t N, const void* bias, float* workspace,
+                         int32_t* counters, void* out, void* stream);
 
 /* The per-block parameters of quantized_ops::quantize_affine
  * (quantized.py:884-948): for blocks of `block_size` elements along the one

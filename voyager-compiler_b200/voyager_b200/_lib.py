@@ -151,10 +151,8 @@ _SIGNATURES = {
                                              ctypes.c_void_p]),
     "vq_w4_pack_weights": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p,
                                           ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
-    "vq_a8_dequant": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p,
-                                     ctypes.c_void_p]),
-    "vq_w4a8_linear_small": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                                            ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+    "vq_w4a8_linear_small": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p,
+                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                             ctypes.c_void_p]),
     "vq_rounder_check_hw": (ctypes.c_int, [P(VqRounder), ctypes.c_void_p, ctypes.c_void_p]),

@@ -11,7 +11,10 @@ own block size (``_dequantize_mx``, ``quantized.py:455-472``), then
 
 Paths:
   * M <= 16 tokens (HBM-bound): ``vq_w4a8_linear_small`` streams the packed
-    weights (0.5625 B per weight) through mma.sync f16 tiles;
+    weights (0.5625 B per weight) in one launch: 16-byte loads of rows
+    permuted at pack time, f16 mma.sync tiles on exact operands (weights
+    times their E4M3 scales, raw E4M3 token codes), token scales on the
+    float32 block sums, split-K finished by the last CTA of each row block;
   * larger M (compute-bound): both operands dequantized by this library's
     kernels (the weight once, cached) and multiplied by cuBLAS in bf16.
 """
@@ -28,6 +31,7 @@ from voyager_b200._cache import TensorCache
 SMALL_M = 16
 _wpack = TensorCache()
 _wdeq = TensorCache()
+_wwork = TensorCache()
 
 
 def _packed_weight(w_codes, w_scale):
@@ -47,6 +51,30 @@ def _packed_weight(w_codes, w_scale):
     _lib.check(st, "w4a8 weight pack")
     ok = int(bad.item()) == 0
     return _wpack.put(w_codes, key, (wq, ws, ok))
+
+
+def _exact_tokens(a_codes, a_scale, a2, s2) -> bool:
+    """The kernel takes the token codes as E4M3 values and their scales as
+    powers of two (then every product is the reference's bf16 value):
+    vouched for when this package's quantize_mx made them, else checked (one
+    host synchronisation)."""
+    from voyager_b200 import mxgemm
+
+    if mxgemm._vouched_entry(a_codes, a_scale) is not None:
+        return True
+    return mxgemm._pack(a2, s2, 128, True)[2]
+
+
+def _workspace(w_codes, N):
+    """The self-cleaning split-K workspace of one weight: float32 [16 * N]
+    and the row-block counters, zero when made and left zero by each call."""
+    hit = _wwork.get(w_codes, "ws")
+    if hit is None:
+        dev = w_codes.device
+        hit = _wwork.put(w_codes, "ws", (torch.zeros(16 * N, dtype=torch.float32, device=dev),
+                                         torch.zeros((N + 255) // 256, dtype=torch.int32,
+                                                     device=dev)))
+    return hit
 
 
 def _dequant_weight(w_codes, w_scale):
@@ -77,21 +105,17 @@ def linear(a_codes: torch.Tensor, a_scale: torch.Tensor, w_codes: torch.Tensor,
     dev = a_codes.device
     if applies_small(a_codes, w_codes):
         wq, ws, wok = _packed_weight(w_codes, w_scale)
-        if wok:
-            a2 = a_codes.reshape(M, K).contiguous()
-            s2 = a_scale.reshape(M, K // 32).contiguous()
-            a16 = torch.empty((16, K), dtype=torch.bfloat16, device=dev)
-            lib = _lib.load()
-            _lib.check(lib.vq_a8_dequant(_ops._ref(_ops._vt(a2)), _ops._ref(_ops._vt(s2)),
-                                         a16.data_ptr(), _ops._stream(dev)),
-                       "w4a8 activation dequantize")
-            ws_acc = torch.empty(M * N, dtype=torch.float32, device=dev)
+        a2 = a_codes.reshape(M, K).contiguous()
+        s2 = a_scale.reshape(M, K // 32).contiguous()
+        if wok and _exact_tokens(a_codes, a_scale, a2, s2):
+            acc, done = _workspace(w_codes, N)
             out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
             b = bias.contiguous() if bias is not None else None
-            _lib.check(lib.vq_w4a8_linear_small(
-                a16.data_ptr(), wq.data_ptr(), ws.data_ptr(), M, N, K,
-                b.data_ptr() if b is not None else None, ctypes.c_void_p(ws_acc.data_ptr()),
-                out.data_ptr(), _ops._stream(dev)), "w4a8 linear")
+            _lib.check(_lib.load().vq_w4a8_linear_small(
+                _ops._ref(_ops._vt(a2)), _ops._ref(_ops._vt(s2)), wq.data_ptr(), ws.data_ptr(),
+                N, b.data_ptr() if b is not None else None, ctypes.c_void_p(acc.data_ptr()),
+                ctypes.c_void_p(done.data_ptr()), out.data_ptr(), _ops._stream(dev)),
+                "w4a8 linear")
             return out.reshape(tuple(lead) + (N,))
     a = _ops.dequantize(a_codes, a_scale, None, None, 32)
     w = _dequant_weight(w_codes, w_scale)
