@@ -471,13 +471,14 @@ def run_c5(dev, pg, world, bf16_peak, reps=8, warm=2):
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         ms = float(t.item())
     tf = cfg.flops(B, S) / (ms / 1e3) / 1e12
-    peak = 2 * bf16_peak
+    peak = 2 * bf16_peak * world  # the whole job's dense FP8 denominator
     dec.check_errors()
     del dec, xs
     torch.cuda.empty_cache()
     return {"ms": round(ms, 2), "TFLOPs": round(tf, 1), "gpus": world,
             "frac_fp8_dense": round(tf / peak, 3),
             "fp8_dense_peak_TFLOPs": peak,
+            "peak_note": "2 x measured cuBLAS bf16 burst per GPU, times the GPUs",
             "flop_per_forward": cfg.flops(B, S),
             "parallelism": ("1 GPU" if world == 1 else
                             f"tp{world}, column-parallel linears, operands all-gathered by "
