@@ -296,7 +296,6 @@ class ColumnParallelLayer:
         self.o = quant(w["o"][hsl])
         self.gu = quant(torch.cat([w["gate"][fsl], w["up"][fsl]], 0))
         self.down = quant(pad_k_chunks(w["down"][hsl], g))
-        self.err = torch.zeros(1, dtype=torch.int32, device=self.ln1.device)
 
     def operands(self) -> Dict[str, int]:
         h = self.cfg.hidden
@@ -314,7 +313,7 @@ class ColumnParallelLayer:
         st = _lib().vq_gemm_mxf8_ex(
             a_p, a_s, pw.data_ptr(), pws.data_ptr(), ws.T, N, K, None,
             None if residual is None else residual.data_ptr(), N, out.data_ptr(), N, 0,
-            self.err.data_ptr(), _stream(out.device))
+            ws.gemm_err.data_ptr(), _stream(out.device))
         _check(st, "column-parallel decoder GEMM")
 
     def _norm(self, ws, x, weight, name, rd, fl2q, stream):
@@ -386,7 +385,9 @@ def _check(st, what):
 class Decoder:
     """``cfg.layers`` decoder layers, tensor parallel over ``group`` (the
     default process group when one is initialised; ``parallel=False`` keeps
-    the whole model on this rank); ``ops`` defaults to
+    the whole model on this rank; in the column split ``micro_batches``
+    groups of sequences run on separate streams so that communication
+    overlaps compute); ``ops`` defaults to
     ``torch.ops.quantized_ops`` (this library's CUDA kernels).  ``attn``:
     "sdpa" -- the graph of a model exported with scaled-dot-product attention,
     converted to ``sdpa_mx`` (one fused kernel); "eager" -- the eager
@@ -399,7 +400,7 @@ class Decoder:
     def __init__(self, cfg: DecoderConfig, weights: List[Dict[str, torch.Tensor]], *,
                  table: Optional[torch.Tensor] = None, ops=None, group=None,
                  attn: str = "sdpa", fused: Optional[bool] = None, parallel: bool = True,
-                 tp_mode: str = "auto"):
+                 tp_mode: str = "auto", micro_batches: int = 2):
         self.cfg = cfg
         self.tp = TensorParallel(group, parallel)
         self.ops = ops if ops is not None else _CudaOps()
@@ -425,7 +426,9 @@ class Decoder:
             self.layers = [DecoderLayer(cfg, w, table, self.ops, self.tp, attn, fused)
                            for w in weights]
         self._tabs = {}
-        self._ws = None
+        self._ws = []
+        self._streams = []
+        self.micro_batches = micro_batches
 
     def _tables(self, seq: int, device, dtype):
         key = (seq, device, dtype)
@@ -453,25 +456,62 @@ class Decoder:
         T = y.shape[0]
         return parts.view(g, T, -1).permute(1, 0, 2).reshape(T, -1)
 
-    def _workspace(self, tokens: int, device):
+    def _workspace(self, i: int, tokens: int, device):
+        """The symmetric workspace of micro-batch i (its own operand buffers
+        and barrier flags, so micro-batches on different streams never wait
+        on each other's flags)."""
         from voyager_b200.tp import Workspace
 
-        if self._ws is None or self._ws.T != tokens:
-            self._ws = None
-            self._ws = Workspace(self.tp.group, tokens, self.layers[0].operands(), device)
-        return self._ws
+        while len(self._ws) <= i:
+            self._ws.append(None)
+        if self._ws[i] is None or self._ws[i].T != tokens:
+            self._ws[i] = None
+            self._ws[i] = Workspace(self.tp.group, tokens, self.layers[0].operands(), device)
+            self._ws[i].gemm_err = torch.zeros(1, dtype=torch.int32, device=device)
+        return self._ws[i]
+
+    def _micro_batches(self, batch: int, tokens: int) -> int:
+        """Two micro-batches (independent sequences) on two streams when the
+        batch splits evenly into 128-token multiples: one half's NVLink
+        stores and barrier waits overlap the other half's GEMMs."""
+        n = self.micro_batches
+        if n > 1 and batch % n == 0 and (tokens // n) % 128 == 0:
+            return n
+        return 1
 
     @torch.no_grad()
     def forward_shard(self, x: torch.Tensor, batch: int) -> torch.Tensor:
         """x: this rank's shard (``shard``) -> the shard after all layers."""
         if self.columns:
-            T = x.shape[0]
-            cos, sin, _ = self._tables(T // batch, x.device, x.dtype)
-            ws = self._workspace(T, x.device)
-            x = x.clone()
-            for layer in self.layers:
-                x = layer(x, ws, batch, cos, sin)
-            return x
+            T, dev = x.shape[0], x.device
+            cos, sin, _ = self._tables(T // batch, dev, x.dtype)
+            nb = self._micro_batches(batch, T)
+            if nb == 1:
+                ws = self._workspace(0, T, dev)
+                x = x.clone()
+                for layer in self.layers:
+                    x = layer(x, ws, batch, cos, sin)
+                return x
+            main = torch.cuda.current_stream(dev)
+            while len(self._streams) < nb:
+                self._streams.append(torch.cuda.Stream(dev))
+            tm = T // nb
+            wss = [self._workspace(i, tm, dev) for i in range(nb)]
+            start = torch.cuda.Event()
+            start.record(main)
+            outs = []
+            for i in range(nb):
+                st = self._streams[i]
+                st.wait_event(start)
+                with torch.cuda.stream(st):
+                    xi = x[i * tm:(i + 1) * tm].clone()
+                    for layer in self.layers:
+                        xi = layer(xi, wss[i], batch // nb, cos, sin)
+                outs.append(xi)
+            for i in range(nb):
+                main.wait_stream(self._streams[i])
+                outs[i].record_stream(main)
+            return torch.cat(outs, 0)
         S = x.shape[0] * self.tp.world // batch
         cos, sin, mask = self._tables(S, x.device, x.dtype)
         for layer in self.layers:
@@ -480,12 +520,11 @@ class Decoder:
 
     def check_errors(self):
         """Raise if a bounded device wait gave up since the workspace was made."""
-        if self._ws is not None:
-            self._ws.check()
-        for layer in self.layers:
-            err = getattr(layer, "err", None)
-            if err is not None and int(err.item()):
-                raise RuntimeError(f"decoder GEMM: device wait timed out ({int(err.item())})")
+        for ws in self._ws:
+            if ws is not None:
+                ws.check()
+                if int(ws.gemm_err.item()):
+                    raise RuntimeError("decoder GEMM: device wait timed out")
 
     @torch.no_grad()
     def forward(self, x: torch.Tensor) -> torch.Tensor:
