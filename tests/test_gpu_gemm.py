@@ -48,8 +48,10 @@ def _run(ca, sa, cw, sw, bias=None):
     return to_np(out)
 
 
+# M >= 256 takes the CTA-pair kernel (256-row tiles; an odd number of
+# 128-row chunks leaves the second CTA of the last pair on padding rows)
 SHAPES = [(128, 128, 256), (1, 128, 8), (130, 256, 264), (256, 512, 512), (96, 96, 40),
-          (300, 4096, 11008), (1024, 4096, 4096)]
+          (300, 4096, 11008), (1024, 4096, 4096), (520, 640, 1000)]
 
 
 @pytest.mark.parametrize("m,k,n", SHAPES)

@@ -31,6 +31,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "vq_numerics.cuh"
@@ -80,6 +81,83 @@ struct GemmArgs {
   int MT, NT128, NTILE_N, ntiles;
   int* err;
 };
+
+// One 128-row x 256-column accumulator tile of this CTA's TMEM -> out rows
+// (bias, bf16, optional residual add, optional multicast stores).  Two warps
+// per TMEM lane quarter (q), each on 128 columns (half); the accumulator is
+// read into registers and released (release()) before the global stores.
+template <typename Release>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem, int q, int half,
+                                              int lane, int row, int colh, Release release) {
+  uint32_t packed[64];
+#pragma unroll
+  for (int c2 = 0; c2 < 2; ++c2) {
+    uint32_t r0[32], r1[32];
+    const uint32_t taddr =
+        tmem + ((uint32_t)(q * 32) << 16) + ACC_COL + half * 128 + c2 * 64;
+    tmem_ld32(taddr, r0);
+    tmem_ld32(taddr + 32, r1);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float v0 = __uint_as_float(r0[2 * i]), v1 = __uint_as_float(r0[2 * i + 1]);
+      float w0 = __uint_as_float(r1[2 * i]), w1 = __uint_as_float(r1[2 * i + 1]);
+      if (g.bias) {
+        const int c = colh + c2 * 64 + 2 * i;
+        v0 += bf2f(g.bias[min(c, g.N - 1)]);
+        v1 += bf2f(g.bias[min(c + 1, g.N - 1)]);
+        w0 += bf2f(g.bias[min(c + 32, g.N - 1)]);
+        w1 += bf2f(g.bias[min(c + 33, g.N - 1)]);
+      }
+      __nv_bfloat162 b0 = __floats2bfloat162_rn(v0, v1), b1 = __floats2bfloat162_rn(w0, w1);
+      packed[c2 * 32 + i] = *reinterpret_cast<uint32_t*>(&b0);
+      packed[c2 * 32 + 16 + i] = *reinterpret_cast<uint32_t*>(&b1);
+    }
+  }
+  tc_fence_before();
+  release();
+  if (row < g.M && colh < g.N) {
+    uint16_t* orow = g.out + (int64_t)row * g.ldo;
+    if (g.residual) {
+      // out = bf16(bf16(acc) + residual): the residual add that follows
+      // the linear in the graph, one rounding per op
+      const uint4* rrow = reinterpret_cast<const uint4*>(g.residual + (int64_t)row * g.ldr + colh);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (colh + 8 * i >= g.N) break;
+        const uint4 rv = rrow[i];
+        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t pw = packed[4 * i + k];
+          __nv_bfloat162 b = __floats2bfloat162_rn(
+              __uint_as_float(pw << 16) + __uint_as_float(rw[k] << 16),
+              __uint_as_float(pw & 0xFFFF0000u) + __uint_as_float(rw[k] & 0xFFFF0000u));
+          packed[4 * i + k] = *reinterpret_cast<uint32_t*>(&b);
+        }
+      }
+    }
+    // N is a multiple of 8: whole 16-byte groups up to the last column
+    uint4* dst = reinterpret_cast<uint4*>(orow + colh);
+    if (g.out_mc) {
+      // one store reaches every rank's copy of the output
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (colh + 8 * i < g.N)
+          asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                           dst + i),
+                       "f"(__uint_as_float(packed[4 * i])), "f"(__uint_as_float(packed[4 * i + 1])),
+                       "f"(__uint_as_float(packed[4 * i + 2])),
+                       "f"(__uint_as_float(packed[4 * i + 3]))
+                       : "memory");
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (colh + 8 * i < g.N)
+          dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+    }
+  }
+}
 
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm_mxf8(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
@@ -217,80 +295,166 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int row = tm * BM + row_in_tile;
       const int colh = tn * BN + half * 128;
-      uint32_t packed[64];
-#pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
-        uint32_t r0[32], r1[32];
-        const uint32_t taddr =
-            tmem + ((uint32_t)(q * 32) << 16) + ACC_COL + half * 128 + c2 * 64;
-        tmem_ld32(taddr, r0);
-        tmem_ld32(taddr + 32, r1);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float v0 = __uint_as_float(r0[2 * i]), v1 = __uint_as_float(r0[2 * i + 1]);
-          float w0 = __uint_as_float(r1[2 * i]), w1 = __uint_as_float(r1[2 * i + 1]);
-          if (g.bias) {
-            const int c = colh + c2 * 64 + 2 * i;
-            v0 += bf2f(g.bias[min(c, g.N - 1)]);
-            v1 += bf2f(g.bias[min(c + 1, g.N - 1)]);
-            w0 += bf2f(g.bias[min(c + 32, g.N - 1)]);
-            w1 += bf2f(g.bias[min(c + 33, g.N - 1)]);
-          }
-          __nv_bfloat162 b0 = __floats2bfloat162_rn(v0, v1), b1 = __floats2bfloat162_rn(w0, w1);
-          packed[c2 * 32 + i] = *reinterpret_cast<uint32_t*>(&b0);
-          packed[c2 * 32 + 16 + i] = *reinterpret_cast<uint32_t*>(&b1);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(acc_empty);
-      if (row < g.M && colh < g.N) {
-        uint16_t* orow = g.out + (int64_t)row * g.ldo;
-        if (g.residual) {
-          // out = bf16(bf16(acc) + residual): the residual add that follows
-          // the linear in the graph, one rounding per op
-          const uint4* rrow = reinterpret_cast<const uint4*>(g.residual + (int64_t)row * g.ldr + colh);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            if (colh + 8 * i >= g.N) break;
-            const uint4 rv = rrow[i];
-            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint32_t pw = packed[4 * i + k];
-              __nv_bfloat162 b = __floats2bfloat162_rn(
-                  __uint_as_float(pw << 16) + __uint_as_float(rw[k] << 16),
-                  __uint_as_float(pw & 0xFFFF0000u) + __uint_as_float(rw[k] & 0xFFFF0000u));
-              packed[4 * i + k] = *reinterpret_cast<uint32_t*>(&b);
-            }
-          }
-        }
-        // N is a multiple of 8: whole 16-byte groups up to the last column
-        uint4* dst = reinterpret_cast<uint4*>(orow + colh);
-        if (g.out_mc) {
-          // one store reaches every rank's copy of the output
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (colh + 8 * i < g.N)
-              asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
-                               dst + i),
-                           "f"(__uint_as_float(packed[4 * i])), "f"(__uint_as_float(packed[4 * i + 1])),
-                           "f"(__uint_as_float(packed[4 * i + 2])),
-                           "f"(__uint_as_float(packed[4 * i + 3]))
-                           : "memory");
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (colh + 8 * i < g.N)
-              dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
-        }
-      }
+      epilogue_tile(g, tmem, q, half, lane, row, colh, [&] { mbar_arrive(acc_empty); });
     }
   }
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant: a cluster of 2 CTAs on two SMs computes a 256 x 256 tile
+// with tcgen05.mma.cta_group::2 (M = 256: 128 rows in each CTA's TMEM).  Each
+// CTA loads its own 128 rows of A and its own 128 rows (half) of B per K
+// tile -- 33.5 KB per stage instead of 49.5 KB, so 6 stages fit -- plus the
+// full B scale atoms (each CTA's TMEM needs all 256 columns' scales).  Both
+// CTAs' TMA loads count on the even CTA's "full" barrier; the even CTA's
+// single MMA thread issues the pair's copies and MMAs and releases stages
+// and accumulators in both CTAs with multicast commits; both epilogues
+// release the accumulator on the even CTA's barrier.  No TMA multicast.
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = 128 * BK, P_B_BYTES = 128 * BK;  // this CTA's halves
+constexpr int P_TX = P_A_BYTES + P_B_BYTES + SFA_BYTES + SFB_BYTES;  // per CTA and stage
+constexpr int P_STAGE_BYTES = (P_TX + 1023) / 1024 * 1024;
+constexpr int P_BARS = P_STAGES * P_STAGE_BYTES;
+constexpr int P_SMEM = P_BARS + 256;
+
+__global__ void __launch_bounds__(THREADS, 1)
+    k_gemm_mxf8_pair(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                     const __grid_constant__ CUtensorMap tma_sfa,
+                     const __grid_constant__ CUtensorMap tma_sfb, const __grid_constant__ GemmArgs g) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P_BARS);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + P_STAGES);
+  const uint32_t acc_full = smem_u32(bars + 2 * P_STAGES), acc_empty = smem_u32(bars + 2 * P_STAGES + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * P_STAGES + 2);
+  const uint32_t rank = cluster_ctarank();  // 0: issues the pair's MMAs
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int pair_id = blockIdx.x / 2, npairs = gridDim.x / 2;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 2 * 256);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers exist before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_b)) : "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair_id; t < g.ntiles && ok; t += npairs) {
+        const int tm = t / g.NTILE_N, tn = t % g.NTILE_N;  // 256-row, 256-column tile
+        for (int kt = 0; kt < g.KT; ++kt) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, g.err, ERR_TIMEOUT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sbase = smem_u32(smem + stage * P_STAGE_BYTES);
+          const uint32_t fb = mapa_shared(full0 + 8 * stage, 0);  // the even CTA's barrier
+          if (rank == 0) mbar_expect_tx(full0 + 8 * stage, 2 * P_TX);
+          tma_load_2d_pair(sbase, &tma_a, kt * BK, tm * 256 + (int)rank * 128, fb);
+          tma_load_2d_pair(sbase + P_A_BYTES, &tma_b, kt * BK, tn * 256 + (int)rank * 128, fb);
+          // scale atoms: this CTA's 128 A rows, both 128-row chunks of B
+          tma_load_2d_pair(sbase + P_A_BYTES + P_B_BYTES, &tma_sfa, 0,
+                           (kt * g.MT + tm * 2 + (int)rank) * 2, fb);
+          tma_load_2d_pair(sbase + P_A_BYTES + P_B_BYTES + SFA_BYTES, &tma_sfb, 0,
+                           (kt * g.NT128 + 2 * tn) * 2, fb);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (even CTA) ----------------
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      const uint32_t id0 = tc::idesc_mxf8(0, 256, 256), id1 = tc::idesc_mxf8(1, 256, 256),
+                     id2 = tc::idesc_mxf8(2, 256, 256), id3 = tc::idesc_mxf8(3, 256, 256);
+      const uint32_t ids[4] = {id0, id1, id2, id3};
+      for (int t = pair_id; t < g.ntiles && ok; t += npairs) {
+        // both CTAs' epilogues have drained the accumulator of the last tile
+        if (!mbar_wait(acc_empty, acc_phase ^ 1, g.err, ERR_TIMEOUT_ACC)) break;
+        acc_phase ^= 1;
+        tc_fence_after();
+        for (int kt = 0; kt < g.KT; ++kt) {
+          if (!mbar_wait(full0 + 8 * stage, phase, g.err, ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sbase = smem_u32(smem + stage * P_STAGE_BYTES);
+          const uint32_t sa = sbase, sb = sbase + P_A_BYTES;
+          const uint32_t ssfa = sbase + P_A_BYTES + P_B_BYTES, ssfb = ssfa + SFA_BYTES;
+          cp_sf_pair(tmem + SFA_COL, ssfa);
+          cp_sf_pair(tmem + SFB_COL, ssfb);
+          cp_sf_pair(tmem + SFB_COL + 4, ssfb + 512);
+#pragma unroll
+          for (uint32_t j = 0; j < 4; ++j)
+            mma_mxf8_pair(tmem + ACC_COL, sw128_desc(sa + j * 32), sw128_desc(sb + j * 32), ids[j],
+                          (kt > 0 || j > 0) ? 1u : 0u, tmem + SFA_COL + (j << 30),
+                          tmem + SFB_COL + (j << 30));
+          tc_commit_pair(empty0 + 8 * stage, 0x3);  // frees the stage in both CTAs
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(acc_full, 0x3);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_in_tile = q * 32 + lane;
+    const uint32_t acc_empty0 = mapa_shared(acc_empty, 0);
+    uint32_t acc_phase = 0;
+    for (int t = pair_id; t < g.ntiles; t += npairs) {
+      const int tm = t / g.NTILE_N, tn = t % g.NTILE_N;
+      if (!mbar_wait_warp(acc_full, acc_phase, g.err, ERR_TIMEOUT_ACC)) break;
+      acc_phase ^= 1;
+      tc_fence_after();
+      const int row = tm * 256 + (int)rank * 128 + row_in_tile;
+      const int colh = tn * BN + half * 128;
+      epilogue_tile(g, tmem, q, half, lane, row, colh,
+                    [&] { mbar_arrive_cluster(acc_empty0); });
+    }
+  }
+  __syncthreads();
+  // neither CTA leaves (or frees TMEM) while the other may still touch its
+  // barriers or its TMEM
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
   }
 }
 
@@ -389,11 +553,34 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols_byt
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_map_plain(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols_bytes,
+                    uint32_t box_cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols_bytes, rows};
+  cuuint64_t strides[1] = {cols_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int sm_count() {
   int dev = 0, n = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   return n > 0 ? n : 148;
+}
+
+// The CTA-pair kernel is used unless VQ_GEMM_PAIR=0 is set in the environment.
+bool pair_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("VQ_GEMM_PAIR");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
 }
 
 // ---------------------------------------------------------------------------
@@ -531,11 +718,43 @@ int vq_gemm_mxf8_ex(const void* a, const void* a_sf, const void* b, const void* 
   g.ntiles = (int)(MT * NTILE_N);
   g.err = d_err;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(d_err, 0, sizeof(int32_t), st) != cudaSuccess) return VQ_ERR_CUDA;
+  if (M >= 256 && pair_enabled()) {
+    // CTA pairs: 256 x 256 tiles, B loaded in 128-row halves; scale atoms
+    // through plain (unswizzled) maps of 256-byte rows
+    CUtensorMap mbh, msa, msb;
+    if (!make_map(&mbh, b, NTILE_N * 2 * 128, Kp, 128) ||
+        !make_map_plain(&msa, a_sf, (uint64_t)KT * MT * 2, 256, 256, 2) ||
+        !make_map_plain(&msb, b_sf, (uint64_t)KT * NTILE_N * 2 * 2, 256, 256, 4))
+      return VQ_ERR_CUDA;
+    GemmArgs gp = g;
+    const int64_t MT2 = (M + 255) / 256;
+    gp.ntiles = (int)(MT2 * NTILE_N);
+    const int smem = P_SMEM + 1024;
+    if (cudaFuncSetAttribute(k_gemm_mxf8_pair, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem) != cudaSuccess)
+      return VQ_ERR_CUDA;
+    const int pairs = (int)std::min<int64_t>(gp.ntiles, sm_count() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, k_gemm_mxf8_pair, ma, mbh, msa, msb, gp) != cudaSuccess)
+      return VQ_ERR_CUDA;
+    return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
+  }
   const int smem = SmemLayout::kTotal + 1024;
   if (cudaFuncSetAttribute(k_gemm_mxf8, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
       cudaSuccess)
     return VQ_ERR_CUDA;
-  if (cudaMemsetAsync(d_err, 0, sizeof(int32_t), st) != cudaSuccess) return VQ_ERR_CUDA;
   const int grid = (int)std::min<int64_t>(g.ntiles, sm_count());
   k_gemm_mxf8<<<grid, THREADS, smem, st>>>(ma, mb, g);
   return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;

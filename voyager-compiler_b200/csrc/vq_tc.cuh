@@ -157,6 +157,61 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ---- CTA pairs (tcgen05 cta_group::2) ---------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of the same shared variable in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// TMA tile load into this CTA's shared memory whose completion is counted on
+// an mbarrier of either CTA of the pair (no multicast).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+// Pair MMA (issued by the even CTA): D (+)= A . B^T over both CTAs' shared
+// memory (same offsets), each CTA's TMEM holding its half of the rows.
+__device__ __forceinline__ void mma_mxf8_pair(uint32_t d_tmem, uint64_t da, uint64_t db,
+                                              uint32_t idesc, uint32_t accum, uint32_t sfa_tmem,
+                                              uint32_t sfb_tmem) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], "
+      "p;\n\t}" ::"r"(d_tmem),
+      "l"(da), "l"(db), "r"(idesc), "r"(accum), "r"(sfa_tmem), "r"(sfb_tmem));
+}
+// Scale atoms of both CTAs (same shared offset) into their own TMEM.
+__device__ __forceinline__ void cp_sf_pair(uint32_t tmem_col, uint32_t saddr) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col),
+               "l"(sf_desc(saddr)));
+}
+// Arrive on the mbarrier at this offset in the CTAs of `mask` once the pair's
+// tcgen05 operations issued so far have completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+
 }  // namespace tc
 
 namespace mx {
@@ -165,6 +220,9 @@ namespace mx {
 // vq_gemm.cu).
 bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols_bytes,
               uint32_t box_rows);
+// Same without swizzle and with a box of box_cols bytes x box_rows rows.
+bool make_map_plain(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols_bytes,
+                    uint32_t box_cols, uint32_t box_rows);
 int sm_count();
 }  // namespace mx
 }  // namespace vq
