@@ -341,12 +341,21 @@ def run_ours(args):
         if rank == 0:
             secondary["c3_tp_linear"] = tp
     if not args.no_secondary:
-        try:
-            c5 = run_c5(dev, pg, world, peaks.get("bf16_tflops", 1590.0))
-        except Exception as e:  # report, do not hide
-            c5 = {"error": repr(e)[:200]}
-        if rank == 0:
-            secondary["c5_decoder"] = c5
+        # C5 on all ranks: tensor parallel within NVLink pairs with the
+        # sequences split across pairs (the split that keeps each GPU's
+        # NVLink traffic below its compute), and, for N > 2, tensor parallel
+        # over all N ranks
+        bf16 = peaks.get("bf16_tflops", 1590.0)
+        variants = [("c5_decoder", 2 if world % 2 == 0 else world)]
+        if world > 2:
+            variants.append((f"c5_decoder_tp{world}", world))
+        for key, tp in variants:
+            try:
+                c5 = run_c5(dev, pg, world, bf16, tp=tp)
+            except Exception as e:  # report, do not hide
+                c5 = {"error": repr(e)[:200]}
+            if rank == 0:
+                secondary[key] = c5
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -435,34 +444,52 @@ def run_tp_linear(dev, pg, world):
             "gpus": world, "note": f"weight N-sharded, {mode}"}
 
 
-def run_c5(dev, pg, world, bf16_peak, reps=8, warm=2):
+def run_c5(dev, pg, world, bf16_peak, reps=8, warm=2, tp=None):
     """C5: the 4-layer LLaMA-style decoder forward (hidden 4096, 32 heads,
-    ffn 11008, B=8, S=2048) through the MXFP8 quantized graph; tensor
-    parallel over the ranks when world > 1 (strong scaling of one forward).
-    Random-init weights N(0, 0.02) and N(0, 1) hidden states, made on the
-    device from fixed seeds."""
+    ffn 11008, B=8, S=2048) through the MXFP8 quantized graph, strong
+    scaling of one forward over the ranks: tensor parallel over groups of
+    `tp` ranks (default: all of them), the 8 sequences split evenly across
+    the world / tp groups.  Random-init weights N(0, 0.02) and N(0, 1)
+    hidden states, made on the device from fixed seeds (every rank makes the
+    same ones)."""
     import torch
+    import torch.distributed as dist
 
     from voyager_b200.decoder import Decoder, DecoderConfig, init_weights
 
     cfg, B, S = DecoderConfig(), 8, 2048
-    dec = Decoder(cfg, init_weights(cfg, 0, dev), group=None)
+    tp = world if tp is None else tp
+    if world % tp or B % (world // tp):
+        raise ValueError(f"tp {tp} does not split {world} ranks over {B} sequences")
+    dp = world // tp
+    group = None
+    if world > 1:
+        rank = dist.get_rank()
+        # every rank creates every group, in the same order
+        groups = [dist.new_group(list(range(d * tp, (d + 1) * tp))) for d in range(dp)] \
+            if dp > 1 else [None]
+        group = groups[rank // tp]
+        d = rank // tp
+    else:
+        d = 0
+    dec = Decoder(cfg, init_weights(cfg, 0, dev), group=group)
     columns = dec.columns
     torch.cuda.empty_cache()
     g = torch.Generator(device=dev).manual_seed(1)
     x = torch.randn((B * S, cfg.hidden), generator=g, device=dev).bfloat16()
-    xs = dec.shard(x)
+    seqs = B // dp
+    xs = dec.shard(x[d * seqs * S:(d + 1) * seqs * S])
     del x
     stream = torch.cuda.current_stream(dev)
     for _ in range(warm):
-        dec.forward_shard(xs, B)
+        dec.forward_shard(xs, seqs)
     torch.cuda.synchronize()
     if pg:
         pg.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(reps):
-        dec.forward_shard(xs, B)
+        dec.forward_shard(xs, seqs)
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
@@ -475,15 +502,18 @@ def run_c5(dev, pg, world, bf16_peak, reps=8, warm=2):
     dec.check_errors()
     del dec, xs
     torch.cuda.empty_cache()
+    if world == 1:
+        par = "1 GPU"
+    else:
+        split = ("column-parallel linears, operands all-gathered by NVLS multicast stores"
+                 if columns else "Megatron, sequence-parallel norms, NCCL")
+        par = f"tp{tp} ({split})" + (f" x dp{dp} (sequences split across the groups)"
+                                    if dp > 1 else "")
     return {"ms": round(ms, 2), "TFLOPs": round(tf, 1), "gpus": world,
             "frac_fp8_dense": round(tf / peak, 3),
             "fp8_dense_peak_TFLOPs": peak,
             "peak_note": "2 x measured cuBLAS bf16 burst per GPU, times the GPUs",
-            "flop_per_forward": cfg.flops(B, S),
-            "parallelism": ("1 GPU" if world == 1 else
-                            f"tp{world}, column-parallel linears, operands all-gathered by "
-                            "NVLS multicast stores" if columns else
-                            f"tp{world} (Megatron, sequence-parallel norms, NCCL)")}
+            "flop_per_forward": cfg.flops(B, S), "parallelism": par}
 
 
 def _time_cold_ms(fn, stream, dev, reps=20, warm=3):
