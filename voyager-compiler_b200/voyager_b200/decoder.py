@@ -182,6 +182,20 @@ class DecoderLayer:
         return self.ops.linear_mx(codes, w[0], None, input_scale=scale, weight_scale=w[1],
                                   block_size=self.cfg.block_size)
 
+    def _linear_add(self, codes, scale, w, x):
+        """x + linear_mx(...): on one GPU with this library's ops, the add is
+        done by the GEMM epilogue (bf16(linear) + x, the same two roundings);
+        otherwise the row-parallel product is reduce-scattered and added."""
+        if self.fused and self.tp.world == 1 and isinstance(self.ops, _CudaOps):
+            from voyager_b200 import mxgemm
+
+            if mxgemm.applies(codes, w[0], scale, w[1], self.cfg.block_size, None, None, "kc",
+                              "linear"):
+                out = mxgemm.linear(codes, w[0], None, scale, w[1], residual=x.contiguous())
+                if out is not None:
+                    return out
+        return x + self.tp.reduce_scatter_rows(self._linear(codes, scale, w))
+
     def _gathered_qmx(self, x: torch.Tensor, norm_w: Optional[torch.Tensor] = None):
         """quantize_mx of the token shard (RMSNorm'd first when ``norm_w`` is
         given), then all-gather codes and scales."""
@@ -241,7 +255,7 @@ class DecoderLayer:
                               weight_scale=sv.transpose(-1, -2), block_size=bs)
         o = o.transpose(1, 2).reshape(T, hl)
         so, co = self._qmx(o)
-        x = x + tp.reduce_scatter_rows(self._linear(co, so, self.o))
+        x = self._linear_add(co, so, self.o, x)
         # --- SwiGLU MLP ----------------------------------------------------
         codes, scale = self._gathered_qmx(x, self.ln2)
         gu = self._linear(codes, scale, self.gu)
@@ -252,7 +266,7 @@ class DecoderLayer:
         else:
             g, u = gu.chunk(2, -1)
             sa, ca = self._qmx(torch.nn.functional.silu(g) * u)
-        return x + tp.reduce_scatter_rows(self._linear(ca, sa, self.down))
+        return self._linear_add(ca, sa, self.down, x)
 
 
 class ColumnParallelLayer:

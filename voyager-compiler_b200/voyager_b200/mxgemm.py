@@ -106,9 +106,11 @@ def packed_weight(weight, weight_scale):
     return _wcache.put(weight, key, (pc, ps, ok))
 
 
-def linear(input, weight, bias, input_scale, weight_scale):
+def linear(input, weight, bias, input_scale, weight_scale, residual=None):
     """MXFP8 linear; returns None when an operand turns out not to be exact
-    E4M3 / power-of-two (the caller then takes the dequantize path)."""
+    E4M3 / power-of-two (the caller then takes the dequantize path).  With
+    ``residual`` ([.., N] bf16) the result is bf16(linear) + residual, the
+    graph's residual add done in the GEMM epilogue (the same rounding)."""
     if bias is not None and (bias.dtype != torch.bfloat16 or bias.dim() != 1
                              or bias.shape[0] != weight.shape[0] or not bias.is_cuda):
         return None
@@ -131,9 +133,17 @@ def linear(input, weight, bias, input_scale, weight_scale):
     b = bias.contiguous() if bias is not None else None
     from voyager_b200.ops import _stream
 
-    st = _lib.load().vq_gemm_mxf8(pa.data_ptr(), pas.data_ptr(), pw.data_ptr(), pws.data_ptr(),
-                                  M, N, K, b.data_ptr() if b is not None else None,
-                                  out.data_ptr(), N, err.data_ptr(), _stream(input.device))
+    r = None
+    if residual is not None:
+        r = residual.reshape(M, N)
+        if r.dtype != torch.bfloat16 or not r.is_contiguous():
+            return None
+    st = _lib.load().vq_gemm_mxf8_ex(pa.data_ptr(), pas.data_ptr(), pw.data_ptr(),
+                                     pws.data_ptr(), M, N, K,
+                                     b.data_ptr() if b is not None else None,
+                                     r.data_ptr() if r is not None else None, N,
+                                     out.data_ptr(), N, 0, err.data_ptr(),
+                                     _stream(input.device))
     _lib.check(st, "quantized_ops::linear_mx (tcgen05 MXFP8)")
     if CHECK_ERRORS and int(err.item()) != 0:
         raise _lib.VqError(f"linear_mx: device wait timed out (code {int(err.item())})")
