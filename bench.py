@@ -36,6 +36,11 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 
 ROWS, COLS = 11008, 4096
+# per-launch DRAM bytes (read + write) of the C2 kernels, from one ncu capture
+# (ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum; recorded with the
+# command in profiles/quantize_c2_weights.md)
+NCU_TRAFFIC = {"int8_channel": int(313.5e6), "nf4_g64": int(310.4e6),
+               "posit8_tensor": int(312.8e6)}
 BYTES_PER_ELEM = {"nf4_g64": 4 + 4 + 4.0 / 64, "posit8_tensor": 8.0, "int8_channel": 8.0}
 
 
@@ -377,7 +382,12 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
                          "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
-                         "traffic": None},
+                         "traffic": NCU_TRAFFIC.get(dom),
+                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per "
+                                         "launch from one ncu capture of this kernel "
+                                         "(profiles/quantize_c2_weights.md); writes still "
+                                         "draining from L2 at the kernel's end are not "
+                                         "counted"},
             "kernels": kernels,
             "clocks": clk.summary(),
             "gpu_launches": 3 * args.steps,
