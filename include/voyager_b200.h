@@ -26,6 +26,7 @@
 #ifndef VOYAGER_B200_H_
 #define VOYAGER_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -401,6 +402,75 @@ int vq_quantize_affine_qparams(const vq_tensor* input, const int64_t* axes, int3
                                int64_t block_size, float quant_min, float quant_max,
                                const vq_rounder* scale_qmap, vq_tensor* scale_out,
                                vq_tensor* zero_point_out, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Outlier CSR side-stream (quantized.py:958-1327)
+ * ------------------------------------------------------------------------- */
+
+/* The compare |x| > threshold of filter_outlier (quantized.py:1007) as a
+ * bit test: the double is rounded to float32 and, for VQ_BF16, to bfloat16
+ * (as torch converts a Python scalar to the tensor's dtype); the result lo1
+ * satisfies |x| > threshold <=> lo1 <= (bits of |x|) <= (bits of +inf). */
+uint32_t vq_outlier_threshold_bits(double threshold, int32_t dtype);
+
+/* Bytes of device scratch vq_filter_outlier needs for `input`. */
+size_t vq_filter_outlier_workspace_bytes(const vq_tensor* input);
+
+/* quantized_ops::filter_outlier (quantized.py:995-1045) on input [..., R, C]
+ * (bf16 or float32, R * C < 2^31), one pass:
+ *   data    [nb, max_nnz] input dtype   outlier values in row-major order
+ *   indices [nb, max_nnz] int32         their columns
+ *   indptr  [nb, R + 1]   int32         row pointers (+ indptr_offset,
+ *                                       quantize_mx_outlier's argument)
+ *   inliers [..., R, C]   (may be NULL) the input with outliers set to +0
+ * Outliers are |x| > threshold (see vq_outlier_threshold_bits) and x != 0;
+ * nb is the product of the batch dims.  Past max_nnz entries are dropped and
+ * row pointers clamped to max_nnz; unused slots hold 0 / -1 (_pad_csr,
+ * quantized.py:964-990).  `workspace` holds vq_filter_outlier_workspace_bytes
+ * bytes; *d_err (device) becomes nonzero if a tile's bounded wait for its
+ * predecessor's count gave up. */
+int vq_filter_outlier(const vq_tensor* input, double threshold, int64_t max_nnz,
+                      int32_t indptr_offset, void* data, int32_t* indices, int32_t* indptr,
+                      void* inliers, void* workspace, size_t workspace_bytes, int32_t* d_err,
+                      void* stream);
+
+/* quantize_mx along the last dim of the input with its outliers (as
+ * vq_filter_outlier defines them) quantized as +0: the quantize_mx half of
+ * quantized_ops::quantize_mx_outlier (quantized.py:1078-1130) without
+ * materialising the inliers.  Optionally also writes the MXFP8 GEMM operand
+ * (as vq_quantize_mx_packed; both pointers or neither).  Returns
+ * VQ_ERR_UNSUPPORTED for layouts the fused kernel does not take. */
+int vq_quantize_mx_masked(const vq_tensor* input, const vq_rounder* qmap, int64_t block_size,
+                          float quant_max, int32_t pow2, int32_t floor_log2_qmax,
+                          const vq_rounder* scale_qmap, double threshold, vq_tensor* scale_out,
+                          vq_tensor* codes_out, void* packed_codes, void* packed_sf,
+                          void* stream);
+
+/* quantized_ops::spmm_csr (quantized.py:1245-1311) after B is decoded,
+ * scaled and laid out [K, N]: out[b, r, :] = sum over the row's entries j of
+ * data[b, j] * B[(b,) indices[b, j], :], float32 fused multiply-adds in CSR
+ * order, rounded to B's dtype.  data [nb, L] (bf16 / float32), indices and
+ * indptr [nb, rows + 1] int32, B [K, N] or [nb, K, N], out [nb, rows, N].
+ * Row bounds are cummax(clamp(indptr - indptr[0], 0, L)) and columns are
+ * clamped to [0, K - 1], as the reference rebases them.  `workspace`: int32
+ * [nb, rows + 1]. */
+int vq_spmm_csr(const vq_tensor* data, const int32_t* indices, const int32_t* indptr,
+                int64_t rows, const vq_tensor* b, vq_tensor* out, int32_t* workspace,
+                void* stream);
+
+/* quantized_ops::slice_csr_tensor (quantized.py:1173-1216) of a CSR matrix
+ * with `rows` rows (data / indices [L], indptr [rows + 1], int32):
+ *   dim 0: rows [start, end) -> new_indptr [end - start + 1]
+ *   dim 1: columns [start, end) -> new_indptr [rows + 1], columns - start
+ * into max_out slots (0 / -1 past the entries; clamped row pointers when
+ * they do not fit).  workspace: int32 [2 * rows + 1] (dim 1 only). */
+int vq_slice_csr(const vq_tensor* data, const int32_t* indices, const int32_t* indptr,
+                 int64_t rows, int32_t dim, int64_t start, int64_t end, int64_t max_out,
+                 void* new_data, int32_t* new_indices, int32_t* new_indptr, int32_t* workspace,
+                 void* stream);
+
+/* dst [..., C, R] = src [..., R, C] transposed (2- or 4-byte elements). */
+int vq_transpose(const vq_tensor* src, vq_tensor* dst, void* stream);
 
 #ifdef __cplusplus
 }

@@ -312,14 +312,34 @@ def dequantize_mx(x, scale, code, block_size):
     return x
 
 
+def _with_outliers(dense, A_data, A_indices, A_indptr, weight, weight_scale, weight_code,
+                   block_size, weight_layout):
+    """``dense_out + spmm_csr(A_*, weight, ...)`` (``quantized.py:560-572``)."""
+    if A_data is None:
+        return dense
+    from oracle.outlier import add_spmm, spmm_csr
+
+    sp = spmm_csr(A_data, A_indices, A_indptr, weight, weight_scale, weight_code, block_size,
+                  weight_layout)
+    return add_spmm(dense, sp)
+
+
 def linear_mx(x, weight, bias=None, *, input_scale=None, weight_scale=None,
-              block_size=None, input_code=None, weight_code=None,
-              weight_layout="kc", out_fp32=False) -> np.ndarray:
-    """``quantized.py:522-586``: dequantize both operands, then a GEMM that
+              block_size=None, input_code=None, weight_code=None, A_data=None,
+              A_indices=None, A_indptr=None, weight_layout="kc",
+              out_fp32=False) -> np.ndarray:
+    """``quantized.py:522-574``: dequantize both operands, then a GEMM that
     accumulates in float32 and rounds once to the operands' dtype, as the
-    reference's ``aten.linear`` does.  ``out_fp32`` skips that rounding.
+    reference's ``aten.linear`` does (plus the outlier CSR's ``spmm_csr``
+    with the weight, when given).  ``out_fp32`` skips that rounding.
     GEMM results are compared within a relative-L2 tolerance, not bitwise:
     the summation order is the implementation's."""
+    if A_data is not None:
+        dense = linear_mx(x, weight, bias, input_scale=input_scale, weight_scale=weight_scale,
+                          block_size=block_size, input_code=input_code,
+                          weight_code=weight_code, weight_layout=weight_layout)
+        return _with_outliers(dense, A_data, A_indices, A_indptr, weight, weight_scale,
+                              weight_code, block_size, weight_layout)
     xa = dequantize_mx(x, input_scale, input_code, block_size)
     wa = dequantize_mx(weight, weight_scale, weight_code, block_size)
     a, w = to_f32(xa), to_f32(wa)
@@ -336,9 +356,17 @@ def linear_mx(x, weight, bias=None, *, input_scale=None, weight_scale=None,
 
 
 def matmul_mx(x, other, *, input_scale=None, weight_scale=None,
-              block_size=None, input_code=None, weight_code=None,
-              weight_layout="ck", out_fp32=False) -> np.ndarray:
-    """``quantized.py:589-648``; rounding as in ``linear_mx``."""
+              block_size=None, input_code=None, weight_code=None, A_data=None,
+              A_indices=None, A_indptr=None, weight_layout="ck",
+              out_fp32=False) -> np.ndarray:
+    """``quantized.py:589-637``; rounding and the outlier CSR as in
+    ``linear_mx``."""
+    if A_data is not None:
+        dense = matmul_mx(x, other, input_scale=input_scale, weight_scale=weight_scale,
+                          block_size=block_size, input_code=input_code,
+                          weight_code=weight_code, weight_layout=weight_layout)
+        return _with_outliers(dense, A_data, A_indices, A_indptr, other, weight_scale,
+                              weight_code, block_size, weight_layout)
     xa = dequantize_mx(x, input_scale, input_code, block_size)
     ba = dequantize_mx(other, weight_scale, weight_code, block_size)
     a, b = to_f32(xa), to_f32(ba)

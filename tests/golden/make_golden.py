@@ -94,7 +94,7 @@ def to_np(t: torch.Tensor) -> np.ndarray:
         return t.view(torch.int16).numpy().view(np.uint16).copy()
     if t.dtype == torch.float32:
         return t.numpy().copy()
-    if t.dtype == torch.int64:
+    if t.dtype in (torch.int64, torch.int32):
         return t.numpy().copy()
     raise TypeError(t.dtype)
 
@@ -351,6 +351,90 @@ def main():
             query_scale=sq_, key_scale=sk, value_scale=sv, block_size=32,
             probs_qmap="table:fp8_e4m3", probs_quant_max=448.0,
             force_scale_power_of_two=True)
+
+    # outlier CSR side-stream: filter_outlier, quantize_mx_outlier,
+    # slice_csr_tensor, spmm_csr and linear_mx / matmul_mx with A_data
+    def spiky(shape, frac=0.02, mult=50.0, sd=1.0):
+        x = (rng.standard_normal(shape) * sd).astype(np.float32)
+        n = x.size
+        pos = rng.choice(n, size=max(1, int(n * frac)), replace=False)
+        x.reshape(-1)[pos] *= mult
+        return x
+
+    def bf(x):
+        return synth.f32_to_bf16_bits(x.astype(np.float32))
+
+    xo = bf(spiky((2, 3, 40, 64)))
+    xo.reshape(-1)[:16] = [0x0000, 0x8000, 0x7F80, 0xFF80, 0x7FC0, 0xFFFF, 0x4270, 0xC270,
+                           0x406D, 0xC06D, 0x406E, 0x0001, 0x8001, 0x7F7F, 0xFF7F, 0x3F80]
+    run("filter_outlier_bf16_batched", "filter_outlier", [xo], threshold=3.7, max_pct=0.05)
+    run("filter_outlier_overflow", "filter_outlier", [bf(spiky((64, 128)))], threshold=0.5,
+        max_pct=0.01)
+    xf = spiky((33, 70))
+    xf.reshape(-1)[:8] = [0.0, -0.0, np.inf, -np.inf, np.nan, 2.0, -2.0, 2.0000002]
+    run("filter_outlier_f32_ragged", "filter_outlier", [xf], threshold=2.0, max_pct=0.1)
+    xz = bf(spiky((8, 24)))
+    xz.reshape(-1)[:6] = [0x0000, 0x8000, 0x0000, 0x7FC0, 0x3F80, 0xBF80]
+    run("filter_outlier_negative_threshold", "filter_outlier", [xz], threshold=-1.0,
+        max_pct=1.0)
+    run("filter_outlier_empty_stream", "filter_outlier", [bf(spiky((4, 16)))], threshold=1e9,
+        max_pct=0.0)
+
+    xn = bf(spiky((64, 256), frac=0.01))
+    run("quantize_mx_outlier_nvfp4", "quantize_mx_outlier", [xn],
+        qmap="table:fp4_e2m1", axes=[-1], block_size=16, quant_max=6.0, force_scale_power_of_two=False,
+        scale_qmap="table:fp8_e4m3", threshold=6.0, max_pct=0.02)
+    run("quantize_mx_outlier_mxfp8_offset", "quantize_mx_outlier",
+        [bf(spiky((3, 64, 128), frac=0.01))], qmap="table:fp8_e4m3", axes=[-1], block_size=32,
+        quant_max=448.0, force_scale_power_of_two=True, threshold=3.0, max_pct=0.01,
+        indptr_offset=7)
+    run("quantize_mx_outlier_int8_axis0", "quantize_mx_outlier",
+        [bf(spiky((64, 48)))], qmap="table:int8", axes=[-2], block_size=32, quant_max=127.0,
+        threshold=2.5, max_pct=0.05)
+    run("quantize_mx_outlier_f32", "quantize_mx_outlier",
+        [spiky((32, 96))], qmap="table:fp8_e4m3", axes=[-1], block_size=32, quant_max=448.0,
+        force_scale_power_of_two=True, threshold=4.0, max_pct=0.03)
+
+    d0, i0, p0, _ = (to_np(t) for t in Q.filter_outlier(to_t(xn), 2.0, 0.05))
+    run("slice_csr_rows", "slice_csr_tensor", [d0, i0, p0], dim=0, start=8, end=40)
+    run("slice_csr_rows_truncated", "slice_csr_tensor", [d0, i0, p0], dim=0, start=0,
+        end=64, size_factor=0.5)
+    run("slice_csr_cols", "slice_csr_tensor", [d0, i0, p0], dim=1, start=32, end=96,
+        size_factor=0.5)
+    run("slice_csr_cols_neg_dim_truncated", "slice_csr_tensor", [d0, i0, p0], dim=-1,
+        start=100, end=256, size_factor=0.25)
+
+    # spmm_csr: KC weight with MXFP8 codes and block scales; CK batched B;
+    # codebook-decoded B
+    xa = bf(spiky((48, 256), frac=0.03))
+    da, ia, pa, _ = (to_np(t) for t in Q.filter_outlier(to_t(xa), 3.0, 0.05))
+    wkc = bf(rng.standard_normal((96, 256)) * 0.05)
+    sw_, cw_ = Q.quantize_mx(to_t(wkc), gqm("fp8_e4m3"), [-1], 32, 448.0, True)
+    run("spmm_csr_kc_mxfp8", "spmm_csr", [da, ia, pa, to_np(cw_)], B_scale=to_np(sw_),
+        block_size=32, weight_layout="kc")
+    xb3 = bf(spiky((2, 32, 64), frac=0.05))
+    db, ib, pb, _ = (to_np(t) for t in Q.filter_outlier(to_t(xb3), 2.5, 0.1))
+    run("spmm_csr_ck_batched", "spmm_csr", [db, ib, pb, bf(rng.standard_normal((2, 64, 40)))],
+        weight_layout="ck")
+    code = bf(np.linspace(-1.0, 1.0, 16).astype(np.float32))
+    bidx = bf(rng.integers(0, 16, size=(256, 24)).astype(np.float32))
+    run("spmm_csr_ck_codebook", "spmm_csr", [da, ia, pa, bidx], B_code=code,
+        weight_layout="ck")
+    run("spmm_csr_f32_B", "spmm_csr", [da, ia, pa, rng.standard_normal((24, 256)).astype(
+        np.float32)], weight_layout="kc")
+
+    # the GEMMs with the side-stream
+    a_d, a_i, a_p, a_s, a_c = (to_np(t) for t in Q.quantize_mx_outlier(
+        to_t(bf(spiky((128, 256), frac=0.01))), gqm("fp8_e4m3"), [-1], 32, 448.0, True,
+        None, None, 4.0, 0.02))
+    run("linear_mx_outlier_mxfp8", "linear_mx", [a_c, to_np(cw_)], input_scale=a_s,
+        weight_scale=to_np(sw_), block_size=32, A_data=a_d, A_indices=a_i, A_indptr=a_p)
+    wck = np.ascontiguousarray(to_np(cw_).T)
+    swck = np.ascontiguousarray(to_np(sw_).T)
+    sck, cck = Q.quantize_mx(to_t(np.ascontiguousarray(wkc.T)), gqm("fp8_e4m3"), [-2], 32,
+                             448.0, True)
+    run("matmul_mx_outlier_ck", "matmul_mx", [a_c, to_np(cck)], input_scale=a_s,
+        weight_scale=to_np(sck), block_size=32, A_data=a_d, A_indices=a_i, A_indptr=a_p)
 
     np.savez_compressed(os.path.join(HERE, "ops_small.npz"), **arrays)
     with open(os.path.join(HERE, "ops_small.json"), "w") as f:

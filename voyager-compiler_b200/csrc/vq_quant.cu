@@ -164,6 +164,10 @@ struct QmxArgs {
   uint8_t* packed;
   uint8_t* packed_sf;
   int32_t packed_rt;
+  // quantize_mx_outlier: elements with mask_lo1 <= |x| bits <= +inf bits are
+  // outliers and quantized as +0 (filter_outlier's inliers), when mask_on
+  int32_t mask_on;
+  uint32_t mask_lo1;
 };
 
 // One block of bs = TPB * VPT * VEC elements per TPB threads; lane l holds
@@ -204,6 +208,24 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
           v[u][j] = __ldcs(reinterpret_cast<const uint4*>(
               reinterpret_cast<const TIn*>(a.in) + base[u] + (j * TPB + lane) * VEC));
       }
+    }
+    if (a.mask_on) {
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u)
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          uint32_t* q = reinterpret_cast<uint32_t*>(&v[u][j]);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (BF) {
+              const uint32_t ab = q[k] & 0x7FFF7FFFu;
+              q[k] &= ~(__vcmpgeu2(ab, a.mask_lo1 * 0x10001u) & __vcmpleu2(ab, 0x7F807F80u));
+            } else {
+              const uint32_t ab = q[k] & 0x7FFFFFFFu;
+              if (ab >= a.mask_lo1 && ab <= 0x7F800000u) q[k] = 0;
+            }
+          }
+        }
     }
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
@@ -1693,6 +1715,67 @@ int vq_quantize_mx_packed(const vq_tensor* input, const vq_rounder* qmap, int32_
   a.packed_sf = (uint8_t*)packed_sf;
   a.packed_rt = (int32_t)((R + 127) / 128);
   return launch_qmx_kind<uint16_t>(a, K_HW_E4M3, nv, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int vq_quantize_mx_masked(const vq_tensor* input, const vq_rounder* qmap, int64_t block_size,
+                          float quant_max, int32_t pow2, int32_t floor_log2_qmax,
+                          const vq_rounder* scale_qmap, double threshold, vq_tensor* scale_out,
+                          vq_tensor* codes_out, void* packed_codes, void* packed_sf,
+                          void* stream) {
+  if (!input || !qmap || !codes_out) return VQ_ERR_NULL;
+  const int64_t axes[1] = {-1};
+  int blocked[VQ_MAX_DIMS];
+  int st = validate_mx(input, axes, 1, block_size, scale_qmap, scale_out, blocked);
+  if (st) return st;
+  if ((st = check_rounder(qmap))) return st;
+  if (codes_out->dtype != input->dtype || codes_out->ndim != input->ndim) return VQ_ERR_SHAPE;
+  for (int d = 0; d < input->ndim; ++d)
+    if (codes_out->shape[d] != input->shape[d]) return VQ_ERR_SHAPE;
+  if (numel(*input) == 0) return VQ_OK;
+  if (!codes_out->data) return VQ_ERR_NULL;
+  const int nv = qmx_last_fast_ok(*input, blocked, block_size);
+  if (!nv || !aligned16(codes_out->data)) return VQ_ERR_UNSUPPORTED;
+  const int K = elem_kind(qmap);
+  const int64_t C = input->shape[input->ndim - 1];
+  const int64_t rows = numel(*input) / C;
+  const bool pack = packed_codes || packed_sf;
+  if (pack) {
+    // the MXFP8 GEMM operand, as vq_quantize_mx_packed writes it
+    if (!packed_codes || !packed_sf) return VQ_ERR_NULL;
+    if (input->dtype != VQ_BF16 || K != K_HW_E4M3 || block_size != 32 || !pow2 || scale_qmap ||
+        C % 128 != 0)
+      return VQ_ERR_UNSUPPORTED;
+    if (!aligned16(packed_codes) || !aligned16(packed_sf)) return VQ_ERR_ALIGNMENT;
+  }
+  QmxArgs a;
+  memset(&a, 0, sizeof(a));
+  const int64_t nb = (C + block_size - 1) / block_size;
+  a.in = input->data;
+  a.codes = codes_out->data;
+  a.scale = scale_out->data;
+  a.C = (uint32_t)C;
+  a.bs = (uint32_t)block_size;
+  a.nb = FastDiv::make((uint32_t)nb);
+  a.ngroups = (uint32_t)(rows * nb);
+  a.quant_max = quant_max;
+  a.pow2 = pow2;
+  a.fl2q = floor_log2_qmax;
+  a.has_sq = scale_qmap != nullptr;
+  if (scale_qmap) {
+    a.sq = *scale_qmap;
+    a.sq_table = scale_qmap->table;
+  }
+  a.qr = *qmap;
+  if (pack) {
+    a.packed = (uint8_t*)packed_codes;
+    a.packed_sf = (uint8_t*)packed_sf;
+    a.packed_rt = (int32_t)((rows + 127) / 128);
+  }
+  a.mask_on = 1;
+  a.mask_lo1 = vq_outlier_threshold_bits(threshold, input->dtype);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  return input->dtype == VQ_BF16 ? launch_qmx_kind<uint16_t>(a, K, nv, cs)
+                                 : launch_qmx_kind<float>(a, K, nv, cs);
 }
 
 int vq_rounder_check_hw(const vq_rounder* r, int32_t* d_mismatches, void* stream) {

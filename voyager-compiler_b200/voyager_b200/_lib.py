@@ -160,6 +160,24 @@ _SIGNATURES = {
                                                   ctypes.c_int64, ctypes.c_float, ctypes.c_float,
                                                   P(VqRounder), P(VqTensor), P(VqTensor),
                                                   ctypes.c_void_p]),
+    "vq_outlier_threshold_bits": (ctypes.c_uint32, [ctypes.c_double, ctypes.c_int32]),
+    "vq_filter_outlier_workspace_bytes": (ctypes.c_size_t, [P(VqTensor)]),
+    "vq_filter_outlier": (ctypes.c_int, [P(VqTensor), ctypes.c_double, ctypes.c_int64,
+                                         ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                         ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_quantize_mx_masked": (ctypes.c_int, [P(VqTensor), P(VqRounder), ctypes.c_int64,
+                                             ctypes.c_float, ctypes.c_int32, ctypes.c_int32,
+                                             P(VqRounder), ctypes.c_double, P(VqTensor),
+                                             P(VqTensor), ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_void_p]),
+    "vq_spmm_csr": (ctypes.c_int, [P(VqTensor), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                   P(VqTensor), P(VqTensor), ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_slice_csr": (ctypes.c_int, [P(VqTensor), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                    ctypes.c_int32, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_transpose": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p]),
 }
 
 _lib = None

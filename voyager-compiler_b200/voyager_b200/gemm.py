@@ -10,8 +10,11 @@ Paths, chosen per call:
     (``voyager_b200.mxgemm``), weights packed once and cached;
   * everything else: the operands are dequantized by this library's kernels
     and multiplied by cuBLAS (bf16, float32 accumulate).
-The outlier CSR side-stream (``A_data`` / ``A_indices`` / ``A_indptr``) is not
-provided and raises.
+With the outlier CSR side-stream (``A_data`` / ``A_indices`` / ``A_indptr``)
+the result is the dense product plus ``spmm_csr`` of the CSR with the
+decoded weight (``quantized.py:560-574``, ``:625-637``); on the MXFP8 path
+the addition is the GEMM epilogue's residual add (one bf16 rounding of the
+dense product, then the bf16 sum, as the reference's two bf16 tensors add).
 """
 
 from typing import Optional
@@ -50,39 +53,52 @@ def _weight_dequant(w, scale, code, bs):
     return _wcache.put(w, key, dequantize_mx(w, scale, code, bs))
 
 
-def _no_outliers(A_data):
-    if A_data is not None:
-        raise NotImplementedError(
-            "quantized_ops on CUDA: the outlier CSR side-stream (A_data/A_indices/A_indptr) "
-            "is not provided")
+def _outliers(A_data, A_indices, A_indptr, weight, weight_scale, weight_code, block_size,
+              weight_layout):
+    """spmm_csr of the CSR side-stream with the weight, or None."""
+    if A_data is None:
+        return None
+    from voyager_b200.outlier import spmm_csr
+
+    return spmm_csr(A_data, A_indices, A_indptr, weight, weight_scale, weight_code, block_size,
+                    weight_layout)
 
 
 def linear_mx(input, weight, bias=None, *, input_scale=None, weight_scale=None,
               block_size=None, input_code=None, weight_code=None, A_data=None,
               A_indices=None, A_indptr=None, weight_layout="kc"):
     assert weight_layout in ("kc", "ck"), weight_layout
-    _no_outliers(A_data)
     from voyager_b200 import mxgemm
 
+    sp = _outliers(A_data, A_indices, A_indptr, weight, weight_scale, weight_code, block_size,
+                   weight_layout)
     if mxgemm.applies(input, weight, input_scale, weight_scale, block_size, input_code,
                       weight_code, weight_layout, "linear"):
-        out = mxgemm.linear(input, weight, bias, input_scale, weight_scale)
-        if out is not None:
-            return out
+        res = None
+        if sp is not None and sp.dtype == torch.bfloat16 and sp.shape[-1] == weight.shape[0] \
+                and sp.numel() == input.numel() // input.shape[-1] * weight.shape[0]:
+            res = sp.contiguous()
+        if sp is None or res is not None:
+            out = mxgemm.linear(input, weight, bias, input_scale, weight_scale, residual=res)
+            if out is not None:
+                return out
     a = dequantize_mx(input, input_scale, input_code, block_size)
     w = _weight_dequant(weight, weight_scale, weight_code, block_size)
     if weight_layout == "ck":
         w = w.transpose(-1, -2)
-    return F.linear(a, w, bias)
+    out = F.linear(a, w, bias)
+    return out if sp is None else out + sp
 
 
 def matmul_mx(self, other, *, input_scale=None, weight_scale=None, block_size=None,
               input_code=None, weight_code=None, A_data=None, A_indices=None, A_indptr=None,
               weight_layout="ck"):
     assert weight_layout in ("kc", "ck"), weight_layout
-    _no_outliers(A_data)
+    sp = _outliers(A_data, A_indices, A_indptr, other, weight_scale, weight_code, block_size,
+                   weight_layout)
     a = dequantize_mx(self, input_scale, input_code, block_size)
     b = dequantize_mx(other, weight_scale, weight_code, block_size)
     if weight_layout == "kc":
         b = b.transpose(-1, -2)
-    return torch.matmul(a, b)
+    out = torch.matmul(a, b)
+    return out if sp is None else out + sp

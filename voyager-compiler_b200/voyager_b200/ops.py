@@ -307,6 +307,38 @@ def sdpa_mx(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False,
                 force_scale_power_of_two=force_scale_power_of_two)
 
 
+def filter_outlier(input, threshold, max_pct=0.01):
+    """``quantized.py:995-1045``."""
+    from voyager_b200.outlier import filter_outlier as impl
+
+    return impl(input, threshold, max_pct)
+
+
+def quantize_mx_outlier(input, qmap, axes, block_size, quant_max,
+                        force_scale_power_of_two=False, scale_qmap=None, output_code=None,
+                        threshold=None, max_pct=0.01, indptr_offset=0):
+    """``quantized.py:1078-1130``."""
+    from voyager_b200.outlier import quantize_mx_outlier as impl
+
+    return impl(input, qmap, axes, block_size, quant_max, force_scale_power_of_two,
+                scale_qmap, output_code, threshold, max_pct, indptr_offset)
+
+
+def slice_csr_tensor(data, indices, indptr, dim=0, start=None, end=None, size_factor=1.0):
+    """``quantized.py:1173-1216``."""
+    from voyager_b200.outlier import slice_csr_tensor as impl
+
+    return impl(data, indices, indptr, dim, start, end, size_factor)
+
+
+def spmm_csr(data, indices, indptr, B, B_scale=None, B_code=None, block_size=None,
+             weight_layout="kc"):
+    """``quantized.py:1245-1311``."""
+    from voyager_b200.outlier import spmm_csr as impl
+
+    return impl(data, indices, indptr, B, B_scale, B_code, block_size, weight_layout)
+
+
 # ---------------------------------------------------------------------------
 # registration
 # ---------------------------------------------------------------------------
@@ -353,6 +385,23 @@ SCHEMAS = {
         "quantize_affine(Tensor self, Tensor qmap, SymInt[] axes, int block_size, "
         "float quant_min, float quant_max, Tensor scale_qmap=None) "
         "-> (Tensor, Tensor, Tensor)"),
+    "filter_outlier": (
+        "filter_outlier(Tensor input, float threshold, float max_pct=0.01) "
+        "-> (Tensor, Tensor, Tensor, Tensor)"),
+    "quantize_mx_outlier": (
+        "quantize_mx_outlier(Tensor self, Tensor qmap, SymInt[] axes, "
+        "int block_size, float quant_max, bool force_scale_power_of_two=False, "
+        "Tensor scale_qmap=None, Tensor output_code=None, float? threshold=None, "
+        "float max_pct=0.01, SymInt indptr_offset=0) "
+        "-> (Tensor, Tensor, Tensor, Tensor, Tensor)"),
+    "slice_csr_tensor": (
+        "slice_csr_tensor(Tensor data, Tensor indices, Tensor indptr, int dim=0, "
+        "SymInt? start=None, SymInt? end=None, float size_factor=1.0) "
+        "-> (Tensor, Tensor, Tensor)"),
+    "spmm_csr": (
+        "spmm_csr(Tensor data, Tensor indices, Tensor indptr, Tensor B, "
+        "Tensor? B_scale=None, Tensor? B_code=None, int? block_size=None, "
+        'str weight_layout="kc") -> Tensor'),
 }
 
 CUDA_IMPLS = {
@@ -365,6 +414,10 @@ CUDA_IMPLS = {
     "linear_mx": linear_mx,
     "matmul_mx": matmul_mx,
     "sdpa_mx": sdpa_mx,
+    "filter_outlier": filter_outlier,
+    "quantize_mx_outlier": quantize_mx_outlier,
+    "slice_csr_tensor": slice_csr_tensor,
+    "spmm_csr": spmm_csr,
 }
 
 
@@ -413,9 +466,36 @@ def _meta_impls():
     def sdpa(query, key, value, *a, **kw):
         return query.new_empty(list(query.shape[:-1]) + [value.shape[-1]])
 
+    def csr_fake(input, max_pct):
+        batch, mat = list(input.shape[:-2]), list(input.shape[-2:])
+        nnz = int(math.prod(mat) * max_pct)
+        return (input.new_empty(batch + [nnz]),
+                input.new_empty(batch + [nnz], dtype=torch.int32),
+                input.new_empty(batch + [mat[0] + 1], dtype=torch.int32))
+
+    def fo(input, threshold, max_pct=0.01):
+        return (*csr_fake(input, max_pct), torch.empty_like(input))
+
+    def qmxo(input, qmap, axes, block_size, quant_max, force_scale_power_of_two=False,
+             scale_qmap=None, output_code=None, threshold=None, max_pct=0.01, indptr_offset=0):
+        return (*csr_fake(input, max_pct), mxq(input, axes, block_size, quant_max),
+                torch.empty_like(input, memory_format=torch.contiguous_format))
+
+    def slc(data, indices, indptr, dim=0, start=None, end=None, size_factor=1.0):
+        p = indptr.new_empty(indptr.shape)
+        if dim in (0, -2):
+            p = p[start:end + 1]
+        return torch.empty_like(data), torch.empty_like(indices), p
+
+    def spmm(data, indices, indptr, B, B_scale=None, B_code=None, block_size=None,
+             weight_layout="kc"):
+        n = B.shape[-1] if weight_layout == "ck" else B.shape[-2]
+        return data.new_empty(list(indptr.shape[:-1]) + [indptr.shape[-1] - 1, n])
+
     return {"quantize": q, "dequantize": dq, "vmap": vm, "calculate_mx_qparam": mxq,
             "quantize_mx": qmx, "quantize_affine": qaff, "linear_mx": lin, "matmul_mx": mm,
-            "sdpa_mx": sdpa}
+            "sdpa_mx": sdpa, "filter_outlier": fo, "quantize_mx_outlier": qmxo,
+            "slice_csr_tensor": slc, "spmm_csr": spmm}
 
 
 _LIBS = []
