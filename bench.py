@@ -12,8 +12,10 @@ whole job (all ranks).  Multi-GPU: every rank quantizes its own weight matrix
 (weak scaling, no collective on the data path).
 
 Secondary results in the same line ("secondary"): C1 NVFP4 round trip GB/s,
-C3 MXFP8 quantized-linear TFLOP/s, the C4 W4A8 sweep on one GPU, and the C5
-4-layer decoder forward (tensor parallel over the ranks when N > 1).
+C3 MXFP8 quantized-linear TFLOP/s, the C4 W4A8 sweep on one GPU, the outlier
+CSR side-stream (quantize_mx_outlier on C1's input, C3 with a 1 % activation
+CSR), and the C5 4-layer decoder forward (tensor parallel over the ranks when
+N > 1).
 
 --impl reference times the reference algorithm's CPU restatement (the oracle
 port under oracle/) on this host's cores, on a bounded row sample of the
@@ -53,7 +55,8 @@ def parse():
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", default=None, choices=["c1", "c2", "c3", "c4", "c5", "attn"],
+    ap.add_argument("--only", default=None,
+                    choices=["c1", "c2", "c3", "c4", "c5", "attn", "outlier", "spmm"],
                     help="profiling aid: run only this workload's kernels, no JSON line")
     return ap.parse_args()
 
@@ -547,6 +550,37 @@ def _time_cold_ms(fn, stream, dev, reps=20, warm=3):
     return ms
 
 
+def _time_graph_cold_ms(fn, dev, reps=20, warm=3):
+    """Device time of fn with the L2 cold and no host in the loop: a CUDA
+    graph of (256 MB flush, fn) replayed, minus a graph of the flush alone."""
+    import torch
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    g0, g1 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g0):
+        flush.zero_()
+    with torch.cuda.graph(g1):
+        flush.zero_()
+        fn()
+    st = torch.cuda.current_stream()
+    res = []
+    for g in (g0, g1):
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        for _ in range(reps):
+            g.replay()
+        b.record(st)
+        torch.cuda.synchronize()
+        res.append(a.elapsed_time(b) / reps)
+    del g0, g1, flush
+    return max(res[1] - res[0], 1e-6)
+
+
 def _time_graph_ms(fn, stream, reps=20, warm=3):
     """Device time of fn replayed from a CUDA graph (for µs-scale calls whose
     eager time is the host's launch cost, as in a graph-captured decode)."""
@@ -620,7 +654,93 @@ def run_secondary(dev, hbm_peak, peaks):
         out["c4_w4a8_sweep"] = run_c4_sweep(dev, hbm_peak)
     except Exception as e:
         out["c4_error"] = repr(e)[:200]
+    try:
+        out["outlier"] = run_outlier(dev, hbm_peak)
+    except Exception as e:
+        out["outlier_error"] = repr(e)[:200]
     return out
+
+
+def outlier_c3_operands(dev):
+    """C3's operands with 1 % of the activations scaled by 50 (the C1
+    recipe), quantized with their outliers above 4.0 split into a CSR."""
+    import torch
+
+    from voyager_b200 import synth
+    from voyager_b200.tables import get_quantization_map
+
+    Q = torch.ops.quantized_ops
+    a_np, w_np = synth.c3_operands()
+    a = torch.from_numpy(a_np.view(np.int16)).view(torch.bfloat16).to(dev)
+    g = torch.Generator(device=dev).manual_seed(1)
+    pos = torch.randperm(a.numel(), generator=g, device=dev)[: a.numel() // 100]
+    a.view(-1)[pos] = (a.view(-1)[pos].float() * 50).bfloat16()
+    wq = torch.from_numpy(w_np.view(np.int16)).view(torch.bfloat16).to(dev)
+    e4m3 = get_quantization_map("fp8_e4m3", dev)
+    d, i, p, sa, ca = Q.quantize_mx_outlier(a, e4m3, [-1], 32, 448.0, True, None, None, 4.0,
+                                            0.02)
+    sw, cw = Q.quantize_mx(wq, e4m3, [-1], 32, 448.0, True)
+    return a, (d, i, p, sa, ca), (sw, cw)
+
+
+def run_outlier(dev, hbm_peak):
+    """The outlier CSR side-stream: quantize_mx_outlier / filter_outlier on
+    C1's input (1 % outliers), and C3's linear_mx with a 1 % activation CSR
+    (dense MXFP8 GEMM + spmm_csr in its epilogue)."""
+    import torch
+
+    from voyager_b200 import synth
+    from voyager_b200.tables import get_quantization_map
+
+    Q = torch.ops.quantized_ops
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+    x = torch.from_numpy(synth.c1_input().view(np.int16)).view(torch.bfloat16).to(dev)
+    e2m1 = get_quantization_map("fp4_e2m1", dev)
+    e4m3 = get_quantization_map("fp8_e4m3", dev)
+    n, R = x.numel(), x.shape[0]
+    cap = int(n * 0.02)
+    csr_bytes = cap * 6 + (R + 1) * 4
+    out = Q.quantize_mx_outlier(x, e2m1, [-1], 16, 6.0, False, e4m3, None, 6.0, 0.02)
+    nse = int(out[2][-1])
+    # µs-scale launch sequences: graph replay with the L2 flushed (the eager
+    # time would include the host's launch gaps)
+    tq = _time_graph_cold_ms(lambda: Q.quantize_mx_outlier(x, e2m1, [-1], 16, 6.0, False, e4m3,
+                                                           None, 6.0, 0.02), dev)
+    tf = _time_graph_cold_ms(lambda: Q.filter_outlier(x, 6.0, 0.02), dev)
+    tqm = _time_graph_cold_ms(lambda: Q.quantize_mx(x, e2m1, [-1], 16, 6.0, False, e4m3), dev)
+    qb = n * 4.125 + csr_bytes
+    fb = n * 4.0 + csr_bytes
+    res["c1_quantize_mx_outlier"] = {
+        "ms": round(tq, 4), "GBps": round(qb / (tq / 1e3) / 1e9, 1),
+        "frac_hbm": round(qb / (tq / 1e3) / 1e9 / hbm_peak, 3), "outliers": nse,
+        "capacity": cap, "bytes": int(qb),
+        "quantize_mx_alone_ms": round(tqm, 4),
+        "note": "NVFP4 bs16 + e4m3 scales of the inliers, CSR of |x| > 6; CUDA-graph "
+                "replay, L2 flushed before each call (flush time subtracted)"}
+    res["c1_filter_outlier"] = {"ms": round(tf, 4), "GBps": round(fb / (tf / 1e3) / 1e9, 1),
+                                "frac_hbm": round(fb / (tf / 1e3) / 1e9 / hbm_peak, 3)}
+    del x, out
+    a, (d, i, p, sa, ca), (sw, cw) = outlier_c3_operands(dev)
+    nnz = int(p[-1])
+    lin = lambda: Q.linear_mx(ca, cw, None, input_scale=sa, weight_scale=sw, block_size=32,
+                              A_data=d, A_indices=i, A_indptr=p)
+    dense = lambda: Q.linear_mx(ca, cw, None, input_scale=sa, weight_scale=sw, block_size=32)
+    spmm = lambda: Q.spmm_csr(d, i, p, cw, sw, None, 32, "kc")
+    tl = _time_ms(lin, stream, reps=10)
+    td = _time_ms(dense, stream, reps=10)
+    ts = _time_ms(spmm, stream, reps=10)
+    M, K, N = 8192, 4096, 11008
+    fl = 2.0 * M * N * K + 2.0 * nnz * N
+    gather = nnz * N * 2  # B rows read (bf16), mostly from L2
+    res["c3_linear_mx_outliers"] = {
+        "ms": round(tl, 4), "dense_ms": round(td, 4), "spmm_ms": round(ts, 4),
+        "TFLOPs": round(fl / (tl / 1e3) / 1e12, 1), "outliers": nnz,
+        "spmm_gather_GBps": round(gather / (ts / 1e3) / 1e9, 1),
+        "spmm_out_GBps": round((M * N * 2 + K * N * 2) / (ts / 1e3) / 1e9, 1),
+        "note": "M=8192 K=4096 N=11008, 1% of activations x50, CSR of |x| > 4; spmm "
+                "output added in the GEMM epilogue"}
+    return res
 
 
 def c4_operands(dev, m, k, n, seed, keep_input=False):
@@ -728,6 +848,23 @@ def run_only(args):
             Q.sdpa_mx(cq, ck, cv.transpose(-1, -2), is_causal=True, query_scale=sq, key_scale=sk,
                       value_scale=sv.transpose(-1, -2), block_size=32, probs_qmap=e4m3,
                       probs_quant_max=448.0, force_scale_power_of_two=True)
+    elif args.only == "outlier":
+        x = torch.from_numpy(synth.c1_input().view(np.int16)).view(torch.bfloat16).to(dev)
+        e2m1, e4m3 = get_quantization_map("fp4_e2m1", dev), get_quantization_map("fp8_e4m3", dev)
+        a, (d, i, p, sa, ca), (sw, cw) = outlier_c3_operands(dev)
+        for _ in range(args.warmup + args.steps):
+            Q.quantize_mx_outlier(x, e2m1, [-1], 16, 6.0, False, e4m3, None, 6.0, 0.02)
+            Q.linear_mx(ca, cw, None, input_scale=sa, weight_scale=sw, block_size=32, A_data=d,
+                        A_indices=i, A_indptr=p)
+    elif args.only == "spmm":
+        # spmm_csr of the first 2048 rows of C3's outlier CSR (small enough
+        # for a full counter capture of one launch)
+        a, (d, i, p, sa, ca), (sw, cw) = outlier_c3_operands(dev)
+        rows = 2048
+        n = int(p[rows])
+        d2, i2, p2 = d[:n].contiguous(), i[:n].contiguous(), p[:rows + 1].contiguous()
+        for _ in range(args.warmup + args.steps):
+            Q.spmm_csr(d2, i2, p2, cw, sw, None, 32, "kc")
     elif args.only == "c4":
         from voyager_b200 import w4a8
 

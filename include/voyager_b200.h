@@ -417,7 +417,7 @@ uint32_t vq_outlier_threshold_bits(double threshold, int32_t dtype);
 size_t vq_filter_outlier_workspace_bytes(const vq_tensor* input);
 
 /* quantized_ops::filter_outlier (quantized.py:995-1045) on input [..., R, C]
- * (bf16 or float32, R * C < 2^31), one pass:
+ * (bf16 or float32, R * C < 2^31):
  *   data    [nb, max_nnz] input dtype   outlier values in row-major order
  *   indices [nb, max_nnz] int32         their columns
  *   indptr  [nb, R + 1]   int32         row pointers (+ indptr_offset,
@@ -426,9 +426,9 @@ size_t vq_filter_outlier_workspace_bytes(const vq_tensor* input);
  * Outliers are |x| > threshold (see vq_outlier_threshold_bits) and x != 0;
  * nb is the product of the batch dims.  Past max_nnz entries are dropped and
  * row pointers clamped to max_nnz; unused slots hold 0 / -1 (_pad_csr,
- * quantized.py:964-990).  `workspace` holds vq_filter_outlier_workspace_bytes
- * bytes; *d_err (device) becomes nonzero if a tile's bounded wait for its
- * predecessor's count gave up. */
+ * quantized.py:964-990).  Three launches (count per tile, scan, scatter),
+ * no waits between CTAs.  `workspace` holds
+ * vq_filter_outlier_workspace_bytes bytes; d_err is not used (may be NULL). */
 int vq_filter_outlier(const vq_tensor* input, double threshold, int64_t max_nnz,
                       int32_t indptr_offset, void* data, int32_t* indices, int32_t* indptr,
                       void* inliers, void* workspace, size_t workspace_bytes, int32_t* d_err,

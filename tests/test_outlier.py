@@ -222,12 +222,12 @@ def test_outlier_entries_reject_bad_arguments():
                                  ws, 1 << 20, 0x40, None) == 2
     # too little workspace
     need = lib.vq_filter_outlier_workspace_bytes(B(_t([3, 64, 4096])))
-    assert need == 3 * 64 * 8 + 16
+    assert need == (2 * 3 * 32 + 3) * 4 + 16  # tiles of 8192 bf16 elements
     assert lib.vq_filter_outlier(B(_t([3, 64, 4096])), 1.0, 4, 0, 0x10, 0x20, 0x30, None, ws,
                                  need - 1, 0x40, None) == 8
-    # missing error word / row pointers
-    assert lib.vq_filter_outlier(B(_t([8, 8])), 1.0, 4, 0, 0x10, 0x20, 0x30, None, ws, 1 << 20,
-                                 None, None) == 6
+    # missing row pointers / workspace
+    assert lib.vq_filter_outlier(B(_t([8, 8])), 1.0, 4, 0, 0x10, 0x20, 0x30, None, None,
+                                 1 << 20, None, None) == 6
     assert lib.vq_filter_outlier(B(_t([8, 8])), 1.0, 4, 0, 0x10, 0x20, None, None, ws, 1 << 20,
                                  0x40, None) == 6
     # negative capacity

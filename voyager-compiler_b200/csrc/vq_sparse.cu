@@ -1,14 +1,14 @@
 // The outlier CSR side-stream of quantized_ops (quantized.py:958-1327):
 //
-//   k_outlier_filter   filter_outlier: one pass over the dense input builds
-//                      the CSR of the outliers (|x| > threshold, x != 0; row
-//                      pointers, column indices, values) and optionally the
-//                      inliers (outliers replaced by +0).  Tiles of 4096
-//                      elements are numbered in row-major order by an atomic
-//                      ticket; each tile finds its output offset by a
-//                      decoupled look-back over its predecessors' published
-//                      counts, so the CSR comes out in to_sparse_csr's order
-//                      without a second pass.
+//   k_outlier_count / k_outlier_scan / k_outlier_scatter
+//                      filter_outlier in three launches with no waits between
+//                      CTAs: outliers (|x| > threshold, x != 0) counted per
+//                      tile of 8192 (bf16) / 4096 (f32) elements, the counts
+//                      scanned per matrix, then each tile writes its CSR
+//                      entries (values, columns) in row-major order, the row
+//                      pointers of the rows starting in it, the inliers
+//                      (outliers replaced by +0) and its share of the unused
+//                      slots -- the order to_sparse_csr produces.
 //   k_spmm_rows        spmm_csr's row bounds: cummax(clamp(indptr - indptr[0],
 //                      0, L)), exactly the reference's rebasing.
 //   k_spmm_csr         spmm_csr: out[r, :] = sum_j data[j] * B[col_j, :] with
@@ -42,27 +42,10 @@ namespace sparse {
 
 constexpr uint32_t FULL = 0xFFFFFFFFu;
 constexpr int F_THREADS = 256;
-constexpr int F_EPT = 16;                  // elements per thread
-constexpr int F_TILE = F_THREADS * F_EPT;  // elements per tile
 constexpr int F_WARPS = F_THREADS / 32;
-constexpr uint64_t WAIT_NS = 2000000000ull;
-constexpr uint32_t MAX_SPINS = 1u << 28;
-constexpr unsigned long long ST_AGG = 1, ST_INCL = 2;
-
-__device__ __forceinline__ uint64_t now_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void st_release(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_acquire(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
+// elements per thread (64 bytes) and per tile
+__host__ __device__ constexpr int f_ept(bool bf) { return bf ? 32 : 16; }
+__host__ __device__ constexpr int f_tile(bool bf) { return F_THREADS * f_ept(bf); }
 __device__ __forceinline__ int64_t imin(int64_t a, int64_t b) { return a < b ? a : b; }
 __device__ __forceinline__ int64_t imax(int64_t a, int64_t b) { return a > b ? a : b; }
 
@@ -84,9 +67,9 @@ struct FilterArgs {
   void* data;
   int32_t* indices;
   int32_t* indptr;
-  unsigned long long* state;  // [nb * tiles], zero before the launch
-  uint32_t* counter;          // zero before the launch
-  int32_t* err;
+  uint32_t* tile_cnt;  // [nb * tiles] outliers per tile
+  uint32_t* tile_off;  // [nb * tiles] exclusive prefix within the matrix
+  uint32_t* total;     // [nb] outliers per matrix
   uint64_t RC;  // elements per matrix
   uint32_t R, C;
   uint32_t tiles;  // tiles per matrix
@@ -96,31 +79,24 @@ struct FilterArgs {
   int32_t vec;      // 16-byte loads and stores allowed
 };
 
-// One tile per CTA; thread i holds elements [16 i, 16 i + 16) of the tile.
+// Thread `tid` of tile `t` of matrix `b`: its EPT elements (from element e0
+// of the matrix) as 16 words of raw bits, and how many of them exist.
 template <bool BF>
-__global__ void __launch_bounds__(F_THREADS) k_outlier_filter(const __grid_constant__ FilterArgs a) {
-  constexpr int NW = BF ? 8 : 16;  // 32-bit words per thread
-  constexpr int VE = BF ? 8 : 4;   // elements per 16-byte vector
+__device__ __forceinline__ void load_tile(const FilterArgs& a, uint32_t b, uint32_t t, int tid,
+                                          uint32_t (&w)[16], uint64_t& e0, uint32_t& nvalid,
+                                          uint64_t& first) {
+  constexpr int F_EPT = f_ept(BF);
+  constexpr int VE = BF ? 8 : 4;
   constexpr int ES = BF ? 2 : 4;
-  __shared__ uint32_t s_tile, s_excl;
-  __shared__ uint32_t s_warp[F_WARPS];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) s_tile = atomicAdd(a.counter, 1u);
-  __syncthreads();
-  const uint32_t g = s_tile;
-  const uint32_t b = g / a.tiles, t = g - b * a.tiles;
-  const uint64_t e0 = (uint64_t)t * F_TILE + (uint64_t)tid * F_EPT;
-  const uint32_t nvalid = e0 < a.RC ? (uint32_t)imin(F_EPT, (int64_t)(a.RC - e0)) : 0u;
-  const uint64_t first = (uint64_t)b * a.RC + e0;  // element index in the whole input
-
-  uint32_t w[NW];
+  e0 = (uint64_t)t * f_tile(BF) + (uint64_t)tid * F_EPT;
+  nvalid = e0 < a.RC ? (uint32_t)imin(F_EPT, (int64_t)(a.RC - e0)) : 0u;
+  first = (uint64_t)b * a.RC + e0;
 #pragma unroll
-  for (int k = 0; k < NW; ++k) w[k] = 0;
+  for (int k = 0; k < 16; ++k) w[k] = 0;
   if (a.vec) {
-    const uint4* src = reinterpret_cast<const uint4*>(
-        reinterpret_cast<const char*>(a.in) + first * ES);
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.in) + first * ES);
 #pragma unroll
-    for (int v = 0; v < NW / 4; ++v)
+    for (int v = 0; v < 4; ++v)
       if ((uint32_t)(v * VE) < nvalid) {
         const uint4 q = src[v];
         w[4 * v] = q.x, w[4 * v + 1] = q.y, w[4 * v + 2] = q.z, w[4 * v + 3] = q.w;
@@ -137,28 +113,112 @@ __global__ void __launch_bounds__(F_THREADS) k_outlier_filter(const __grid_const
         }
       }
   }
+}
 
-  // outlier masks: "out" zeroes the inlier, "csr" (also x != 0) is stored
-  const uint32_t lo1 = a.lo1, lo1c = max(lo1, 1u);
-  uint32_t csrbits = 0;
+// Bit i set <=> element i is stored in the CSR (outlier and nonzero); with
+// INL the words become the inliers (outliers replaced by +0).
+template <bool BF, bool INL>
+__device__ __forceinline__ uint32_t csr_bits(uint32_t (&w)[16], uint32_t lo1, uint32_t nvalid) {
+  const uint32_t lo1c = max(lo1, 1u);
+  uint32_t bits = 0;
 #pragma unroll
-  for (int k = 0; k < NW; ++k) {
+  for (int k = 0; k < 16; ++k) {
     if (BF) {
       const uint32_t ab = w[k] & 0x7FFF7FFFu;
       const uint32_t fin = __vcmpleu2(ab, 0x7F807F80u);
-      const uint32_t mo = __vcmpgeu2(ab, lo1 * 0x10001u) & fin;
       const uint32_t mc = __vcmpgeu2(ab, lo1c * 0x10001u) & fin;
-      csrbits |= ((mc & 1u) | ((mc >> 15) & 2u)) << (2 * k);
-      w[k] &= ~mo;
+      bits |= ((mc & 1u) | ((mc >> 15) & 2u)) << (2 * k);
+      if (INL) w[k] &= ~(__vcmpgeu2(ab, lo1 * 0x10001u) & fin);
     } else {
       const uint32_t ab = w[k] & 0x7FFFFFFFu;
       const bool fin = ab <= 0x7F800000u;
-      csrbits |= (uint32_t)(fin && ab >= lo1c) << k;
-      if (fin && ab >= lo1) w[k] = 0;
+      bits |= (uint32_t)(fin && ab >= lo1c) << k;
+      if (INL && fin && ab >= lo1) w[k] = 0;
     }
   }
-  if ((uint32_t)F_EPT > nvalid) csrbits &= (1u << nvalid) - 1u;
+  if ((uint32_t)f_ept(BF) > nvalid) bits &= (1u << nvalid) - 1u;
+  return bits;
+}
 
+// block-wide sum (F_THREADS threads)
+__device__ __forceinline__ uint32_t block_sum(uint32_t x, uint32_t* s_warp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) x += __shfl_xor_sync(FULL, x, o);
+  if (lane == 0) s_warp[warp] = x;
+  __syncthreads();
+  uint32_t t = 0;
+#pragma unroll
+  for (int i = 0; i < F_WARPS; ++i) t += s_warp[i];
+  return t;
+}
+
+template <bool BF>
+__global__ void __launch_bounds__(F_THREADS) k_outlier_count(const __grid_constant__ FilterArgs a) {
+  __shared__ uint32_t s_warp[F_WARPS];
+  const uint32_t g = blockIdx.x, b = g / a.tiles, t = g - b * a.tiles;
+  uint32_t w[16];
+  uint64_t e0, first;
+  uint32_t nvalid;
+  load_tile<BF>(a, b, t, threadIdx.x, w, e0, nvalid, first);
+  const uint32_t n = block_sum(__popc(csr_bits<BF, false>(w, a.lo1, nvalid)), s_warp);
+  if (threadIdx.x == 0) a.tile_cnt[g] = n;
+}
+
+// exclusive prefix of the tile counts of matrix blockIdx.x; one CTA each
+__global__ void __launch_bounds__(1024) k_outlier_scan(const __grid_constant__ FilterArgs a) {
+  __shared__ uint32_t s_w[32];
+  __shared__ uint32_t s_carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint64_t base = (uint64_t)blockIdx.x * a.tiles;
+  if (tid == 0) s_carry = 0;
+  __syncthreads();
+  for (uint32_t c = 0; c < a.tiles; c += 1024) {
+    const uint32_t i = c + tid;
+    const uint32_t x = i < a.tiles ? a.tile_cnt[base + i] : 0u;
+    uint32_t v = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(FULL, v, o);
+      if (lane >= o) v += y;
+    }
+    if (lane == 31) s_w[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t z = s_w[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(FULL, z, o);
+        if (lane >= o) z += y;
+      }
+      s_w[lane] = z;
+    }
+    __syncthreads();
+    const uint32_t carry = s_carry;
+    const uint32_t incl = v + (warp > 0 ? s_w[warp - 1] : 0u) + carry;
+    if (i < a.tiles) a.tile_off[base + i] = incl - x;
+    __syncthreads();
+    if (tid == 1023) s_carry = incl;
+    __syncthreads();
+  }
+  if (tid == 0) a.total[blockIdx.x] = s_carry;
+}
+
+// One tile per CTA; thread i holds elements [EPT i, EPT i + EPT) of the tile.
+template <bool BF>
+__global__ void __launch_bounds__(F_THREADS) k_outlier_scatter(const __grid_constant__ FilterArgs a) {
+  constexpr int F_EPT = f_ept(BF);
+  constexpr int VE = BF ? 8 : 4;
+  constexpr int ES = BF ? 2 : 4;
+  __shared__ uint32_t s_warp[F_WARPS];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t g = blockIdx.x, b = g / a.tiles, t = g - b * a.tiles;
+  uint32_t w[16];
+  uint64_t e0, first;
+  uint32_t nvalid;
+  load_tile<BF>(a, b, t, tid, w, e0, nvalid, first);
+  const uint32_t csrbits = a.inliers ? csr_bits<BF, true>(w, a.lo1, nvalid)
+                                     : csr_bits<BF, false>(w, a.lo1, nvalid);
   // block-wide exclusive scan of the per-thread counts
   const uint32_t cnt = __popc(csrbits);
   uint32_t inc = cnt;
@@ -169,56 +229,29 @@ __global__ void __launch_bounds__(F_THREADS) k_outlier_filter(const __grid_const
   }
   if (lane == 31) s_warp[warp] = inc;
   __syncthreads();
-  if (warp == 0) {
-    const uint32_t v = lane < F_WARPS ? s_warp[lane] : 0u;
-    uint32_t vi = v;
+  uint32_t wofs = 0;
 #pragma unroll
-    for (int o = 1; o < F_WARPS; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(FULL, vi, o);
-      if (lane >= o) vi += y;
-    }
-    const uint32_t agg = __shfl_sync(FULL, vi, F_WARPS - 1);
-    if (lane < F_WARPS) s_warp[lane] = vi - v;
-    if (lane == 0) {
-      // decoupled look-back: predecessors of this tile hold earlier tickets,
-      // so they are resident or done and every wait ends
-      unsigned long long* st = a.state + (uint64_t)b * a.tiles;
-      uint32_t excl = 0;
-      if (t == 0) {
-        st_release(st, ((unsigned long long)agg << 32) | ST_INCL);
-      } else {
-        st_release(st + t, ((unsigned long long)agg << 32) | ST_AGG);
-        int64_t j = (int64_t)t - 1;
-        const uint64_t t0 = now_ns();
-        uint32_t spins = 0;
-        while (j >= 0) {
-          const unsigned long long s = ld_acquire(st + j);
-          const uint32_t f = (uint32_t)(s & 3ull);
-          if (f == 0) {
-            if (++spins >= MAX_SPINS || ((spins & 255u) == 0 && now_ns() - t0 > WAIT_NS)) {
-              atomicExch(a.err, 1);
-              break;
-            }
-            continue;
-          }
-          excl += (uint32_t)(s >> 32);
-          if (f == ST_INCL) break;
-          --j;
-        }
-        st_release(st + t, ((unsigned long long)(excl + agg) << 32) | ST_INCL);
-      }
-      s_excl = excl;
+  for (int i = 0; i < F_WARPS; ++i) wofs += i < warp ? s_warp[i] : 0u;
+  const uint32_t pos0 = a.tile_off[g] + wofs + inc - cnt;
+  const uint64_t slot0 = (uint64_t)b * (uint64_t)a.max_nnz;
+
+  // unused slots of this matrix: value 0, column -1 (each tile a share)
+  {
+    const int64_t nse = a.total[b];
+    for (int64_t p = nse + (int64_t)t * F_THREADS + tid; p < a.max_nnz;
+         p += (int64_t)a.tiles * F_THREADS) {
+      if (BF) reinterpret_cast<uint16_t*>(a.data)[slot0 + p] = 0;
+      else reinterpret_cast<uint32_t*>(a.data)[slot0 + p] = 0;
+      a.indices[slot0 + p] = -1;
     }
   }
-  __syncthreads();
   if (!nvalid) return;
-  const uint32_t pos0 = s_excl + s_warp[warp] + inc - cnt;
 
   if (a.inliers) {
     if (a.vec) {
       uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.inliers) + first * ES);
 #pragma unroll
-      for (int v = 0; v < NW / 4; ++v)
+      for (int v = 0; v < 4; ++v)
         if ((uint32_t)(v * VE) < nvalid)
           dst[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
     } else {
@@ -238,7 +271,6 @@ __global__ void __launch_bounds__(F_THREADS) k_outlier_filter(const __grid_const
   const uint32_t c0 = (uint32_t)(e0 - r0 * a.C);
   // the CSR entries of this thread's elements (few: outliers are rare)
   if (csrbits) {
-    const uint64_t slot0 = (uint64_t)b * (uint64_t)a.max_nnz;
     uint32_t bits = csrbits, p = pos0;
     while (bits) {
       const int i = __ffs(bits) - 1;
@@ -358,16 +390,29 @@ __device__ __forceinline__ void b_row(const SpmmArgs& a, int64_t bb, int32_t row
   }
 }
 
-// One CTA per (row, chunk of S_THREADS * VEC columns); the row's entries are
-// staged in shared memory 256 at a time and every thread accumulates its
-// VEC columns over them in CSR order.
+// a * b + c rounded once, a and b bfloat16 (exact product), c float32
+__device__ __forceinline__ float fma_bf16(uint16_t a, uint16_t b, float c) {
+  float d;
+  asm("fma.rn.f32.bf16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ void halves(uint32_t w, uint16_t& lo, uint16_t& hi) {
+  asm("mov.b32 {%0, %1}, %2;" : "=h"(lo), "=h"(hi) : "r"(w));
+}
+
+// One CTA per (row, chunk of S_THREADS * VEC columns), chunk-major so the
+// CTAs running together read one column slice of B (kept in L2); the row's
+// entries are staged in shared memory 256 at a time and every thread
+// accumulates its VEC columns over them in CSR order, 8 B rows in flight.
 template <bool DBF, bool BBF, int VEC>
 __global__ void __launch_bounds__(S_THREADS) k_spmm_csr(const __grid_constant__ SpmmArgs a) {
   __shared__ float s_v[S_THREADS];
+  __shared__ uint16_t s_vb[S_THREADS];
   __shared__ int32_t s_c[S_THREADS];
   const int tid = threadIdx.x;
   const int64_t bid = blockIdx.x;
-  const int64_t chunk = bid % a.chunks, rest = bid / a.chunks;
+  const int64_t rows_all = (int64_t)gridDim.x / a.chunks;
+  const int64_t chunk = bid / rows_all, rest = bid - chunk * rows_all;
   const int64_t r = rest % a.X, b = rest / a.X;
   const int32_t* cr = a.crow + b * (a.X + 1);
   const int64_t start = cr[r], end = cr[r + 1];
@@ -376,6 +421,7 @@ __global__ void __launch_bounds__(S_THREADS) k_spmm_csr(const __grid_constant__ 
   const int64_t boff = b * a.L;
   const int64_t bb = a.b_batched ? b * a.Kc * a.N : 0;
   const int64_t q4 = (end - start) / 4 * 4;  // entries in whole groups of four (pairs mode)
+  constexpr bool MIXED = DBF && BBF && VEC == 8;
   float acc[VEC];
 #pragma unroll
   for (int i = 0; i < VEC; ++i) acc[i] = 0.0f;
@@ -384,8 +430,13 @@ __global__ void __launch_bounds__(S_THREADS) k_spmm_csr(const __grid_constant__ 
     __syncthreads();
     if (tid < cnt) {
       const int64_t j = boff + s0 + tid;
-      s_v[tid] = DBF ? bf2f(reinterpret_cast<const uint16_t*>(a.data)[j])
-                     : reinterpret_cast<const float*>(a.data)[j];
+      if (DBF) {
+        const uint16_t vb = reinterpret_cast<const uint16_t*>(a.data)[j];
+        s_vb[tid] = vb;
+        s_v[tid] = bf2f(vb);
+      } else {
+        s_v[tid] = reinterpret_cast<const float*>(a.data)[j];
+      }
       const int64_t c = reinterpret_cast<const int32_t*>(a.indices)[j];
       s_c[tid] = (int32_t)imin(imax(c, 0), a.Kc - 1);
     }
@@ -393,13 +444,48 @@ __global__ void __launch_bounds__(S_THREADS) k_spmm_csr(const __grid_constant__ 
     if (!live) continue;
     if (!a.pairs) {
       // fused multiply-add chain
-#pragma unroll 4
-      for (int j = 0; j < cnt; ++j) {
-        float x[VEC];
-        b_row<BBF, VEC>(a, bb, s_c[j], n0, x);
-        const float v = s_v[j];
+      if (MIXED) {
+        const uint16_t* B16 = reinterpret_cast<const uint16_t*>(a.B) + bb + n0;
+        int j = 0;
+        for (; j + 8 <= cnt; j += 8) {
+          uint4 q[8];
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) acc[i] = fmaf(v, x[i], acc[i]);
+          for (int u = 0; u < 8; ++u)
+            q[u] = __ldg(reinterpret_cast<const uint4*>(B16 + (int64_t)s_c[j + u] * a.N));
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint16_t v = s_vb[j + u];
+            const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              uint16_t lo, hi;
+              halves(w[k], lo, hi);
+              acc[2 * k] = fma_bf16(v, lo, acc[2 * k]);
+              acc[2 * k + 1] = fma_bf16(v, hi, acc[2 * k + 1]);
+            }
+          }
+        }
+        for (; j < cnt; ++j) {
+          const uint4 q = __ldg(reinterpret_cast<const uint4*>(B16 + (int64_t)s_c[j] * a.N));
+          const uint16_t v = s_vb[j];
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            uint16_t lo, hi;
+            halves(w[k], lo, hi);
+            acc[2 * k] = fma_bf16(v, lo, acc[2 * k]);
+            acc[2 * k + 1] = fma_bf16(v, hi, acc[2 * k + 1]);
+          }
+        }
+      } else {
+#pragma unroll 4
+        for (int j = 0; j < cnt; ++j) {
+          float x[VEC];
+          b_row<BBF, VEC>(a, bb, s_c[j], n0, x);
+          const float v = s_v[j];
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) acc[i] = fmaf(v, x[i], acc[i]);
+        }
       }
       continue;
     }
@@ -458,7 +544,7 @@ __global__ void __launch_bounds__(S_THREADS) k_spmm_csr(const __grid_constant__ 
 template <bool DBF, bool BBF, int VEC>
 int launch_spmm(SpmmArgs& a, int64_t nb, cudaStream_t st) {
   a.chunks = (int32_t)((a.N + (int64_t)S_THREADS * VEC - 1) / ((int64_t)S_THREADS * VEC));
-  const int64_t blocks = nb * a.X * a.chunks;
+  const int64_t blocks = nb * a.X * a.chunks;  // chunk-major: [chunks][nb][X]
   if (blocks == 0) return VQ_OK;
   if (blocks > INT32_MAX) return VQ_ERR_TOO_LARGE;
   k_spmm_csr<DBF, BBF, VEC><<<(unsigned)blocks, S_THREADS, 0, st>>>(a);
@@ -656,7 +742,10 @@ int matrix_dims(const vq_tensor* t, int64_t* nb, int64_t* R, int64_t* C) {
   return VQ_OK;
 }
 
-int64_t filter_tiles(int64_t R, int64_t C) { return (R * C + F_TILE - 1) / F_TILE; }
+int64_t filter_tiles(int64_t R, int64_t C, int dtype) {
+  const int64_t tile = f_tile(dtype == VQ_BF16);
+  return (R * C + tile - 1) / tile;
+}
 
 }  // namespace
 
@@ -669,35 +758,36 @@ uint32_t vq_outlier_threshold_bits(double threshold, int32_t dtype) {
 size_t vq_filter_outlier_workspace_bytes(const vq_tensor* input) {
   int64_t nb, R, C;
   if (!input || matrix_dims(input, &nb, &R, &C)) return 0;
-  return (size_t)(nb * filter_tiles(R, C)) * 8 + 16;
+  return (size_t)(2 * nb * filter_tiles(R, C, input->dtype) + nb) * 4 + 16;
 }
 
 int vq_filter_outlier(const vq_tensor* input, double threshold, int64_t max_nnz,
                       int32_t indptr_offset, void* data, int32_t* indices, int32_t* indptr,
                       void* inliers, void* workspace, size_t workspace_bytes, int32_t* d_err,
                       void* stream) {
-  if (!input || !indptr || !workspace || !d_err) return VQ_ERR_NULL;
+  (void)d_err;  // no device waits: nothing to report
+  if (!input || !indptr || !workspace) return VQ_ERR_NULL;
   if (input->dtype != VQ_BF16 && input->dtype != VQ_F32) return VQ_ERR_UNSUPPORTED;
   int64_t nb, R, C;
   int st = matrix_dims(input, &nb, &R, &C);
   if (st) return st;
   if (max_nnz < 0 || nb < 0 || R < 0 || C < 0) return VQ_ERR_INVALID;
-  if (R * C >= ((int64_t)1 << 31) || R >= INT32_MAX || nb * filter_tiles(R, C) >= INT32_MAX)
+  if (R * C >= ((int64_t)1 << 31) || R >= INT32_MAX ||
+      nb * filter_tiles(R, C, input->dtype) >= INT32_MAX)
     return VQ_ERR_TOO_LARGE;
   if (nb * max_nnz > 0 && (!data || !indices)) return VQ_ERR_NULL;
   if (nb * R * C > 0 && !input->data) return VQ_ERR_NULL;
-  const int64_t tiles = filter_tiles(R, C);
-  if (workspace_bytes < (size_t)(nb * tiles) * 8 + 16) return VQ_ERR_TOO_LARGE;
+  const int64_t tiles = filter_tiles(R, C, input->dtype);
+  if (workspace_bytes < (size_t)(2 * nb * tiles + nb) * 4 + 16) return VQ_ERR_TOO_LARGE;
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   const int es = esize(input->dtype);
-  // unused CSR slots: value 0, column -1
-  if (nb * max_nnz > 0) {
-    if (cudaMemsetAsync(data, 0, (size_t)(nb * max_nnz) * es, cs) != cudaSuccess ||
-        cudaMemsetAsync(indices, 0xFF, (size_t)(nb * max_nnz) * 4, cs) != cudaSuccess)
-      return VQ_ERR_CUDA;
-  }
   if (nb == 0) return VQ_OK;
   if (R * C == 0) {
+    // no elements: every slot unused, every row pointer the offset
+    if (nb * max_nnz > 0 &&
+        (cudaMemsetAsync(data, 0, (size_t)(nb * max_nnz) * es, cs) != cudaSuccess ||
+         cudaMemsetAsync(indices, 0xFF, (size_t)(nb * max_nnz) * 4, cs) != cudaSuccess))
+      return VQ_ERR_CUDA;
     const int64_t n = nb * (R + 1);
     k_fill_i32<<<(unsigned)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, cs>>>(
         indptr, n, indptr_offset);
@@ -710,9 +800,9 @@ int vq_filter_outlier(const vq_tensor* input, double threshold, int64_t max_nnz,
   a.data = data;
   a.indices = indices;
   a.indptr = indptr;
-  a.state = reinterpret_cast<unsigned long long*>(workspace);
-  a.counter = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(workspace) + nb * tiles * 8);
-  a.err = d_err;
+  a.tile_cnt = reinterpret_cast<uint32_t*>(workspace);
+  a.tile_off = a.tile_cnt + nb * tiles;
+  a.total = a.tile_off + nb * tiles;
   a.RC = (uint64_t)(R * C);
   a.R = (uint32_t)R;
   a.C = (uint32_t)C;
@@ -722,13 +812,12 @@ int vq_filter_outlier(const vq_tensor* input, double threshold, int64_t max_nnz,
   a.lo1 = outlier_lo1(threshold, input->dtype);
   const int ve = 16 / es;
   a.vec = (R * C) % ve == 0 && aligned16(input->data) && (!inliers || aligned16(inliers));
-  if (cudaMemsetAsync(workspace, 0, (size_t)(nb * tiles) * 8 + 16, cs) != cudaSuccess)
-    return VQ_ERR_CUDA;
   const unsigned blocks = (unsigned)(nb * tiles);
-  if (input->dtype == VQ_BF16)
-    k_outlier_filter<true><<<blocks, F_THREADS, 0, cs>>>(a);
-  else
-    k_outlier_filter<false><<<blocks, F_THREADS, 0, cs>>>(a);
+  if (input->dtype == VQ_BF16) k_outlier_count<true><<<blocks, F_THREADS, 0, cs>>>(a);
+  else k_outlier_count<false><<<blocks, F_THREADS, 0, cs>>>(a);
+  k_outlier_scan<<<(unsigned)nb, 1024, 0, cs>>>(a);
+  if (input->dtype == VQ_BF16) k_outlier_scatter<true><<<blocks, F_THREADS, 0, cs>>>(a);
+  else k_outlier_scatter<false><<<blocks, F_THREADS, 0, cs>>>(a);
   return cuda_status(cudaGetLastError());
 }
 

@@ -8,8 +8,9 @@ by a column window.  ``linear_mx`` / ``matmul_mx`` add ``spmm_csr`` of their
 ``A_data`` / ``A_indices`` / ``A_indptr`` to the dense product
 (``voyager_b200.gemm``).
 
-Kernels (``csrc/vq_sparse.cu``): the filter is one pass over the input with
-a decoupled look-back for the CSR offsets; ``quantize_mx_outlier`` along the
+Kernels (``csrc/vq_sparse.cu``): the filter counts outliers per tile, scans
+the counts and scatters the CSR in row-major order (three launches, no waits
+between CTAs); ``quantize_mx_outlier`` along the
 last dim masks the outliers inside ``quantize_mx``'s kernel instead of
 writing and re-reading the inliers; ``spmm_csr`` is a gather of B rows
 accumulated with float32 fused multiply-adds in CSR order (what the CPU
@@ -26,28 +27,8 @@ from voyager_b200 import ops as _ops
 from voyager_b200._cache import TensorCache
 from voyager_b200.tables import QMAP_SIZE, floor_log2, rounder_for
 
-_errs = {}
 _tcache = TensorCache()
 _I32 = (-(1 << 31), (1 << 31) - 1)
-
-
-def _err_word(dev: torch.device) -> torch.Tensor:
-    """The device error word of the filter's bounded waits (one per device)."""
-    k = (dev.type, dev.index)
-    e = _errs.get(k)
-    if e is None:
-        e = _errs[k] = torch.zeros(1, dtype=torch.int32, device=dev)
-    return e
-
-
-def check_errors(dev: Optional[torch.device] = None):
-    """Raise if a filter launch on ``dev`` reported a wait that gave up
-    (reads the device word: synchronises)."""
-    for k, e in list(_errs.items()):
-        if dev is not None and (dev.type, dev.index) != k:
-            continue
-        if int(e.item()):
-            raise _lib.VqError("filter_outlier: a tile's wait for its predecessor timed out")
 
 
 def _max_nnz(mat_shape, max_pct: float) -> int:
@@ -85,8 +66,7 @@ def _filter(input: torch.Tensor, threshold, max_pct: float, offset: int, want_in
                              data.data_ptr() if data.numel() else None,
                              indices.data_ptr() if indices.numel() else None, indptr.data_ptr(),
                              inliers.data_ptr() if inliers is not None and inliers.numel() else None,
-                             ws.data_ptr(), ws.numel(), _err_word(dev).data_ptr(),
-                             _ops._stream(dev))
+                             ws.data_ptr(), ws.numel(), None, _ops._stream(dev))
     _lib.check(st, "quantized_ops::filter_outlier")
     return data, indices, indptr, inliers
 
