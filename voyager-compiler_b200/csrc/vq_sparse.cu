@@ -57,6 +57,16 @@ int64_t numel(const vq_tensor& t) {
   return n;
 }
 int esize(int dt) { return dt == VQ_BF16 ? 2 : 4; }
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+  }
+  return n;
+}
 
 // ---------------------------------------------------------------------------
 // filter_outlier
@@ -153,16 +163,35 @@ __device__ __forceinline__ uint32_t block_sum(uint32_t x, uint32_t* s_warp) {
   return t;
 }
 
+// Persistent: CTA c counts tiles c, c + grid, ...; the next tile's loads
+// are in flight while the current one is reduced.
 template <bool BF>
-__global__ void __launch_bounds__(F_THREADS) k_outlier_count(const __grid_constant__ FilterArgs a) {
-  __shared__ uint32_t s_warp[F_WARPS];
-  const uint32_t g = blockIdx.x, b = g / a.tiles, t = g - b * a.tiles;
+__global__ void __launch_bounds__(F_THREADS) k_outlier_count(const __grid_constant__ FilterArgs a,
+                                                             uint32_t ntiles) {
+  __shared__ uint32_t s_warp[2][F_WARPS];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t g = blockIdx.x;
+  if (g >= ntiles) return;
   uint32_t w[16];
   uint64_t e0, first;
   uint32_t nvalid;
-  load_tile<BF>(a, b, t, threadIdx.x, w, e0, nvalid, first);
-  const uint32_t n = block_sum(__popc(csr_bits<BF, false>(w, a.lo1, nvalid)), s_warp);
-  if (threadIdx.x == 0) a.tile_cnt[g] = n;
+  load_tile<BF>(a, g / a.tiles, g % a.tiles, threadIdx.x, w, e0, nvalid, first);
+  for (int buf = 0; g < ntiles; buf ^= 1) {
+    uint32_t n = __popc(csr_bits<BF, false>(w, a.lo1, nvalid));
+    const uint32_t gn = g + gridDim.x;
+    if (gn < ntiles) load_tile<BF>(a, gn / a.tiles, gn % a.tiles, threadIdx.x, w, e0, nvalid, first);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) n += __shfl_xor_sync(FULL, n, o);
+    if (lane == 0) s_warp[buf][warp] = n;
+    __syncthreads();  // s_warp[buf] complete; s_warp[buf ^ 1] free again
+    if (threadIdx.x == 0) {
+      uint32_t t = 0;
+#pragma unroll
+      for (int i = 0; i < F_WARPS; ++i) t += s_warp[buf][i];
+      a.tile_cnt[g] = t;
+    }
+    g = gn;
+  }
 }
 
 // exclusive prefix of the tile counts of matrix blockIdx.x; one CTA each
@@ -313,44 +342,59 @@ __global__ void k_fill_i32(int32_t* p, int64_t n, int32_t v) {
 // ---------------------------------------------------------------------------
 // spmm_csr
 // ---------------------------------------------------------------------------
-// crow[b][r] = cummax over r' <= r of clamp(indptr[b][r'] - indptr[b][0], 0, L)
+// crow[b][r] = cummax over r' <= r of clamp(indptr[b][r'] - indptr[b][0], 0, L);
+// one CTA per matrix, 8 consecutive rows per thread per step.
 __global__ void __launch_bounds__(1024) k_spmm_rows(const int32_t* indptr, int64_t rows1, int64_t L,
                                                     int32_t* crow) {
   __shared__ int32_t s_w[32];
   __shared__ int32_t s_carry;
+  constexpr int PER = 8;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int32_t* ip = indptr + (int64_t)blockIdx.x * rows1;
   int32_t* out = crow + (int64_t)blockIdx.x * rows1;
   const int64_t base = ip[0];
   if (tid == 0) s_carry = 0;
   __syncthreads();
-  for (int64_t c = 0; c < rows1; c += 1024) {
-    const int64_t r = c + tid;
-    int32_t v = 0;
-    if (r < rows1) v = (int32_t)imin(imax((int64_t)ip[r] - base, 0), L);
+  for (int64_t c = 0; c < rows1; c += 1024 * PER) {
+    const int64_t r0 = c + (int64_t)tid * PER;
+    int32_t v[PER];
+    int32_t m = 0;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int64_t r = r0 + k;
+      v[k] = r < rows1 ? (int32_t)imin(imax((int64_t)ip[r] - base, 0), L) : 0;
+      m = max(m, v[k]);
+      v[k] = m;  // running max within the thread's rows
+    }
+    int32_t x = m;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int32_t y = __shfl_up_sync(FULL, v, o);
-      if (lane >= o) v = max(v, y);
+      const int32_t y = __shfl_up_sync(FULL, x, o);
+      if (lane >= o) x = max(x, y);
     }
-    if (lane == 31) s_w[warp] = v;
+    if (lane == 31) s_w[warp] = x;
     __syncthreads();
     if (warp == 0) {
-      int32_t x = s_w[lane];
+      int32_t z = s_w[lane];
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const int32_t y = __shfl_up_sync(FULL, x, o);
-        if (lane >= o) x = max(x, y);
+        const int32_t y = __shfl_up_sync(FULL, z, o);
+        if (lane >= o) z = max(z, y);
       }
-      s_w[lane] = x;
+      s_w[lane] = z;
     }
     __syncthreads();
-    const int32_t carry = s_carry;
-    if (warp > 0) v = max(v, s_w[warp - 1]);
-    v = max(v, carry);
-    if (r < rows1) out[r] = v;
+    // max over everything before this thread's rows
+    int32_t before = max(s_carry, warp > 0 ? s_w[warp - 1] : 0);
+    const int32_t xl = __shfl_up_sync(FULL, x, 1);
+    if (lane > 0) before = max(before, xl);
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int64_t r = r0 + k;
+      if (r < rows1) out[r] = max(v[k], before);
+    }
     __syncthreads();
-    if (tid == 1023) s_carry = v;
+    if (tid == 1023) s_carry = max(before, x);
     __syncthreads();
   }
 }
@@ -813,8 +857,9 @@ int vq_filter_outlier(const vq_tensor* input, double threshold, int64_t max_nnz,
   const int ve = 16 / es;
   a.vec = (R * C) % ve == 0 && aligned16(input->data) && (!inliers || aligned16(inliers));
   const unsigned blocks = (unsigned)(nb * tiles);
-  if (input->dtype == VQ_BF16) k_outlier_count<true><<<blocks, F_THREADS, 0, cs>>>(a);
-  else k_outlier_count<false><<<blocks, F_THREADS, 0, cs>>>(a);
+  const unsigned cblocks = (unsigned)std::min<int64_t>(nb * tiles, (int64_t)num_sms() * 6);
+  if (input->dtype == VQ_BF16) k_outlier_count<true><<<cblocks, F_THREADS, 0, cs>>>(a, blocks);
+  else k_outlier_count<false><<<cblocks, F_THREADS, 0, cs>>>(a, blocks);
   k_outlier_scan<<<(unsigned)nb, 1024, 0, cs>>>(a);
   if (input->dtype == VQ_BF16) k_outlier_scatter<true><<<blocks, F_THREADS, 0, cs>>>(a);
   else k_outlier_scatter<false><<<blocks, F_THREADS, 0, cs>>>(a);
