@@ -317,6 +317,165 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
 }
 
 // ---------------------------------------------------------------------------
+// k_qmx_nvfp4: quantize_mx for NVFP4 (the C1 configuration) -- bf16 input,
+// E2M1 element table and E4M3 scale table both reproduced by the hardware
+// conversions (verified), blocks of 16 along rows whose length is a multiple
+// of 16 (so block g starts at element 16 g).  One thread per block.
+//
+// Per block: amax (and min) on magnitude bits; a block holding a NaN, a
+// scale whose reciprocal is not a normal float, or a quotient too close to
+// a bf16 tie takes the generic path (IEEE division, hw_pair); otherwise the
+// quotients are x * fl(1/s) (their bf16 is that of x / s, see Divisor),
+// rounded to bf16 in pairs, converted to E2M1 pairs and back through a
+// 256-entry table of the E2M1 values as bf16 (the -0 code stays -0).  When
+// every quotient of the block is a normal float the tie test runs on the
+// FMA pipe (q scaled by 1 -+ 2^-21, both rounded to bf16 and compared);
+// blocks with zeros or tiny values test the low 16 bits and turn a -0 index
+// into +0, as the table has it.
+// ---------------------------------------------------------------------------
+// bf16 bits of an E2M1 code (4 bits: sign, 2 exponent bits with bias 1, 1
+// mantissa bit): 0, 0.5, 1, 1.5, 2, 3, 4, 6 and their negatives (-0 too)
+__device__ __forceinline__ uint32_t e2m1_bf16(uint32_t nib) {
+  const uint32_t e = (nib >> 1) & 3u, f = nib & 1u;
+  const uint32_t mag = e == 0 ? (f ? 0x3F00u : 0u) : (((e + 126u) << 7) | (f << 6));
+  return mag | ((nib & 8u) << 12);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+__device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u32.u8 %0, t;\n\t}"
+      : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// E4M3 rounding (round-half-even, saturating) of a non-negative float, as
+// bf16 bits: the value quantize's E4M3 table gives for it (verified
+// hardware rounder).  A NaN gives a NaN (the caller's "not > 0" then takes
+// the scale 1).
+__device__ __forceinline__ uint32_t e4m3_bf16(float v) {
+  uint32_t h;
+  asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e4m3x2.f32 t, %1, %1;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(h) : "f"(v));
+  return __float_as_uint(__half2float(__ushort_as_half((unsigned short)(h & 0xFFFFu)))) >> 16;
+}
+
+template <bool MASK>
+__global__ void __launch_bounds__(256) k_qmx_nvfp4(const __grid_constant__ QmxArgs a) {
+  __shared__ uint32_t lut[256];
+  if (threadIdx.x < 256) lut[threadIdx.x] = e2m1_bf16(threadIdx.x) | (e2m1_bf16(threadIdx.x >> 4) << 16);
+  __syncthreads();
+  const uint32_t nthr = gridDim.x * blockDim.x;
+  for (uint32_t g0 = blockIdx.x * blockDim.x + threadIdx.x; g0 < a.ngroups; g0 += 2 * nthr) {
+    uint32_t w[2][8];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const uint32_t g = g0 + u * nthr;
+      if (g < a.ngroups) {
+        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.in) +
+                                                          (uint64_t)g * 16);
+        const uint4 q0 = __ldcs(src), q1 = __ldcs(src + 1);
+        w[u][0] = q0.x, w[u][1] = q0.y, w[u][2] = q0.z, w[u][3] = q0.w;
+        w[u][4] = q1.x, w[u][5] = q1.y, w[u][6] = q1.z, w[u][7] = q1.w;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const uint32_t g = g0 + u * nthr;
+      if (g >= a.ngroups) continue;
+      // block max / min of |x| as bf16x2 (NaN-propagating max: a NaN
+      // magnitude sorts above +inf in the bits, so amax > 0x7F80 finds it)
+      __nv_bfloat162 mx2 = __floats2bfloat162_rn(0.0f, 0.0f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t ab = w[u][k] & 0x7FFF7FFFu;
+        mx2 = __hmax2_nan(mx2, *reinterpret_cast<const __nv_bfloat162*>(&ab));
+      }
+      uint32_t mx = *reinterpret_cast<uint32_t*>(&mx2);
+      uint32_t amax = max(mx & 0xFFFFu, mx >> 16);
+      if (MASK && amax >= a.mask_lo1) {
+        // quantize_mx_outlier: this block holds outliers, quantized as +0
+        mx = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t ab = w[u][k] & 0x7FFF7FFFu;
+          w[u][k] &= ~(__vcmpgeu2(ab, a.mask_lo1 * 0x10001u) & __vcmpleu2(ab, 0x7F807F80u));
+          mx = __vmaxu2(mx, w[u][k] & 0x7FFF7FFFu);
+        }
+        amax = max(mx & 0xFFFFu, mx >> 16);
+      }
+      __nv_bfloat162 mn2 = __floats2bfloat162_rn(__int_as_float(0x7F800000), __int_as_float(0x7F800000));
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t ab = w[u][k] & 0x7FFF7FFFu;
+        mn2 = __hmin2(mn2, *reinterpret_cast<const __nv_bfloat162*>(&ab));
+      }
+      const float amin = fminf(__low2float(mn2), __high2float(mn2));  // a NaN is ignored
+      // scale = e4m3(bf16(amax / quant_max)), 1 where not > 0
+      const float s0 = round_bf(fdiv_rn(bf2f(amax), a.quant_max));
+      const float sv = bf2f(e4m3_bf16(s0));
+      const float s = sv > 0.0f ? sv : 1.0f;
+      reinterpret_cast<uint16_t*>(a.scale)[g] = (uint16_t)f2bf(s);
+      const uint32_t e = (f2u(s) >> 23) & 0xFFu;
+      bool slow = amax > 0x7F80u || e < 1u || e > 252u;
+      uint32_t out[8];
+      if (!slow) {
+        const float r = fdiv_rn(1.0f, s);
+        if (__fmul_rn(amin, r) >= 0x1p-126f) {
+          // every quotient is a normal float (no zero index): q * (1 -+ 2^-21)
+          // lie at least 3.5 float ulps below / above q, so if they round to
+          // the same bf16, so does every value within 3 patterns of q
+          uint32_t tie = 0;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float q0 = __fmul_rn(__uint_as_float(w[u][k] << 16), r);
+            const float q1 = __fmul_rn(__uint_as_float(w[u][k] & 0xFFFF0000u), r);
+            const uint32_t lo = bf16x2_rn(__fmul_rn(q0, 1.0f - 0x1p-21f), __fmul_rn(q1, 1.0f - 0x1p-21f));
+            const uint32_t hi = bf16x2_rn(__fmul_rn(q0, 1.0f + 0x1p-21f), __fmul_rn(q1, 1.0f + 0x1p-21f));
+            tie |= lo ^ hi;
+            const uint32_t idx = bf16x2_rn(q0, q1);
+            out[k] = lut[e2m1x2(__uint_as_float(idx << 16), __uint_as_float(idx & 0xFFFF0000u))];
+          }
+          slow = tie != 0;
+        } else {
+          uint32_t tie = 0;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float q0 = __fmul_rn(__uint_as_float(w[u][k] << 16), r);
+            const float q1 = __fmul_rn(__uint_as_float(w[u][k] & 0xFFFF0000u), r);
+            tie |= __vcmpleu2(__vsub2(__byte_perm(__float_as_uint(q0), __float_as_uint(q1), 0x5410),
+                                      0x7FFC7FFCu),
+                              0x00080008u);
+            const uint32_t idx = bf16x2_rn(q0, q1);
+            uint32_t o = lut[e2m1x2(__uint_as_float(idx << 16), __uint_as_float(idx & 0xFFFF0000u))];
+            // a -0 index gives +0
+            o &= ~(__vcmpeq2(idx & 0x7FFF7FFFu, 0u) & 0x80008000u);
+            out[k] = o;
+          }
+          slow = tie != 0;
+        }
+      }
+      if (slow) {
+        // generic: IEEE quotients, the verified hardware pair rounder
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float q0 = div_slow(__uint_as_float(w[u][k] << 16), s);
+          const float q1 = div_slow(__uint_as_float(w[u][k] & 0xFFFF0000u), s);
+          out[k] = hw_pair<K_HW_E2M1>(f2bf(q0) | (f2bf(q1) << 16), a.qr.nan_bits);
+        }
+      }
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.codes) + (uint64_t)g * 16);
+      __stcs(dst, make_uint4(out[0], out[1], out[2], out[3]));
+      __stcs(dst + 1, make_uint4(out[4], out[5], out[6], out[7]));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // k_qparam: calculate_mx_qparam over one or two blocked axes (generic)
 // ---------------------------------------------------------------------------
 struct QparamArgs {
@@ -1247,6 +1406,69 @@ void fill_operand(OperandMap& om, const vq_tensor* t, const DimMap* m, int vec) 
   om.uniform_vec = (m[kElemDims - 1].str == 0) || (m[kElemDims - 1].div % vec == 0);
 }
 
+// dequantize(codes, scale, block_size) with bf16 codes and bf16 scales whose
+// blocks of 2^shift elements run along the last dim (rows a multiple of the
+// block): out = bf16(code * scale), the product exact in float32 and rounded
+// once.  8 elements per 16-byte vector, 4 vectors per thread in flight.
+__global__ void __launch_bounds__(256) k_deq_blocks_bf16(const uint16_t* __restrict__ in,
+                                                         const uint16_t* __restrict__ scale,
+                                                         uint16_t* __restrict__ out, uint32_t nvec,
+                                                         int shift) {
+  constexpr int U = 4;
+  const uint32_t nthr = gridDim.x * blockDim.x;
+  for (uint32_t v0 = blockIdx.x * blockDim.x + threadIdx.x; v0 < nvec; v0 += U * nthr) {
+    uint4 q[U];
+    float sc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t v = v0 + u * nthr;
+      if (v < nvec) {
+        q[u] = __ldcs(reinterpret_cast<const uint4*>(in) + v);
+        sc[u] = bf2f(scale[((uint64_t)v * 8) >> shift]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t v = v0 + u * nthr;
+      if (v >= nvec) continue;
+      const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        __nv_bfloat162 b = __floats2bfloat162_rn(__fmul_rn(__uint_as_float(w[k] << 16), sc[u]),
+                                                 __fmul_rn(__uint_as_float(w[k] & 0xFFFF0000u), sc[u]));
+        o[k] = *reinterpret_cast<uint32_t*>(&b);
+      }
+      __stcs(reinterpret_cast<uint4*>(out) + v, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+  }
+}
+
+// The layout k_deq_blocks_bf16 takes; 0 when it does not apply.
+int launch_deq_blocks(const vq_tensor* input, const vq_tensor* scale, const vq_tensor* zp,
+                      int64_t bs, const vq_rounder* inq, const vq_rounder* outq,
+                      const vq_tensor* out, cudaStream_t st, int* status) {
+  if (zp || inq || outq || bs < 8 || (bs & (bs - 1))) return 0;
+  if (input->dtype != VQ_BF16 || scale->dtype != VQ_BF16 || out->dtype != VQ_BF16) return 0;
+  const int nd = input->ndim;
+  if (nd < 1 || scale->ndim != nd) return 0;
+  const int64_t C = input->shape[nd - 1];
+  if (C % bs || scale->shape[nd - 1] != C / bs) return 0;
+  for (int d = 0; d < nd - 1; ++d)
+    if (scale->shape[d] != input->shape[d]) return 0;
+  if (!aligned16(input->data) || !aligned16(out->data)) return 0;
+  const int64_t nvec = numel(*input) / 8;
+  if (nvec >= ((int64_t)1 << 31) || nvec == 0) return 0;
+  int shift = 0;
+  while ((1ll << shift) < bs) ++shift;
+  const int blocks = (int)std::min<int64_t>((nvec + 255) / 256, (int64_t)num_sms() * 8);
+  k_deq_blocks_bf16<<<blocks, 256, 0, st>>>((const uint16_t*)input->data,
+                                            (const uint16_t*)scale->data, (uint16_t*)out->data,
+                                            (uint32_t)nvec, shift);
+  *status = cuda_status(cudaGetLastError());
+  return 1;
+}
+
 // Shared driver of quantize (DEQ=false) and dequantize (DEQ=true).
 template <bool DEQ>
 int run_elementwise(const vq_tensor* input, const vq_tensor* scale, const vq_tensor* zp,
@@ -1276,6 +1498,12 @@ int run_elementwise(const vq_tensor* input, const vq_tensor* scale, const vq_ten
   const int64_t n = numel(*input);
   if (n == 0) return VQ_OK;
   if (!input->data || !out->data || !scale->data || (zp && !zp->data)) return VQ_ERR_NULL;
+  if (DEQ) {
+    int dst = 0;
+    if (launch_deq_blocks(input, scale, zp, bs, inq, outq, out,
+                          reinterpret_cast<cudaStream_t>(stream), &dst))
+      return dst;
+  }
 
   DimMap ms[VQ_MAX_DIMS], mz[VQ_MAX_DIMS];
   if ((st = operand_map(*input, *scale, bs, ms))) return st;
@@ -1518,6 +1746,28 @@ int launch_qmx_kind(QmxArgs& a, int K, int nv, cudaStream_t st) {
   }
 }
 
+// The NVFP4 configuration k_qmx_nvfp4 takes: returns 0 when it does not
+// apply (the caller uses k_qmx_last).
+int launch_qmx_nvfp4(const vq_tensor& x, const int* blocked, int64_t bs, int pow2,
+                     const vq_rounder* qmap, const vq_rounder* sq, QmxArgs& a, cudaStream_t st,
+                     int* status) {
+  if (x.dtype != VQ_BF16 || bs != 16 || pow2 || !sq || !qmap) return 0;
+  if (elem_kind(qmap) != K_HW_E2M1 || sq->kind != VQ_R_MINIFLOAT || sq->hw != VQ_HW_E4M3) return 0;
+  for (int d = 0; d < x.ndim - 1; ++d)
+    if (blocked[d]) return 0;
+  if (!blocked[x.ndim - 1]) return 0;
+  const int64_t C = x.shape[x.ndim - 1];
+  if (C % 16 || !aligned16(x.data) || !aligned16(a.codes)) return 0;
+  const int64_t groups = numel(x) / 16;
+  if (groups >= ((int64_t)1 << 31)) return 0;
+  a.ngroups = (uint32_t)groups;
+  const int blocks = (int)std::min<int64_t>((groups + 255) / 256, (int64_t)num_sms() * 8);
+  if (a.mask_on) k_qmx_nvfp4<true><<<blocks, 256, 0, st>>>(a);
+  else k_qmx_nvfp4<false><<<blocks, 256, 0, st>>>(a);
+  *status = cuda_status(cudaGetLastError());
+  return 1;
+}
+
 int run_qparam_generic(const vq_tensor* input, const int* blocked, int64_t bs, float qmax,
                        int pow2, int fl2q, const vq_rounder* sq, vq_tensor* scale_out,
                        cudaStream_t st) {
@@ -1668,6 +1918,9 @@ int vq_quantize_mx(const vq_tensor* input, const vq_rounder* qmap, const int64_t
     }
     a.qr = *qmap;
     const int K = elem_kind(qmap);
+    int nst = 0;
+    if (launch_qmx_nvfp4(*input, blocked, block_size, pow2, qmap, scale_qmap, a, cs, &nst))
+      return nst;
     return input->dtype == VQ_BF16 ? launch_qmx_kind<uint16_t>(a, K, nv, cs)
                                    : launch_qmx_kind<float>(a, K, nv, cs);
   }
@@ -1774,6 +2027,9 @@ int vq_quantize_mx_masked(const vq_tensor* input, const vq_rounder* qmap, int64_
   a.mask_on = 1;
   a.mask_lo1 = vq_outlier_threshold_bits(threshold, input->dtype);
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  int nst = 0;
+  if (!pack && launch_qmx_nvfp4(*input, blocked, block_size, pow2, qmap, scale_qmap, a, cs, &nst))
+    return nst;
   return input->dtype == VQ_BF16 ? launch_qmx_kind<uint16_t>(a, K, nv, cs)
                                  : launch_qmx_kind<float>(a, K, nv, cs);
 }
