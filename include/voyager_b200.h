@@ -114,6 +114,13 @@ typedef struct vq_rounder {
    * device; 0 = evaluate analytically. */
   int32_t hw;
   int32_t pad2_;
+  /* TABLE (and the POSIT / STEP kinds the kernels evaluate as a table):
+   * optional byte-coded copy of a table with at most 256 distinct patterns,
+   * table8[i] indexing palette[256] (device, caller-owned, 16-byte aligned);
+   * the kernels then stage 64.5 KB of shared memory instead of 128 KB, which
+   * lets two 1024-thread CTAs share an SM.  NULL: use `table`. */
+  const uint8_t* table8;
+  const uint16_t* palette;
 } vq_rounder;
 
 enum { VQ_HW_NONE = 0, VQ_HW_E4M3 = 1, VQ_HW_E5M2 = 2, VQ_HW_E2M1 = 3 };

@@ -52,6 +52,9 @@ __device__ __forceinline__ float div_scale_k(float amax, float qmax, bool is_bf1
 // Small helpers
 // ---------------------------------------------------------------------------
 constexpr int kTableBytes = 65536 * 2;
+constexpr int kTable8Bytes = 65536 + 512;  // byte codes + bf16 palette
+// shared memory a TABLE rounder's kernels stage
+inline int table_smem(const vq_rounder& r) { return r.table8 ? kTable8Bytes : kTableBytes; }
 
 // Division by a run-time invariant (Granlund-Montgomery, round-up variant):
 // q = (umulhi(n, m) + n) >> s, exact for every 32-bit n.
@@ -99,6 +102,10 @@ __device__ __forceinline__ uint32_t round_elem(const vq_rounder& r, uint32_t b,
   if (K == VQ_R_IDENTITY) return b & 0xFFFFu;
   if (K == VQ_R_MINIFLOAT) return round_minifloat(r, b);
   if (K == VQ_R_INT) return round_int(r, b);
+  if (r.table8) {
+    const uint8_t* codes = reinterpret_cast<const uint8_t*>(stab);
+    return reinterpret_cast<const uint16_t*>(codes + 65536)[codes[b & 0xFFFFu]];
+  }
   return stab[b & 0xFFFFu];
 }
 
@@ -115,9 +122,16 @@ __device__ __forceinline__ uint32_t to_bf16_index(float q) {
 template <int K>
 __device__ __forceinline__ void stage_table(const vq_rounder& r, uint16_t* stab) {
   if (K != VQ_R_TABLE) return;
-  const uint4* src = reinterpret_cast<const uint4*>(r.table);
   uint4* dst = reinterpret_cast<uint4*>(stab);
-  for (int i = threadIdx.x; i < kTableBytes / 16; i += blockDim.x) dst[i] = __ldg(src + i);
+  if (r.table8) {
+    const uint4* codes = reinterpret_cast<const uint4*>(r.table8);
+    const uint4* pal = reinterpret_cast<const uint4*>(r.palette);
+    for (int i = threadIdx.x; i < 65536 / 16; i += blockDim.x) dst[i] = __ldg(codes + i);
+    for (int i = threadIdx.x; i < 512 / 16; i += blockDim.x) dst[65536 / 16 + i] = __ldg(pal + i);
+  } else {
+    const uint4* src = reinterpret_cast<const uint4*>(r.table);
+    for (int i = threadIdx.x; i < kTableBytes / 16; i += blockDim.x) dst[i] = __ldg(src + i);
+  }
   __syncthreads();
 }
 
@@ -138,6 +152,12 @@ __global__ void k_check_hw(const __grid_constant__ vq_rounder r, int32_t* mism) 
   else o = hw_pair<K_HW_E2M1>(idx2, r.nan_bits);
   const int bad = ((o & 0xFFFFu) != r.table[2 * i]) + ((o >> 16) != r.table[2 * i + 1]);
   if (bad) atomicAdd(mism, bad);
+}
+
+// bf16x2 of two floats, round-to-nearest-even (hardware; NaN -> 0x7FFF)
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
 }
 
 // ---------------------------------------------------------------------------
@@ -272,6 +292,9 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
       }
       if (a.codes == nullptr || !live[u]) continue;
       const Divisor dv = make_divisor(s);
+      // float32 input: a NaN-free block with a normal reciprocal takes the
+      // hardware bf16 rounding and the FMA-pipe tie test below
+      const bool fastq = !BF && dv.fast && m <= 0x7F800000u;
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const uint32_t off = (j * TPB + lane) * VEC;
@@ -300,13 +323,41 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
             *reinterpret_cast<uint2*>(a.packed + base[u] + off) = make_uint2(pb[0], pb[1]);
           }
         } else {
+          bool exact = true;
+          if (fastq) {
+            // quotients x * fl(1/s); the bf16 rounding of q - d and q + d
+            // agrees (d = |q| 2^-21 + 2^-146, computed on the FMA pipe) unless
+            // fl(x / s), which lies within 1.5 * 2^-23 |q| (3 subnormal ulps
+            // below 2^-126) of q, could round to another bf16.  No NaN here
+            // (finite r, NaN-free block), so the hardware rounding gives the
+            // index the table takes.
+            float q[4];
+            uint32_t tie = 0, c[2];
 #pragma unroll
-          for (int k = 0; k < 4; k += 2) {
-            const float q0 = div_to_bf16_domain(u2f(w[k]), dv);
-            const float q1 = div_to_bf16_domain(u2f(w[k + 1]), dv);
-            const uint32_t c2 = round_pair<K>(a.qr, pair_index<K>(q0, q1), smem);
-            w[k] = c2 << 16;
-            w[k + 1] = c2 & 0xFFFF0000u;
+            for (int k = 0; k < 4; ++k) q[k] = __fmul_rn(u2f(w[k]), dv.r);
+#pragma unroll
+            for (int k = 0; k < 4; k += 2) {
+              const float d0 = __fmaf_rn(fabsf(q[k]), 0x1p-21f, 0x1p-146f);
+              const float d1 = __fmaf_rn(fabsf(q[k + 1]), 0x1p-21f, 0x1p-146f);
+              tie |= bf16x2_rn(__fsub_rn(q[k], d0), __fsub_rn(q[k + 1], d1)) ^
+                     bf16x2_rn(__fadd_rn(q[k], d0), __fadd_rn(q[k + 1], d1));
+              c[k / 2] = round_pair<K>(a.qr, bf16x2_rn(q[k], q[k + 1]), smem);
+            }
+            if (!tie) {
+              w[0] = c[0] << 16, w[1] = c[0] & 0xFFFF0000u;
+              w[2] = c[1] << 16, w[3] = c[1] & 0xFFFF0000u;
+              exact = false;
+            }
+          }
+          if (exact) {
+#pragma unroll
+            for (int k = 0; k < 4; k += 2) {
+              const float q0 = div_to_bf16_domain(u2f(w[k]), dv);
+              const float q1 = div_to_bf16_domain(u2f(w[k + 1]), dv);
+              const uint32_t c2 = round_pair<K>(a.qr, pair_index<K>(q0, q1), smem);
+              w[k] = c2 << 16;
+              w[k + 1] = c2 & 0xFFFF0000u;
+            }
           }
         }
         __stcs(reinterpret_cast<uint4*>(reinterpret_cast<TIn*>(a.codes) + base[u] + off),
@@ -339,11 +390,6 @@ __device__ __forceinline__ uint32_t e2m1_bf16(uint32_t nib) {
   const uint32_t e = (nib >> 1) & 3u, f = nib & 1u;
   const uint32_t mag = e == 0 ? (f ? 0x3F00u : 0u) : (((e + 126u) << 7) | (f << 6));
   return mag | ((nib & 8u) << 12);
-}
-
-__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
-  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&b);
 }
 
 __device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
@@ -888,20 +934,54 @@ __global__ void __launch_bounds__(1024) k_rows(const __grid_constant__ RowsArgs 
         uint32_t ob[VEC];
         float of[VEC];
         if (!DEQ) {
-          float t[VEC];
+          bool exact = true;
+          if (!IN_BF && K == VQ_R_TABLE && dv.fast) {
+            // float32 input into a table (the index costs most): quotients
+            // x * fl(1/s), bf16-rounded by the hardware, unless the FMA-pipe
+            // tie test (q -+ |q| 2^-21 + 2^-146 round alike) or a NaN index
+            // (the table wants 0xFFFF for it) sends the vector to the exact path
+            float q[VEC];
+            uint32_t flag = 0, c2v[VEC / 2];
 #pragma unroll
-          for (int j = 0; j < VEC; ++j) {
-            const float xf = IN_BF ? bf2f(*reinterpret_cast<const uint16_t*>(&x[j]))
-                                   : *reinterpret_cast<const float*>(&x[j]);
-            t[j] = div_to_bf16_domain(xf, dv);
+            for (int j = 0; j < VEC; ++j) q[j] = __fmul_rn(*reinterpret_cast<const float*>(&x[j]), dv.r);
+#pragma unroll
+            for (int j = 0; j < VEC; j += 2) {
+              const float d0 = __fmaf_rn(fabsf(q[j]), 0x1p-21f, 0x1p-146f);
+              const float d1 = __fmaf_rn(fabsf(q[j + 1]), 0x1p-21f, 0x1p-146f);
+              const uint32_t idx = bf16x2_rn(q[j], q[j + 1]);
+              flag |= (bf16x2_rn(__fsub_rn(q[j], d0), __fsub_rn(q[j + 1], d1)) ^
+                       bf16x2_rn(__fadd_rn(q[j], d0), __fadd_rn(q[j + 1], d1))) |
+                      (((idx & 0x7FFF7FFFu) + 0x007F007Fu) & 0x80008000u);
+              c2v[j / 2] = round_pair<K>(a.qr, idx, smem);
+            }
+            if (!flag) {
+#pragma unroll
+              for (int j = 0; j < VEC; j += 2) {
+                const uint32_t c2 = c2v[j / 2];
+                ob[j] = c2 & 0xFFFFu;
+                ob[j + 1] = c2 >> 16;
+                of[j] = __uint_as_float(c2 << 16);
+                of[j + 1] = __uint_as_float(c2 & 0xFFFF0000u);
+              }
+              exact = false;
+            }
           }
+          if (exact) {
+            float t[VEC];
 #pragma unroll
-          for (int j = 0; j < VEC; j += 2) {
-            const uint32_t c2 = round_pair<K>(a.qr, pair_index<K>(t[j], t[j + 1]), smem);
-            ob[j] = c2 & 0xFFFFu;
-            ob[j + 1] = c2 >> 16;
-            of[j] = __uint_as_float(c2 << 16);
-            of[j + 1] = __uint_as_float(c2 & 0xFFFF0000u);
+            for (int j = 0; j < VEC; ++j) {
+              const float xf = IN_BF ? bf2f(*reinterpret_cast<const uint16_t*>(&x[j]))
+                                     : *reinterpret_cast<const float*>(&x[j]);
+              t[j] = div_to_bf16_domain(xf, dv);
+            }
+#pragma unroll
+            for (int j = 0; j < VEC; j += 2) {
+              const uint32_t c2 = round_pair<K>(a.qr, pair_index<K>(t[j], t[j + 1]), smem);
+              ob[j] = c2 & 0xFFFFu;
+              ob[j + 1] = c2 >> 16;
+              of[j] = __uint_as_float(c2 << 16);
+              of[j + 1] = __uint_as_float(c2 & 0xFFFF0000u);
+            }
           }
         } else {
 #pragma unroll
@@ -1126,6 +1206,8 @@ int check_rounder(const vq_rounder* r) {
       r->table == nullptr)
     return VQ_ERR_NULL;
   if (r->kind == VQ_R_TABLE && !aligned16(r->table)) return VQ_ERR_ALIGNMENT;
+  if (r->table8 && (!r->palette || !aligned16(r->table8) || !aligned16(r->palette)))
+    return VQ_ERR_ALIGNMENT;
   if (r->kind == VQ_R_STEP && (r->nsteps < 0 || r->nsteps > VQ_STEP_MAX)) return VQ_ERR_INVALID;
   return VQ_OK;
 }
@@ -1223,7 +1305,7 @@ int make_plan(const vq_tensor& x, const DimMap* m0, const DimMap* m1, Plan* p) {
 template <typename TIn, typename TOut, bool DEQ, int K, int VEC>
 int launch_elem(ElemArgs& a, cudaStream_t st) {
   auto kern = k_elem<TIn, TOut, DEQ, K, VEC>;
-  int smem = (!DEQ && K == VQ_R_TABLE) ? kTableBytes : 0;
+  int smem = (!DEQ && K == VQ_R_TABLE) ? table_smem(a.qr) : 0;
   int threads = 256;
   int sms = num_sms();
   int blocks;
@@ -1275,7 +1357,7 @@ template <typename TIn, typename TOut, bool DEQ, int K, int VEC, int SL, bool QM
 int launch_2d(Elem2DArgs& a, cudaStream_t st) {
   constexpr int UNROLL = 2;
   auto kern = k_elem2d<TIn, TOut, DEQ, K, VEC, SL, QM, UNROLL>;
-  const int smem = (!DEQ && K == VQ_R_TABLE) ? kTableBytes : 0;
+  const int smem = (!DEQ && K == VQ_R_TABLE) ? table_smem(a.qr) : 0;
   int threads = 256, sms = num_sms(), blocks;
   if (smem) {
     threads = 1024;
@@ -1352,7 +1434,7 @@ int launch_rows(RowsArgs& a, cudaStream_t st) {
   // the analytic kinds keep eight CTAs per SM and do better without it
   constexpr int U = (!DEQ && K == VQ_R_TABLE) ? 2 : 1;
   auto kern = k_rows<TIn, TOut, DEQ, K, SL, U>;
-  const int smem = (!DEQ && K == VQ_R_TABLE) ? kTableBytes : 0;
+  const int smem = (!DEQ && K == VQ_R_TABLE) ? table_smem(a.qr) : 0;
   const int sms = num_sms();
   int threads, blocks;
   if (smem) {
@@ -1360,7 +1442,9 @@ int launch_rows(RowsArgs& a, cudaStream_t st) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return VQ_ERR_CUDA;
-    blocks = sms;
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+    blocks = sms * std::max(per_sm, 1);
   } else {
     threads = 256;
     blocks = sms * 8;
@@ -1692,7 +1776,7 @@ template <typename TIn, int K, int SK, int TPB, int VPT>
 int launch_qmx(QmxArgs& a, cudaStream_t st) {
   constexpr int UNROLL = 2;
   auto kern = k_qmx_last<TIn, K, SK, TPB, VPT, UNROLL>;
-  int smem = K == VQ_R_TABLE ? kTableBytes : 0;
+  int smem = K == VQ_R_TABLE ? table_smem(a.qr) : 0;
   int threads = 256, sms = num_sms(), blocks;
   if (smem) {
     threads = 1024;  // one resident CTA per SM holds the table

@@ -61,6 +61,8 @@ class VqRounder(ctypes.Structure):
         ("table", ctypes.c_void_p),
         ("hw", ctypes.c_int32),
         ("pad2_", ctypes.c_int32),
+        ("table8", ctypes.c_void_p),
+        ("palette", ctypes.c_void_p),
     ]
 
     def describe(self) -> str:

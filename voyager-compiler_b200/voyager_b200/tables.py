@@ -127,12 +127,14 @@ def table_to_bf16_bits(q: torch.Tensor) -> np.ndarray:
 class Rounder:
     """A classified table: the C struct plus the device table it may read."""
 
-    __slots__ = ("c", "device_table", "host_table", "__weakref__")
+    __slots__ = ("c", "device_table", "host_table", "coded", "__weakref__")
 
-    def __init__(self, c: "_lib.VqRounder", device_table: Optional[torch.Tensor], host_table):
+    def __init__(self, c: "_lib.VqRounder", device_table: Optional[torch.Tensor], host_table,
+                 coded=None):
         self.c = c
         self.device_table = device_table
         self.host_table = host_table
+        self.coded = coded  # (byte codes, palette) on the device, or None
 
     @property
     def kind(self) -> str:
@@ -167,6 +169,26 @@ def _verify_hw(c: "_lib.VqRounder", device) -> None:
         c.hw = 0
 
 
+def _byte_coded(c: "_lib.VqRounder", bits: np.ndarray, device):
+    """For a rounder the kernels evaluate as a table (TABLE, POSIT, STEP)
+    whose entries take at most 256 distinct patterns: byte codes into a
+    palette, on the device (64.5 KB of shared memory instead of 128 KB)."""
+    if c.kind not in (_lib.VQ_R_TABLE, _lib.VQ_R_POSIT, _lib.VQ_R_STEP):
+        return None
+    if torch.device(device).type != "cuda":
+        return None
+    uniq, inv = np.unique(bits, return_inverse=True)
+    if uniq.size > 256:
+        return None
+    pal = np.zeros(256, dtype=np.uint16)
+    pal[: uniq.size] = uniq
+    t8 = torch.from_numpy(inv.astype(np.uint8).reshape(-1)).to(device)
+    p16 = torch.from_numpy(pal.view(np.int16).copy()).to(device)
+    c.table8 = t8.data_ptr()
+    c.palette = p16.data_ptr()
+    return t8, p16
+
+
 def rounder_for(qmap: torch.Tensor, device: torch.device) -> Rounder:
     """The rounder of a 65,536-entry table, with its bf16 device copy on
     ``device``.  Cached per tensor object (and its version counter) and per
@@ -191,7 +213,8 @@ def rounder_for(qmap: torch.Tensor, device: torch.device) -> Rounder:
         c.table = dev.data_ptr()
         if c.hw and torch.device(device).type == "cuda":
             _verify_hw(c, device)
-        rd = Rounder(c, dev, bits)
+        coded = _byte_coded(c, bits, device)
+        rd = Rounder(c, dev, bits, coded)
         with _lock:
             _content_cache[ck] = rd
     return _cache.put(qmap, key, rd)
