@@ -41,8 +41,8 @@ ROWS, COLS = 11008, 4096
 # per-launch DRAM bytes (read + write) of the C2 kernels, from one ncu capture
 # (ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum; recorded with the
 # command in profiles/quantize_c2_weights.md)
-NCU_TRAFFIC = {"int8_channel": int(313.5e6), "nf4_g64": int(310.4e6),
-               "posit8_tensor": int(312.8e6)}
+NCU_TRAFFIC = {"int8_channel": int(311.5e6), "nf4_g64": int(310.4e6),
+               "posit8_tensor": int(308.9e6)}
 BYTES_PER_ELEM = {"nf4_g64": 4 + 4 + 4.0 / 64, "posit8_tensor": 8.0, "int8_channel": 8.0}
 
 

@@ -1779,13 +1779,19 @@ int launch_qmx(QmxArgs& a, cudaStream_t st) {
   int smem = K == VQ_R_TABLE ? table_smem(a.qr) : 0;
   int threads = 256, sms = num_sms(), blocks;
   if (smem) {
-    threads = 1024;  // one resident CTA per SM holds the table
+    // each resident CTA holds the table: the CTA size that keeps the most
+    // threads resident under the shared-memory and register limits
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return VQ_ERR_CUDA;
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
-    blocks = sms * std::max(per_sm, 1);
+    int best = 0, best_per_sm = 1;
+    threads = 1024;
+    for (int t : {1024, 768, 640, 512}) {
+      int per_sm = 0;
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, t, smem);
+      if (per_sm * t > best) best = per_sm * t, best_per_sm = per_sm, threads = t;
+    }
+    blocks = sms * std::max(best_per_sm, 1);
   } else {
     blocks = sms * 8;
   }
