@@ -476,6 +476,17 @@ int vq_slice_csr(const vq_tensor* data, const int32_t* indices, const int32_t* i
                  void* new_data, int32_t* new_indices, int32_t* new_indptr, int32_t* workspace,
                  void* stream);
 
+/* Codebook lookup per region (encode / decode of quantized.py:211-337 with a
+ * codebook [*counts, k]): counts[d] (ncounts == ndim) splits dim d of the
+ * input into equal regions, numbered row-major over the counts;
+ * out[i] = tables[region(i) * 65536 + bf16 pattern of input[i]], the tables
+ * (device, nregions x 65,536 entries) holding the output dtype (bf16 or
+ * float32).  A float32 input is rounded to bf16 for the pattern, as
+ * encode's `input.bfloat16()`; decode's tables map the patterns of the
+ * integers 0..k-1. */
+int vq_codebook_lookup(const vq_tensor* input, const int64_t* counts, int32_t ncounts,
+                       const void* tables, int64_t nregions, vq_tensor* out, void* stream);
+
 /* dst [..., C, R] = src [..., R, C] transposed (2- or 4-byte elements). */
 int vq_transpose(const vq_tensor* src, vq_tensor* dst, void* stream);
 

@@ -81,19 +81,80 @@ def vmap(x: np.ndarray, qmap: np.ndarray) -> np.ndarray:
     return out if d == BF16 else bf16_bits_to_f32(out)
 
 
+def codebook_edges(cb: np.ndarray) -> np.ndarray:
+    """``(codebook[..., :-1] + codebook[..., 1:]) / 2`` in the codebook's
+    dtype (``quantized.py:292-293``): a bfloat16 codebook rounds the sum to
+    bfloat16 (the halving is then exact), a float32 one stays float32."""
+    cb = np.asarray(cb)
+    if cb.dtype == np.uint16:
+        s = f32_to_bf16_bits((to_f32(cb[..., :-1]) + to_f32(cb[..., 1:])).astype(np.float32))
+        return to_f32(f32_to_bf16_bits((to_f32(s) / np.float32(2)).astype(np.float32)))
+    c = cb.astype(np.float32)
+    return ((c[..., :-1] + c[..., 1:]) / np.float32(2)).astype(np.float32)
+
+
+def region_view(x: np.ndarray, counts):
+    """``_region_view`` (``quantized.py:211-248``): the tensor split into
+    ``counts[i]`` regions along each axis, region axes first; returns the
+    view and the permutation that puts the axes back."""
+    counts = tuple(counts)
+    if len(counts) != x.ndim:
+        raise ValueError(
+            f"a {list(counts)} region codebook tiles {len(counts)} axes, "
+            f"but the tensor reaching it has {x.ndim}")
+    if any(e % c for e, c in zip(x.shape, counts)):
+        raise ValueError(
+            f"a {list(counts)} region codebook does not divide the {list(x.shape)} tensor "
+            "reaching it")
+    split = []
+    for e, c in zip(x.shape, counts):
+        split += [c, e // c]
+    order = list(range(0, 2 * len(counts), 2)) + list(range(1, 2 * len(counts), 2))
+    inverse = [0] * len(order)
+    for pos, ax in enumerate(order):
+        inverse[ax] = pos
+    return x.reshape(split).transpose(order), inverse
+
+
 def _encode(x: np.ndarray, codebook: np.ndarray, bounds) -> np.ndarray:
-    """``quantized.py:212-309`` for a 1-D codebook: search the midpoints of
-    the bfloat16-rounded input; return the entry, or the index when
-    ``bounds`` are given."""
+    """``quantized.py:251-309``: search the midpoints of the bfloat16-rounded
+    input; return the entry, or the index when ``bounds`` are given.  A
+    codebook ``[*counts, k]`` holds one table per region of the input."""
     cb = np.asarray(codebook)
     cbf = to_f32(cb) if cb.dtype == np.uint16 else cb.astype(np.float32)
-    if bounds is None:
-        edges = ((cbf[:-1] + cbf[1:]) / np.float32(2)).astype(np.float32)
-    else:
-        edges = to_f32(np.asarray(bounds))
+    edges = codebook_edges(cb) if bounds is None else to_f32(np.asarray(bounds))
     xr = bf16_bits_to_f32(f32_to_bf16_bits(to_f32(x)))
-    index = np.searchsorted(edges, xr, side="left")
-    picked = index.astype(np.float32) if bounds is not None else cbf[index]
+    if cb.ndim == 1:
+        index = np.searchsorted(edges, xr, side="left")
+        picked = index.astype(np.float32) if bounds is not None else cbf[index]
+        return round_to(picked.astype(np.float32), dtype_of(x))
+    moved, inverse = region_view(xr, cb.shape[:-1])
+    regions = cb.size // cb.shape[-1]
+    flat = moved.reshape(regions, -1)
+    table = cbf.reshape(regions, -1)
+    edge = edges.reshape(regions, -1)
+    out = np.empty(flat.shape, dtype=np.float32)
+    for r in range(regions):
+        index = np.searchsorted(edge[r], flat[r], side="left")
+        out[r] = index.astype(np.float32) if bounds is not None else table[r][index]
+    out = out.reshape(moved.shape).transpose(inverse).reshape(np.shape(x))
+    return round_to(out, dtype_of(x))
+
+
+def decode(x: np.ndarray, codebook: np.ndarray) -> np.ndarray:
+    """``quantized.py:312-337``: each stored index read back as its entry
+    (one table per region for a ``[*counts, k]`` codebook), in the input's
+    dtype."""
+    cb = np.asarray(codebook)
+    cbf = to_f32(cb) if cb.dtype == np.uint16 else cb.astype(np.float32)
+    idx = to_f32(x).astype(np.int64)
+    if cb.ndim == 1:
+        return round_to(cbf[idx], dtype_of(x))
+    moved, inverse = region_view(idx, cb.shape[:-1])
+    regions = cb.size // cb.shape[-1]
+    table = cbf.reshape(regions, -1)
+    picked = np.take_along_axis(table, moved.reshape(regions, -1), axis=1)
+    picked = picked.reshape(moved.shape).transpose(inverse).reshape(idx.shape)
     return round_to(picked.astype(np.float32), dtype_of(x))
 
 
@@ -303,10 +364,7 @@ def dequantize_mx(x, scale, code, block_size):
     if code is None and scale is None:
         return x
     if code is not None:
-        cb = np.asarray(code)
-        cbf = to_f32(cb) if cb.dtype == np.uint16 else cb.astype(np.float32)
-        idx = to_f32(x).astype(np.int64)
-        x = round_to(cbf[idx], dtype_of(x))
+        x = decode(x, code)
     if scale is not None:
         x = _binary(x, expand(scale, x.shape, block_size), np.multiply)
     return x

@@ -436,6 +436,39 @@ def main():
     run("matmul_mx_outlier_ck", "matmul_mx", [a_c, to_np(cck)], input_scale=a_s,
         weight_scale=to_np(sck), block_size=32, A_data=a_d, A_indices=a_i, A_indptr=a_p)
 
+    # codebooks: region grids ([*counts, k], one table per region) and the
+    # midpoint rounding of a bfloat16 codebook
+    def levels(shape):
+        v = np.sort(rng.standard_normal(shape).astype(np.float32), axis=-1)
+        return v
+
+    xq = bf(rng.standard_normal((2, 4, 8, 32)))
+    half = np.array(0.5, dtype=np.float32)
+    run("quantize_region_per_head_f32", "quantize", [xq, half], qmap=levels((1, 4, 1, 1, 16)))
+    cbb = bf(levels((1, 4, 1, 1, 16)))
+    cbt = to_t(cbb)
+    bnd = to_np((cbt[..., :-1] + cbt[..., 1:]) / 2)
+    run("quantize_region_per_head_bf16_index", "quantize", [xq, half], qmap=cbb,
+        output_code=bnd)
+    run("quantize_region_per_head_bf16", "quantize", [xq, half], qmap=cbb)
+    xg = rng.standard_normal((8, 64)).astype(np.float32)
+    sg = (np.abs(xg).max(axis=1, keepdims=True) / np.float32(2)).astype(np.float32)
+    run("quantize_region_channel_groups", "quantize", [xg, sg], qmap=levels((1, 4, 8)))
+    tie_cb = bf(np.array([-2.0, -1.0, 0.0, 1.0, 1.0234375, 1.5, 2.0], dtype=np.float32))
+    xt = bf(np.concatenate([np.array([1.015625, 1.0078125, 1.01171875, -1.5, 1.25, 1.2578125],
+                                     dtype=np.float32), rng.standard_normal(58).astype(np.float32)
+                            ]).reshape(8, 8))
+    run("quantize_codebook_bf16_midpoint_tie", "quantize", [xt, np.array(1.0, dtype=np.float32)],
+        qmap=tie_cb)
+    idx_a = bf(rng.integers(0, 16, size=(1, 2, 16, 32)).astype(np.float32))
+    other = bf(rng.standard_normal((1, 2, 32, 16)) * 0.1)
+    run("matmul_mx_region_code", "matmul_mx", [idx_a, other],
+        input_code=bf(levels((1, 2, 1, 1, 16))))
+    idx_w = bf(rng.integers(0, 8, size=(24, 64)).astype(np.float32))
+    xa = bf(rng.standard_normal((16, 64)))
+    run("linear_mx_region_weight_code", "linear_mx", [xa, idx_w],
+        weight_code=levels((4, 1, 8)))
+
     np.savez_compressed(os.path.join(HERE, "ops_small.npz"), **arrays)
     with open(os.path.join(HERE, "ops_small.json"), "w") as f:
         json.dump(cases, f, indent=1)

@@ -180,6 +180,9 @@ _SIGNATURES = {
                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                     ctypes.c_void_p, ctypes.c_void_p]),
     "vq_transpose": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p]),
+    "vq_codebook_lookup": (ctypes.c_int, [P(VqTensor), P(ctypes.c_int64), ctypes.c_int32,
+                                          ctypes.c_void_p, ctypes.c_int64, P(VqTensor),
+                                          ctypes.c_void_p]),
 }
 
 _lib = None

@@ -35,9 +35,13 @@ def dequantize_mx(x: torch.Tensor, scale: Optional[torch.Tensor], code: Optional
     if code is None and scale is None:
         return x
     if code is not None:
-        from voyager_b200.codebook import decode_table
+        from voyager_b200 import codebook as cbm
 
-        x = _ops.vmap(x, decode_table(code, x.dtype, x.device))
+        try:
+            x = _ops.vmap(x, cbm.decode_table(code, x.dtype, x.device))
+        except NotImplementedError:
+            # one table per region, or float32 entries bf16 cannot hold
+            x = cbm.decode(x, code.to(x.device))
     if scale is not None:
         x = _ops.dequantize(x, scale, None, None, block_size)
     return x

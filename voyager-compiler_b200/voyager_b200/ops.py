@@ -117,9 +117,24 @@ def quantize(input: torch.Tensor, scale: torch.Tensor, zero_point=None, axes=Non
     r2 = r1 if z is None else _promote(r1, x.dim(), z.dtype, z.dim())
     if not (qmap.numel() == QMAP_SIZE and qmap.dim() == 1):
         # a codebook: encode() is a function of the bf16 pattern, i.e. a table
-        from voyager_b200.codebook import encode_table
+        from voyager_b200 import codebook as cbm
 
-        qmap = encode_table(qmap, output_code, r2, dev)
+        table = None
+        if qmap.dim() == 1:
+            try:
+                table = cbm.encode_table(qmap, output_code, r2, dev)
+            except NotImplementedError:
+                table = None
+        if table is None:
+            # one table per region (or float32 entries bf16 cannot hold):
+            # the bf16-rounded quotients through the identity table, then
+            # each element through its region's table
+            counts = cbm.region_counts(qmap, x.shape)
+            t = quantize(x, s, z, axes, block_size, _identity(dev))
+            tabs = cbm.encode_tables(qmap, _on(output_code, dev) if output_code is not None
+                                     else None, r2, dev)
+            return cbm.lookup(t, counts, tabs, r2)
+        qmap = table
     out = torch.empty(x.shape, dtype=r2, device=dev)
     rd = rounder_for(qmap, dev)
     st = lib().vq_quantize(_ref(_vt(x)), _ref(_vt(s)), _ref(_vt(z)),
@@ -148,6 +163,17 @@ def dequantize(input: torch.Tensor, scale: torch.Tensor, zero_point=None, axes=N
 
 
 _ONES = {}
+_IDENT = {}
+
+
+def _identity(dev):
+    """The identity table (entry = its bf16 pattern) on ``dev``."""
+    t = _IDENT.get(str(dev))
+    if t is None:
+        t = torch.arange(QMAP_SIZE, dtype=torch.int32).to(torch.int16).view(
+            torch.bfloat16).to(dev)
+        _IDENT[str(dev)] = t
+    return t
 
 
 def _one(dev, dtype):
