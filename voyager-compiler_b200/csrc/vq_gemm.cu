@@ -17,11 +17,12 @@
 //   warp 0  TMA producer: A tile 128x128 B, B tile 256x128 B (SWIZZLE_128B),
 //           scale atoms by bulk copy, 4-stage mbarrier pipeline;
 //   warp 1  TMEM owner and MMA issuer: per K tile, tcgen05.cp of the scale
-//           atoms into TMEM, then 4 x tcgen05.mma.kind::mxf8f6f4.block_scale
-//           (M=128, N=256, K=32) accumulating in TMEM (fp32, 256 columns);
+//           atoms into the stage's own TMEM slot, then 4 x
+//           tcgen05.mma.kind::mxf8f6f4.block_scale (M=128, N=256, K=32)
+//           accumulating in TMEM (fp32, 256 columns);
 //   warps 2-9 epilogue: tcgen05.ld of the accumulator (two warps per lane
 //           quarter, 128 columns each), + bias, round to bf16; the
-//           accumulator is released before the global stores, so the MMA
+//           accumulator is released as soon as the loads land, so the MMA
 //           warp waits only for the TMEM reads.
 // Every wait is bounded; a wait that gives up sets *err and the kernel ends.
 // No TMA multicast is used.
@@ -50,8 +51,12 @@ constexpr int TX_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;  // per stag
 constexpr int STAGE_BYTES = (TX_BYTES + 1023) / 1024 * 1024;  // stages stay 1024-aligned
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;    // 256 fp32 columns
-constexpr int SFA_COL = 256;  // 4 columns
-constexpr int SFB_COL = 260;  // 8 columns
+// Scale factors: one 16-column slot per pipeline stage (A: 4 columns, B: 8),
+// so the copies of the next K tile's scales write columns that the MMAs of
+// the K tiles still in flight do not read.
+constexpr int SF_COL = 256;
+constexpr int SF_SLOT = 16;
+constexpr int SFA_OFF = 0, SFB_OFF = 4;
 constexpr int THREADS = 320;
 
 enum { ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_TIMEOUT_ACC = 3 };
@@ -82,22 +87,56 @@ struct GemmArgs {
   int* err;
 };
 
+// Transpose of 16-byte chunks among the 8 lanes of a group (u = lane % 8):
+// on entry e[base + 4c .. +3] is chunk c (c = 0..7) of this lane's row; on
+// exit it is chunk u of the row of lane c of the group.  Three butterfly
+// stages (lane masks 1, 2, 4); at each, a lane keeps the chunks whose index
+// bit equals its own lane bit and swaps the others with its partner.
+__device__ __forceinline__ void transpose_chunks8(uint32_t (&e)[64], int base, int u) {
+#pragma unroll
+  for (int b = 0; b < 3; ++b) {
+    const int m = 1 << b;
+    const bool hi = (u >> b) & 1;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      if (c & m) continue;
+      const int c1 = c | m;
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const uint32_t send = hi ? e[base + 4 * c + x] : e[base + 4 * c1 + x];
+        const uint32_t recv = __shfl_xor_sync(0xFFFFFFFFu, send, m);
+        if (hi)
+          e[base + 4 * c + x] = recv;
+        else
+          e[base + 4 * c1 + x] = recv;
+      }
+    }
+  }
+}
+
 // One 128-row x 256-column accumulator tile of this CTA's TMEM -> out rows
 // (bias, bf16, optional residual add, optional multicast stores).  Two warps
 // per TMEM lane quarter (q), each on 128 columns (half); the accumulator is
-// read into registers and released (release()) before the global stores.
+// read into registers and released (release()) before any arithmetic.
 template <typename Release>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem, int q, int half,
                                               int lane, int row, int colh, Release release) {
+  // all four TMEM loads, one wait, then the accumulator goes back to the
+  // MMA warp before any arithmetic
+  uint32_t raw[4][32];
+  const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + ACC_COL + half * 128;
+  tmem_ld32(taddr, raw[0]);
+  tmem_ld32(taddr + 32, raw[1]);
+  tmem_ld32(taddr + 64, raw[2]);
+  tmem_ld32(taddr + 96, raw[3]);
+  tmem_ld_wait();
+  tc_fence_before();
+  release();
   uint32_t packed[64];
 #pragma unroll
   for (int c2 = 0; c2 < 2; ++c2) {
-    uint32_t r0[32], r1[32];
-    const uint32_t taddr =
-        tmem + ((uint32_t)(q * 32) << 16) + ACC_COL + half * 128 + c2 * 64;
-    tmem_ld32(taddr, r0);
-    tmem_ld32(taddr + 32, r1);
-    tmem_ld_wait();
+    const uint32_t* r0 = raw[2 * c2];
+    const uint32_t* r1 = raw[2 * c2 + 1];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       float v0 = __uint_as_float(r0[2 * i]), v1 = __uint_as_float(r0[2 * i + 1]);
@@ -114,47 +153,46 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem, 
       packed[c2 * 32 + 16 + i] = *reinterpret_cast<uint32_t*>(&b1);
     }
   }
-  tc_fence_before();
-  release();
-  if (row < g.M && colh < g.N) {
-    uint16_t* orow = g.out + (int64_t)row * g.ldo;
-    if (g.residual) {
-      // out = bf16(bf16(acc) + residual): the residual add that follows
-      // the linear in the graph, one rounding per op
-      const uint4* rrow = reinterpret_cast<const uint4*>(g.residual + (int64_t)row * g.ldr + colh);
+  // Stores: each lane holds 128 columns of its own row, so a direct store
+  // instruction would touch 32 rows 16 bytes each.  Within each group of 8
+  // lanes (8 consecutive rows) the 16-byte chunks of a 64-column segment are
+  // transposed with shuffles: lane u then holds chunk u of the group's 8
+  // rows, and one store instruction writes 4 rows x 128 contiguous bytes.
+  // The residual is read the same way.  Every lane takes part in the
+  // shuffles; rows past M and columns past N are skipped at the stores.
+  const int u = lane & 7;
+  const int row0 = row - u;  // this lane group's first row
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        if (colh + 8 * i >= g.N) break;
-        const uint4 rv = rrow[i];
+  for (int s = 0; s < 2; ++s) {
+    transpose_chunks8(packed, s * 32, u);
+    const int col = colh + 64 * s + 8 * u;  // N is a multiple of 8: whole chunks
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = row0 + k;
+      if (r >= g.M || col >= g.N) continue;
+      uint32_t* w = packed + s * 32 + 4 * k;
+      if (g.residual) {
+        // out = bf16(bf16(acc) + residual): the residual add that follows
+        // the linear in the graph, one rounding per op
+        const uint4 rv = *reinterpret_cast<const uint4*>(g.residual + (int64_t)r * g.ldr + col);
         const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t pw = packed[4 * i + k];
+        for (int x = 0; x < 4; ++x) {
           __nv_bfloat162 b = __floats2bfloat162_rn(
-              __uint_as_float(pw << 16) + __uint_as_float(rw[k] << 16),
-              __uint_as_float(pw & 0xFFFF0000u) + __uint_as_float(rw[k] & 0xFFFF0000u));
-          packed[4 * i + k] = *reinterpret_cast<uint32_t*>(&b);
+              __uint_as_float(w[x] << 16) + __uint_as_float(rw[x] << 16),
+              __uint_as_float(w[x] & 0xFFFF0000u) + __uint_as_float(rw[x] & 0xFFFF0000u));
+          w[x] = *reinterpret_cast<uint32_t*>(&b);
         }
       }
-    }
-    // N is a multiple of 8: whole 16-byte groups up to the last column
-    uint4* dst = reinterpret_cast<uint4*>(orow + colh);
-    if (g.out_mc) {
-      // one store reaches every rank's copy of the output
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (colh + 8 * i < g.N)
-          asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
-                           dst + i),
-                       "f"(__uint_as_float(packed[4 * i])), "f"(__uint_as_float(packed[4 * i + 1])),
-                       "f"(__uint_as_float(packed[4 * i + 2])),
-                       "f"(__uint_as_float(packed[4 * i + 3]))
-                       : "memory");
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (colh + 8 * i < g.N)
-          dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+      uint4* dst = reinterpret_cast<uint4*>(g.out + (int64_t)r * g.ldo + col);
+      if (g.out_mc)
+        // one store reaches every rank's copy of the output
+        asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst),
+                     "f"(__uint_as_float(w[0])), "f"(__uint_as_float(w[1])),
+                     "f"(__uint_as_float(w[2])), "f"(__uint_as_float(w[3]))
+                     : "memory");
+      else
+        *dst = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 }
@@ -244,11 +282,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t sa = sbase, sb = sbase + A_BYTES;
           const uint32_t ssfa = sbase + A_BYTES + B_BYTES, ssfb = ssfa + SFA_BYTES;
           // scale atoms -> TMEM (ordered before the MMAs that read them)
-          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem + SFA_COL),
+          const uint32_t sfc = tmem + SF_COL + stage * SF_SLOT;
+          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + SFA_OFF),
                        "l"(sf_desc(ssfa)));
-          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem + SFB_COL),
+          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + SFB_OFF),
                        "l"(sf_desc(ssfb)));
-          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem + SFB_COL + 4),
+          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + SFB_OFF + 4),
                        "l"(sf_desc(ssfb + 512)));
 #pragma unroll
           for (uint32_t j = 0; j < 4; ++j) {
@@ -259,8 +298,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
                 "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], "
                 "p;\n\t}" ::"r"(tmem + ACC_COL),
-                "l"(da), "l"(db), "r"(idesc_mxf8(j)), "r"(accum), "r"(tmem + SFA_COL + (j << 30)),
-                "r"(tmem + SFB_COL + (j << 30)));
+                "l"(da), "l"(db), "r"(idesc_mxf8(j)), "r"(accum), "r"(sfc + SFA_OFF + (j << 30)),
+                "r"(sfc + SFB_OFF + (j << 30)));
           }
           // frees the stage once these MMAs (and copies) have read it
           asm volatile(
@@ -321,6 +360,8 @@ constexpr int P_TX = P_A_BYTES + P_B_BYTES + SFA_BYTES + SFB_BYTES;  // per CTA 
 constexpr int P_STAGE_BYTES = (P_TX + 1023) / 1024 * 1024;
 constexpr int P_BARS = P_STAGES * P_STAGE_BYTES;
 constexpr int P_SMEM = P_BARS + 256;
+static_assert(SF_COL + STAGES * SF_SLOT <= TMEM_COLS && SF_COL + P_STAGES * SF_SLOT <= TMEM_COLS,
+              "scale-factor slots exceed the TMEM allocation");
 
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm_mxf8_pair(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
@@ -408,17 +449,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sbase = smem_u32(smem + stage * P_STAGE_BYTES);
-          const uint32_t sa = sbase, sb = sbase + P_A_BYTES;
-          const uint32_t ssfa = sbase + P_A_BYTES + P_B_BYTES, ssfb = ssfa + SFA_BYTES;
-          cp_sf_pair(tmem + SFA_COL, ssfa);
-          cp_sf_pair(tmem + SFB_COL, ssfb);
-          cp_sf_pair(tmem + SFB_COL + 4, ssfb + 512);
+          const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES), sb = sa + P_A_BYTES;
+          const uint32_t ssfa = sb + P_B_BYTES, ssfb = ssfa + SFA_BYTES;
+          const uint32_t sfc = tmem + SF_COL + stage * SF_SLOT;
+          cp_sf_pair(sfc + SFA_OFF, ssfa);
+          cp_sf_pair(sfc + SFB_OFF, ssfb);
+          cp_sf_pair(sfc + SFB_OFF + 4, ssfb + 512);
 #pragma unroll
           for (uint32_t j = 0; j < 4; ++j)
             mma_mxf8_pair(tmem + ACC_COL, sw128_desc(sa + j * 32), sw128_desc(sb + j * 32), ids[j],
-                          (kt > 0 || j > 0) ? 1u : 0u, tmem + SFA_COL + (j << 30),
-                          tmem + SFB_COL + (j << 30));
+                          (kt > 0 || j > 0) ? 1u : 0u, sfc + SFA_OFF + (j << 30),
+                          sfc + SFB_OFF + (j << 30));
           tc_commit_pair(empty0 + 8 * stage, 0x3);  // frees the stage in both CTAs
           if (++stage == P_STAGES) {
             stage = 0;
