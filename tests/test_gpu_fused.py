@@ -131,3 +131,50 @@ def test_fused_decoder_matches_unfused():
     a = Decoder(cfg, w, fused=True)(x)
     b = Decoder(cfg, w, fused=False)(x)
     assert rel_l2(a, b) < 1e-2, rel_l2(a, b)
+
+
+def test_rope_vt_rmsnorm_special_values():
+    """Values that leave the conversions' common case: zeros, -0, a quotient
+    that rounds to a bf16 zero (a tiny value beside a large one in the same
+    block of 32), infinities and NaN.  Codes and scales stay bit-exact."""
+    from voyager_b200 import fused
+    from voyager_b200.decoder import apply_rope, rms_norm, rope_tables
+
+    B, S, H = 1, 128, 2
+    hl = H * 128
+    g = torch.Generator(device="cuda").manual_seed(5)
+    qkv = torch.randn((B * S, 3 * hl), generator=g, device="cuda").bfloat16()
+    special = torch.tensor([0.0, -0.0, 3e4, -1e-38, 1e-38, -2.0, float("inf"), float("nan")])
+    qkv[0, :8] = special.bfloat16()           # q of token 0, head 0
+    qkv[1, hl + 64:hl + 70] = special[:6].bfloat16()  # k of token 1
+    qkv[:8, 2 * hl + 5] = special.bfloat16()  # v: one dim over 8 tokens
+    qkv[32:64, 2 * hl + 9] = 0.0              # v: a whole block of zeros
+    qkv[64, 2 * hl + 11] = -0.0
+    qkv[65, 2 * hl + 11] = 5e4                # v: a tiny quotient beside a large value
+    qkv[66, 2 * hl + 11] = -1e-30
+    cos, sin = rope_tables(S, 128, 10000.0, "cuda", torch.bfloat16)
+    (sq, cq), (sk, ck) = fused.rope_quantize_qk(qkv, 0, hl, cos, sin, B, S, H, _table())
+    sv, cv = fused.quantize_vt(qkv, 2 * hl, B, S, H, _table())
+    q, k, v = (t.reshape(B, S, H, 128).transpose(1, 2) for t in qkv.split(hl, -1))
+
+    def same_or_nan(a, b):
+        nan = torch.isnan(a.float()) & torch.isnan(b.float())
+        return torch.equal(a.view(torch.int16)[~nan], b.view(torch.int16)[~nan])
+
+    for (s, c), ref in (((sq, cq), apply_rope(q, cos, sin)), ((sk, ck), apply_rope(k, cos, sin)),
+                        ((sv, cv), v.transpose(-1, -2))):
+        ws, wc = _qmx(ref)
+        assert _same(s, ws) and same_or_nan(c, wc)
+    # RMSNorm: zero and -0 entries, a tiny value beside a large one
+    x = torch.randn((4, 256), generator=g, device="cuda").bfloat16()
+    x[0, :32] = 0.0
+    x[1, 0], x[1, 1], x[1, 2] = -0.0, 3e4, -1e-30
+    w = torch.ones(256, device="cuda").bfloat16()
+    s, c = fused.rmsnorm_quantize_mx(x, w, 1e-5, _table())
+    ws, wc = _qmx(rms_norm(x, w, 1e-5))
+    # the row statistic is summed in the kernel's own order (an ulp of rsqrt
+    # may move a code elsewhere); the planted entries and the zero block's
+    # scale must match exactly
+    assert _same(c[0, :32], wc[0, :32]) and _same(s[0, :1], ws[0, :1])
+    assert _same(c[1, :3], wc[1, :3]) and _same(s[1, :1], ws[1, :1])
+    assert (c.view(torch.int16) != wc.view(torch.int16)).float().mean().item() < 1e-2

@@ -55,26 +55,66 @@ __device__ __forceinline__ uint32_t e4m3_bytes(uint32_t codes2) {
   return b;
 }
 
+// E4M3 of a pair of bf16 quotients idx2 (lo | hi << 16) by the saturating
+// round-to-nearest conversion: returns the two E4M3 bytes (lo byte = lo
+// element) and sets code2 to their values as bf16 (every E4M3 value is a
+// bf16).  This is the table rounding wherever neither quotient is -0 or NaN
+// (hw_pair's two special cases), which the callers establish first.
+__device__ __forceinline__ uint32_t e4m3_pair(uint32_t idx2, uint32_t& code2) {
+  uint32_t b, h2;
+  asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e4m3x2.f32 t, %2, %3;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, t;\n\tcvt.u32.u16 %0, t;\n\t}"
+      : "=r"(b), "=r"(h2)
+      : "f"(hi_f(idx2)), "f"(lo_f(idx2)));
+  code2 = pack_rn(__half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu))),
+                  __half2float(__ushort_as_half((unsigned short)(h2 >> 16))));
+  return b;
+}
+
+// Whether the quotients x * inv of a lane's values (smallest magnitude mn,
+// largest mx, as bf16 magnitude bits) avoid hw_pair's special cases: the
+// scale is a normal power of two (the quotient is the product with its exact
+// reciprocal), no value is NaN or zero, and no quotient is small enough to
+// round to a bf16 zero (|q| <= 2^-134), so no quotient index is -0 or NaN.
+__device__ __forceinline__ bool plain_quotients(uint32_t E, float inv, uint32_t mn, uint32_t mx) {
+  return E >= 1u && E <= 253u && mx <= 0x7F80u && mn != 0u &&
+         __uint_as_float(mn << 16) * inv > 0x1p-134f;
+}
+
 // MXFP8 quantization of 8 consecutive bf16 values (4 packed pairs) held by
 // each of 4 consecutive lanes (lane % 4 = 0..3, all four active) that
 // together cover one block of 32.  Returns
 // the block's scale (bf16 bits); codes as bf16 pairs and E4M3 bytes.
 __device__ __forceinline__ uint32_t mx8_quant8(const uint32_t (&v)[4], int fl2q, uint32_t nan_bits,
                                                uint32_t (&codes)[4], uint32_t (&bytes)[2]) {
-  uint32_t m = __vmaxu2(__vmaxu2(v[0] & 0x7FFF7FFFu, v[1] & 0x7FFF7FFFu),
-                        __vmaxu2(v[2] & 0x7FFF7FFFu, v[3] & 0x7FFF7FFFu));
+  const uint32_t a0 = v[0] & 0x7FFF7FFFu, a1 = v[1] & 0x7FFF7FFFu, a2 = v[2] & 0x7FFF7FFFu,
+                 a3 = v[3] & 0x7FFF7FFFu;
+  uint32_t m = __vmaxu2(__vmaxu2(a0, a1), __vmaxu2(a2, a3));
+  uint32_t mn = __vminu2(__vminu2(a0, a1), __vminu2(a2, a3));
   m = max(m & 0xFFFFu, m >> 16);
+  mn = min(mn & 0xFFFFu, mn >> 16);
+  const uint32_t lane_max = m;
   const unsigned quad = 0xFu << ((threadIdx.x & 31) & 28);  // the block's 4 lanes
   m = max(m, __shfl_xor_sync(quad, m, 1));
   m = max(m, __shfl_xor_sync(quad, m, 2));
   const uint32_t sbits = pow2_scale_bf16(m, fl2q);
+  const uint32_t E = (sbits >> 7) & 0xFFu;
+  const float inv = __uint_as_float((254u - E) << 23);
+  uint32_t b16[4];
+  if (plain_quotients(E, inv, mn, lane_max)) {
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float q0 = div_pow2(lo_f(v[k]), sbits), q1 = div_pow2(hi_f(v[k]), sbits);
-    codes[k] = hw_pair<K_HW_E4M3>(pair_index<K_HW_E4M3>(q0, q1), nan_bits);
+    for (int k = 0; k < 4; ++k)
+      b16[k] = e4m3_pair(pack_rn(lo_f(v[k]) * inv, hi_f(v[k]) * inv), codes[k]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float q0 = div_pow2(lo_f(v[k]), sbits), q1 = div_pow2(hi_f(v[k]), sbits);
+      codes[k] = hw_pair<K_HW_E4M3>(pair_index<K_HW_E4M3>(q0, q1), nan_bits);
+      b16[k] = e4m3_bytes(codes[k]);
+    }
   }
-  bytes[0] = e4m3_bytes(codes[0]) | (e4m3_bytes(codes[1]) << 16);
-  bytes[1] = e4m3_bytes(codes[2]) | (e4m3_bytes(codes[3]) << 16);
+  bytes[0] = b16[0] | (b16[1] << 16);
+  bytes[1] = b16[2] | (b16[3] << 16);
   return sbits;
 }
 
@@ -129,7 +169,7 @@ struct RmsArgs {
 };
 
 // One warp per row: sum of squares, then the normalised row quantized.
-__global__ void __launch_bounds__(256) k_rms_qmx(const __grid_constant__ RmsArgs a) {
+__global__ void __launch_bounds__(256, 6) k_rms_qmx(const __grid_constant__ RmsArgs a) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= a.R) return;
@@ -180,14 +220,15 @@ struct RopeArgs {
 // 16 lanes per (token, head) row of 128: lane j holds dims 8j..8j+7; the
 // rotate-half partner is lane j ^ 8.
 __global__ void __launch_bounds__(256) k_rope_qmx(const __grid_constant__ RopeArgs a) {
-  const int64_t gid = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  const int64_t rows = (int64_t)a.B * a.S * a.H;
-  const int64_t row = gid >> 4;  // token-major: (b, s, h)
+  // rows < 2^27 (checked by the host): 32-bit index arithmetic
+  const uint32_t gid = blockIdx.x * 256u + threadIdx.x;
+  const uint32_t rows = (uint32_t)a.B * a.S * a.H;
+  const uint32_t row = gid >> 4;  // token-major: (b, s, h)
   const int j = (int)(gid & 15);
   if (row >= rows) return;  // whole 16-lane groups leave together
-  const int h = (int)(row % a.H);
-  const int64_t t = row / a.H;  // b * S + s
-  const int s = (int)(t % a.S), b = (int)(t / a.S);
+  const int h = (int)(row % (uint32_t)a.H);
+  const uint32_t t = row / (uint32_t)a.H;  // b * S + s
+  const int s = (int)(t % (uint32_t)a.S), b = (int)(t / (uint32_t)a.S);
   const int d0 = j * 8;
   const uint4 cu = *reinterpret_cast<const uint4*>(a.cos + (int64_t)s * 128 + d0);
   const uint4 su = *reinterpret_cast<const uint4*>(a.sin + (int64_t)s * 128 + d0);
@@ -227,37 +268,60 @@ struct VtArgs {
 
 // One thread per (b, h, block of 32 tokens, pair of dims): the 32 x 2
 // values, a scale per dim, codes written along the tokens.
-__global__ void __launch_bounds__(256) k_vt_qmx(const __grid_constant__ VtArgs a) {
-  const int64_t gid = (int64_t)blockIdx.x * 256 + threadIdx.x;
-  const int nsb = a.S / 32;
-  const int64_t total = (int64_t)a.B * a.H * nsb * 64;
+__global__ void __launch_bounds__(256, 3) k_vt_qmx(const __grid_constant__ VtArgs a) {
+  // total < 2^31 (checked by the host): 32-bit index arithmetic
+  const uint32_t gid = blockIdx.x * 256u + threadIdx.x;
+  const uint32_t nsb = (uint32_t)a.S / 32;
+  const uint32_t total = (uint32_t)a.B * a.H * nsb * 64;
   if (gid >= total) return;
   const int dp = (int)(gid & 63);          // dims 2dp, 2dp + 1
-  const int64_t r = gid >> 6;
-  const int h = (int)(r % a.H);
-  const int64_t r2 = r / a.H;
+  const uint32_t r = gid >> 6;
+  const int h = (int)(r % (uint32_t)a.H);
+  const uint32_t r2 = r / (uint32_t)a.H;
   const int sb = (int)(r2 % nsb), b = (int)(r2 / nsb);
   const uint16_t* src = a.qkv + ((int64_t)b * a.S + sb * 32) * a.ld + a.v_off + h * 128 + 2 * dp;
   uint32_t w[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) w[i] = *reinterpret_cast<const uint32_t*>(src + i * a.ld);
+  // magnitudes of both dims at once: lo half = dim 2dp, hi half = 2dp + 1
+  uint32_t mx2 = 0, mn2 = 0xFFFFFFFFu;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    mx2 = __vmaxu2(mx2, w[i] & 0x7FFF7FFFu);
+    mn2 = __vminu2(mn2, w[i] & 0x7FFF7FFFu);
+  }
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
-    uint32_t m = 0;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) m = max(m, (half ? (w[i] >> 16) : w[i]) & 0x7FFFu);
+    const uint32_t m = half ? mx2 >> 16 : mx2 & 0xFFFFu;
+    const uint32_t mn = half ? mn2 >> 16 : mn2 & 0xFFFFu;
     const uint32_t sbits = pow2_scale_bf16(m, a.fl2q);
+    const uint32_t E = (sbits >> 7) & 0xFFu;
+    const float inv = __uint_as_float((254u - E) << 23);
     uint32_t codes[16], bytes[8];
+    if (plain_quotients(E, inv, mn, m)) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint32_t e0 = half ? (w[2 * i] >> 16) : (w[2 * i] & 0xFFFFu);
-      const uint32_t e1 = half ? (w[2 * i + 1] >> 16) : (w[2 * i + 1] & 0xFFFFu);
-      const float q0 = div_pow2(bf2f(e0), sbits), q1 = div_pow2(bf2f(e1), sbits);
-      codes[i] = hw_pair<K_HW_E4M3>(pair_index<K_HW_E4M3>(q0, q1), a.nan_bits);
+      for (int i = 0; i < 8; ++i) {
+        uint32_t b[2];
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const uint32_t e0 = half ? (w[4 * i + 2 * x] >> 16) : (w[4 * i + 2 * x] & 0xFFFFu);
+          const uint32_t e1 = half ? (w[4 * i + 2 * x + 1] >> 16) : (w[4 * i + 2 * x + 1] & 0xFFFFu);
+          b[x] = e4m3_pair(pack_rn(bf2f(e0) * inv, bf2f(e1) * inv), codes[2 * i + x]);
+        }
+        bytes[i] = b[0] | (b[1] << 16);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t e0 = half ? (w[2 * i] >> 16) : (w[2 * i] & 0xFFFFu);
+        const uint32_t e1 = half ? (w[2 * i + 1] >> 16) : (w[2 * i + 1] & 0xFFFFu);
+        const float q0 = div_pow2(bf2f(e0), sbits), q1 = div_pow2(bf2f(e1), sbits);
+        codes[i] = hw_pair<K_HW_E4M3>(pair_index<K_HW_E4M3>(q0, q1), a.nan_bits);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        bytes[i] = e4m3_bytes(codes[2 * i]) | (e4m3_bytes(codes[2 * i + 1]) << 16);
     }
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      bytes[i] = e4m3_bytes(codes[2 * i]) | (e4m3_bytes(codes[2 * i + 1]) << 16);
     const int64_t row = ((int64_t)b * a.H + h) * 128 + 2 * dp + half;
     uint4* dc = reinterpret_cast<uint4*>(a.o.codes + row * a.o.C + sb * 32);
 #pragma unroll
@@ -284,12 +348,20 @@ struct SwigluArgs {
 
 // One thread per 8 outputs; a row's padding columns by the threads of its
 // last 32-column group.
-__global__ void __launch_bounds__(256) k_swiglu_qmx(const __grid_constant__ SwigluArgs a) {
+__global__ void __launch_bounds__(256, 8) k_swiglu_qmx(const __grid_constant__ SwigluArgs a) {
   const int64_t gid = (int64_t)blockIdx.x * 256 + threadIdx.x;
   const int per_row = a.o.C / 8;
   if (gid >= a.R * per_row) return;  // per_row % 4 == 0: blocks stay whole
-  const int64_t row = gid / per_row;
-  const int c = (int)(gid % per_row) * 8;
+  int64_t row;
+  int c;
+  if (a.R * per_row <= 0xFFFFFFFFll) {  // 32-bit division where it suffices
+    const uint32_t g32 = (uint32_t)gid;
+    row = g32 / (uint32_t)per_row;
+    c = (int)(g32 - (uint32_t)row * (uint32_t)per_row) * 8;
+  } else {
+    row = gid / per_row;
+    c = (int)(gid % per_row) * 8;
+  }
   const uint4 gu4 = *reinterpret_cast<const uint4*>(a.gu + row * a.ld + c);
   const uint4 uu4 = *reinterpret_cast<const uint4*>(a.gu + row * a.ld + a.up_off + c);
   const uint32_t g[4] = {gu4.x, gu4.y, gu4.z, gu4.w}, u[4] = {uu4.x, uu4.y, uu4.z, uu4.w};

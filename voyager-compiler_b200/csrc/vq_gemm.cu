@@ -87,33 +87,6 @@ struct GemmArgs {
   int* err;
 };
 
-// Transpose of 16-byte chunks among the 8 lanes of a group (u = lane % 8):
-// on entry e[base + 4c .. +3] is chunk c (c = 0..7) of this lane's row; on
-// exit it is chunk u of the row of lane c of the group.  Three butterfly
-// stages (lane masks 1, 2, 4); at each, a lane keeps the chunks whose index
-// bit equals its own lane bit and swaps the others with its partner.
-__device__ __forceinline__ void transpose_chunks8(uint32_t (&e)[64], int base, int u) {
-#pragma unroll
-  for (int b = 0; b < 3; ++b) {
-    const int m = 1 << b;
-    const bool hi = (u >> b) & 1;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      if (c & m) continue;
-      const int c1 = c | m;
-#pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        const uint32_t send = hi ? e[base + 4 * c + x] : e[base + 4 * c1 + x];
-        const uint32_t recv = __shfl_xor_sync(0xFFFFFFFFu, send, m);
-        if (hi)
-          e[base + 4 * c + x] = recv;
-        else
-          e[base + 4 * c1 + x] = recv;
-      }
-    }
-  }
-}
-
 // One 128-row x 256-column accumulator tile of this CTA's TMEM -> out rows
 // (bias, bf16, optional residual add, optional multicast stores).  Two warps
 // per TMEM lane quarter (q), each on 128 columns (half); the accumulator is
@@ -153,46 +126,45 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem, 
       packed[c2 * 32 + 16 + i] = *reinterpret_cast<uint32_t*>(&b1);
     }
   }
-  // Stores: each lane holds 128 columns of its own row, so a direct store
-  // instruction would touch 32 rows 16 bytes each.  Within each group of 8
-  // lanes (8 consecutive rows) the 16-byte chunks of a 64-column segment are
-  // transposed with shuffles: lane u then holds chunk u of the group's 8
-  // rows, and one store instruction writes 4 rows x 128 contiguous bytes.
-  // The residual is read the same way.  Every lane takes part in the
-  // shuffles; rows past M and columns past N are skipped at the stores.
-  const int u = lane & 7;
-  const int row0 = row - u;  // this lane group's first row
+  if (row < g.M && colh < g.N) {
+    uint16_t* orow = g.out + (int64_t)row * g.ldo;
+    if (g.residual) {
+      // out = bf16(bf16(acc) + residual): the residual add that follows
+      // the linear in the graph, one rounding per op
+      const uint4* rrow = reinterpret_cast<const uint4*>(g.residual + (int64_t)row * g.ldr + colh);
 #pragma unroll
-  for (int s = 0; s < 2; ++s) {
-    transpose_chunks8(packed, s * 32, u);
-    const int col = colh + 64 * s + 8 * u;  // N is a multiple of 8: whole chunks
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int r = row0 + k;
-      if (r >= g.M || col >= g.N) continue;
-      uint32_t* w = packed + s * 32 + 4 * k;
-      if (g.residual) {
-        // out = bf16(bf16(acc) + residual): the residual add that follows
-        // the linear in the graph, one rounding per op
-        const uint4 rv = *reinterpret_cast<const uint4*>(g.residual + (int64_t)r * g.ldr + col);
+      for (int i = 0; i < 16; ++i) {
+        if (colh + 8 * i >= g.N) break;
+        const uint4 rv = rrow[i];
         const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
-        for (int x = 0; x < 4; ++x) {
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t pw = packed[4 * i + k];
           __nv_bfloat162 b = __floats2bfloat162_rn(
-              __uint_as_float(w[x] << 16) + __uint_as_float(rw[x] << 16),
-              __uint_as_float(w[x] & 0xFFFF0000u) + __uint_as_float(rw[x] & 0xFFFF0000u));
-          w[x] = *reinterpret_cast<uint32_t*>(&b);
+              __uint_as_float(pw << 16) + __uint_as_float(rw[k] << 16),
+              __uint_as_float(pw & 0xFFFF0000u) + __uint_as_float(rw[k] & 0xFFFF0000u));
+          packed[4 * i + k] = *reinterpret_cast<uint32_t*>(&b);
         }
       }
-      uint4* dst = reinterpret_cast<uint4*>(g.out + (int64_t)r * g.ldo + col);
-      if (g.out_mc)
-        // one store reaches every rank's copy of the output
-        asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst),
-                     "f"(__uint_as_float(w[0])), "f"(__uint_as_float(w[1])),
-                     "f"(__uint_as_float(w[2])), "f"(__uint_as_float(w[3]))
-                     : "memory");
-      else
-        *dst = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    // N is a multiple of 8: whole 16-byte groups up to the last column
+    uint4* dst = reinterpret_cast<uint4*>(orow + colh);
+    if (g.out_mc) {
+      // one store reaches every rank's copy of the output
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (colh + 8 * i < g.N)
+          asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                           dst + i),
+                       "f"(__uint_as_float(packed[4 * i])), "f"(__uint_as_float(packed[4 * i + 1])),
+                       "f"(__uint_as_float(packed[4 * i + 2])),
+                       "f"(__uint_as_float(packed[4 * i + 3]))
+                       : "memory");
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (colh + 8 * i < g.N)
+          dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
     }
   }
 }
