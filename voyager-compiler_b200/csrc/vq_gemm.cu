@@ -239,6 +239,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       int stage = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
+      // the descriptors of stage 0; a stage's are these moved by its offset
+      const uint32_t s0 = smem_u32(smem);
+      const uint64_t dA0 = sw128_desc(s0), dB0 = sw128_desc(s0 + A_BYTES);
+      const uint64_t dS0 = sf_desc(s0 + A_BYTES + B_BYTES);
       for (int t = blockIdx.x; t < g.ntiles && ok; t += gridDim.x) {
         // the epilogue has drained the accumulator of the previous tile
         if (!mbar_wait(acc_empty, acc_phase ^ 1, g.err, ERR_TIMEOUT_ACC)) break;
@@ -250,21 +254,19 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sbase = smem_u32(smem + stage * STAGE_BYTES);
-          const uint32_t sa = sbase, sb = sbase + A_BYTES;
-          const uint32_t ssfa = sbase + A_BYTES + B_BYTES, ssfb = ssfa + SFA_BYTES;
+          const uint32_t soff = stage * (STAGE_BYTES / 16);
           // scale atoms -> TMEM (ordered before the MMAs that read them)
           const uint32_t sfc = tmem + SF_COL + stage * SF_SLOT;
           asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + SFA_OFF),
-                       "l"(sf_desc(ssfa)));
+                       "l"(desc_at(dS0, soff)));
           asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + SFB_OFF),
-                       "l"(sf_desc(ssfb)));
+                       "l"(desc_at(dS0, soff + SFA_BYTES / 16)));
           asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + SFB_OFF + 4),
-                       "l"(sf_desc(ssfb + 512)));
+                       "l"(desc_at(dS0, soff + (SFA_BYTES + 512) / 16)));
 #pragma unroll
           for (uint32_t j = 0; j < 4; ++j) {
-            const uint64_t da = sw128_desc(sa + j * 32);
-            const uint64_t db = sw128_desc(sb + j * 32);
+            const uint64_t da = desc_at(dA0, soff + 2 * j);
+            const uint64_t db = desc_at(dB0, soff + 2 * j);
             const uint32_t accum = (kt > 0 || j > 0) ? 1u : 0u;
             asm volatile(
                 "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -332,6 +334,8 @@ constexpr int P_TX = P_A_BYTES + P_B_BYTES + SFA_BYTES + SFB_BYTES;  // per CTA 
 constexpr int P_STAGE_BYTES = (P_TX + 1023) / 1024 * 1024;
 constexpr int P_BARS = P_STAGES * P_STAGE_BYTES;
 constexpr int P_SMEM = P_BARS + 256;
+static_assert(P_SMEM + 1024 <= (1 << 18) && SmemLayout::kTotal + 1024 <= (1 << 18),
+              "descriptor offsets assume shared addresses below 2^18");
 static_assert(SF_COL + STAGES * SF_SLOT <= TMEM_COLS && SF_COL + P_STAGES * SF_SLOT <= TMEM_COLS,
               "scale-factor slots exceed the TMEM allocation");
 
@@ -355,7 +359,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(empty0 + 8 * s, 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 2 * 256);
+    mbar_init(acc_empty, 2 * 8);  // one arrival per epilogue warp of both CTAs
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -377,23 +381,29 @@ __global__ void __launch_bounds__(THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      const uint32_t s0 = smem_u32(smem);
+      const uint32_t fb0 = mapa_shared(full0, 0);  // the even CTA's barriers
       for (int t = pair_id; t < g.ntiles && ok; t += npairs) {
         const int tm = t / g.NTILE_N, tn = t % g.NTILE_N;  // 256-row, 256-column tile
+        const int ya = tm * 256 + (int)rank * 128, yb = tn * 256 + (int)rank * 128;
+        // scale-atom rows of K tile kt: (kt * MT + 2 tm + rank) * 2 and
+        // (kt * NT128 + 2 tn) * 2, stepped by 2 MT / 2 NT128 per K tile
+        int ysa = (2 * tm + (int)rank) * 2, ysb = (2 * tn) * 2;
         for (int kt = 0; kt < g.KT; ++kt) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, g.err, ERR_TIMEOUT_EMPTY)) {
             ok = false;
             break;
           }
-          const uint32_t sbase = smem_u32(smem + stage * P_STAGE_BYTES);
-          const uint32_t fb = mapa_shared(full0 + 8 * stage, 0);  // the even CTA's barrier
+          const uint32_t sbase = s0 + stage * P_STAGE_BYTES;
+          const uint32_t fb = fb0 + 8 * stage;
           if (rank == 0) mbar_expect_tx(full0 + 8 * stage, 2 * P_TX);
-          tma_load_2d_pair(sbase, &tma_a, kt * BK, tm * 256 + (int)rank * 128, fb);
-          tma_load_2d_pair(sbase + P_A_BYTES, &tma_b, kt * BK, tn * 256 + (int)rank * 128, fb);
+          tma_load_2d_pair(sbase, &tma_a, kt * BK, ya, fb);
+          tma_load_2d_pair(sbase + P_A_BYTES, &tma_b, kt * BK, yb, fb);
           // scale atoms: this CTA's 128 A rows, both 128-row chunks of B
-          tma_load_2d_pair(sbase + P_A_BYTES + P_B_BYTES, &tma_sfa, 0,
-                           (kt * g.MT + tm * 2 + (int)rank) * 2, fb);
-          tma_load_2d_pair(sbase + P_A_BYTES + P_B_BYTES + SFA_BYTES, &tma_sfb, 0,
-                           (kt * g.NT128 + 2 * tn) * 2, fb);
+          tma_load_2d_pair(sbase + P_A_BYTES + P_B_BYTES, &tma_sfa, 0, ysa, fb);
+          tma_load_2d_pair(sbase + P_A_BYTES + P_B_BYTES + SFA_BYTES, &tma_sfb, 0, ysb, fb);
+          ysa += 2 * g.MT;
+          ysb += 2 * g.NT128;
           if (++stage == P_STAGES) {
             stage = 0;
             phase ^= 1;
@@ -410,6 +420,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t id0 = tc::idesc_mxf8(0, 256, 256), id1 = tc::idesc_mxf8(1, 256, 256),
                      id2 = tc::idesc_mxf8(2, 256, 256), id3 = tc::idesc_mxf8(3, 256, 256);
       const uint32_t ids[4] = {id0, id1, id2, id3};
+      // the descriptors of stage 0; a stage's are these moved by its offset
+      // (one add per operand instead of rebuilding each descriptor)
+      const uint32_t s0 = smem_u32(smem);
+      const uint64_t dA0 = sw128_desc(s0), dB0 = sw128_desc(s0 + P_A_BYTES);
+      const uint64_t dS0 = sf_desc(s0 + P_A_BYTES + P_B_BYTES);
+      uint32_t soff = 0;                 // stage * P_STAGE_BYTES / 16
+      uint32_t sfc = tmem + SF_COL;      // the stage's scale-factor slot
       for (int t = pair_id; t < g.ntiles && ok; t += npairs) {
         // both CTAs' epilogues have drained the accumulator of the last tile
         if (!mbar_wait(acc_empty, acc_phase ^ 1, g.err, ERR_TIMEOUT_ACC)) break;
@@ -421,21 +438,25 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES), sb = sa + P_A_BYTES;
-          const uint32_t ssfa = sb + P_B_BYTES, ssfb = ssfa + SFA_BYTES;
-          const uint32_t sfc = tmem + SF_COL + stage * SF_SLOT;
-          cp_sf_pair(sfc + SFA_OFF, ssfa);
-          cp_sf_pair(sfc + SFB_OFF, ssfb);
-          cp_sf_pair(sfc + SFB_OFF + 4, ssfb + 512);
+          cp_sf_pair_desc(sfc + SFA_OFF, desc_at(dS0, soff));
+          cp_sf_pair_desc(sfc + SFB_OFF, desc_at(dS0, soff + SFA_BYTES / 16));
+          cp_sf_pair_desc(sfc + SFB_OFF + 4, desc_at(dS0, soff + (SFA_BYTES + 512) / 16));
+          mma_mxf8_pair(tmem + ACC_COL, desc_at(dA0, soff), desc_at(dB0, soff), ids[0],
+                        kt > 0 ? 1u : 0u, sfc + SFA_OFF, sfc + SFB_OFF);
 #pragma unroll
-          for (uint32_t j = 0; j < 4; ++j)
-            mma_mxf8_pair(tmem + ACC_COL, sw128_desc(sa + j * 32), sw128_desc(sb + j * 32), ids[j],
-                          (kt > 0 || j > 0) ? 1u : 0u, sfc + SFA_OFF + (j << 30),
-                          sfc + SFB_OFF + (j << 30));
+          for (uint32_t j = 1; j < 4; ++j)
+            mma_mxf8_pair_acc(tmem + ACC_COL, desc_at(dA0, soff + 2 * j),
+                              desc_at(dB0, soff + 2 * j), ids[j], sfc + SFA_OFF + (j << 30),
+                              sfc + SFB_OFF + (j << 30));
           tc_commit_pair(empty0 + 8 * stage, 0x3);  // frees the stage in both CTAs
           if (++stage == P_STAGES) {
             stage = 0;
             phase ^= 1;
+            soff = 0;
+            sfc = tmem + SF_COL;
+          } else {
+            soff += P_STAGE_BYTES / 16;
+            sfc += SF_SLOT;
           }
         }
         if (!ok) break;
@@ -456,8 +477,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int row = tm * 256 + (int)rank * 128 + row_in_tile;
       const int colh = tn * BN + half * 128;
-      epilogue_tile(g, tmem, q, half, lane, row, colh,
-                    [&] { mbar_arrive_cluster(acc_empty0); });
+      epilogue_tile(g, tmem, q, half, lane, row, colh, [&] {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc_empty0);
+      });
     }
   }
   __syncthreads();

@@ -197,10 +197,29 @@ __device__ __forceinline__ void mma_mxf8_pair(uint32_t d_tmem, uint64_t da, uint
       "p;\n\t}" ::"r"(d_tmem),
       "l"(da), "l"(db), "r"(idesc), "r"(accum), "r"(sfa_tmem), "r"(sfb_tmem));
 }
+// The same, accumulating (D += A . B^T).
+__device__ __forceinline__ void mma_mxf8_pair_acc(uint32_t d_tmem, uint64_t da, uint64_t db,
+                                                  uint32_t idesc, uint32_t sfa_tmem,
+                                                  uint32_t sfb_tmem) {
+  asm volatile(
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], 1;" ::"r"(
+          d_tmem),
+      "l"(da), "l"(db), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem));
+}
 // Scale atoms of both CTAs (same shared offset) into their own TMEM.
 __device__ __forceinline__ void cp_sf_pair(uint32_t tmem_col, uint32_t saddr) {
   asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col),
                "l"(sf_desc(saddr)));
+}
+// Scale atoms of both CTAs into their own TMEM, from a prepared descriptor.
+__device__ __forceinline__ void cp_sf_pair_desc(uint32_t tmem_col, uint64_t desc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col), "l"(desc));
+}
+// A shared-memory descriptor moved by off16 x 16 bytes: the start address
+// field is the low 14 bits (address / 16); for shared addresses below 2^18
+// the sum stays inside the field, so only the low word changes.
+__device__ __forceinline__ uint64_t desc_at(uint64_t d0, uint32_t off16) {
+  return (d0 & 0xFFFFFFFF00000000ull) | (uint32_t)((uint32_t)d0 + off16);
 }
 // Arrive on the mbarrier at this offset in the CTAs of `mask` once the pair's
 // tcgen05 operations issued so far have completed.
