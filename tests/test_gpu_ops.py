@@ -297,3 +297,44 @@ def test_hardware_rounders_verified():
     for name, hw in (("fp8_e4m3", 1), ("fp8_e5m2", 2), ("fp4_e2m1", 3)):
         rd = rounder_for(to_dev(G.tables()[name]), torch.device("cuda", 0))
         assert rd.c.hw == hw, (name, rd.c.describe())
+
+
+@pytest.mark.parametrize("bs", [32, 64])
+def test_quantize_mx_e4m3_special_values(bs):
+    """MXFP8 (E4M3 table, power-of-two scales) on blocks that leave the
+    conversions' common case: zeros and -0, a quotient that rounds to a bf16
+    zero (a tiny value beside a large one), a whole zero block, NaN and
+    infinities, next to ordinary blocks.  Codes and scales bit-exact against
+    the oracle; the GEMM operand written in the same pass equals
+    vq_mx_pack's packing of the returned codes wherever the scale has a
+    UE8M0 form."""
+    from voyager_b200 import mxgemm
+    from voyager_b200.synth import f32_to_bf16_bits
+
+    rng = np.random.Generator(np.random.PCG64(77))
+    x = rng.standard_normal((8, 256)).astype(np.float32)
+    x[0, :4] = [0.0, -0.0, 3.0, -1.0]
+    x[1, :3] = [3e4, -1e-35, 1e-35]
+    x[2, :bs] = 0.0
+    x[3, 5] = -0.0
+    x[4, 7] = np.nan
+    x[5, 9] = np.inf
+    x[6, :bs] = -1e-36
+    x[6, 1] = 2e3
+    x[7, :3] = [3e4, -1e-40, 1e-40]  # quotients of 2^-139: a bf16 -0 and +0
+    xb = f32_to_bf16_bits(x)
+    qm = quantization_map("fp8_e4m3")
+    ws, wc = oracle.quantize_mx(xb, qm, [-1], bs, 448.0, True)
+    xs = to_dev(xb)
+    gs, gc = Q.quantize_mx(xs, to_dev(qm), [-1], bs, 448.0, True)
+    assert len(G.bit_mismatches(to_np(gs), ws)) == 0
+    assert len(G.bit_mismatches(to_np(gc), wc)) == 0
+    if bs == 32:
+        entry = mxgemm._vouched_entry(gc, gs)
+        if entry is not None and entry[1] is not None:
+            pc, ps = entry[1]
+            ok_rows = [r for r in range(8) if r not in (4, 5)]  # NaN / inf scales: no UE8M0
+            rc, rs, _ = mxgemm._pack(gc.contiguous(), gs.contiguous(), 128, False)
+            got = pc.view(-1, 256)[ok_rows]
+            want = rc.view(-1, 256)[ok_rows]
+            assert torch.equal(got, want)

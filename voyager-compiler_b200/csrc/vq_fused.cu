@@ -55,32 +55,6 @@ __device__ __forceinline__ uint32_t e4m3_bytes(uint32_t codes2) {
   return b;
 }
 
-// E4M3 of a pair of bf16 quotients idx2 (lo | hi << 16) by the saturating
-// round-to-nearest conversion: returns the two E4M3 bytes (lo byte = lo
-// element) and sets code2 to their values as bf16 (every E4M3 value is a
-// bf16).  This is the table rounding wherever neither quotient is -0 or NaN
-// (hw_pair's two special cases), which the callers establish first.
-__device__ __forceinline__ uint32_t e4m3_pair(uint32_t idx2, uint32_t& code2) {
-  uint32_t b, h2;
-  asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e4m3x2.f32 t, %2, %3;\n\t"
-      "cvt.rn.f16x2.e4m3x2 %1, t;\n\tcvt.u32.u16 %0, t;\n\t}"
-      : "=r"(b), "=r"(h2)
-      : "f"(hi_f(idx2)), "f"(lo_f(idx2)));
-  code2 = pack_rn(__half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu))),
-                  __half2float(__ushort_as_half((unsigned short)(h2 >> 16))));
-  return b;
-}
-
-// Whether the quotients x * inv of a lane's values (smallest magnitude mn,
-// largest mx, as bf16 magnitude bits) avoid hw_pair's special cases: the
-// scale is a normal power of two (the quotient is the product with its exact
-// reciprocal), no value is NaN or zero, and no quotient is small enough to
-// round to a bf16 zero (|q| <= 2^-134), so no quotient index is -0 or NaN.
-__device__ __forceinline__ bool plain_quotients(uint32_t E, float inv, uint32_t mn, uint32_t mx) {
-  return E >= 1u && E <= 253u && mx <= 0x7F80u && mn != 0u &&
-         __uint_as_float(mn << 16) * inv > 0x1p-134f;
-}
-
 // MXFP8 quantization of 8 consecutive bf16 values (4 packed pairs) held by
 // each of 4 consecutive lanes (lane % 4 = 0..3, all four active) that
 // together cover one block of 32.  Returns

@@ -55,4 +55,34 @@ __device__ __forceinline__ uint32_t pair_index(float q0, float q1) {
   return *reinterpret_cast<uint32_t*>(&b);
 }
 
+// E4M3 of a pair of bf16 quotients idx2 (lo | hi << 16) by the saturating
+// round-to-nearest conversion: returns the two E4M3 bytes (lo byte = lo
+// element) and sets code2 to their values as bf16 (every E4M3 value is a
+// bf16).  This is hw_pair<K_HW_E4M3>'s result wherever neither quotient
+// index is -0 or NaN (its two special cases), which callers establish first
+// (plain_quotients).
+__device__ __forceinline__ uint32_t e4m3_pair(uint32_t idx2, uint32_t& code2) {
+  uint32_t b, h2;
+  asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e4m3x2.f32 t, %2, %3;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, t;\n\tcvt.u32.u16 %0, t;\n\t}"
+      : "=r"(b), "=r"(h2)
+      : "f"(__uint_as_float(idx2 & 0xFFFF0000u)), "f"(__uint_as_float(idx2 << 16)));
+  __nv_bfloat162 c = __floats2bfloat162_rn(
+      __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu))),
+      __half2float(__ushort_as_half((unsigned short)(h2 >> 16))));
+  code2 = *reinterpret_cast<uint32_t*>(&c);
+  return b;
+}
+
+// Whether the quotients x * inv of a group of bf16 values (smallest
+// magnitude mn, largest mx, as bf16 magnitude bits) avoid hw_pair's special
+// cases: the power-of-two scale has exponent field E in [1, 253] (inv =
+// 2^(127 - E) is exact and every quotient is the product), no value is NaN
+// or zero, and no quotient is small enough to round to a bf16 zero
+// (|q| <= 2^-134), so no quotient index is -0 or NaN.
+__device__ __forceinline__ bool plain_quotients(uint32_t E, float inv, uint32_t mn, uint32_t mx) {
+  return E >= 1u && E <= 253u && mx <= 0x7F80u && mn != 0u &&
+         __uint_as_float(mn << 16) * inv > 0x1p-134f;
+}
+
 }  // namespace vq

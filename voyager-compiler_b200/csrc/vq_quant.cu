@@ -252,18 +252,25 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
       // block amax on the magnitude bits: non-negative IEEE patterns order
       // like integers and every NaN sorts above +inf, so this max propagates
       // NaN exactly like torch.amax.
-      uint32_t m = 0;
+      uint32_t m = 0, mn = 0xFFFFu;  // mn: this lane's smallest bf16 magnitude
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         if (BF) {
-          uint32_t w = __vmaxu2(__vmaxu2(v[u][j].x & 0x7FFF7FFFu, v[u][j].y & 0x7FFF7FFFu),
-                                __vmaxu2(v[u][j].z & 0x7FFF7FFFu, v[u][j].w & 0x7FFF7FFFu));
+          const uint32_t a0 = v[u][j].x & 0x7FFF7FFFu, a1 = v[u][j].y & 0x7FFF7FFFu,
+                         a2 = v[u][j].z & 0x7FFF7FFFu, a3 = v[u][j].w & 0x7FFF7FFFu;
+          const uint32_t w = __vmaxu2(__vmaxu2(a0, a1), __vmaxu2(a2, a3));
           m = max(m, max(w & 0xFFFFu, w >> 16));
+          if (K == K_HW_E4M3 && SK == 0) {
+            // columns past C hold zeros and send the lane down the exact path
+            const uint32_t z = __vminu2(__vminu2(a0, a1), __vminu2(a2, a3));
+            mn = min(mn, min(z & 0xFFFFu, z >> 16));
+          }
         } else {
           m = max(m, max(max(v[u][j].x & 0x7FFFFFFFu, v[u][j].y & 0x7FFFFFFFu),
                          max(v[u][j].z & 0x7FFFFFFFu, v[u][j].w & 0x7FFFFFFFu)));
         }
       }
+      const uint32_t lane_max = m;
 #pragma unroll
       for (int o = TPB / 2; o >= 1; o >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, o, TPB));
       // block scale
@@ -295,12 +302,28 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
       // float32 input: a NaN-free block with a normal reciprocal takes the
       // hardware bf16 rounding and the FMA-pipe tie test below
       const bool fastq = !BF && dv.fast && m <= 0x7F800000u;
+      // bf16 input, E4M3 hardware rounder, power-of-two scale: the quotients
+      // are the exact products x * (1 / s), and where none is -0 or NaN the
+      // codes and bytes come from one conversion per pair
+      const bool e4m3_plain = BF && K == K_HW_E4M3 && SK == 0 && a.pow2 && dv.fast &&
+                              plain_quotients((sbits >> 7) & 0xFFu, dv.r, mn, lane_max);
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const uint32_t off = (j * TPB + lane) * VEC;
         if (cb[u] + off >= a.C) continue;
         uint32_t w[4] = {v[u][j].x, v[u][j].y, v[u][j].z, v[u][j].w};
-        if (BF) {
+        if (BF && K == K_HW_E4M3 && e4m3_plain) {
+          // one saturating conversion per pair gives both the code and its
+          // GEMM byte (plain_quotients rules out hw_pair's special cases)
+          uint32_t b16[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            b16[k] = e4m3_pair(bf16x2_rn(bf2f(w[k] & 0xFFFFu) * dv.r, bf2f(w[k] >> 16) * dv.r),
+                               w[k]);
+          if (a.packed)
+            *reinterpret_cast<uint2*>(a.packed + base[u] + off) =
+                make_uint2(b16[0] | (b16[1] << 16), b16[2] | (b16[3] << 16));
+        } else if (BF) {
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const float q0 = div_to_bf16_domain(bf2f(w[k] & 0xFFFFu), dv);
