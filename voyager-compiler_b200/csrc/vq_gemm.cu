@@ -334,12 +334,15 @@ constexpr int P_TX = P_A_BYTES + P_B_BYTES + SFA_BYTES + SFB_BYTES;  // per CTA 
 constexpr int P_STAGE_BYTES = (P_TX + 1023) / 1024 * 1024;
 constexpr int P_BARS = P_STAGES * P_STAGE_BYTES;
 constexpr int P_SMEM = P_BARS + 256;
+constexpr int P_THREADS = THREADS + 32;  // + warp 10: the scale-copy issuer
+// barrier words: full, empty, sf_full per stage, acc_full, acc_empty, TMEM slot
+static_assert((3 * P_STAGES + 3) * 8 <= P_SMEM - P_BARS, "pair barriers exceed their area");
 static_assert(P_SMEM + 1024 <= (1 << 18) && SmemLayout::kTotal + 1024 <= (1 << 18),
               "descriptor offsets assume shared addresses below 2^18");
 static_assert(SF_COL + STAGES * SF_SLOT <= TMEM_COLS && SF_COL + P_STAGES * SF_SLOT <= TMEM_COLS,
               "scale-factor slots exceed the TMEM allocation");
 
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(P_THREADS, 1)
     k_gemm_mxf8_pair(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_sfa,
                      const __grid_constant__ CUtensorMap tma_sfb, const __grid_constant__ GemmArgs g) {
@@ -350,6 +353,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + P_STAGES);
   const uint32_t acc_full = smem_u32(bars + 2 * P_STAGES), acc_empty = smem_u32(bars + 2 * P_STAGES + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * P_STAGES + 2);
+  // per stage: the stage's scale atoms are in TMEM (even CTA)
+  const uint32_t sf_full0 = smem_u32(bars + 2 * P_STAGES + 3);
   const uint32_t rank = cluster_ctarank();  // 0: issues the pair's MMAs
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int pair_id = blockIdx.x / 2, npairs = gridDim.x / 2;
@@ -357,6 +362,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int s = 0; s < P_STAGES; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
+      mbar_init(sf_full0 + 8 * s, 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 2 * 8);  // one arrival per epilogue warp of both CTAs
@@ -424,7 +430,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       // (one add per operand instead of rebuilding each descriptor)
       const uint32_t s0 = smem_u32(smem);
       const uint64_t dA0 = sw128_desc(s0), dB0 = sw128_desc(s0 + P_A_BYTES);
-      const uint64_t dS0 = sf_desc(s0 + P_A_BYTES + P_B_BYTES);
       uint32_t soff = 0;                 // stage * P_STAGE_BYTES / 16
       uint32_t sfc = tmem + SF_COL;      // the stage's scale-factor slot
       for (int t = pair_id; t < g.ntiles && ok; t += npairs) {
@@ -433,14 +438,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         acc_phase ^= 1;
         tc_fence_after();
         for (int kt = 0; kt < g.KT; ++kt) {
-          if (!mbar_wait(full0 + 8 * stage, phase, g.err, ERR_TIMEOUT_FULL)) {
+          // the stage's operands landed and warp 10 copied its scales
+          if (!mbar_wait(sf_full0 + 8 * stage, phase, g.err, ERR_TIMEOUT_FULL)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          cp_sf_pair_desc(sfc + SFA_OFF, desc_at(dS0, soff));
-          cp_sf_pair_desc(sfc + SFB_OFF, desc_at(dS0, soff + SFA_BYTES / 16));
-          cp_sf_pair_desc(sfc + SFB_OFF + 4, desc_at(dS0, soff + (SFA_BYTES + 512) / 16));
           mma_mxf8_pair(tmem + ACC_COL, desc_at(dA0, soff), desc_at(dB0, soff), ids[0],
                         kt > 0 ? 1u : 0u, sfc + SFA_OFF, sfc + SFB_OFF);
 #pragma unroll
@@ -461,6 +464,41 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (!ok) break;
         tc_commit_pair(acc_full, 0x3);
+      }
+    }
+  } else if (warp == 10) {
+    // ---------------- scale-copy issuer (even CTA) ----------------
+    // Per stage: once its operands land, the pair's scale atoms go into the
+    // stage's TMEM slot and sf_full[stage] fires when the copies complete.
+    // The slot was last read by the MMAs of this stage's previous round,
+    // which completed before the stage was refilled (its "full" phase).
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      const uint64_t dS0 = sf_desc(smem_u32(smem) + P_A_BYTES + P_B_BYTES);
+      uint32_t soff = 0, sfc = tmem + SF_COL;
+      for (int t = pair_id; t < g.ntiles && ok; t += npairs) {
+        for (int kt = 0; kt < g.KT; ++kt) {
+          if (!mbar_wait(full0 + 8 * stage, phase, g.err, ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          cp_sf_pair_desc(sfc + SFA_OFF, desc_at(dS0, soff));
+          cp_sf_pair_desc(sfc + SFB_OFF, desc_at(dS0, soff + SFA_BYTES / 16));
+          cp_sf_pair_desc(sfc + SFB_OFF + 4, desc_at(dS0, soff + (SFA_BYTES + 512) / 16));
+          tc_commit_pair(sf_full0 + 8 * stage, 0x1);  // the even CTA's barrier
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+            soff = 0;
+            sfc = tmem + SF_COL;
+          } else {
+            soff += P_STAGE_BYTES / 16;
+            sfc += SF_SLOT;
+          }
+        }
       }
     }
   } else {
@@ -773,7 +811,7 @@ int vq_gemm_mxf8_ex(const void* a, const void* a_sf, const void* b, const void* 
     const int pairs = (int)std::min<int64_t>(gp.ntiles, sm_count() / 2);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.blockDim = dim3(P_THREADS, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
