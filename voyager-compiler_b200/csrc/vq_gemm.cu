@@ -13,11 +13,14 @@
 // + j for row r and K block j (0..3) of the tile; atoms ordered
 // [k_tile][row_chunk].
 //
-// Kernel: persistent, one CTA (6 warps) per SM.
+// Kernel: persistent, one CTA (11 warps) per SM.
 //   warp 0  TMA producer: A tile 128x128 B, B tile 256x128 B (SWIZZLE_128B),
 //           scale atoms by bulk copy, 4-stage mbarrier pipeline;
-//   warp 1  TMEM owner and MMA issuer: per K tile, tcgen05.cp of the scale
-//           atoms into the stage's own TMEM slot, then 4 x
+//   warp 10 scale-copy issuer: per K tile, once the stage lands, tcgen05.cp
+//           of its scale atoms into the stage's own TMEM slot, committed to
+//           the stage's sf_full barrier (issued apart from the MMAs, the
+//           copies overlap them in the tensor pipe);
+//   warp 1  TMEM owner and MMA issuer: per K tile, after sf_full, 4 x
 //           tcgen05.mma.kind::mxf8f6f4.block_scale (M=128, N=256, K=32)
 //           accumulating in TMEM (fp32, 256 columns);
 //   warps 2-9 epilogue: tcgen05.ld of the accumulator (two warps per lane
@@ -169,7 +172,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem, 
   }
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS + 32, 1)
     k_gemm_mxf8(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                 const __grid_constant__ GemmArgs g) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -177,16 +180,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::kBars);
-  // bars[0..S) full, [S..2S) empty, [2S] acc_full, [2S+1] acc_empty, [2S+2] tmem slot
+  // bars[0..S) full, [S..2S) empty, [2S] acc_full, [2S+1] acc_empty, [2S+2] tmem slot,
+  // [2S+3..3S+3) sf_full (the stage's scale atoms are in TMEM)
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
   const uint32_t acc_full = smem_u32(bars + 2 * STAGES), acc_empty = smem_u32(bars + 2 * STAGES + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2);
+  const uint32_t sf_full0 = smem_u32(bars + 2 * STAGES + 3);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
+      mbar_init(sf_full0 + 8 * s, 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 256);
@@ -242,27 +248,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       // the descriptors of stage 0; a stage's are these moved by its offset
       const uint32_t s0 = smem_u32(smem);
       const uint64_t dA0 = sw128_desc(s0), dB0 = sw128_desc(s0 + A_BYTES);
-      const uint64_t dS0 = sf_desc(s0 + A_BYTES + B_BYTES);
       for (int t = blockIdx.x; t < g.ntiles && ok; t += gridDim.x) {
         // the epilogue has drained the accumulator of the previous tile
         if (!mbar_wait(acc_empty, acc_phase ^ 1, g.err, ERR_TIMEOUT_ACC)) break;
         acc_phase ^= 1;
         tc_fence_after();
         for (int kt = 0; kt < g.KT; ++kt) {
-          if (!mbar_wait(full0 + 8 * stage, phase, g.err, ERR_TIMEOUT_FULL)) {
+          // the stage's operands landed and warp 10 copied its scales
+          if (!mbar_wait(sf_full0 + 8 * stage, phase, g.err, ERR_TIMEOUT_FULL)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t soff = stage * (STAGE_BYTES / 16);
-          // scale atoms -> TMEM (ordered before the MMAs that read them)
           const uint32_t sfc = tmem + SF_COL + stage * SF_SLOT;
-          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + SFA_OFF),
-                       "l"(desc_at(dS0, soff)));
-          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + SFB_OFF),
-                       "l"(desc_at(dS0, soff + SFA_BYTES / 16)));
-          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + SFB_OFF + 4),
-                       "l"(desc_at(dS0, soff + (SFA_BYTES + 512) / 16)));
 #pragma unroll
           for (uint32_t j = 0; j < 4; ++j) {
             const uint64_t da = desc_at(dA0, soff + 2 * j);
@@ -290,6 +289,44 @@ __global__ void __launch_bounds__(THREADS, 1)
             "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                 acc_full)
             : "memory");
+      }
+    }
+  } else if (warp == 10) {
+    // ---------------- scale-copy issuer ----------------
+    // Per stage: once its operands land, the scale atoms go into the stage's
+    // TMEM slot and sf_full[stage] fires when the copies complete (from a
+    // thread of their own they overlap the MMAs).  The slot was last read by
+    // the MMAs of this stage's previous round, which completed before the
+    // stage was refilled.
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      const uint64_t dS0 = sf_desc(smem_u32(smem) + A_BYTES + B_BYTES);
+      for (int t = blockIdx.x; t < g.ntiles && ok; t += gridDim.x) {
+        for (int kt = 0; kt < g.KT; ++kt) {
+          if (!mbar_wait(full0 + 8 * stage, phase, g.err, ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t soff = stage * (STAGE_BYTES / 16);
+          const uint32_t sfc = tmem + SF_COL + stage * SF_SLOT;
+          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + SFA_OFF),
+                       "l"(desc_at(dS0, soff)));
+          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + SFB_OFF),
+                       "l"(desc_at(dS0, soff + SFA_BYTES / 16)));
+          asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + SFB_OFF + 4),
+                       "l"(desc_at(dS0, soff + (SFA_BYTES + 512) / 16)));
+          asm volatile(
+              "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                  sf_full0 + 8 * stage)
+              : "memory");
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
       }
     }
   } else {
@@ -325,9 +362,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 // tile -- 33.5 KB per stage instead of 49.5 KB, so 6 stages fit -- plus the
 // full B scale atoms (each CTA's TMEM needs all 256 columns' scales).  Both
 // CTAs' TMA loads count on the even CTA's "full" barrier; the even CTA's
-// single MMA thread issues the pair's copies and MMAs and releases stages
-// and accumulators in both CTAs with multicast commits; both epilogues
-// release the accumulator on the even CTA's barrier.  No TMA multicast.
+// single MMA thread issues the pair's MMAs (its warp 10 the pair's scale
+// copies) and releases stages and accumulators in both CTAs with multicast
+// commits; both epilogues release the accumulator on the even CTA's
+// barrier.  No TMA multicast.
 constexpr int P_STAGES = 6;
 constexpr int P_A_BYTES = 128 * BK, P_B_BYTES = 128 * BK;  // this CTA's halves
 constexpr int P_TX = P_A_BYTES + P_B_BYTES + SFA_BYTES + SFB_BYTES;  // per CTA and stage
@@ -337,6 +375,8 @@ constexpr int P_SMEM = P_BARS + 256;
 constexpr int P_THREADS = THREADS + 32;  // + warp 10: the scale-copy issuer
 // barrier words: full, empty, sf_full per stage, acc_full, acc_empty, TMEM slot
 static_assert((3 * P_STAGES + 3) * 8 <= P_SMEM - P_BARS, "pair barriers exceed their area");
+static_assert((3 * STAGES + 3) * 8 <= SmemLayout::kTotal - SmemLayout::kBars,
+              "barriers exceed their area");
 static_assert(P_SMEM + 1024 <= (1 << 18) && SmemLayout::kTotal + 1024 <= (1 << 18),
               "descriptor offsets assume shared addresses below 2^18");
 static_assert(SF_COL + STAGES * SF_SLOT <= TMEM_COLS && SF_COL + P_STAGES * SF_SLOT <= TMEM_COLS,
@@ -830,7 +870,7 @@ int vq_gemm_mxf8_ex(const void* a, const void* a_sf, const void* b, const void* 
       cudaSuccess)
     return VQ_ERR_CUDA;
   const int grid = (int)std::min<int64_t>(g.ntiles, sm_count());
-  k_gemm_mxf8<<<grid, THREADS, smem, st>>>(ma, mb, g);
+  k_gemm_mxf8<<<grid, THREADS + 32, smem, st>>>(ma, mb, g);
   return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
 }
 
