@@ -206,12 +206,8 @@ __device__ __forceinline__ void mma_mxf8_pair_acc(uint32_t d_tmem, uint64_t da, 
           d_tmem),
       "l"(da), "l"(db), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem));
 }
-// Scale atoms of both CTAs (same shared offset) into their own TMEM.
-__device__ __forceinline__ void cp_sf_pair(uint32_t tmem_col, uint32_t saddr) {
-  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col),
-               "l"(sf_desc(saddr)));
-}
-// Scale atoms of both CTAs into their own TMEM, from a prepared descriptor.
+// Scale atoms of both CTAs (same shared offset) into their own TMEM, from a
+// prepared descriptor (sf_desc).
 __device__ __forceinline__ void cp_sf_pair_desc(uint32_t tmem_col, uint64_t desc) {
   asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col), "l"(desc));
 }
