@@ -2,7 +2,10 @@
 
 Run in the build container, where the reference checkout is readable:
 
-    python tests/golden/make_golden.py [--reference-src DIR]
+    python tests/golden/make_golden.py --reference-src DIR
+
+DIR is the reference checkout's ``src`` directory (or set
+``VOYAGER_REFERENCE_SRC``).
 
 It imports ``voyager_compiler.ops`` and ``get_quantization_map`` from the
 reference source tree with three shims (the reference's top-level package
@@ -127,9 +130,12 @@ def edge_values_bf16(rng, n):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-src", default="/root/reference/src")
+    ap.add_argument("--reference-src", default=os.environ.get("VOYAGER_REFERENCE_SRC"),
+                    help="the reference checkout's src directory")
     ap.add_argument("--skip-full", action="store_true")
     args = ap.parse_args()
+    if not args.reference_src:
+        ap.error("give --reference-src (or set VOYAGER_REFERENCE_SRC)")
     torch.set_num_threads(os.cpu_count())
     gqm = load_reference(args.reference_src)
     Q = torch.ops.quantized_ops
