@@ -141,3 +141,30 @@ def test_mx_rejects_bad_arguments():
     # empty input: nothing to launch
     assert lib.vq_calculate_mx_qparam(B(_t([0, 32])), axes, 1, 16, 6.0, 0, 0, None,
                                       B(_t([0, 2])), None) == 0
+
+
+def test_table_kinds_fit_the_byte_coded_form():
+    """The kinds the kernels evaluate from shared memory (TABLE, POSIT,
+    STEP) are staged as byte codes into a 256-entry palette when the table
+    has at most 256 distinct patterns: every such reference table does but
+    posit16_1 (7,168 patterns), which keeps the 128 KB bf16 form.  The
+    palette gathers back to the table exactly."""
+    lib = _lib.load()
+    staged = (_lib.VQ_R_TABLE, _lib.VQ_R_POSIT, _lib.VQ_R_STEP)
+    wide = []
+    for name, t in G.tables().items():
+        if name == "lut4_index":
+            continue
+        t = np.ascontiguousarray(t)
+        r = _lib.VqRounder()
+        assert lib.vq_rounder_from_table(t.ctypes.data, ctypes.byref(r)) == 0
+        if r.kind not in staged:
+            continue
+        uniq, inv = np.unique(t, return_inverse=True)
+        if uniq.size > 256:
+            wide.append(name)
+            continue
+        pal = np.zeros(256, dtype=np.uint16)
+        pal[:uniq.size] = uniq
+        assert np.array_equal(pal[inv.astype(np.uint8).reshape(-1)], t), name
+    assert wide == ["posit16_1"], wide
