@@ -136,3 +136,19 @@ def test_values_outside_the_formats_are_refused():
     p = packed.pack_mxfp8(c, s)
     cc, ss = packed.unpack(p)
     assert np.array_equal(cc, c) and np.array_equal(ss, s)
+
+
+def test_to_device_checks_the_operand_role():
+    """The GEMM indexes scale atoms with RT = ceil(M / 128) for the
+    activation and 2 ceil(N / 256) for the weight: each role takes its own
+    row multiple (checked before anything touches a device)."""
+    from voyager_b200 import packed
+
+    scale, codes = _mxfp8((8, 64), 2)
+    with pytest.raises(ValueError):
+        packed.to_device(packed.pack_mxfp8(codes, scale, 128), "cpu", weight=True)
+    with pytest.raises(ValueError):
+        packed.to_device(packed.pack_mxfp8(codes, scale, 256), "cpu", weight=False)
+    with pytest.raises(ValueError):
+        packed.to_device(packed.pack_nvfp4(np.zeros((1, 16), np.uint16),
+                                           np.full((1, 1), 0x3F80, np.uint16)), "cpu")

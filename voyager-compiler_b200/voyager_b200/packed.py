@@ -286,8 +286,12 @@ def to_device(p: PackedMX, device, weight: bool = False, verify: bool = True):
 
     if p.fmt != "mxfp8":
         raise ValueError("to_device registers MXFP8 GEMM operands")
+    # the GEMM indexes scale atoms with RT = ceil(M / 128) for the
+    # activation and 2 ceil(N / 256) for the weight
     if weight and p.row_multiple != 256:
         raise ValueError("a weight operand is packed with row_multiple=256")
+    if not weight and p.row_multiple != 128:
+        raise ValueError("an activation operand is packed with row_multiple=128")
     c, s = unpack(p)
     dev = torch.device(device)
     codes = torch.from_numpy(c.view(np.int16).copy()).view(torch.bfloat16).to(dev)
