@@ -1,6 +1,6 @@
 """Benchmark of the quantization hot path on B200 (one JSON line on rank 0).
 
-Headline workload ("C2"): quantize float32 weights
+Headline workload (the second benchmark configuration, "C2"): quantize float32 weights
 [11008, 4096] ~ N(0, 0.02^2) three ways per step, through the reference's op
 API (torch.ops.quantized_ops):
   * NF4 per-group 64: quantize_mx(w, lut4 index table, [-1], 64, 1.0)
@@ -38,9 +38,14 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 
 ROWS, COLS = 11008, 4096
+# one metric string for both arms (the driver pairs the lines by it)
+METRIC = ("C2 weight quantize throughput (NF4 g64 + posit8 per-tensor + int8 "
+          "per-channel), algorithmic bytes")
+DATA = "synthetic (seeded PCG64 N(0,0.02^2))"
+WORKLOAD = ("C2 fp32 [11008,4096]: NF4 g64 quantize_mx / posit8_1 per-tensor / int8 "
+            "per-channel quantize")
 # per-launch DRAM bytes (read + write) of the C2 kernels, from one ncu capture
-# (ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum; recorded with the
-# command in profiles/quantize_c2_weights.md)
+# (ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum of the C2 kernels)
 NCU_TRAFFIC = {"int8_channel": int(311.5e6), "nf4_g64": int(310.4e6),
                "posit8_tensor": int(308.9e6)}
 BYTES_PER_ELEM = {"nf4_g64": 4 + 4 + 4.0 / 64, "posit8_tensor": 8.0, "int8_channel": 8.0}
@@ -93,6 +98,19 @@ def cpu_step(w_rows, tables, threads):
         list(ex.map(work, range(threads)))
 
 
+def load_synth():
+    """The seeded input generators, loaded by file path: the reference arm
+    must not import the voyager_b200 package (that maps the CUDA library
+    and registers its kernels)."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location(
+        "vq_bench_synth", os.path.join(ROOT, "voyager-compiler_b200", "voyager_b200", "synth.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def cpu_tables():
     from oracle.numerics import index_table, quantization_map
 
@@ -104,7 +122,7 @@ def bytes_per_row():
 
 
 def cpu_baseline(sample_rows=1024, reps=3):
-    from voyager_b200 import synth
+    synth = load_synth()
 
     threads = os.cpu_count() or 1
     w = synth.c2_weight()[:sample_rows]
@@ -124,7 +142,7 @@ def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    from voyager_b200 import synth
+    synth = load_synth()
 
     threads = os.cpu_count() or 1
     sample_rows = 768
@@ -141,13 +159,11 @@ def run_reference(args):
     dt = sum(times) / len(times)
     val = sample_rows * bytes_per_row() / dt / 1e9
     line = {
-        "impl": "reference", "metric": "C2 weight quantize throughput (NF4 g64 + posit8 "
-        "per-tensor + int8 per-channel)", "value": round(val, 3), "unit": "GB/s",
+        "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": "C2 fp32 [11008,4096] N(0,0.02): NF4 g64 / posit8_1 "
-                   "per-tensor / int8 per-channel", "sample_rows_per_step": sample_rows},
+        "vs_baseline": None, "dtype": "fp32", "data": DATA,
+        "config": {"workload": WORKLOAD, "sample_rows_per_step": sample_rows},
         "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads,
                          "kind": "port", "sample": f"{sample_rows} rows per step"},
         "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -286,6 +302,8 @@ def run_ours(args):
         torch.cuda.synchronize()
     if pg:
         pg.barrier()
+    # no kernel of the library gave up a bounded wait (outside the timing)
+    voyager_b200.check_errors(dev)
     ms = t_start.elapsed_time(t_end)
     per = {n: [ev[i][j].elapsed_time(ev[i][j + 1]) for i in range(args.steps)]
            for j, n in enumerate(names)}
@@ -365,20 +383,19 @@ def run_ours(args):
             if rank == 0:
                 secondary[key] = c5
 
+    voyager_b200.check_errors(dev)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline()
 
     if rank == 0:
         line = {
-            "metric": "C2 weight quantize throughput (NF4 g64 + posit8 per-tensor + int8 "
-                      "per-channel), algorithmic bytes",
+            "metric": METRIC,
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic (seeded PCG64 N(0,0.02^2))",
-            "config": {"workload": "C2 fp32 [11008,4096]: NF4 g64 quantize_mx / posit8_1 "
-                                   "per-tensor / int8 per-channel quantize",
+            "data": DATA,
+            "config": {"workload": WORKLOAD,
                        "per_gpu_bytes_per_step": int(elems * sum(BYTES_PER_ELEM.values())),
                        "l2": "inputs (180 MB) and outputs larger than the 126 MB L2",
                        "parallelism": f"replicas x{world} (row-sharded weak scaling)"},
@@ -387,10 +404,9 @@ def run_ours(args):
                          "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
                          "traffic": NCU_TRAFFIC.get(dom),
                          "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per "
-                                         "launch from one ncu capture of this kernel "
-                                         "(profiles/quantize_c2_weights.md); writes still "
-                                         "draining from L2 at the kernel's end are not "
-                                         "counted"},
+                                         "launch from one ncu capture of this kernel; "
+                                         "writes still draining from L2 at the kernel's "
+                                         "end are not counted"},
             "kernels": kernels,
             "clocks": clk.summary(),
             "gpu_launches": 3 * args.steps,

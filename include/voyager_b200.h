@@ -266,6 +266,22 @@ int vq_gemm_mxf8_ex(const void* a, const void* a_sf, const void* b, const void* 
 int vq_linear_mxf8_noalloc(const vq_tensor* a_codes, const vq_tensor* a_scale,
                            const void* w_packed, const void* w_sf_packed, int64_t N,
                            const void* bias, void* out, int64_t ldo, void* stream);
+/* The error word of the last vq_linear_mxf8_noalloc call on this device
+ * (kept in the same fixed array): 0, or the code of a bounded wait in the
+ * kernel that gave up (the output is then incomplete).  Ordered on `stream`
+ * after the calls queued there; copies the word to *code (host memory) and
+ * synchronises the stream.  Allocates nothing. */
+int vq_linear_mxf8_noalloc_status(int32_t* code, void* stream);
+
+/* Sticky wait-timeout status of this library's tcgen05 and barrier kernels
+ * on the current device: *code (host) = 0, or the first code any launch
+ * recorded since the last clear -- GEMM 1-4, tensor-parallel barrier
+ * 100 + rank, attention 200 + its code.  The per-call error words report to
+ * one caller; this one lets the host ask, after a batch of work, whether any
+ * launch gave up.  clear != 0 resets the word.  Synchronises `stream`.  The
+ * reference raises on the host and has no device waits; this has no
+ * counterpart there. */
+int vq_device_errors(int32_t* code, int32_t clear, void* stream);
 
 /* ---- Fused MXFP8 attention (tcgen05) ---------------------------------------
  * quantized_ops::sdpa_mx (src/voyager_compiler/ops/quantized.py:651-784)
@@ -346,6 +362,10 @@ int vq_swiglu_quantize_mx(const void* gate_up, int64_t ld, int64_t up_off, int64
  * sets *d_err = 100 + j and returns. */
 int vq_tp_barrier(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int32_t world,
                   uint32_t epoch, int32_t* d_err, void* stream);
+/* vq_tp_barrier with the wait limit given: timeout_ns of %globaltimer time
+ * per flag (1 us .. 10 s), after which *d_err = 100 + j and the kernel ends. */
+int vq_tp_barrier_ex(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int32_t world,
+                     uint32_t epoch, uint64_t timeout_ns, int32_t* d_err, void* stream);
 /* rows x row_bytes from src (row stride src_ld bytes) into every rank's copy
  * of a symmetric buffer through its multicast address (row stride dst_ld
  * bytes); all sizes and addresses 16-byte aligned. */

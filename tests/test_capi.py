@@ -168,3 +168,35 @@ def test_table_kinds_fit_the_byte_coded_form():
         pal[:uniq.size] = uniq
         assert np.array_equal(pal[inv.astype(np.uint8).reshape(-1)], t), name
     assert wide == ["posit16_1"], wide
+
+
+def test_noalloc_rejects_before_touching_its_scratch():
+    """vq_linear_mxf8_noalloc refuses what the GEMM would refuse before it
+    packs into the shared array (no device pointer is touched here)."""
+    lib = _lib.load()
+    B = ctypes.byref
+    a, s = _t([64, 256]), _t([64, 8])
+    w, wsf, out = 0x10000, 0x20000, 0x30000
+    # N not a multiple of 8
+    assert lib.vq_linear_mxf8_noalloc(B(a), B(s), w, wsf, 12, None, out, 16, None) == 2
+    # ldo below N, and not a multiple of 8
+    assert lib.vq_linear_mxf8_noalloc(B(a), B(s), w, wsf, 16, None, out, 8, None) == 2
+    assert lib.vq_linear_mxf8_noalloc(B(a), B(s), w, wsf, 16, None, out, 20, None) == 2
+    # misaligned output, weight or scale atoms, odd bias address
+    assert lib.vq_linear_mxf8_noalloc(B(a), B(s), w, wsf, 16, None, out + 8, 16, None) == 3
+    assert lib.vq_linear_mxf8_noalloc(B(a), B(s), w + 4, wsf, 16, None, out, 16, None) == 3
+    assert lib.vq_linear_mxf8_noalloc(B(a), B(s), w, wsf + 2, 16, None, out, 16, None) == 3
+    assert lib.vq_linear_mxf8_noalloc(B(a), B(s), w, wsf, 16, 0x40001, out, 16, None) == 3
+    # NULL status pointer
+    assert lib.vq_linear_mxf8_noalloc_status(None, None) == 6
+    assert lib.vq_device_errors(None, 0, None) == 6
+
+
+def test_barrier_rejects_bad_limits():
+    lib = _lib.load()
+    flags, mine, err = 0x10000, 0x20000, 0x30000
+    # the wait limit must lie in [1 us, 10 s]; checked before the launch
+    assert lib.vq_tp_barrier_ex(flags, mine, 0, 2, 1, 999, err, None) == 1
+    assert lib.vq_tp_barrier_ex(flags, mine, 0, 2, 1, 10_000_000_001, err, None) == 1
+    assert lib.vq_tp_barrier_ex(flags, mine, 2, 2, 1, 10**6, err, None) == 1
+    assert lib.vq_tp_barrier_ex(None, mine, 0, 2, 1, 10**6, err, None) == 6

@@ -58,6 +58,17 @@ def _noalloc(ca, sa, pw, pws, n, bias=None):
     return to_np(out)
 
 
+def _status():
+    from voyager_b200 import _lib
+    from voyager_b200.ops import _stream
+
+    code = ctypes.c_int32(-1)
+    st = _lib.load().vq_linear_mxf8_noalloc_status(ctypes.byref(code),
+                                                   _stream(torch.device("cuda")))
+    assert st == 0, _lib.STATUS.get(st, st)
+    return code.value
+
+
 def test_noalloc_matches_allocating_path_twice():
     from voyager_b200 import mxgemm
 
@@ -67,14 +78,20 @@ def test_noalloc_matches_allocating_path_twice():
     dcw, dsw = to_dev(cw), to_dev(sw)
     pw, pws, ok = mxgemm.packed_weight(dcw, dsw)
     assert ok
-    for m in (300, 77):  # two calls in a row, different shapes and data
+    from voyager_b200.synth import f32_to_bf16_bits
+
+    bias = f32_to_bf16_bits((rng.standard_normal(N) * 0.5).astype(np.float32))
+    for m, b in ((300, None), (77, bias)):  # two calls in a row, different shapes and data
         ca, sa = _mx(rng, (m, K), 1.0)
-        want = to_np(mxgemm.linear(to_dev(ca), dcw, None, to_dev(sa), dsw))
-        got = _noalloc(ca, sa, pw, pws, N)
+        db = None if b is None else to_dev(b)
+        want = to_np(mxgemm.linear(to_dev(ca), dcw, db, to_dev(sa), dsw))
+        got = _noalloc(ca, sa, pw, pws, N, db)
         assert got.shape == want.shape
         assert G.rel_l2(got, want) < 1e-3
-        ref = oracle.linear_mx(ca, cw, None, input_scale=sa, weight_scale=sw, block_size=32)
+        ref = oracle.linear_mx(ca, cw, b, input_scale=sa, weight_scale=sw, block_size=32)
         assert G.rel_l2(got, ref) < 1e-3
+        # the kernel's error word in the fixed array: no bounded wait gave up
+        assert _status() == 0
 
 
 def test_noalloc_rejects_oversize():

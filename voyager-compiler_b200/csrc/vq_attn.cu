@@ -471,6 +471,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// This file's sticky wait-timeout word (vq_device_errors).
+int sticky_attn(int* out, int clear, cudaStream_t st) { return vq::tc::sticky_read(out, clear, st); }
+
 }  // namespace attn
 }  // namespace vq
 

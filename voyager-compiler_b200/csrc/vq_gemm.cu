@@ -62,7 +62,21 @@ constexpr int SF_SLOT = 16;
 constexpr int SFA_OFF = 0, SFB_OFF = 4;
 constexpr int THREADS = 320;
 
-enum { ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_TIMEOUT_ACC = 3 };
+enum { ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_TIMEOUT_ACC = 3, ERR_TIMEOUT_DRAIN = 4 };
+
+// Before a CTA frees its TMEM and exits, each thread that issued
+// asynchronous work waits (bounded) for it: the TMA producer for the loads
+// of the last round of stages it armed (a stage never armed reads as
+// complete at parity 1), the MMA and scale-copy threads for every tcgen05
+// operation they issued (a commit to a barrier of their own).  On the
+// normal path all of these have completed already; after a wait that gave
+// up they keep TMEM and shared memory alive until the work in flight lands.
+template <int NSTAGES>
+__device__ __forceinline__ void drain_loads(uint32_t full0, int stage, uint32_t phase, int* err) {
+#pragma unroll 1
+  for (int s = 0; s < NSTAGES; ++s)
+    tc::mbar_wait(full0 + 8 * s, s < stage ? phase : phase ^ 1, err, ERR_TIMEOUT_DRAIN);
+}
 
 struct SmemLayout {
   // stages first (1024-byte aligned for SWIZZLE_128B), then barriers
@@ -181,11 +195,13 @@ __global__ void __launch_bounds__(THREADS + 32, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::kBars);
   // bars[0..S) full, [S..2S) empty, [2S] acc_full, [2S+1] acc_empty, [2S+2] tmem slot,
-  // [2S+3..3S+3) sf_full (the stage's scale atoms are in TMEM)
+  // [2S+3..3S+3) sf_full (the stage's scale atoms are in TMEM), [3S+3] drain
+  // of the MMA thread's tcgen05 operations, [3S+4] of the scale copies
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
   const uint32_t acc_full = smem_u32(bars + 2 * STAGES), acc_empty = smem_u32(bars + 2 * STAGES + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2);
   const uint32_t sf_full0 = smem_u32(bars + 2 * STAGES + 3);
+  const uint32_t drain_mma = smem_u32(bars + 3 * STAGES + 3), drain_sf = drain_mma + 8;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
@@ -196,6 +212,8 @@ __global__ void __launch_bounds__(THREADS + 32, 1)
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 256);
+    mbar_init(drain_mma, 1);
+    mbar_init(drain_sf, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -238,6 +256,7 @@ __global__ void __launch_bounds__(THREADS + 32, 1)
           }
         }
       }
+      drain_loads<STAGES>(full0, stage, phase, g.err);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -290,6 +309,8 @@ __global__ void __launch_bounds__(THREADS + 32, 1)
                 acc_full)
             : "memory");
       }
+      tc_commit(drain_mma);
+      mbar_wait(drain_mma, 0, g.err, ERR_TIMEOUT_DRAIN);
     }
   } else if (warp == 10) {
     // ---------------- scale-copy issuer ----------------
@@ -328,6 +349,8 @@ __global__ void __launch_bounds__(THREADS + 32, 1)
           }
         }
       }
+      tc_commit(drain_sf);
+      mbar_wait(drain_sf, 0, g.err, ERR_TIMEOUT_DRAIN);
     }
   } else {
     // ---------------- epilogue (warps 2..9) ----------------
@@ -373,9 +396,10 @@ constexpr int P_STAGE_BYTES = (P_TX + 1023) / 1024 * 1024;
 constexpr int P_BARS = P_STAGES * P_STAGE_BYTES;
 constexpr int P_SMEM = P_BARS + 256;
 constexpr int P_THREADS = THREADS + 32;  // + warp 10: the scale-copy issuer
-// barrier words: full, empty, sf_full per stage, acc_full, acc_empty, TMEM slot
-static_assert((3 * P_STAGES + 3) * 8 <= P_SMEM - P_BARS, "pair barriers exceed their area");
-static_assert((3 * STAGES + 3) * 8 <= SmemLayout::kTotal - SmemLayout::kBars,
+// barrier words: full, empty, sf_full per stage, acc_full, acc_empty, TMEM
+// slot, two drains
+static_assert((3 * P_STAGES + 5) * 8 <= P_SMEM - P_BARS, "pair barriers exceed their area");
+static_assert((3 * STAGES + 5) * 8 <= SmemLayout::kTotal - SmemLayout::kBars,
               "barriers exceed their area");
 static_assert(P_SMEM + 1024 <= (1 << 18) && SmemLayout::kTotal + 1024 <= (1 << 18),
               "descriptor offsets assume shared addresses below 2^18");
@@ -393,8 +417,10 @@ __global__ void __launch_bounds__(P_THREADS, 1)
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + P_STAGES);
   const uint32_t acc_full = smem_u32(bars + 2 * P_STAGES), acc_empty = smem_u32(bars + 2 * P_STAGES + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * P_STAGES + 2);
-  // per stage: the stage's scale atoms are in TMEM (even CTA)
+  // per stage: the stage's scale atoms are in TMEM (even CTA); then the
+  // drains of the MMA thread's and the scale copies' tcgen05 operations
   const uint32_t sf_full0 = smem_u32(bars + 2 * P_STAGES + 3);
+  const uint32_t drain_mma = smem_u32(bars + 3 * P_STAGES + 3), drain_sf = drain_mma + 8;
   const uint32_t rank = cluster_ctarank();  // 0: issues the pair's MMAs
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int pair_id = blockIdx.x / 2, npairs = gridDim.x / 2;
@@ -406,6 +432,8 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 2 * 8);  // one arrival per epilogue warp of both CTAs
+    mbar_init(drain_mma, 1);
+    mbar_init(drain_sf, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -456,6 +484,9 @@ __global__ void __launch_bounds__(P_THREADS, 1)
           }
         }
       }
+      // both CTAs' loads complete on the even CTA's barriers, so its wait
+      // covers the pair (the cluster barrier below holds the odd CTA)
+      if (rank == 0) drain_loads<P_STAGES>(full0, stage, phase, g.err);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (even CTA) ----------------
@@ -505,6 +536,8 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         if (!ok) break;
         tc_commit_pair(acc_full, 0x3);
       }
+      tc_commit_pair(drain_mma, 0x1);
+      mbar_wait(drain_mma, 0, g.err, ERR_TIMEOUT_DRAIN);
     }
   } else if (warp == 10) {
     // ---------------- scale-copy issuer (even CTA) ----------------
@@ -540,6 +573,8 @@ __global__ void __launch_bounds__(P_THREADS, 1)
           }
         }
       }
+      tc_commit_pair(drain_sf, 0x1);
+      mbar_wait(drain_sf, 0, g.err, ERR_TIMEOUT_DRAIN);
     }
   } else {
     // ---------------- epilogue (warps 2..9, both CTAs) ----------------
@@ -730,6 +765,12 @@ uint8_t* noalloc_scratch_ptr(int* status) {
 }
 
 }  // namespace mx
+namespace attn {
+int sticky_attn(int* out, int clear, cudaStream_t st);
+}
+namespace tp {
+int sticky_tp(int* out, int clear, cudaStream_t st);
+}
 }  // namespace vq
 
 using namespace vq::mx;
@@ -882,6 +923,13 @@ int vq_linear_mxf8_noalloc(const vq_tensor* a_codes, const vq_tensor* a_scale,
   if (a_codes->ndim != 2) return VQ_ERR_SHAPE;
   const int64_t M = a_codes->shape[0], K = a_codes->shape[1];
   if (M <= 0 || K <= 0 || N <= 0) return VQ_ERR_INVALID;
+  // everything the GEMM would reject is rejected here, before the packing
+  // overwrites the shared scratch
+  if (N % 8 != 0 || ldo < N || ldo % 8 != 0 || M > (1 << 30) || N > (1 << 30))
+    return VQ_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(w_packed) & 15) ||
+      (reinterpret_cast<uintptr_t>(w_sf_packed) & 15) || (reinterpret_cast<uintptr_t>(bias) & 1))
+    return VQ_ERR_ALIGNMENT;
   int64_t cb = 0, sb = 0, ld = 0;
   int st = vq_mx_pack_sizes(M, K, 128, &cb, &sb, &ld);
   if (st) return st;
@@ -896,6 +944,32 @@ int vq_linear_mxf8_noalloc(const vq_tensor* a_codes, const vq_tensor* a_scale,
     return st;
   return vq_gemm_mxf8(base + codes_off, base + sf_off, w_packed, w_sf_packed, M, N, K, bias, out,
                       ldo, err, stream);
+}
+
+int vq_linear_mxf8_noalloc_status(int32_t* code, void* stream) {
+  if (!code) return VQ_ERR_NULL;
+  int st = VQ_OK;
+  uint8_t* base = noalloc_scratch_ptr(&st);
+  if (!base) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  if (cudaMemcpyAsync(&v, base, sizeof(int32_t), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return VQ_ERR_CUDA;
+  *code = v;
+  return VQ_OK;
+}
+
+int vq_device_errors(int32_t* code, int32_t clear, void* stream) {
+  if (!code) return VQ_ERR_NULL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int v[3] = {0, 0, 0};
+  if (vq::tc::sticky_read(&v[0], clear, s) || vq::attn::sticky_attn(&v[1], clear, s) ||
+      vq::tp::sticky_tp(&v[2], clear, s))
+    return VQ_ERR_CUDA;
+  // the first nonzero word: GEMM 1-4, tensor-parallel barrier 100 + rank, attention 200 + code
+  *code = v[0] ? v[0] : (v[1] ? 200 + v[1] : v[2]);
+  return VQ_OK;
 }
 
 }  // extern "C"

@@ -13,6 +13,38 @@ namespace tc {
 
 constexpr uint64_t WAIT_NS = 2000000000ull;  // a wait gives up after 2 s
 
+// The first wait-timeout code that any kernel of this translation unit
+// recorded on this device since it was last cleared: the per-call error
+// words tell one caller about its own launch, this word lets the host ask
+// afterwards whether any launch gave up (vq_device_errors).  One copy per
+// translation unit that includes this header.
+static __device__ int g_sticky_err;
+
+// Record a wait that gave up: the launch's own error word and the sticky one.
+__device__ __forceinline__ void note_err(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+  atomicCAS(&g_sticky_err, 0, code);
+}
+
+// Host side: read (and with clear, reset) this translation unit's sticky
+// word on the current device; synchronises `st`.
+static inline int sticky_read(int* out, int clear, cudaStream_t st) {
+  int v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_sticky_err, sizeof(int), 0, cudaMemcpyDeviceToHost, st) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return -1;
+  if (clear && v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbolAsync(g_sticky_err, &z, sizeof(int), 0, cudaMemcpyHostToDevice, st) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+      return -1;
+  }
+  *out = v;
+  return 0;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
@@ -52,7 +84,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
       if (mbar_try_wait(bar, parity)) return true;
     if (globaltimer_ns() - t0 > WAIT_NS) break;
   }
-  atomicCAS(err, 0, code);
+  note_err(err, code);
   return false;
 }
 

@@ -31,6 +31,7 @@
 
 #include "vq_hw.cuh"
 #include "vq_numerics.cuh"
+#include "vq_tc.cuh"
 
 namespace vq {
 namespace tp {
@@ -65,9 +66,10 @@ __device__ __forceinline__ void mc_st_f32(void* addr, uint32_t a) {
 // ---------------------------------------------------------------------------
 // Barrier: thread j tells rank j "rank `rank` reached epoch", then waits for
 // rank j's flag in this rank's array.  Flags only grow (epoch is the
-// caller's call counter), so no reset is needed.
+// caller's call counter), so no reset is needed.  A wait that has not seen
+// its flag after timeout_ns of %globaltimer time records 100 + j and ends.
 __global__ void k_tp_barrier(const uint64_t* peer_flags, uint32_t* my_flags, int rank, int world,
-                             uint32_t epoch, int* err) {
+                             uint32_t epoch, uint64_t timeout_ns, int* err) {
   const int j = threadIdx.x;
   if (j < world) {
     __threadfence_system();
@@ -79,8 +81,8 @@ __global__ void k_tp_barrier(const uint64_t* peer_flags, uint32_t* my_flags, int
       uint32_t v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(src) : "memory");
       if ((int32_t)(v - epoch) >= 0) break;
-      if (now_ns() - t0 > WAIT_NS) {
-        atomicCAS(err, 0, 100 + j);
+      if (now_ns() - t0 > timeout_ns) {
+        vq::tc::note_err(err, 100 + j);
         break;
       }
     }
@@ -302,6 +304,9 @@ int check_dest(const Dest& d, int C) {
   return VQ_OK;
 }
 
+// This file's sticky wait-timeout word (vq_device_errors).
+int sticky_tp(int* out, int clear, cudaStream_t st) { return vq::tc::sticky_read(out, clear, st); }
+
 int e4m3(const vq_rounder* r) {
   if (!r) return VQ_ERR_NULL;
   return (r->kind == VQ_R_MINIFLOAT && r->hw == VQ_HW_E4M3) ? VQ_OK : VQ_ERR_UNSUPPORTED;
@@ -314,13 +319,20 @@ using namespace vq::tp;
 
 extern "C" {
 
-int vq_tp_barrier(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int32_t world,
-                  uint32_t epoch, int32_t* d_err, void* stream) {
+int vq_tp_barrier_ex(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int32_t world,
+                     uint32_t epoch, uint64_t timeout_ns, int32_t* d_err, void* stream) {
   if (!peer_flag_ptrs || !my_flags || !d_err) return VQ_ERR_NULL;
   if (world < 1 || world > 64 || rank < 0 || rank >= world) return VQ_ERR_INVALID;
+  if (timeout_ns < 1000 || timeout_ns > 10000000000ull) return VQ_ERR_INVALID;
   k_tp_barrier<<<1, 64, 0, (cudaStream_t)stream>>>((const uint64_t*)peer_flag_ptrs,
-                                                   (uint32_t*)my_flags, rank, world, epoch, d_err);
+                                                   (uint32_t*)my_flags, rank, world, epoch,
+                                                   timeout_ns, d_err);
   return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
+}
+
+int vq_tp_barrier(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int32_t world,
+                  uint32_t epoch, int32_t* d_err, void* stream) {
+  return vq_tp_barrier_ex(peer_flag_ptrs, my_flags, rank, world, epoch, WAIT_NS, d_err, stream);
 }
 
 int vq_tp_copy_multicast(const void* src, int64_t src_ld, int64_t rows, int64_t row_bytes,

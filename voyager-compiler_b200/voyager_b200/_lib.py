@@ -131,6 +131,11 @@ _SIGNATURES = {
     "vq_tp_barrier": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                      ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p,
                                      ctypes.c_void_p]),
+    "vq_tp_barrier_ex": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                        ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint64,
+                                        ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_linear_mxf8_noalloc_status": (ctypes.c_int, [P(ctypes.c_int32), ctypes.c_void_p]),
+    "vq_device_errors": (ctypes.c_int, [P(ctypes.c_int32), ctypes.c_int32, ctypes.c_void_p]),
     "vq_tp_copy_multicast": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                             ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
                                             ctypes.c_void_p]),

@@ -3,7 +3,7 @@
 Applies when both operands are E4M3 codes (bf16 values) with power-of-two
 block-32 scales along K, blocks along the last dim of both ``input`` [.., K]
 and ``weight`` [N, K] (``weight_layout="kc"``), no codebooks, bf16 everywhere
-(SURVEY config C3: ``fp8_e4m3,qs=microscaling,bs=32`` with
+(the C3 benchmark configuration: ``fp8_e4m3,qs=microscaling,bs=32`` with
 ``--force_scale_power_of_two``).  The product equals the reference's
 dequantize-then-matmul (``quantized.py:455-586``) up to the float32
 summation order: E4M3 x 2^e values are exact in bf16, and the tensor cores

@@ -1,4 +1,4 @@
-"""W4A8 linear: NVFP4 weights x MXFP8 activations.
+"""W4A8 linear: NVFP4 weights x MXFP8 activations (the C4 benchmark sweep).
 
 Weights: E2M1 codes (bf16 values) [N, K] with E4M3 scales per 16 along K
 (`fp4_e2m1,qs=microscaling,bs=16,ax=-1,scale=fp8_e4m3`); activations: E4M3
