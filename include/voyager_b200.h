@@ -242,6 +242,29 @@ int vq_gemm_mxf8_ex(const void* a, const void* a_sf, const void* b, const void* 
                     void* out, int64_t ldo, int32_t out_multicast, int32_t* d_err,
                     void* stream);
 
+/* quantized_ops::matmul_mx (src/voyager_compiler/ops/quantized.py:589-648)
+ * for MXFP8 operands with leading (batch) dims: vq_mx_pack of `batch`
+ * matrices at once.  codes bf16 [batch, R, K] with scale [batch, R, K/32]
+ * (k_axis 2: blocks along the last dim), or codes [batch, K, R] with scale
+ * [batch, K/32, R] (k_axis 1: blocks along dim -2, the right operand of a
+ * matmul stored [.., K, N]).  Output: with RTb = round_up(R, row_multiple)
+ * / 128 row tiles per batch, codes [batch * RTb * 128, Kp] bytes and scale
+ * atoms [Kp / 128][batch * RTb][512] (batch b's tiles at b * RTb); sizes
+ * batch * RTb * 128 * Kp and (Kp / 128) * batch * RTb * 512 bytes. */
+int vq_mx_pack_batched(const vq_tensor* codes, const vq_tensor* scale, int64_t block_size,
+                       int32_t row_multiple, int32_t k_axis, void* packed_codes, void* packed_sf,
+                       int32_t* d_inexact, void* stream);
+
+/* `batch` MXFP8 GEMMs in one launch: out[b] = A[b] . B[b]^T from operands
+ * packed by vq_mx_pack_batched (A with a_rows_per_batch packed rows per
+ * batch -- a multiple of 128, at least M; B with row_multiple 256), or one
+ * B for every batch (b_shared: packed by vq_mx_pack, row_multiple 256).
+ * out[b] = out + b * out_batch_stride elements, rows ldo apart. */
+int vq_gemm_mxf8_batched(const void* a, const void* a_sf, const void* b, const void* b_sf,
+                         int64_t batch, int64_t a_rows_per_batch, int64_t M, int64_t N, int64_t K,
+                         int32_t b_shared, const void* bias, void* out, int64_t ldo,
+                         int64_t out_batch_stride, int32_t* d_err, void* stream);
+
 /* MXFP8 linear that allocates nothing: for callers that cannot call
  * cudaMalloc -- an allocator-free runtime, code running under a caller-owned
  * memory budget, or a library hook invoked where allocating is not allowed.

@@ -132,3 +132,69 @@ def test_fused_pack_matches_separate_pack():
     want = oracle.linear_mx(to_np(ca), to_np(cw), None, input_scale=to_np(sa),
                             weight_scale=to_np(sw), block_size=32)
     assert G.rel_l2(to_np(fused), want) < 1e-3
+
+
+# ---------------------------------------------------------------------------
+# matmul_mx with MXFP8 operands on the same kernels (batched)
+# ---------------------------------------------------------------------------
+def _mx_along(x, axis):
+    qm = quantization_map("fp8_e4m3")
+    s, c = oracle.quantize_mx(x, qm, [axis], 32, 448.0, True)
+    return c, s
+
+
+def _bf16(rng, shape, std):
+    from voyager_b200.synth import f32_to_bf16_bits
+
+    return f32_to_bf16_bits((rng.standard_normal(shape) * std).astype(np.float32))
+
+
+# (batch dims, M, K, N, layout, right operand shared across the batch)
+MATMUL_CASES = [((2, 3), 128, 128, 256, "ck", False), ((4,), 300, 256, 264, "ck", False),
+                ((2,), 77, 96, 40, "kc", False), ((3,), 512, 128, 512, "ck", True),
+                ((), 1000, 640, 520, "ck", False), ((2,), 256, 4096, 1024, "kc", True),
+                ((1, 2), 2048, 128, 2048, "ck", False)]
+
+
+@pytest.mark.parametrize("bdims,m,k,n,layout,shared", MATMUL_CASES)
+def test_mxf8_matmul(bdims, m, k, n, layout, shared):
+    from voyager_b200 import mxgemm
+
+    rng = np.random.default_rng(m + k + n + len(bdims))
+    a = _bf16(rng, bdims + (m, k), 1.0)
+    bshape = ((k, n) if layout == "ck" else (n, k))
+    b = _bf16(rng, (bshape if shared else bdims + bshape), 0.5)
+    ca, sa = _mx_along(a, -1)
+    cb, sb = _mx_along(b, -2 if layout == "ck" else -1)
+    want = oracle.matmul_mx(ca, cb, input_scale=sa, weight_scale=sb, block_size=32,
+                            weight_layout=layout)
+    dca, dsa, dcb, dsb = to_dev(ca), to_dev(sa), to_dev(cb), to_dev(sb)
+    assert mxgemm.matmul_applies(dca, dcb, dsa, dsb, 32, None, None, layout)
+    out = mxgemm.matmul(dca, dcb, dsa, dsb, layout)
+    assert out is not None, "operands were not accepted as exact MXFP8"
+    got = to_np(out)
+    assert got.shape == want.shape
+    assert G.rel_l2(got, want) < 1e-3
+    # and through the op, twice (the shared operand's pack is cached)
+    for _ in range(2):
+        got2 = to_np(torch.ops.quantized_ops.matmul_mx(dca, dcb, input_scale=dsa,
+                                                       weight_scale=dsb, block_size=32,
+                                                       weight_layout=layout))
+        assert np.array_equal(got2, got)
+
+
+def test_mxf8_matmul_from_quantize_mx():
+    """Operands straight from the CUDA quantize_mx (vouched, packed in the
+    same pass for the left operand) give the same product."""
+    Q = torch.ops.quantized_ops
+    from voyager_b200.tables import get_quantization_map
+
+    rng = np.random.default_rng(5)
+    a, b = _bf16(rng, (2, 4, 256, 128), 1.0), _bf16(rng, (2, 4, 128, 256), 1.0)
+    e4m3 = get_quantization_map("fp8_e4m3", torch.device("cuda"))
+    sa, ca = Q.quantize_mx(to_dev(a), e4m3, [-1], 32, 448.0, True)
+    sb, cb = Q.quantize_mx(to_dev(b), e4m3, [-2], 32, 448.0, True)
+    got = to_np(Q.matmul_mx(ca, cb, input_scale=sa, weight_scale=sb, block_size=32))
+    want = oracle.matmul_mx(to_np(ca), to_np(cb), input_scale=to_np(sa), weight_scale=to_np(sb),
+                            block_size=32)
+    assert G.rel_l2(got, want) < 1e-3

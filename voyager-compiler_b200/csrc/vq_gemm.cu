@@ -90,19 +90,36 @@ using namespace vq::tc;
 // Instruction descriptor of this kernel's MMA (M = 128, N = 256).
 __device__ __forceinline__ uint32_t idesc_mxf8(uint32_t j) { return tc::idesc_mxf8(j, BM, BN); }
 
+// Batched problems (matmul_mx over leading dims): batch b's A rows are
+// the packed rows [b * MTb * 128, (b + 1) * MTb * 128) and its scale atoms
+// the 128-row tiles b * MTb .. of each K tile; B likewise with b_step
+// 128-row chunks per batch (0: one B shared by every batch).  Rows of a
+// tile past the batch's M read the next batch's operands and are never
+// stored.
 struct GemmArgs {
   const uint8_t* sfa;  // [KT][MT][512]
   const uint8_t* sfb;  // [KT][NT128][512]
   const uint16_t* bias;  // bf16 [N] or null
   const uint16_t* residual;  // bf16 [M, ldr] added after the bf16 rounding, or null
   int64_t ldr;
-  uint16_t* out;         // bf16 [M, ldo] (may be the residual itself)
-  int64_t ldo;
+  uint16_t* out;         // bf16 [batch][M, ldo] (may be the residual itself)
+  int64_t ldo, out_bs;   // out_bs: elements between batches
   int out_mc;            // out is an NVLS multicast address: multimem stores
-  int M, N, KT;          // KT = Kp / 128
-  int MT, NT128, NTILE_N, ntiles;
+  int M, N, KT;          // M per batch; KT = Kp / 128
+  int MT, NT128, NTILE_N, ntiles;  // MT, NT128: atom rows over all batches
+  int MTb, MT2b, b_step;  // per batch: 128-row A tiles, 256-row tiles, B chunks
   int* err;
 };
+
+// Tile t -> (batch, row tile of `mtiles` per batch, 256-column tile).
+__device__ __forceinline__ void tile_of(const GemmArgs& g, int t, int mtiles, int& b, int& tm,
+                                        int& tn) {
+  const int per_b = mtiles * g.NTILE_N;
+  b = t / per_b;
+  const int r = t - b * per_b;
+  tm = r / g.NTILE_N;
+  tn = r - tm * g.NTILE_N;
+}
 
 // One 128-row x 256-column accumulator tile of this CTA's TMEM -> out rows
 // (bias, bf16, optional residual add, optional multicast stores).  Two warps
@@ -110,7 +127,7 @@ struct GemmArgs {
 // read into registers and released (release()) before any arithmetic.
 template <typename Release>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem, int q, int half,
-                                              int lane, int row, int colh, Release release) {
+                                              int lane, int b, int row, int colh, Release release) {
   // all four TMEM loads, one wait, then the accumulator goes back to the
   // MMA warp before any arithmetic
   uint32_t raw[4][32];
@@ -144,7 +161,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& g, uint32_t tmem, 
     }
   }
   if (row < g.M && colh < g.N) {
-    uint16_t* orow = g.out + (int64_t)row * g.ldo;
+    uint16_t* orow = g.out + (int64_t)b * g.out_bs + (int64_t)row * g.ldo;
     if (g.residual) {
       // out = bf16(bf16(acc) + residual): the residual add that follows
       // the linear in the graph, one rounding per op
@@ -236,7 +253,9 @@ __global__ void __launch_bounds__(THREADS + 32, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < g.ntiles && ok; t += gridDim.x) {
-        const int tm = t / g.NTILE_N, tn = t % g.NTILE_N;
+        int b, tm, tn;
+        tile_of(g, t, g.MTb, b, tm, tn);
+        const int ga = b * g.MTb + tm, gb = b * g.b_step + 2 * tn;  // atom rows
         for (int kt = 0; kt < g.KT; ++kt) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, g.err, ERR_TIMEOUT_EMPTY)) {
             ok = false;
@@ -245,11 +264,11 @@ __global__ void __launch_bounds__(THREADS + 32, 1)
           const uint32_t sbase = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t fb = full0 + 8 * stage;
           mbar_expect_tx(fb, TX_BYTES);
-          tma_load_2d(sbase, &tma_a, kt * BK, tm * BM, fb);
-          tma_load_2d(sbase + A_BYTES, &tma_b, kt * BK, tn * BN, fb);
-          bulk_load(sbase + A_BYTES + B_BYTES, g.sfa + ((size_t)kt * g.MT + tm) * 512, SFA_BYTES, fb);
+          tma_load_2d(sbase, &tma_a, kt * BK, ga * BM, fb);
+          tma_load_2d(sbase + A_BYTES, &tma_b, kt * BK, gb * 128, fb);
+          bulk_load(sbase + A_BYTES + B_BYTES, g.sfa + ((size_t)kt * g.MT + ga) * 512, SFA_BYTES, fb);
           bulk_load(sbase + A_BYTES + B_BYTES + SFA_BYTES,
-                    g.sfb + ((size_t)kt * g.NT128 + 2 * tn) * 512, SFB_BYTES, fb);
+                    g.sfb + ((size_t)kt * g.NT128 + gb) * 512, SFB_BYTES, fb);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -362,13 +381,14 @@ __global__ void __launch_bounds__(THREADS + 32, 1)
     const int row_in_tile = q * 32 + lane;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < g.ntiles; t += gridDim.x) {
-      const int tm = t / g.NTILE_N, tn = t % g.NTILE_N;
+      int b, tm, tn;
+      tile_of(g, t, g.MTb, b, tm, tn);
       if (!mbar_wait_warp(acc_full, acc_phase, g.err, ERR_TIMEOUT_ACC)) break;
       acc_phase ^= 1;
       tc_fence_after();
       const int row = tm * BM + row_in_tile;
       const int colh = tn * BN + half * 128;
-      epilogue_tile(g, tmem, q, half, lane, row, colh, [&] { mbar_arrive(acc_empty); });
+      epilogue_tile(g, tmem, q, half, lane, b, row, colh, [&] { mbar_arrive(acc_empty); });
     }
   }
   __syncthreads();
@@ -458,11 +478,13 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       const uint32_t s0 = smem_u32(smem);
       const uint32_t fb0 = mapa_shared(full0, 0);  // the even CTA's barriers
       for (int t = pair_id; t < g.ntiles && ok; t += npairs) {
-        const int tm = t / g.NTILE_N, tn = t % g.NTILE_N;  // 256-row, 256-column tile
-        const int ya = tm * 256 + (int)rank * 128, yb = tn * 256 + (int)rank * 128;
-        // scale-atom rows of K tile kt: (kt * MT + 2 tm + rank) * 2 and
-        // (kt * NT128 + 2 tn) * 2, stepped by 2 MT / 2 NT128 per K tile
-        int ysa = (2 * tm + (int)rank) * 2, ysb = (2 * tn) * 2;
+        int b, tm, tn;  // 256-row, 256-column tile of batch b
+        tile_of(g, t, g.MT2b, b, tm, tn);
+        const int ga = b * g.MTb + 2 * tm + (int)rank, gb = b * g.b_step + 2 * tn;
+        const int ya = ga * 128, yb = (gb + (int)rank) * 128;
+        // scale-atom rows of K tile kt: (kt * MT + ga) * 2 and
+        // (kt * NT128 + gb) * 2, stepped by 2 MT / 2 NT128 per K tile
+        int ysa = ga * 2, ysb = gb * 2;
         for (int kt = 0; kt < g.KT; ++kt) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, g.err, ERR_TIMEOUT_EMPTY)) {
             ok = false;
@@ -584,13 +606,14 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     const uint32_t acc_empty0 = mapa_shared(acc_empty, 0);
     uint32_t acc_phase = 0;
     for (int t = pair_id; t < g.ntiles; t += npairs) {
-      const int tm = t / g.NTILE_N, tn = t % g.NTILE_N;
+      int b, tm, tn;
+      tile_of(g, t, g.MT2b, b, tm, tn);
       if (!mbar_wait_warp(acc_full, acc_phase, g.err, ERR_TIMEOUT_ACC)) break;
       acc_phase ^= 1;
       tc_fence_after();
       const int row = tm * 256 + (int)rank * 128 + row_in_tile;
       const int colh = tn * BN + half * 128;
-      epilogue_tile(g, tmem, q, half, lane, row, colh, [&] {
+      epilogue_tile(g, tmem, q, half, lane, b, row, colh, [&] {
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(acc_empty0);
       });
@@ -611,30 +634,39 @@ __global__ void __launch_bounds__(P_THREADS, 1)
 // Packing: bf16 E4M3 codes -> bytes, bf16 power-of-two scales -> UE8M0 atoms
 // ---------------------------------------------------------------------------
 struct PackArgs {
-  const uint16_t* codes;  // bf16 [R, K]
+  const uint16_t* codes;  // bf16 [R, K] (or, batched, element strides below)
   const uint16_t* scale;  // bf16 [R, nkb]
   uint8_t* out;           // [R_pad, Kp]
   uint8_t* sf;            // [KT][RT][512]
   int R, K, Kp, nkb, RT, KT;
   int* inexact;           // count of codes / scales not representable (may be null)
+  // batched / transposed sources: batch b's R rows are packed rows
+  // [b * RTb * 128, ...); element (b, r, k) of the codes at b * cb + r * cr +
+  // k * ck, scale (b, r, kb) at b * sb + r * sr + kb * sk; RT = batch * RTb
+  int batch, RTb;
+  int64_t cb, cr, ck, sb, sr, sk;
 };
 
-// One thread: 16 codes of a row (16 bytes out).
+// One thread: 16 codes of a row (16 bytes out); rows of every batch
+// (row-major K: batch b's source rows at b * cb, row stride cr).
 __global__ void k_pack_codes(const __grid_constant__ PackArgs p) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int per_row = p.Kp / 16;
   const int64_t total = (int64_t)p.RT * 128 * per_row;
   if (i >= total) return;
-  const int r = (int)(i / per_row), c0 = (int)(i % per_row) * 16;
+  const int64_t rg = i / per_row;  // packed row over all batches
+  const int c0 = (int)(i % per_row) * 16;
+  const int b = (int)(rg / (p.RTb * 128)), r = (int)(rg % (p.RTb * 128));
   uint32_t w[4] = {0, 0, 0, 0};
   int bad = 0;
   if (r < p.R) {
+    const uint16_t* src = p.codes + (int64_t)b * p.cb + (int64_t)r * p.cr;
 #pragma unroll
     for (int k = 0; k < 16; k += 2) {
       const int c = c0 + k;
       float f0 = 0.f, f1 = 0.f;
-      if (c < p.K) f0 = bf2f(p.codes[(int64_t)r * p.K + c]);
-      if (c + 1 < p.K) f1 = bf2f(p.codes[(int64_t)r * p.K + c + 1]);
+      if (c < p.K) f0 = bf2f(src[c]);
+      if (c + 1 < p.K) f1 = bf2f(src[c + 1]);
       uint16_t b;
       asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(b) : "f"(f1), "f"(f0));
       // exact round trip check
@@ -647,7 +679,7 @@ __global__ void k_pack_codes(const __grid_constant__ PackArgs p) {
       w[k / 4] |= (uint32_t)b << (16 * ((k / 2) & 1));
     }
   }
-  *reinterpret_cast<uint4*>(p.out + (int64_t)r * p.Kp + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+  *reinterpret_cast<uint4*>(p.out + rg * p.Kp + c0) = make_uint4(w[0], w[1], w[2], w[3]);
   if (bad && p.inexact) atomicAdd(p.inexact, bad);
 }
 
@@ -668,6 +700,68 @@ __global__ void k_pack_scales(const __grid_constant__ PackArgs p) {
     e = (uint8_t)(ex == 0 ? 0 : (ex == 0xFF ? 0xFE : ex));
   }
   const int kt = kb / 4, j = kb % 4, rt = r / 128, rr = r % 128;
+  p.sf[((int64_t)kt * p.RT + rt) * 512 + (rr % 32) * 16 + (rr / 32) * 4 + j] = e;
+  if (bad && p.inexact) atomicAdd(p.inexact, 1);
+}
+
+// Batched, transposed codes ([batch, K, R]: rows contiguous): one thread per
+// (packed row, 16 codes along K), packed rows fastest so a warp's loads of
+// each K index are contiguous.
+__global__ void k_pack_codes_t(const __grid_constant__ PackArgs p) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int rows_b = p.RTb * 128, per_row = p.Kp / 16;
+  const int64_t total = (int64_t)p.batch * rows_b * per_row;
+  if (i >= total) return;
+  const int64_t rb = i % ((int64_t)p.batch * rows_b);  // packed row over all batches
+  const int c0 = (int)(i / ((int64_t)p.batch * rows_b)) * 16;
+  const int b = (int)(rb / rows_b), r = (int)(rb % rows_b);
+  uint32_t w[4] = {0, 0, 0, 0};
+  int bad = 0;
+  if (r < p.R) {
+    const uint16_t* src = p.codes + (int64_t)b * p.cb + (int64_t)r * p.cr;
+#pragma unroll
+    for (int k = 0; k < 16; k += 2) {
+      const int c = c0 + k;
+      float f0 = 0.f, f1 = 0.f;
+      if (c < p.K) f0 = bf2f(src[(int64_t)c * p.ck]);
+      if (c + 1 < p.K) f1 = bf2f(src[(int64_t)(c + 1) * p.ck]);
+      uint16_t e;
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(e) : "f"(f1), "f"(f0));
+      uint32_t h2;
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(e));
+      const float g0 = __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFF)));
+      const float g1 = __half2float(__ushort_as_half((unsigned short)(h2 >> 16)));
+      bad += (__float_as_uint(g0) != __float_as_uint(f0) && !(g0 == 0.f && f0 == 0.f));
+      bad += (__float_as_uint(g1) != __float_as_uint(f1) && !(g1 == 0.f && f1 == 0.f));
+      w[k / 4] |= (uint32_t)e << (16 * ((k / 2) & 1));
+    }
+  }
+  *reinterpret_cast<uint4*>(p.out + rb * p.Kp + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+  if (bad && p.inexact) atomicAdd(p.inexact, bad);
+}
+
+// Batched scales at any strides: one thread per (packed row, K block), rows
+// fastest; the UE8M0 byte of its atom ([KT][batch * RTb][512]).
+__global__ void k_pack_scales_b(const __grid_constant__ PackArgs p) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int rows_b = p.RTb * 128;
+  const int64_t rows = (int64_t)p.batch * rows_b;
+  const int kb_all = p.KT * 4;
+  if (i >= rows * kb_all) return;
+  const int64_t rb = i % rows;
+  const int kb = (int)(i / rows);
+  const int b = (int)(rb / rows_b), r = (int)(rb % rows_b);
+  uint8_t e = 127;  // 1.0 for padding rows / blocks
+  int bad = 0;
+  if (r < p.R && kb < p.nkb) {
+    const uint32_t s = p.scale[(int64_t)b * p.sb + (int64_t)r * p.sr + (int64_t)kb * p.sk];
+    const uint32_t ex = (s >> 7) & 0xFF;
+    bad = (s & 0x807Fu) != 0 || ex == 0 || ex == 0xFF;
+    e = (uint8_t)(ex == 0 ? 0 : (ex == 0xFF ? 0xFE : ex));
+  }
+  const int kt = kb / 4, j = kb % 4;
+  const int64_t rt = rb / 128;
+  const int rr = (int)(rb % 128);
   p.sf[((int64_t)kt * p.RT + rt) * 512 + (rr % 32) * 16 + (rr / 32) * 4 + j] = e;
   if (bad && p.inexact) atomicAdd(p.inexact, 1);
 }
@@ -764,6 +858,98 @@ uint8_t* noalloc_scratch_ptr(int* status) {
   return ptrs[dev];
 }
 
+// Launch of either GEMM kernel for `batch` problems (batch 1: one linear).
+int gemm_run(const void* a, const void* a_sf, const void* b, const void* b_sf, int64_t batch,
+             int64_t MTb, int64_t M, int64_t N, int64_t K, int b_shared, const void* bias,
+             const void* residual, int64_t ldr, void* out, int64_t ldo, int64_t out_bs,
+             int32_t out_multicast, int32_t* d_err, void* stream) {
+  if (batch > 1 && (residual || out_multicast)) return VQ_ERR_UNSUPPORTED;
+  if (out_multicast && residual) return VQ_ERR_UNSUPPORTED;
+  if (!a || !a_sf || !b || !b_sf || !out || !d_err) return VQ_ERR_NULL;
+  if (residual && (ldr < N || ldr % 8 || (reinterpret_cast<uintptr_t>(residual) & 15)))
+    return VQ_ERR_UNSUPPORTED;
+  if (M <= 0 || N <= 0 || K <= 0) return VQ_ERR_INVALID;
+  if (N % 8 != 0 || ldo < N || ldo % 8 != 0) return VQ_ERR_UNSUPPORTED;
+  if (M > (1 << 30) || N > (1 << 30)) return VQ_ERR_UNSUPPORTED;
+  if (MTb * 128 < M || batch * MTb >= (1 << 24)) return VQ_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(a) & 15) ||
+      (reinterpret_cast<uintptr_t>(b) & 15) || (reinterpret_cast<uintptr_t>(a_sf) & 15) ||
+      (reinterpret_cast<uintptr_t>(b_sf) & 15))
+    return VQ_ERR_ALIGNMENT;
+  const int64_t KT = (K + 127) / 128, Kp = KT * 128;
+  const int64_t MT = batch * MTb;  // 128-row A tiles over all batches
+  // B is packed over 128-row chunks; a 256-wide tile reads two chunks, so
+  // the packed B must hold an even number of chunks per batch (the caller pads).
+  const int64_t NTILE_N = (N + BN - 1) / BN;
+  const int64_t NT128 = (b_shared ? 1 : batch) * NTILE_N * 2;
+  if (NT128 >= (1 << 24) || (int64_t)NTILE_N * MT >= (1ll << 31)) return VQ_ERR_UNSUPPORTED;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, a, MT * 128, Kp, BM) || !make_map(&mb, b, NT128 * 128, Kp, BN))
+    return VQ_ERR_CUDA;
+  GemmArgs g;
+  g.sfa = (const uint8_t*)a_sf;
+  g.sfb = (const uint8_t*)b_sf;
+  g.bias = (const uint16_t*)bias;
+  g.residual = (const uint16_t*)residual;
+  g.ldr = ldr;
+  g.out = (uint16_t*)out;
+  g.ldo = ldo;
+  g.out_bs = out_bs;
+  g.out_mc = out_multicast ? 1 : 0;
+  g.M = (int)M;
+  g.N = (int)N;
+  g.KT = (int)KT;
+  g.MT = (int)MT;
+  g.NT128 = (int)NT128;
+  g.NTILE_N = (int)NTILE_N;
+  g.MTb = (int)MTb;
+  g.MT2b = (int)((M + 255) / 256);
+  g.b_step = b_shared ? 0 : (int)(NTILE_N * 2);
+  g.ntiles = (int)(batch * MTb * NTILE_N);
+  g.err = d_err;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(d_err, 0, sizeof(int32_t), st) != cudaSuccess) return VQ_ERR_CUDA;
+  if (M >= 256 && pair_enabled()) {
+    // CTA pairs: 256 x 256 tiles, B loaded in 128-row halves; scale atoms
+    // through plain (unswizzled) maps of 256-byte rows
+    CUtensorMap mbh, msa, msb;
+    if (!make_map(&mbh, b, NT128 * 128, Kp, 128) ||
+        !make_map_plain(&msa, a_sf, (uint64_t)KT * MT * 2, 256, 256, 2) ||
+        !make_map_plain(&msb, b_sf, (uint64_t)KT * NT128 * 2, 256, 256, 4))
+      return VQ_ERR_CUDA;
+    GemmArgs gp = g;
+    gp.ntiles = (int)(batch * g.MT2b * NTILE_N);
+    const int smem = P_SMEM + 1024;
+    if (cudaFuncSetAttribute(k_gemm_mxf8_pair, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem) != cudaSuccess)
+      return VQ_ERR_CUDA;
+    const int pairs = (int)std::min<int64_t>(gp.ntiles, sm_count() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(P_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, k_gemm_mxf8_pair, ma, mbh, msa, msb, gp) != cudaSuccess)
+      return VQ_ERR_CUDA;
+    return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
+  }
+  const int smem = SmemLayout::kTotal + 1024;
+  if (cudaFuncSetAttribute(k_gemm_mxf8, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
+    return VQ_ERR_CUDA;
+  const int grid = (int)std::min<int64_t>(g.ntiles, sm_count());
+  k_gemm_mxf8<<<grid, THREADS + 32, smem, st>>>(ma, mb, g);
+  return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
+}
+
+
 }  // namespace mx
 namespace attn {
 int sticky_attn(int* out, int clear, cudaStream_t st);
@@ -815,6 +1001,9 @@ int vq_mx_pack(const vq_tensor* codes, const vq_tensor* scale, int64_t block_siz
   p.Kp = p.KT * 128;
   p.nkb = (int)((K + 31) / 32);
   p.inexact = d_inexact;
+  p.batch = 1;
+  p.RTb = p.RT;
+  p.cb = 0, p.cr = K, p.ck = 1, p.sb = 0, p.sr = p.nkb, p.sk = 1;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (d_inexact && cudaMemsetAsync(d_inexact, 0, sizeof(int32_t), st) != cudaSuccess)
     return VQ_ERR_CUDA;
@@ -822,6 +1011,63 @@ int vq_mx_pack(const vq_tensor* codes, const vq_tensor* scale, int64_t block_siz
   k_pack_codes<<<(unsigned)((n1 + 255) / 256), 256, 0, st>>>(p);
   const int64_t n2 = (int64_t)p.RT * 128 * p.KT * 4;
   k_pack_scales<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
+}
+
+int vq_mx_pack_batched(const vq_tensor* codes, const vq_tensor* scale, int64_t block_size,
+                       int32_t row_multiple, int32_t k_axis, void* packed_codes, void* packed_sf,
+                       int32_t* d_inexact, void* stream) {
+  if (!codes || !scale || !packed_codes || !packed_sf) return VQ_ERR_NULL;
+  if (codes->dtype != VQ_BF16 || scale->dtype != VQ_BF16) return VQ_ERR_UNSUPPORTED;
+  if (block_size != 32) return VQ_ERR_UNSUPPORTED;
+  if (codes->ndim != 3 || scale->ndim != 3) return VQ_ERR_SHAPE;
+  if (k_axis != 1 && k_axis != 2) return VQ_ERR_INVALID;
+  if (row_multiple != 128 && row_multiple != 256) return VQ_ERR_INVALID;
+  const int64_t B = codes->shape[0];
+  const int64_t R = k_axis == 2 ? codes->shape[1] : codes->shape[2];
+  const int64_t K = k_axis == 2 ? codes->shape[2] : codes->shape[1];
+  const int64_t nkb = (K + 31) / 32;
+  if (scale->shape[0] != B) return VQ_ERR_SHAPE;
+  if (k_axis == 2 && (scale->shape[1] != R || scale->shape[2] != nkb)) return VQ_ERR_SHAPE;
+  if (k_axis == 1 && (scale->shape[1] != nkb || scale->shape[2] != R)) return VQ_ERR_SHAPE;
+  if (B <= 0 || R <= 0 || K <= 0) return VQ_ERR_INVALID;
+  const int64_t RTb = (R + row_multiple - 1) / row_multiple * (row_multiple / 128);
+  if (B * RTb * 128 >= (1ll << 31) / 4 || K >= (1 << 24)) return VQ_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(packed_codes) & 15) || (reinterpret_cast<uintptr_t>(packed_sf) & 15))
+    return VQ_ERR_ALIGNMENT;
+  PackArgs p;
+  p.codes = (const uint16_t*)codes->data;
+  p.scale = (const uint16_t*)scale->data;
+  p.out = (uint8_t*)packed_codes;
+  p.sf = (uint8_t*)packed_sf;
+  p.R = (int)R;
+  p.K = (int)K;
+  p.KT = (int)((K + 127) / 128);
+  p.Kp = p.KT * 128;
+  p.nkb = (int)nkb;
+  p.batch = (int)B;
+  p.RTb = (int)RTb;
+  p.RT = (int)(B * RTb);
+  p.inexact = d_inexact;
+  p.cb = R * K;
+  p.sb = R * nkb;
+  if (k_axis == 2) {
+    p.cr = K, p.ck = 1, p.sr = nkb, p.sk = 1;
+  } else {
+    p.cr = 1, p.ck = R, p.sr = 1, p.sk = R;
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (d_inexact && cudaMemsetAsync(d_inexact, 0, sizeof(int32_t), st) != cudaSuccess)
+    return VQ_ERR_CUDA;
+  if (k_axis == 2) {
+    const int64_t n1 = B * RTb * 128 * (p.Kp / 16);
+    k_pack_codes<<<(unsigned)((n1 + 255) / 256), 256, 0, st>>>(p);
+  } else {
+    const int64_t n1 = B * RTb * 128 * (p.Kp / 16);
+    k_pack_codes_t<<<(unsigned)((n1 + 255) / 256), 256, 0, st>>>(p);
+  }
+  const int64_t n2 = B * RTb * 128 * p.KT * 4;
+  k_pack_scales_b<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
 }
 
@@ -836,83 +1082,20 @@ int vq_gemm_mxf8_ex(const void* a, const void* a_sf, const void* b, const void* 
                     int64_t N, int64_t K, const void* bias, const void* residual, int64_t ldr,
                     void* out, int64_t ldo, int32_t out_multicast, int32_t* d_err,
                     void* stream) {
-  if (out_multicast && residual) return VQ_ERR_UNSUPPORTED;
-  if (!a || !a_sf || !b || !b_sf || !out || !d_err) return VQ_ERR_NULL;
-  if (residual && (ldr < N || ldr % 8 || (reinterpret_cast<uintptr_t>(residual) & 15)))
-    return VQ_ERR_UNSUPPORTED;
-  if (M <= 0 || N <= 0 || K <= 0) return VQ_ERR_INVALID;
-  if (N % 8 != 0 || ldo < N || ldo % 8 != 0) return VQ_ERR_UNSUPPORTED;
-  if (M > (1 << 30) || N > (1 << 30)) return VQ_ERR_UNSUPPORTED;
-  if ((reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(a) & 15) ||
-      (reinterpret_cast<uintptr_t>(b) & 15) || (reinterpret_cast<uintptr_t>(a_sf) & 15) ||
-      (reinterpret_cast<uintptr_t>(b_sf) & 15))
-    return VQ_ERR_ALIGNMENT;
-  const int64_t KT = (K + 127) / 128, Kp = KT * 128;
-  const int64_t MT = (M + 127) / 128;
-  // B is packed over 128-row chunks; a 256-wide tile reads two chunks, so
-  // the packed B must hold an even number of chunks (the caller pads).
-  const int64_t NTILE_N = (N + BN - 1) / BN;
-  CUtensorMap ma, mb;
-  if (!make_map(&ma, a, MT * 128, Kp, BM) || !make_map(&mb, b, NTILE_N * 2 * 128, Kp, BN))
-    return VQ_ERR_CUDA;
-  GemmArgs g;
-  g.sfa = (const uint8_t*)a_sf;
-  g.sfb = (const uint8_t*)b_sf;
-  g.bias = (const uint16_t*)bias;
-  g.residual = (const uint16_t*)residual;
-  g.ldr = ldr;
-  g.out = (uint16_t*)out;
-  g.ldo = ldo;
-  g.out_mc = out_multicast ? 1 : 0;
-  g.M = (int)M;
-  g.N = (int)N;
-  g.KT = (int)KT;
-  g.MT = (int)MT;
-  g.NT128 = (int)(NTILE_N * 2);
-  g.NTILE_N = (int)NTILE_N;
-  g.ntiles = (int)(MT * NTILE_N);
-  g.err = d_err;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(d_err, 0, sizeof(int32_t), st) != cudaSuccess) return VQ_ERR_CUDA;
-  if (M >= 256 && pair_enabled()) {
-    // CTA pairs: 256 x 256 tiles, B loaded in 128-row halves; scale atoms
-    // through plain (unswizzled) maps of 256-byte rows
-    CUtensorMap mbh, msa, msb;
-    if (!make_map(&mbh, b, NTILE_N * 2 * 128, Kp, 128) ||
-        !make_map_plain(&msa, a_sf, (uint64_t)KT * MT * 2, 256, 256, 2) ||
-        !make_map_plain(&msb, b_sf, (uint64_t)KT * NTILE_N * 2 * 2, 256, 256, 4))
-      return VQ_ERR_CUDA;
-    GemmArgs gp = g;
-    const int64_t MT2 = (M + 255) / 256;
-    gp.ntiles = (int)(MT2 * NTILE_N);
-    const int smem = P_SMEM + 1024;
-    if (cudaFuncSetAttribute(k_gemm_mxf8_pair, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             smem) != cudaSuccess)
-      return VQ_ERR_CUDA;
-    const int pairs = (int)std::min<int64_t>(gp.ntiles, sm_count() / 2);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(P_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, k_gemm_mxf8_pair, ma, mbh, msa, msb, gp) != cudaSuccess)
-      return VQ_ERR_CUDA;
-    return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
-  }
-  const int smem = SmemLayout::kTotal + 1024;
-  if (cudaFuncSetAttribute(k_gemm_mxf8, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-      cudaSuccess)
-    return VQ_ERR_CUDA;
-  const int grid = (int)std::min<int64_t>(g.ntiles, sm_count());
-  k_gemm_mxf8<<<grid, THREADS + 32, smem, st>>>(ma, mb, g);
-  return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
+  return gemm_run(a, a_sf, b, b_sf, 1, (M + 127) / 128, M, N, K, 0, bias, residual, ldr, out, ldo,
+                  0, out_multicast, d_err, stream);
+}
+
+int vq_gemm_mxf8_batched(const void* a, const void* a_sf, const void* b, const void* b_sf,
+                         int64_t batch, int64_t a_rows_per_batch, int64_t M, int64_t N, int64_t K,
+                         int32_t b_shared, const void* bias, void* out, int64_t ldo,
+                         int64_t out_batch_stride, int32_t* d_err, void* stream) {
+  if (batch <= 0 || a_rows_per_batch <= 0 || a_rows_per_batch % 128) return VQ_ERR_INVALID;
+  if (a_rows_per_batch < M || out_batch_stride < 0) return VQ_ERR_INVALID;
+  if (batch > 1 && out_batch_stride < M * ldo) return VQ_ERR_INVALID;
+  if (out_batch_stride % 8) return VQ_ERR_ALIGNMENT;
+  return gemm_run(a, a_sf, b, b_sf, batch, a_rows_per_batch / 128, M, N, K, b_shared ? 1 : 0, bias,
+                  nullptr, 0, out, ldo, out_batch_stride, 0, d_err, stream);
 }
 
 int vq_linear_mxf8_noalloc(const vq_tensor* a_codes, const vq_tensor* a_scale,

@@ -131,6 +131,13 @@ _SIGNATURES = {
     "vq_tp_barrier": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                      ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p,
                                      ctypes.c_void_p]),
+    "vq_mx_pack_batched": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_int64,
+                                          ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_gemm_mxf8_batched": (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 5
+                             + [ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+                                ctypes.c_void_p]),
     "vq_tp_barrier_ex": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                         ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint64,
                                         ctypes.c_void_p, ctypes.c_void_p]),

@@ -98,8 +98,15 @@ def matmul_mx(self, other, *, input_scale=None, weight_scale=None, block_size=No
               input_code=None, weight_code=None, A_data=None, A_indices=None, A_indptr=None,
               weight_layout="ck"):
     assert weight_layout in ("kc", "ck"), weight_layout
+    from voyager_b200 import mxgemm
+
     sp = _outliers(A_data, A_indices, A_indptr, other, weight_scale, weight_code, block_size,
                    weight_layout)
+    if mxgemm.matmul_applies(self, other, input_scale, weight_scale, block_size, input_code,
+                             weight_code, weight_layout):
+        out = mxgemm.matmul(self, other, input_scale, weight_scale, weight_layout)
+        if out is not None:
+            return out if sp is None else out + sp
     a = dequantize_mx(self, input_scale, input_code, block_size)
     b = dequantize_mx(other, weight_scale, weight_code, block_size)
     if weight_layout == "kc":

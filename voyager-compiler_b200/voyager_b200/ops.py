@@ -264,6 +264,13 @@ def quantize_mx(input: torch.Tensor, qmap: torch.Tensor, axes, block_size: int,
         from voyager_b200 import mxgemm
 
         mxgemm.vouch(codes, scale)
+    elif (block_size == 32 and x.dim() >= 2 and ax == [x.dim() - 2] and force_scale_power_of_two
+          and scale_qmap is None and x.dtype == torch.bfloat16
+          and rd.c.kind == _lib.VQ_R_MINIFLOAT and rd.c.hw == 1):
+        # blocks along dim -2: the right operand of a matmul_mx stored [.., K, N]
+        from voyager_b200 import mxgemm
+
+        mxgemm.vouch(codes, scale, axis=-2)
     return scale, codes
 
 
