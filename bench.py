@@ -61,7 +61,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default=None,
-                    choices=["c1", "c2", "c3", "c4", "c5", "attn", "outlier", "spmm"],
+                    choices=["c1", "c2", "c3", "c4", "c5", "attn", "outlier", "spmm", "dq"],
                     help="profiling aid: run only this workload's kernels, no JSON line")
     return ap.parse_args()
 
@@ -674,7 +674,11 @@ def run_secondary(dev, hbm_peak, peaks):
     except Exception as e:  # report, do not hide
         out["c3_error"] = repr(e)[:200]
     try:
-        out["c4_w4a8_sweep"] = run_c4_sweep(dev, hbm_peak)
+        out["c2_weight_linear"] = run_dq_linear(dev, peaks)
+    except Exception as e:
+        out["c2_weight_linear_error"] = repr(e)[:200]
+    try:
+        out["c4_w4a8_sweep"] = run_c4_sweep(dev, hbm_peak, peaks.get("bf16_tflops", 1590.0))
     except Exception as e:
         out["c4_error"] = repr(e)[:200]
     try:
@@ -682,6 +686,56 @@ def run_secondary(dev, hbm_peak, peaks):
     except Exception as e:
         out["outlier_error"] = repr(e)[:200]
     return out
+
+
+def dq_weights(dev, w):
+    """C2's three weight formats applied to a bf16 weight [N, K], as the
+    reference's convert stores them: (name, codes, scale, codebook, block)."""
+    import torch
+
+    from voyager_b200.tables import get_quantization_map, index_table
+
+    Q = torch.ops.quantized_ops
+    lut = get_quantization_map("lut4")
+    levels = torch.unique(lut.float()).bfloat16().to(dev)
+    s_nf4, c_nf4 = Q.quantize_mx(w, index_table(lut).to(dev), [-1], 64, 1.0)
+    K = w.shape[1]
+    s_p8, c_p8 = Q.quantize_mx(w, get_quantization_map("posit8_1", dev), [-1], 32, 4096.0)
+    s_i8, c_i8 = Q.quantize_mx(w, get_quantization_map("int8", dev), [-1], K, 127.0)
+    return [("nf4_g64", c_nf4, s_nf4, levels, 64), ("posit8_bs32", c_p8, s_p8, None, 32),
+            ("int8_per_row", c_i8, s_i8, None, K), ("bf16", w, None, None, None)]
+
+
+def run_dq_linear(dev, peaks):
+    """linear_mx with C2's weight formats (NF4 g64 + codebook, posit8_1 block
+    32, int8 per row) and a plain bf16 weight at C3's shape: bf16 activations
+    [8192, 4096] x weight [11008, 4096], the weight read back inside the
+    tcgen05 bf16 GEMM.  TFLOP/s and the fraction of the measured bf16 peak."""
+    import torch
+
+    from voyager_b200 import dqgemm, synth
+
+    Q = torch.ops.quantized_ops
+    stream = torch.cuda.current_stream(dev)
+    a_np, w_np = synth.c3_operands()
+    a = torch.from_numpy(a_np.view(np.int16)).view(torch.bfloat16).to(dev)
+    w = torch.from_numpy(w_np.view(np.int16)).view(torch.bfloat16).to(dev)
+    peak = peaks.get("bf16_tflops", 1590.0)
+    fl = 2.0 * 8192 * 4096 * 11008
+    res = {}
+    for name, c, sc, cb, bs in dq_weights(dev, w):
+        fn = lambda: Q.linear_mx(a, c, None, weight_scale=sc, block_size=bs, weight_code=cb)
+        fn()
+        pw = dqgemm.packed_weight(c, sc, cb, bs, "kc")
+        ms = _time_ms(fn, stream, reps=10)
+        tf = fl / (ms / 1e3) / 1e12
+        res[name] = {"ms": round(ms, 4), "TFLOPs": round(tf, 1), "frac_bf16": round(tf / peak, 3),
+                     "path": {0: "tcgen05 bf16 (weight by TMA)", 1: "tcgen05 bf16, 4-bit palette "
+                              "decoded in smem", 2: "tcgen05 bf16, 8-bit palette decoded in smem"}
+                     [pw.mode] if pw is not None else "dequant + torch"}
+    res["note"] = ("M=8192 K=4096 N=11008, bf16 activations; denominator: measured cuBLAS bf16 "
+                   "burst")
+    return res
 
 
 def outlier_c3_operands(dev):
@@ -786,7 +840,7 @@ def c4_operands(dev, m, k, n, seed, keep_input=False):
     return ca, sa, cw, sw
 
 
-def run_c4_sweep(dev, hbm_peak):
+def run_c4_sweep(dev, hbm_peak, bf16_peak):
     """C4: W4A8 linear over M x (K, N); TFLOP/s per point, and packed-byte
     GB/s (fraction of HBM) for the weight-streaming points M <= 16."""
     import torch
@@ -812,11 +866,14 @@ def run_c4_sweep(dev, hbm_peak):
             fl = 2.0 * m * n * k
             pt = {"M": m, "K": k, "N": n, "ms": round(ms, 4),
                   "TFLOPs": round(fl / (ms / 1e3) / 1e12, 2),
-                  "path": "packed-weight mma" if w4a8.applies_small(ca, cw) else "dequant + cuBLAS bf16"}
+                  "path": "packed-weight mma" if w4a8.applies_small(ca, cw)
+                  else "tcgen05 bf16, NVFP4 weight decoded in smem"}
             if m <= 16:
                 byts = n * k * (0.5 + 1 / 16) + m * k * (1 + 1 / 32) + 2 * m * n
                 pt["GBps"] = round(byts / (ms / 1e3) / 1e9, 1)
                 pt["frac_hbm"] = round(pt["GBps"] / hbm_peak, 3)
+            else:
+                pt["frac_bf16"] = round(pt["TFLOPs"] / bf16_peak, 3)
             res.append(pt)
         del ca0, sa0, cw, sw, a0
         torch.cuda.empty_cache()
@@ -888,6 +945,16 @@ def run_only(args):
         d2, i2, p2 = d[:n].contiguous(), i[:n].contiguous(), p[:rows + 1].contiguous()
         for _ in range(args.warmup + args.steps):
             Q.spmm_csr(d2, i2, p2, cw, sw, None, 32, "kc")
+    elif args.only == "dq":
+        from voyager_b200 import synth as sy
+
+        a_np, w_np = sy.c3_operands()
+        a = torch.from_numpy(a_np.view(np.int16)).view(torch.bfloat16).to(dev)
+        w = torch.from_numpy(w_np.view(np.int16)).view(torch.bfloat16).to(dev)
+        fmts = dq_weights(dev, w)
+        for _ in range(args.warmup + args.steps):
+            for name, c, sc, cb, bs in fmts:
+                Q.linear_mx(a, c, None, weight_scale=sc, block_size=bs, weight_code=cb)
     elif args.only == "c4":
         from voyager_b200 import w4a8
 

@@ -265,6 +265,56 @@ int vq_gemm_mxf8_batched(const void* a, const void* a_sf, const void* b, const v
                          int32_t b_shared, const void* bias, void* out, int64_t ldo,
                          int64_t out_batch_stride, int32_t* d_err, void* stream);
 
+/* ---- bf16 tcgen05 GEMM with the weight dequantized in shared memory --------
+ * quantized_ops::linear_mx / matmul_mx (src/voyager_compiler/ops/
+ * quantized.py:455-472, 522-648) for every operand format but MXFP8 x
+ * MXFP8: the weight read back as bf16(decode(code) * scale) -- the
+ * reference's _dequantize_mx, one bf16 rounding of the exact product --
+ * inside the kernel, times bf16 activations, float32 sums, bf16 out:
+ *   out[b][m, n] = sum_k A[b][m, k] W[b][n, k] (+ bias[n]).
+ * a    bf16 [batch * M, K] row-major (K a multiple of 8, 16-byte aligned)
+ * mode 0 (TMA): w is a bf16 weight [wb * N, K] (the library's plain bf16 GEMM);
+ *      1 (LUT4) / 2 (LUT8): w holds palette indices as vq_dq_pack writes
+ *      them, palette bf16 [16 | 256], w_scale4 the quarter-step scales of
+ *      vq_dq_pack_scales (or NULL: no scale); all 16-byte aligned.
+ * wb = 1 when w_shared (one weight for every batch), else batch.
+ * out bf16 [batch][M, ldo] at out + b * out_batch_stride; N, ldo multiples of 8.
+ * *d_err (device) is zeroed and set non-zero (11-14) if a bounded wait gave up. */
+int vq_gemm_dq(const void* a, int64_t batch, int64_t M, int64_t K, int32_t mode, const void* w,
+               int32_t w_shared, int64_t N, const void* w_scale4, const void* palette,
+               const void* bias, void* out, int64_t ldo, int64_t out_batch_stride, int32_t* d_err,
+               void* stream);
+/* Bytes of the packed indices and quarter-step scales of wbatch weights
+ * [N, K] (mode 1: 4-bit, 2: 8-bit): with KS = ceil(K / 64) and Npad = N
+ * rounded up to 256, wbatch * KS * Npad * (32 | 64) and wbatch * KS * Npad * 8. */
+int vq_dq_pack_sizes(int64_t wbatch, int64_t N, int64_t K, int32_t mode, int64_t* codes_bytes,
+                     int64_t* scale_bytes);
+/* Weight codes bf16 [wbatch * N, K] -> palette indices, step-major:
+ * [wbatch][KS][Npad][32 | 64 bytes] (element k of a row in step k / 64, LUT4
+ * nibbles low first; rows N..Npad zero).  index_mode 1: each code is the
+ * index itself (a codebook's stored indices, quantized.py:323-337; npal =
+ * the palette size); 0: the code's bf16 bit pattern is looked up in
+ * keys[npal] (ascending bit patterns) and stored as key_index[i] (a palette
+ * position, below 16 / 256).  *d_missing (device, may be NULL) counts codes
+ * with no entry. */
+int vq_dq_pack(const vq_tensor* codes, int64_t wbatch, int32_t mode, int32_t index_mode,
+               const void* keys, const void* key_index, int32_t npal, void* out,
+               int32_t* d_missing, void* stream);
+/* Block scales bf16 [wbatch * N, nkb] (blocks of block_size, a power of two
+ * >= 16, along K; nkb == 1: one per row) -> the scale of every 16-element
+ * quarter of each 64-element step, [wbatch][KS][Npad][4] bf16. */
+int vq_dq_pack_scales(const void* scale, int64_t wbatch, int64_t N, int64_t K, int64_t nkb,
+                      int64_t block_size, void* out, void* stream);
+/* present[bits] = 1 for every bf16 bit pattern in codes (65,536 bytes, zeroed here). */
+int vq_dq_patterns(const vq_tensor* codes, void* present, void* stream);
+/* The GEMM's weight decode alone: out bf16 [N, K] = the dequantized weight
+ * (the first of the packed batches). */
+int vq_dq_decode(const void* w, int64_t N, int64_t K, int32_t mode, const void* w_scale4,
+                 const void* palette, void* out, void* stream);
+/* dst[b][c][r] = src[b][r][c], bf16 [batch][rows, cols]. */
+int vq_transpose_bf16(const void* src, int64_t batch, int64_t rows, int64_t cols, void* dst,
+                      void* stream);
+
 /* MXFP8 linear that allocates nothing: for callers that cannot call
  * cudaMalloc -- an allocator-free runtime, code running under a caller-owned
  * memory budget, or a library hook invoked where allocating is not allowed.

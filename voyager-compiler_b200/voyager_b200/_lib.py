@@ -138,6 +138,25 @@ _SIGNATURES = {
                              + [ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                 ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
                                 ctypes.c_void_p]),
+    "vq_gemm_dq": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                  ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
+                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                  ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                  ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_dq_pack_sizes": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                        ctypes.c_int32, P(ctypes.c_int64), P(ctypes.c_int64)]),
+    "vq_dq_pack": (ctypes.c_int, [P(VqTensor), ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                                  ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_dq_pack_scales": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_dq_patterns": (ctypes.c_int, [P(VqTensor), ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_dq_decode": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_void_p]),
+    "vq_transpose_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
     "vq_tp_barrier_ex": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                         ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint64,
                                         ctypes.c_void_p, ctypes.c_void_p]),

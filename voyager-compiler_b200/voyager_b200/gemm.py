@@ -8,8 +8,12 @@ Paths, chosen per call:
   * MXFP8 x MXFP8 (E4M3 codes, power-of-two block-32 scales along K on both
     operands, bf16): the tcgen05 block-scaled GEMM in ``libvoyager_b200``
     (``voyager_b200.mxgemm``), weights packed once and cached;
-  * everything else: the operands are dequantized by this library's kernels
-    and multiplied by cuBLAS (bf16, float32 accumulate).
+  * every other bf16 operand pair: the tcgen05 bf16 GEMM
+    (``voyager_b200.dqgemm``), the weight read back from palette indices in
+    shared memory (or, when it does not fit that form, by this library's
+    dequantize kernels), the activations by the dequantize kernels;
+  * float32 / float16 operands: dequantized by this library's kernels and
+    multiplied by torch (the tcgen05 kernels multiply bf16 and FP8).
 With the outlier CSR side-stream (``A_data`` / ``A_indices`` / ``A_indptr``)
 the result is the dense product plus ``spmm_csr`` of the CSR with the
 decoded weight (``quantized.py:560-574``, ``:625-637``); on the MXFP8 path
@@ -86,6 +90,12 @@ def linear_mx(input, weight, bias=None, *, input_scale=None, weight_scale=None,
             out = mxgemm.linear(input, weight, bias, input_scale, weight_scale, residual=res)
             if out is not None:
                 return out
+    from voyager_b200 import dqgemm
+
+    out = dqgemm.linear(input, weight, bias, input_scale, weight_scale, block_size, input_code,
+                        weight_code, weight_layout)
+    if out is not None:
+        return out if sp is None else out + sp
     a = dequantize_mx(input, input_scale, input_code, block_size)
     w = _weight_dequant(weight, weight_scale, weight_code, block_size)
     if weight_layout == "ck":
@@ -107,6 +117,12 @@ def matmul_mx(self, other, *, input_scale=None, weight_scale=None, block_size=No
         out = mxgemm.matmul(self, other, input_scale, weight_scale, weight_layout)
         if out is not None:
             return out if sp is None else out + sp
+    from voyager_b200 import dqgemm
+
+    out = dqgemm.matmul(self, other, input_scale, weight_scale, block_size, input_code,
+                        weight_code, weight_layout)
+    if out is not None:
+        return out if sp is None else out + sp
     a = dequantize_mx(self, input_scale, input_code, block_size)
     b = dequantize_mx(other, weight_scale, weight_code, block_size)
     if weight_layout == "kc":

@@ -15,8 +15,10 @@ Paths:
     permuted at pack time, f16 mma.sync tiles on exact operands (weights
     times their E4M3 scales, raw E4M3 token codes), token scales on the
     float32 block sums, split-K finished by the last CTA of each row block;
-  * larger M (compute-bound): both operands dequantized by this library's
-    kernels (the weight once, cached) and multiplied by cuBLAS in bf16.
+  * larger M (compute-bound): the tcgen05 bf16 GEMM (``voyager_b200.dqgemm``)
+    with the weight kept as 4-bit palette indices and its E4M3 block-16
+    scales, read back in shared memory (code x scale, exact in bf16), and
+    the activations read back by the dequantize kernel.
 """
 
 import ctypes
@@ -117,6 +119,13 @@ def linear(a_codes: torch.Tensor, a_scale: torch.Tensor, w_codes: torch.Tensor,
                 ctypes.c_void_p(done.data_ptr()), out.data_ptr(), _ops._stream(dev)),
                 "w4a8 linear")
             return out.reshape(tuple(lead) + (N,))
+    from voyager_b200 import dqgemm
+
     a = _ops.dequantize(a_codes, a_scale, None, None, 32)
+    pw = dqgemm.packed_weight(w_codes, w_scale, None, 16, "kc")
+    if pw is not None and K % 8 == 0 and (bias is None or bias.dtype == torch.bfloat16):
+        a2 = a.reshape(M, K)
+        return dqgemm.gemm(a2 if a2.is_contiguous() else a2.contiguous(), pw,
+                           bias).reshape(tuple(lead) + (N,))
     w = _dequant_weight(w_codes, w_scale)
     return F.linear(a, w, bias)
