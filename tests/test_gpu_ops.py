@@ -57,7 +57,7 @@ def test_golden_case(case):
         elif case["op"] == "sdpa_mx":
             # float32 sums in another order and a hardware exp: the same
             # bound as tests/test_gpu_attention.py, against the reference
-            assert G.rel_l2(g, w) < 2e-3
+            assert G.rel_l2(g, w) < 1e-3
         else:
             bad = G.bit_mismatches(g, w)
             assert len(bad) == 0, f"{len(bad)} mismatches, first at {bad[:5]}"

@@ -33,21 +33,28 @@
 //
 // Kernel: CTA pairs (cluster of 2, tcgen05.mma.cta_group::2.kind::f16, bf16
 // inputs, float32 accumulator), 256 x 256 output tiles, persistent over the
-// tiles.  Per CTA (22 warps):
-//   warp 0      producer: per 64-element K step, this CTA's 128 rows of A by
-//               TMA (counted on the even CTA's "full" barrier) and either its
-//               128-row half of a bf16 weight by TMA (TMA mode) or the step's
-//               packed indices and scales of its 128 weight rows by bulk copy
-//               into the stage (on this CTA's "raw" barrier);
+// tiles.  Per CTA:
+//   warp 0      per 64-element K step, once the stage is free, this CTA's
+//               128 rows of A by TMA (and, TMA mode, its 128-row half of the
+//               bf16 weight), counted on the even CTA's "full" barrier;
 //   warp 1      (even CTA) TMEM owner and MMA issuer: 4 x M256 N256 K16 per
 //               step into one of two accumulators (512 TMEM columns), so the
 //               epilogue of a tile overlaps the next tile's MMAs;
-//   warps 2-17  (LUT modes) weight decoders, four groups of 4 taking every
-//               fourth step: once a stage's raw bytes land, each thread
-//               decodes the step's 64 elements of one weight row from shared
-//               memory into the stage's weight tile, then the warp arrives on
-//               the even CTA's "full" barrier after a proxy fence;
-//   warps 18-21 epilogue: one TMEM lane quarter each, 32 columns at a time,
+//   LUT modes:
+//   warp 2      the packed indices and scales of this CTA's 128 weight rows,
+//               step by step, by bulk copy into "raw" slots (RSG per decoder
+//               group, used by that group's steps in turn; a slot is
+//               refilled once its decoders have read it), so the weight bytes
+//               are on chip long before their stage frees up.  Each group
+//               waits on its own slots in order, so no wait can mistake a
+//               phase two ahead for the one before (mbarrier parity);
+//   warps 3-18  weight decoders, four groups of 4 taking every fourth step:
+//               each thread reads the step's indices and scales of one weight
+//               row, hands the slot back, and once the stage is free writes
+//               the row's 64 bf16 values into the stage's weight tile; the
+//               warp then arrives on the even CTA's "full" barrier after a
+//               proxy fence;
+//   last 4 warps epilogue: one TMEM lane quarter each, 32 columns at a time,
 //               + bias, bf16, row stores; the accumulator is handed back as
 //               soon as its loads land.
 // Every wait is bounded by %globaltimer and records an error code instead
@@ -73,30 +80,51 @@ constexpr int A_BYTES = 128 * 128;         // this CTA's 128 rows x 128 bytes
 constexpr int B_BYTES = 128 * 128;         // this CTA's half of the weight tile
 constexpr int TMEM_COLS = 512;             // two 256-column accumulators
 constexpr int DQ_GROUPS = 4, DQ_WARPS = 4, EPI_WARPS = 4;  // DQ_WARPS per group
-constexpr int EPI_WARP0 = 2 + DQ_GROUPS * DQ_WARPS;
-constexpr int THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
+constexpr int DEC_WARP0 = 3;               // the first decoder warp (LUT modes)
 constexpr int PAL8_BYTES = 256 * 32 * 4;   // LUT8 palette, one copy per bank
 constexpr int SCALE_BYTES = 128 * 8;       // a step's scales of 128 rows
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int BAR_BYTES = 512;
 
 enum { MODE_TMA = 0, MODE_LUT4 = 1, MODE_LUT8 = 2 };
 enum { ERR_FULL = 11, ERR_EMPTY = 12, ERR_ACC = 13, ERR_DRAIN = 14 };
 
 template <int MODE>
 struct Cfg {
+  static constexpr bool LUT = MODE != MODE_TMA;
   static constexpr int STEP_BYTES = MODE == MODE_LUT4 ? 32 : 64;  // indices per row and step
-  static constexpr int RAW_BYTES = MODE == MODE_TMA ? 0 : 128 * STEP_BYTES + SCALE_BYTES;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + RAW_BYTES;
-  static constexpr int STAGES = MODE == MODE_TMA ? 6 : (MODE == MODE_LUT4 ? 5 : 4);
-  static constexpr int PAL_BYTES = MODE == MODE_LUT8 ? PAL8_BYTES : 0;
-  static constexpr int BARS = STAGES * STAGE_BYTES + PAL_BYTES;
-  static constexpr int SMEM = BARS + 256;
+  static constexpr int RAW_BYTES = LUT ? 128 * STEP_BYTES + SCALE_BYTES : 0;  // one raw slot
+  static constexpr int STAGES = MODE == MODE_LUT4 ? 5 : (MODE == MODE_LUT8 ? 4 : 6);
+  static constexpr int RSG = MODE == MODE_LUT4 ? 3 : (MODE == MODE_LUT8 ? 1 : 0);  // per group
+  static constexpr int RSLOTS = RSG * DQ_GROUPS;
+  static constexpr int RAW0 = STAGES * STAGE_BYTES;           // the raw ring
+  static constexpr int PAL0 = RAW0 + RSLOTS * RAW_BYTES;      // LUT8 palette
+  static constexpr int BARS = PAL0 + (MODE == MODE_LUT8 ? PAL8_BYTES : 0);
+  static constexpr int SMEM = BARS + BAR_BYTES;
+  static constexpr int EPI_WARP0 = LUT ? DEC_WARP0 + DQ_GROUPS * DQ_WARPS : 2;
+  static constexpr int THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
 };
 static_assert(Cfg<MODE_TMA>::SMEM + 1024 <= 227 * 1024, "TMA-mode shared memory");
 static_assert(Cfg<MODE_LUT4>::SMEM + 1024 <= 227 * 1024, "LUT4 shared memory");
 static_assert(Cfg<MODE_LUT8>::SMEM + 1024 <= 227 * 1024, "LUT8 shared memory");
-static_assert(Cfg<MODE_LUT4>::STAGE_BYTES % 1024 == 0 && Cfg<MODE_LUT8>::STAGE_BYTES % 1024 == 0,
-              "stages stay 1024-byte aligned");
-static_assert((3 * 6 + 6) * 8 <= 256, "barrier area");
+static_assert(STAGE_BYTES % 1024 == 0 && Cfg<MODE_LUT4>::RAW_BYTES % 16 == 0 &&
+                  Cfg<MODE_LUT8>::RAW_BYTES % 16 == 0,
+              "stages 1024-byte aligned, raw slots 16-byte aligned");
+static_assert((2 * 5 + 2 * 12 + 6) * 8 <= BAR_BYTES && (2 * 6 + 6) * 8 <= BAR_BYTES, "barrier area");
+// A decoder group waits on the "empty" barrier of every DQ_GROUPS-th step;
+// with at least DQ_GROUPS stages the phase it waits for is never two ahead.
+static_assert(Cfg<MODE_LUT4>::STAGES >= DQ_GROUPS && Cfg<MODE_LUT8>::STAGES >= DQ_GROUPS,
+              "decoder empty waits need STAGES >= DQ_GROUPS");
+
+// Raw slot and phase parity of step st: the group's j-th step uses its slot
+// j % RSG.
+template <int MODE>
+__device__ __forceinline__ void raw_slot(int st, int& slot, uint32_t& parity) {
+  constexpr int RSG = Cfg<MODE>::RSG;
+  const int grp = st % DQ_GROUPS, j = st / DQ_GROUPS;
+  slot = grp * RSG + j % RSG;
+  parity = (uint32_t)(j / RSG) & 1u;
+}
 
 struct DqArgs {
   const uint8_t* wq;      // packed indices [wb][KS][Npad][STEP_BYTES]
@@ -275,21 +303,23 @@ __device__ __forceinline__ void read32(const uint8_t* blk, int r, const uint16_t
 
 // ---------------------------------------------------------------------------
 template <int MODE>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     k_gemm_dq(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_w,
               const __grid_constant__ DqArgs g) {
   using C = Cfg<MODE>;
-  constexpr int S = C::STAGES, SB = C::STEP_BYTES;
+  constexpr int S = C::STAGES, RS = C::RSLOTS, SB = C::STEP_BYTES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint32_t* pal32 = reinterpret_cast<uint32_t*>(smem + S * C::STAGE_BYTES);
+  uint32_t* pal32 = reinterpret_cast<uint32_t*>(smem + C::PAL0);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BARS);
-  // full[S], empty[S], raw[S], acc_full[2], acc_empty[2], drain, TMEM slot
-  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S), raw0 = smem_u32(bars + 2 * S);
-  const uint32_t accf0 = smem_u32(bars + 3 * S), acce0 = smem_u32(bars + 3 * S + 2);
-  const uint32_t drain = smem_u32(bars + 3 * S + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 5);
+  // full[S], empty[S], acc_full[2], acc_empty[2], drain, TMEM slot,
+  // raw_full[RS], raw_empty[RS]
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
+  const uint32_t accf0 = smem_u32(bars + 2 * S), acce0 = smem_u32(bars + 2 * S + 2);
+  const uint32_t drain = smem_u32(bars + 2 * S + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  const uint32_t rfull0 = smem_u32(bars + 2 * S + 6), rempty0 = rfull0 + 8 * RS;
   const uint32_t rank = cluster_ctarank();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int pair_id = blockIdx.x / 2, npairs = gridDim.x / 2;
@@ -300,9 +330,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int s = 0; s < S; ++s) {
       // TMA mode: the even CTA's expect_tx arrival; LUT modes: that and one
       // arrival per decoder warp of the step's group in both CTAs
-      mbar_init(full0 + 8 * s, MODE == MODE_TMA ? 1 : 1 + 2 * DQ_WARPS);
+      mbar_init(full0 + 8 * s, C::LUT ? 1 + 2 * DQ_WARPS : 1);
       mbar_init(empty0 + 8 * s, 1);
-      mbar_init(raw0 + 8 * s, 1);
+    }
+    for (int i = 0; i < RS; ++i) {
+      mbar_init(rfull0 + 8 * i, 1);
+      mbar_init(rempty0 + 8 * i, DQ_WARPS);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(accf0 + 8 * i, 1);
@@ -313,7 +346,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   if (MODE == MODE_LUT8) {
     // the palette, one copy per bank: entry e of lane l at word e * 32 + l
-    for (int i = threadIdx.x; i < 256 * 32; i += THREADS) pal32[i] = g.pal[i >> 5];
+    for (int i = threadIdx.x; i < 256 * 32; i += C::THREADS) pal32[i] = g.pal[i >> 5];
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -327,7 +360,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- producer (both CTAs) ----------------
+    // ---------------- A (and TMA-mode weight) producer, both CTAs ----------------
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tma_a)) : "memory");
       const uint32_t s0 = smem_u32(smem);
@@ -339,35 +372,24 @@ __global__ void __launch_bounds__(THREADS, 1)
         int b, tm, tn;
         tile_of(g, pair_id + ti * npairs, b, tm, tn);
         if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, g.err, ERR_EMPTY)) break;
-        const uint32_t sb = s0 + stage * C::STAGE_BYTES;
+        const uint32_t sb = s0 + stage * STAGE_BYTES;
         if (rank == 0)
-          mbar_expect_tx(full0 + 8 * stage, MODE == MODE_TMA ? 2 * (A_BYTES + B_BYTES) : 2 * A_BYTES);
+          mbar_expect_tx(full0 + 8 * stage, C::LUT ? 2 * A_BYTES : 2 * (A_BYTES + B_BYTES));
         tma_load_2d_pair(sb, &tma_a, ks * 128, b * g.M + tm * 256 + (int)rank * 128,
                          fb0 + 8 * stage);
-        if (MODE == MODE_TMA) {
+        if (!C::LUT)
           tma_load_2d_pair(sb + A_BYTES, &tma_w, ks * 128,
                            (g.w_shared ? 0 : b * g.N) + tn * 256 + (int)rank * 128,
                            fb0 + 8 * stage);
-        } else {
-          const int64_t r0 = wrow(g, g.w_shared ? 0 : b, ks, tn * 256 + (int)rank * 128);
-          const uint32_t rb = raw0 + 8 * stage;
-          mbar_expect_tx(rb, 128 * SB + (g.ws4 ? SCALE_BYTES : 0));
-          bulk_load(sb + A_BYTES + B_BYTES, g.wq + r0 * SB, 128 * SB, rb);
-          if (g.ws4)
-            bulk_load(sb + A_BYTES + B_BYTES + 128 * SB, g.ws4 + r0 * 4, SCALE_BYTES, rb);
-        }
         if (++stage == S) {
           stage = 0;
           phase ^= 1;
         }
       }
-      // everything issued has landed before the CTA may leave: this CTA's
-      // raw bytes, and (even CTA) both CTAs' tiles
-      for (int s = 0; s < S; ++s) {
-        const uint32_t p = s < stage ? phase : phase ^ 1;
-        if (MODE != MODE_TMA) mbar_wait(raw0 + 8 * s, p, g.err, ERR_DRAIN);
-        if (rank == 0) mbar_wait(full0 + 8 * s, p, g.err, ERR_DRAIN);
-      }
+      // both CTAs' tiles complete on the even CTA's barriers
+      if (rank == 0)
+        for (int s = 0; s < S; ++s)
+          mbar_wait(full0 + 8 * s, s < stage ? phase : phase ^ 1, g.err, ERR_DRAIN);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (even CTA) ----------------
@@ -390,7 +412,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t soff = stage * (C::STAGE_BYTES / 16);
+          const uint32_t soff = stage * (STAGE_BYTES / 16);
 #pragma unroll
           for (uint32_t j = 0; j < 4; ++j)
             mma_bf16_pair(dacc, desc_at(dA0, soff + 2 * j), desc_at(dB0, soff + 2 * j), id,
@@ -407,51 +429,83 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_commit_pair(drain, 0x1);
       mbar_wait(drain, 0, g.err, ERR_DRAIN);
     }
-  } else if (warp < EPI_WARP0) {
-    // ---------------- weight decoders (LUT modes, both CTAs) ----------------
-    if (MODE != MODE_TMA) {
-      const int grp = (warp - 2) / DQ_WARPS;
-      const int rl = ((warp - 2) % DQ_WARPS) * 32 + lane;  // this thread's weight row
-      const uint32_t full_even0 = mapa_shared(full0, 0);
-      Pal4 p4;
-      if (MODE == MODE_LUT4) p4 = load_pal4(g.pal);
-      const bool scaled = g.ws4 != nullptr;
-      for (int st = grp; st < nsteps; st += DQ_GROUPS) {
-        const int stage = st % S;
-        const uint32_t phase = (uint32_t)(st / S) & 1u;
+  } else if (C::LUT && warp == 2) {
+    // ---------------- raw producer (LUT modes, both CTAs) ----------------
+    if (lane == 0) {
+      const uint32_t r0s = smem_u32(smem + C::RAW0);
+      int issued = 0;
+      for (int st = 0; st < nsteps; ++st) {
         const int ti = st / g.KS, ks = st - ti * g.KS;
         int b, tm, tn;
         tile_of(g, pair_id + ti * npairs, b, tm, tn);
-        // the stage's raw bytes landed (and its weight tile is free: the
-        // producer waited for the stage to empty before loading them)
-        if (!mbar_wait_warp(raw0 + 8 * stage, phase, g.err, ERR_FULL)) break;
-        uint8_t* sbase = smem + stage * C::STAGE_BYTES;
-        const uint8_t* rawc = sbase + A_BYTES + B_BYTES;
-        const uint16_t* raws =
-            scaled ? reinterpret_cast<const uint16_t*>(sbase + A_BYTES + B_BYTES + 128 * SB) + rl * 4
-                   : nullptr;
-        const int n = tn * 256 + (int)rank * 128 + rl;
-        uint8_t* bt = sbase + A_BYTES + rl * 128;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t raw[8], s_lo, s_hi, o[16];
-          read32<MODE>(rawc, rl, raws, h, raw, s_lo, s_hi);
-          const int valid = n < g.N ? min(32, g.K - (ks * KSTEP + h * 32)) : 0;
-          decode32<MODE>(raw, p4, pal32, lane, s_lo, s_hi, scaled, max(valid, 0), o);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int c = 4 * h + j;
-            *reinterpret_cast<uint4*>(bt + ((c ^ (rl & 7)) << 4)) =
-                make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-          }
-        }
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) arrive_release_cluster(full_even0 + 8 * stage);
+        int slot;
+        uint32_t phase;
+        raw_slot<MODE>(st, slot, phase);
+        if (!mbar_wait(rempty0 + 8 * slot, phase ^ 1, g.err, ERR_EMPTY)) break;
+        const int64_t r0 = wrow(g, g.w_shared ? 0 : b, ks, tn * 256 + (int)rank * 128);
+        const uint32_t rb = rfull0 + 8 * slot, dst = r0s + slot * C::RAW_BYTES;
+        mbar_expect_tx(rb, 128 * SB + (g.ws4 ? SCALE_BYTES : 0));
+        bulk_load(dst, g.wq + r0 * SB, 128 * SB, rb);
+        if (g.ws4) bulk_load(dst + 128 * SB, g.ws4 + r0 * 4, SCALE_BYTES, rb);
+        issued = st + 1;
+      }
+      // the last RS steps issued hold each slot's latest phase
+      for (int st = max(0, issued - RS); st < issued; ++st) {
+        int slot;
+        uint32_t phase;
+        raw_slot<MODE>(st, slot, phase);
+        mbar_wait(rfull0 + 8 * slot, phase, g.err, ERR_DRAIN);
       }
     }
-  } else {
-    // ---------------- epilogue (warps 18-21, both CTAs) ----------------
+  } else if (C::LUT && warp < C::EPI_WARP0) {
+    // ---------------- weight decoders (LUT modes, both CTAs) ----------------
+    const int grp = (warp - DEC_WARP0) / DQ_WARPS;
+    const int rl = ((warp - DEC_WARP0) % DQ_WARPS) * 32 + lane;  // this thread's weight row
+    const uint32_t full_even0 = mapa_shared(full0, 0);
+    Pal4 p4;
+    if (MODE == MODE_LUT4) p4 = load_pal4(g.pal);
+    const bool scaled = g.ws4 != nullptr;
+    for (int st = grp; st < nsteps; st += DQ_GROUPS) {
+      const int stage = st % S;
+      int slot;
+      uint32_t rphase;
+      raw_slot<MODE>(st, slot, rphase);
+      const int ti = st / g.KS, ks = st - ti * g.KS;
+      int b, tm, tn;
+      tile_of(g, pair_id + ti * npairs, b, tm, tn);
+      // the step's raw bytes: into registers, then the slot goes back
+      if (!mbar_wait_warp(rfull0 + 8 * slot, rphase, g.err, ERR_FULL)) break;
+      const uint8_t* rawc = smem + C::RAW0 + slot * C::RAW_BYTES;
+      const uint16_t* raws =
+          scaled ? reinterpret_cast<const uint16_t*>(rawc + 128 * SB) + rl * 4 : nullptr;
+      uint32_t raw[2][8], s_lo[2], s_hi[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) read32<MODE>(rawc, rl, raws, h, raw[h], s_lo[h], s_hi[h]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(rempty0 + 8 * slot);
+      // the stage's weight tile is free once the MMAs of its last round are done
+      if (!mbar_wait_warp(empty0 + 8 * stage, ((uint32_t)(st / S) & 1u) ^ 1u, g.err, ERR_EMPTY))
+        break;
+      const int n = tn * 256 + (int)rank * 128 + rl;
+      uint8_t* bt = smem + stage * STAGE_BYTES + A_BYTES + rl * 128;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t o[16];
+        const int valid = n < g.N ? min(32, g.K - (ks * KSTEP + h * 32)) : 0;
+        decode32<MODE>(raw[h], p4, pal32, lane, s_lo[h], s_hi[h], scaled, max(valid, 0), o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = 4 * h + j;
+          *reinterpret_cast<uint4*>(bt + ((c ^ (rl & 7)) << 4)) =
+              make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+        }
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) arrive_release_cluster(full_even0 + 8 * stage);
+    }
+  } else if (warp >= C::EPI_WARP0) {
+    // ---------------- epilogue (last 4 warps, both CTAs) ----------------
     const int q = warp & 3;
     const uint32_t acce_even0 = mapa_shared(acce0, 0);
     uint32_t accp = 0;
@@ -674,7 +728,7 @@ int launch_dq(const CUtensorMap& ma, const CUtensorMap& mw, const DqArgs& g, cud
   const int pairs = (int)std::min<int64_t>(g.ntiles, vq::mx::sm_count() / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.blockDim = dim3(Cfg<MODE>::THREADS, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
