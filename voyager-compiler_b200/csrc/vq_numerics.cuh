@@ -75,7 +75,24 @@ VQ_HD float fdiv_rn(float a, float b) {
   return r;
 #endif
 }
+// 1 / b rounded to nearest (the IEEE reciprocal: the same float as 1.0f / b).
+VQ_HD float frcp_rn(float b) {
+#if defined(__CUDA_ARCH__)
+  return __frcp_rn(b);
+#else
+  volatile float r = 1.0f / b;
+  return r;
+#endif
+}
 VQ_HD bool is_nan_f(float f) { return (f2u(f) & 0x7FFFFFFFu) > 0x7F800000u; }
+// 1 / q when q is a power of two whose reciprocal is a normal float (then
+// x * (1 / q) is exactly the IEEE quotient x / q, both being the rounding
+// of the same real number), else 0.
+VQ_HD float pow2_inverse(float q) {
+  const uint32_t b = f2u(q), e = (b >> 23) & 0xFFu;
+  if ((b & 0x807FFFFFu) != 0 || e < 2u || e > 252u) return 0.0f;
+  return u2f((254u - e) << 23);
+}
 
 // bf16 <-> float32.  float32 -> bf16 rounds to nearest even; every NaN becomes
 // 0xFFFF, the pattern torch's vectorised CPU cast writes.
@@ -266,7 +283,7 @@ VQ_HD Divisor make_divisor(float s) {
   d.s = s;
   const uint32_t e = (f2u(s) >> 23) & 0xFF;  // |s| in [2^-126, 2^126)
   d.fast = (e >= 1u && e <= 252u) ? 1 : 0;    // 1/s then normal too
-  d.r = d.fast ? fdiv_rn(1.0f, s) : 0.0f;
+  d.r = d.fast ? frcp_rn(s) : 0.0f;
   return d;
 }
 

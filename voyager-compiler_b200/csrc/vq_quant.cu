@@ -41,7 +41,9 @@ __device__ __noinline__ uint32_t round_any_dev(const vq_rounder& r, uint32_t b,
 template <int SK>
 __device__ __forceinline__ float div_scale_k(float amax, float qmax, bool is_bf16,
                                              const vq_rounder& sq, const uint16_t* sq_table) {
-  float s = fdiv_rn(amax, qmax);
+  // a power-of-two quant_max (1.0 for NormalFloat) divides by one exact multiply
+  const float iq = pow2_inverse(qmax);
+  float s = iq != 0.0f ? fmul_rn(amax, iq) : fdiv_rn(amax, qmax);
   if (is_bf16) s = round_bf(s);
   if (SK == 1) s = bf2f(round_minifloat(sq, f2bf(s)));
   if (SK == 2) s = bf2f(round_any_dev(sq, f2bf(s), sq_table));
@@ -227,6 +229,18 @@ __global__ void __launch_bounds__(1024) k_qmx_last(const __grid_constant__ QmxAr
         if (live[u] && col < a.C)
           v[u][j] = __ldcs(reinterpret_cast<const uint4*>(
               reinterpret_cast<const TIn*>(a.in) + base[u] + (j * TPB + lane) * VEC));
+      }
+    }
+    if (UNROLL == 1) {
+      // one block per thread keeps the registers (and so the resident
+      // threads) up; the next iteration's block is fetched into L2 meanwhile
+      const uint32_t g = wb + my_off + gstride;
+      if (g < a.ngroups) {
+        const uint32_t r = a.nb.div(g);
+        const uint32_t col = (g - r * a.nb.d) * a.bs + lane * (VPT * VEC);  // the block's lines
+        if (col < a.C)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const TIn*>(a.in) +
+                                                       (uint64_t)r * a.C + col));
       }
     }
     if (a.mask_on) {
@@ -1797,7 +1811,9 @@ int qmx_last_fast_ok(const vq_tensor& x, const int* blocked, int64_t bs) {
 
 template <typename TIn, int K, int SK, int TPB, int VPT>
 int launch_qmx(QmxArgs& a, cudaStream_t st) {
-  constexpr int UNROLL = 2;
+  // float32 blocks through a staged table: one block per thread (registers
+  // decide how many threads stay resident), the next one prefetched to L2
+  constexpr int UNROLL = (sizeof(TIn) == 4 && K == VQ_R_TABLE && TPB >= 4) ? 1 : 2;
   auto kern = k_qmx_last<TIn, K, SK, TPB, VPT, UNROLL>;
   int smem = K == VQ_R_TABLE ? table_smem(a.qr) : 0;
   int threads = 256, sms = num_sms(), blocks;
@@ -1809,7 +1825,7 @@ int launch_qmx(QmxArgs& a, cudaStream_t st) {
       return VQ_ERR_CUDA;
     int best = 0, best_per_sm = 1;
     threads = 1024;
-    for (int t : {1024, 768, 640, 512}) {
+    for (int t : {1024, 960, 896, 768, 640, 512}) {
       int per_sm = 0;
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, t, smem);
       if (per_sm * t > best) best = per_sm * t, best_per_sm = per_sm, threads = t;
