@@ -133,12 +133,26 @@ def main():
     ap.add_argument("--reference-src", default=os.environ.get("VOYAGER_REFERENCE_SRC"),
                     help="the reference checkout's src directory")
     ap.add_argument("--skip-full", action="store_true")
+    ap.add_argument("--schemas-only", action="store_true",
+                    help="only record the op schemas (schemas.json)")
     args = ap.parse_args()
     if not args.reference_src:
         ap.error("give --reference-src (or set VOYAGER_REFERENCE_SRC)")
     torch.set_num_threads(os.cpu_count())
     gqm = load_reference(args.reference_src)
     Q = torch.ops.quantized_ops
+
+    # -- 0. the op schemas, as torch parses the reference's definitions ----
+    schemas = {}
+    for full in sorted(torch._C._dispatch_get_all_op_names()):
+        if not full.startswith("quantized_ops::"):
+            continue
+        name = full.split("::", 1)[1].split(".", 1)[0]
+        schemas[name] = str(getattr(Q, name).default._schema)
+    with open(os.path.join(HERE, "schemas.json"), "w") as f:
+        json.dump(schemas, f, indent=1, sort_keys=True)
+    if args.schemas_only:
+        return
 
     # -- 1. tables ---------------------------------------------------------
     tables = {}

@@ -279,7 +279,10 @@ def to_device(p: PackedMX, device, weight: bool = False, verify: bool = True):
     the loaded bytes instead of packing again: as the weight operand
     (``weight=True``, which needs ``row_multiple=256``) or as an activation
     operand.  With ``verify`` the loaded bytes are compared once with the
-    library's own packing of the same codes and a difference raises."""
+    library's own packing of the same codes and a difference raises.
+    Whatever ``verify``, operands the GEMM does not take (E4M3 NaN bytes,
+    or zero UE8M0 bytes -- a 2^-127 block scale) are not registered: the
+    ops then check and route them as they would any other operand."""
     import torch
 
     from voyager_b200 import mxgemm
@@ -306,9 +309,12 @@ def to_device(p: PackedMX, device, weight: bool = False, verify: bool = True):
             raise ValueError("the GEMM does not take this operand (NaN codes or 2^-127 scales)")
         if not torch.equal(rc, pc) or not torch.equal(rs, ps):
             raise ValueError("the loaded operand differs from the library's packing")
+    # a cheap host check, verified or not: NaN codes (0x7F / 0xFF) or a zero
+    # scale byte keep the operand off the GEMM's fast path
+    clean = not (np.any((p.codes & 0x7F) == 0x7F) or np.any(p.scales == 0))
     if weight:
         key = (codes._version, id(scale), scale._version)
-        mxgemm._wcache.put(codes, key, (pc, ps, True))
-    else:
+        mxgemm._wcache.put(codes, key, (pc, ps, clean))
+    elif clean:
         mxgemm.vouch(codes, scale, (pc, ps))
     return codes, scale
