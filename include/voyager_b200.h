@@ -315,6 +315,26 @@ int vq_dq_decode(const void* w, int64_t N, int64_t K, int32_t mode, const void* 
 int vq_transpose_bf16(const void* src, int64_t batch, int64_t rows, int64_t cols, void* dst,
                       void* stream);
 
+/* ---- NVFP4 x NVFP4 linear (tcgen05 kind::mxf4nvf4, scale_vec::4X) ---------
+ * quantized_ops::linear_mx (src/voyager_compiler/ops/quantized.py:522-586)
+ * with both operands E2M1 codes (bf16 values) and E4M3-valued bf16 scales
+ * per 16 along K (block_size 16): the tensor cores multiply code x scale
+ * exactly and sum in float32.
+ * vq_nvf4_pack: codes [R, K] -> packed E2M1 [RT * 128][ceil(K/256) * 128 bytes]
+ * (element 2i in the low nibble of byte i), scales [R, ceil(K/16)] -> UE4M3
+ * atoms [ceil(K/256)][RT][4][512] (RT: rows rounded up to row_multiple, in
+ * 128-row chunks; A with 128, B with 256); *d_inexact counts codes that are
+ * not E2M1 values and scales that are not positive E4M3 values.
+ * vq_gemm_nvf4: out bf16 [M, ldo] = A . B^T (+ bias); N, ldo multiples of 8;
+ * *d_err as for vq_gemm_mxf8. */
+int vq_nvf4_pack_sizes(int64_t rows, int64_t k, int32_t row_multiple, int64_t* codes_bytes,
+                       int64_t* sf_bytes);
+int vq_nvf4_pack(const vq_tensor* codes, const vq_tensor* scale, int32_t row_multiple,
+                 void* packed_codes, void* packed_sf, int32_t* d_inexact, void* stream);
+int vq_gemm_nvf4(const void* a, const void* a_sf, const void* b, const void* b_sf, int64_t M,
+                 int64_t N, int64_t K, const void* bias, void* out, int64_t ldo, int32_t* d_err,
+                 void* stream);
+
 /* MXFP8 linear that allocates nothing: for callers that cannot call
  * cudaMalloc -- an allocator-free runtime, code running under a caller-owned
  * memory budget, or a library hook invoked where allocating is not allowed.

@@ -198,3 +198,43 @@ def test_mxf8_matmul_from_quantize_mx():
     want = oracle.matmul_mx(to_np(ca), to_np(cb), input_scale=to_np(sa), weight_scale=to_np(sb),
                             block_size=32)
     assert G.rel_l2(got, want) < 1e-3
+
+
+# ---------------------------------------------------------------------------
+# NVFP4 x NVFP4 linear_mx on tcgen05 kind::mxf4nvf4 (scale_vec::4X)
+# ---------------------------------------------------------------------------
+def _nvf4(x):
+    return oracle.quantize_mx(x, quantization_map("fp4_e2m1"), [-1], 16, 6.0, False,
+                              quantization_map("fp8_e4m3"))
+
+
+NVF4_SHAPES = [(128, 256, 256), (1, 256, 8), (300, 4096, 1000), (77, 96, 40), (1024, 2048, 2048),
+               (256, 4104, 264)]
+
+
+@pytest.mark.parametrize("m,k,n", NVF4_SHAPES)
+def test_nvf4_linear(m, k, n, monkeypatch):
+    from voyager_b200 import mxgemm
+    from voyager_b200.synth import f32_to_bf16_bits
+
+    rng = np.random.Generator(np.random.PCG64(m + k + n))
+    a = f32_to_bf16_bits(rng.standard_normal((m, k)).astype(np.float32))
+    w = f32_to_bf16_bits((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    bias = f32_to_bf16_bits((rng.standard_normal(n) * 0.1).astype(np.float32)) if m % 2 else None
+    sa, ca = _nvf4(a)
+    sw, cw = _nvf4(w)
+    calls = {"n": 0}
+    real = mxgemm.nvf4_linear
+
+    def counting(*args, **kw):
+        out = real(*args, **kw)
+        calls["n"] += out is not None
+        return out
+
+    monkeypatch.setattr(mxgemm, "nvf4_linear", counting)
+    got = to_np(torch.ops.quantized_ops.linear_mx(to_dev(ca), to_dev(cw), to_dev(bias),
+                                                  input_scale=to_dev(sa), weight_scale=to_dev(sw),
+                                                  block_size=16))
+    assert calls["n"] == 1, "the NVFP4 kernel did not take the operands"
+    want = oracle.linear_mx(ca, cw, bias, input_scale=sa, weight_scale=sw, block_size=16)
+    assert G.rel_l2(got, want) < 1e-3

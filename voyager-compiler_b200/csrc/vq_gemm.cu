@@ -631,6 +631,284 @@ __global__ void __launch_bounds__(P_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// NVFP4 x NVFP4 (E2M1 codes, UE4M3 scales per 16 along K) on
+// tcgen05.mma.kind::mxf4nvf4.block_scale.scale_vec::4X: the single-CTA
+// kernel above with K tiles of 256 elements (128 bytes of packed E2M1 per
+// row), K = 64 per MMA, and four scale bytes per row per MMA -- so one
+// 512-byte atom per MMA and 128-row chunk (row r's byte t, the scale of
+// elements 16 t .. 16 t + 15 of the MMA's 64, at (r % 32) * 16 + (r / 32) * 4
+// + t), four per chunk and K tile, and a 48-column TMEM scale slot per stage
+// (A: 4 columns per MMA; B: 8).  code x scale is exact in the tensor core,
+// as it is in bf16 for the reference's dequantize.
+constexpr int F4_STAGES = 4;
+constexpr int F4_SFA = 4 * 512, F4_SFB = 8 * 512;  // per K tile: A 128 rows, B 256 rows
+constexpr int F4_TX = A_BYTES + B_BYTES + F4_SFA + F4_SFB;
+constexpr int F4_STAGE = (F4_TX + 1023) / 1024 * 1024;
+constexpr int F4_BARS = F4_STAGES * F4_STAGE;
+constexpr int F4_SMEM = F4_BARS + 256;
+constexpr int F4_SLOT = 48;  // TMEM columns of one stage's scales (A 16, B 32)
+static_assert(SF_COL + F4_STAGES * F4_SLOT <= TMEM_COLS, "NVFP4 scale slots exceed TMEM");
+static_assert(F4_SMEM + 1024 <= 227 * 1024, "NVFP4 shared memory");
+static_assert((3 * F4_STAGES + 5) * 8 <= 256, "NVFP4 barriers");
+
+// E2M1 x E2M1 (format code 1 in both), UE4M3 scales (bit 23 clear), K-major.
+__device__ __forceinline__ uint32_t idesc_nvf4(uint32_t M, uint32_t N) {
+  return (1u << 7) | (1u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+__global__ void __launch_bounds__(THREADS + 32, 1)
+    k_gemm_nvf4(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                const __grid_constant__ GemmArgs g) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + F4_BARS);
+  constexpr int S = F4_STAGES;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
+  const uint32_t acc_full = smem_u32(bars + 2 * S), acc_empty = smem_u32(bars + 2 * S + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 2);
+  const uint32_t sf_full0 = smem_u32(bars + 2 * S + 3);
+  const uint32_t drain_mma = smem_u32(bars + 3 * S + 3), drain_sf = drain_mma + 8;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+      mbar_init(sf_full0 + 8 * s, 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 256);
+    mbar_init(drain_mma, 1);
+    mbar_init(drain_sf, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < g.ntiles && ok; t += gridDim.x) {
+        int b, tm, tn;
+        tile_of(g, t, g.MTb, b, tm, tn);
+        const int ga = b * g.MTb + tm, gb = b * g.b_step + 2 * tn;
+        for (int kt = 0; kt < g.KT; ++kt) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, g.err, ERR_TIMEOUT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sbase = smem_u32(smem + stage * F4_STAGE);
+          const uint32_t fb = full0 + 8 * stage;
+          mbar_expect_tx(fb, F4_TX);
+          tma_load_2d(sbase, &tma_a, kt * BK, ga * BM, fb);
+          tma_load_2d(sbase + A_BYTES, &tma_b, kt * BK, gb * 128, fb);
+          // scale atoms: [kt][row chunk][4 MMAs][512]
+          bulk_load(sbase + A_BYTES + B_BYTES, g.sfa + ((size_t)kt * g.MT + ga) * F4_SFA, F4_SFA,
+                    fb);
+          bulk_load(sbase + A_BYTES + B_BYTES + F4_SFA,
+                    g.sfb + ((size_t)kt * g.NT128 + gb) * (F4_SFB / 2), F4_SFB, fb);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      drain_loads<S>(full0, stage, phase, g.err);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      const uint32_t s0 = smem_u32(smem);
+      const uint64_t dA0 = sw128_desc(s0), dB0 = sw128_desc(s0 + A_BYTES);
+      const uint32_t id = idesc_nvf4(BM, BN);
+      for (int t = blockIdx.x; t < g.ntiles && ok; t += gridDim.x) {
+        if (!mbar_wait(acc_empty, acc_phase ^ 1, g.err, ERR_TIMEOUT_ACC)) break;
+        acc_phase ^= 1;
+        tc_fence_after();
+        for (int kt = 0; kt < g.KT; ++kt) {
+          if (!mbar_wait(sf_full0 + 8 * stage, phase, g.err, ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t soff = stage * (F4_STAGE / 16);
+          const uint32_t sfc = tmem + SF_COL + stage * F4_SLOT;
+#pragma unroll
+          for (uint32_t j = 0; j < 4; ++j) {
+            const uint32_t accum = (kt > 0 || j > 0) ? 1u : 0u;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, "
+                "%3, [%5], [%6], p;\n\t}" ::"r"(tmem + ACC_COL),
+                "l"(desc_at(dA0, soff + 2 * j)), "l"(desc_at(dB0, soff + 2 * j)), "r"(id),
+                "r"(accum), "r"(sfc + 4 * j), "r"(sfc + 16 + 8 * j));
+          }
+          asm volatile(
+              "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                  empty0 + 8 * stage)
+              : "memory");
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        asm volatile(
+            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                acc_full)
+            : "memory");
+      }
+      tc_commit(drain_mma);
+      mbar_wait(drain_mma, 0, g.err, ERR_TIMEOUT_DRAIN);
+    }
+  } else if (warp == 10) {
+    // ---------------- scale-copy issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      const uint64_t dS0 = sf_desc(smem_u32(smem) + A_BYTES + B_BYTES);
+      for (int t = blockIdx.x; t < g.ntiles && ok; t += gridDim.x) {
+        for (int kt = 0; kt < g.KT; ++kt) {
+          if (!mbar_wait(full0 + 8 * stage, phase, g.err, ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t soff = stage * (F4_STAGE / 16);
+          const uint32_t sfc = tmem + SF_COL + stage * F4_SLOT;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            // A: MMA j's atom; B: MMA j's atoms of both 128-row chunks
+            asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + 4 * j),
+                         "l"(desc_at(dS0, soff + (j * 512) / 16)));
+            asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(sfc + 16 + 8 * j),
+                         "l"(desc_at(dS0, soff + (F4_SFA + j * 512) / 16)));
+            asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(
+                             sfc + 16 + 8 * j + 4),
+                         "l"(desc_at(dS0, soff + (F4_SFA + 2048 + j * 512) / 16)));
+          }
+          asm volatile(
+              "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                  sf_full0 + 8 * stage)
+              : "memory");
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      tc_commit(drain_sf);
+      mbar_wait(drain_sf, 0, g.err, ERR_TIMEOUT_DRAIN);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..9) ----------------
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_in_tile = q * 32 + lane;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < g.ntiles; t += gridDim.x) {
+      int b, tm, tn;
+      tile_of(g, t, g.MTb, b, tm, tn);
+      if (!mbar_wait_warp(acc_full, acc_phase, g.err, ERR_TIMEOUT_ACC)) break;
+      acc_phase ^= 1;
+      tc_fence_after();
+      const int row = tm * BM + row_in_tile;
+      const int colh = tn * BN + half * 128;
+      epilogue_tile(g, tmem, q, half, lane, b, row, colh, [&] { mbar_arrive(acc_empty); });
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+// NVFP4 packing: bf16 E2M1 codes [R, K] -> nibbles [RT * 128][KT * 128 bytes]
+// (element 2i in the low nibble); one thread per 32 codes (16 bytes out).
+struct PackF4Args {
+  const uint16_t* codes;  // bf16 [R, K]
+  const uint16_t* scale;  // bf16 [R, K / 16]
+  uint8_t* out;
+  uint8_t* sf;            // [KT][RT][4][512]
+  int R, K, KT, RT, nkb;
+  int* inexact;
+};
+
+__global__ void k_pack_nvf4_codes(const __grid_constant__ PackF4Args p) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_row = p.KT * 8;  // 16-byte pieces per packed row (256 elements per K tile)
+  if (i >= (int64_t)p.RT * 128 * per_row) return;
+  const int r = (int)(i / per_row), c0 = (int)(i % per_row) * 32;
+  uint32_t w[4] = {0, 0, 0, 0};
+  int bad = 0;
+  if (r < p.R) {
+#pragma unroll
+    for (int k = 0; k < 32; k += 2) {
+      const int c = c0 + k;
+      float f0 = 0.f, f1 = 0.f;
+      if (c < p.K) f0 = bf2f(p.codes[(int64_t)r * p.K + c]);
+      if (c + 1 < p.K) f1 = bf2f(p.codes[(int64_t)r * p.K + c + 1]);
+      uint32_t b;
+      asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u32.u8 %0, t;\n\t}"
+          : "=r"(b)
+          : "f"(f1), "f"(f0));
+      uint32_t h2;
+      asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+          : "=r"(h2)
+          : "r"(b));
+      const float g0 = __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFF)));
+      const float g1 = __half2float(__ushort_as_half((unsigned short)(h2 >> 16)));
+      bad += (__float_as_uint(g0) != __float_as_uint(f0) && !(g0 == 0.f && f0 == 0.f));
+      bad += (__float_as_uint(g1) != __float_as_uint(f1) && !(g1 == 0.f && f1 == 0.f));
+      w[k / 8] |= b << (8 * ((k / 2) & 3));
+    }
+  }
+  *reinterpret_cast<uint4*>(p.out + (int64_t)r * (p.KT * 128) + c0 / 2) =
+      make_uint4(w[0], w[1], w[2], w[3]);
+  if (bad && p.inexact) atomicAdd(p.inexact, bad);
+}
+
+// One thread per (row, block of 16): the UE4M3 byte of its scale.
+__global__ void k_pack_nvf4_scales(const __grid_constant__ PackF4Args p) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int kb_all = p.KT * 16;
+  if (i >= (int64_t)p.RT * 128 * kb_all) return;
+  const int r = (int)(i / kb_all), kb = (int)(i % kb_all);
+  uint32_t e = 0x38;  // 1.0 for padding rows / blocks
+  int bad = 0;
+  if (r < p.R && kb < p.nkb) {
+    const float s = bf2f(p.scale[(int64_t)r * p.nkb + kb]);
+    uint16_t pair;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(pair) : "f"(0.0f), "f"(s));
+    e = pair & 0xFFu;
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"((uint16_t)e));
+    const float back = __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFF)));
+    // a positive E4M3 value (UE4M3 has no sign) that round-trips exactly
+    bad = !(s > 0.0f) || __float_as_uint(back) != __float_as_uint(s);
+  }
+  const int kt = kb / 16, j = (kb % 16) / 4, t = kb % 4, rt = r / 128, rr = r % 128;
+  p.sf[(((int64_t)kt * p.RT + rt) * 4 + j) * 512 + (rr % 32) * 16 + (rr / 32) * 4 + t] = (uint8_t)e;
+  if (bad && p.inexact) atomicAdd(p.inexact, 1);
+}
+
+// ---------------------------------------------------------------------------
 // Packing: bf16 E4M3 codes -> bytes, bf16 power-of-two scales -> UE8M0 atoms
 // ---------------------------------------------------------------------------
 struct PackArgs {
@@ -1099,6 +1377,95 @@ int vq_gemm_mxf8_batched(const void* a, const void* a_sf, const void* b, const v
   if (out_batch_stride % 8) return VQ_ERR_ALIGNMENT;
   return gemm_run(a, a_sf, b, b_sf, batch, a_rows_per_batch / 128, M, N, K, b_shared ? 1 : 0, bias,
                   nullptr, 0, out, ldo, out_batch_stride, 0, d_err, stream);
+}
+
+int vq_nvf4_pack_sizes(int64_t rows, int64_t k, int32_t row_multiple, int64_t* codes_bytes,
+                       int64_t* sf_bytes) {
+  if (rows <= 0 || k <= 0 || !codes_bytes || !sf_bytes) return VQ_ERR_INVALID;
+  if (row_multiple != 128 && row_multiple != 256) return VQ_ERR_INVALID;
+  const int64_t RT = (rows + row_multiple - 1) / row_multiple * (row_multiple / 128);
+  const int64_t KT = (k + 255) / 256;
+  *codes_bytes = RT * 128 * KT * 128;
+  *sf_bytes = KT * RT * 4 * 512;
+  return VQ_OK;
+}
+
+int vq_nvf4_pack(const vq_tensor* codes, const vq_tensor* scale, int32_t row_multiple,
+                 void* packed_codes, void* packed_sf, int32_t* d_inexact, void* stream) {
+  if (!codes || !scale || !packed_codes || !packed_sf) return VQ_ERR_NULL;
+  if (codes->dtype != VQ_BF16 || scale->dtype != VQ_BF16) return VQ_ERR_UNSUPPORTED;
+  if (codes->ndim != 2 || scale->ndim != 2) return VQ_ERR_SHAPE;
+  const int64_t R = codes->shape[0], K = codes->shape[1];
+  if (R <= 0 || K <= 0) return VQ_ERR_INVALID;
+  if (scale->shape[0] != R || scale->shape[1] != (K + 15) / 16) return VQ_ERR_SHAPE;
+  if (row_multiple != 128 && row_multiple != 256) return VQ_ERR_INVALID;
+  if (R >= (1ll << 31) / 4 || K >= (1 << 24)) return VQ_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(packed_codes) & 15) || (reinterpret_cast<uintptr_t>(packed_sf) & 15))
+    return VQ_ERR_ALIGNMENT;
+  PackF4Args p;
+  p.codes = (const uint16_t*)codes->data;
+  p.scale = (const uint16_t*)scale->data;
+  p.out = (uint8_t*)packed_codes;
+  p.sf = (uint8_t*)packed_sf;
+  p.R = (int)R;
+  p.K = (int)K;
+  p.KT = (int)((K + 255) / 256);
+  p.RT = (int)((R + row_multiple - 1) / row_multiple * (row_multiple / 128));
+  p.nkb = (int)((K + 15) / 16);
+  p.inexact = d_inexact;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (d_inexact && cudaMemsetAsync(d_inexact, 0, sizeof(int32_t), st) != cudaSuccess)
+    return VQ_ERR_CUDA;
+  const int64_t n1 = (int64_t)p.RT * 128 * p.KT * 8;
+  k_pack_nvf4_codes<<<(unsigned)((n1 + 255) / 256), 256, 0, st>>>(p);
+  const int64_t n2 = (int64_t)p.RT * 128 * p.KT * 16;
+  k_pack_nvf4_scales<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
+}
+
+int vq_gemm_nvf4(const void* a, const void* a_sf, const void* b, const void* b_sf, int64_t M,
+                 int64_t N, int64_t K, const void* bias, void* out, int64_t ldo, int32_t* d_err,
+                 void* stream) {
+  if (!a || !a_sf || !b || !b_sf || !out || !d_err) return VQ_ERR_NULL;
+  if (M <= 0 || N <= 0 || K <= 0) return VQ_ERR_INVALID;
+  if (N % 8 != 0 || ldo < N || ldo % 8 != 0) return VQ_ERR_UNSUPPORTED;
+  if (M > (1 << 30) || N > (1 << 30) || K >= (1 << 24)) return VQ_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(a) & 15) ||
+      (reinterpret_cast<uintptr_t>(b) & 15) || (reinterpret_cast<uintptr_t>(a_sf) & 15) ||
+      (reinterpret_cast<uintptr_t>(b_sf) & 15) || (reinterpret_cast<uintptr_t>(bias) & 1))
+    return VQ_ERR_ALIGNMENT;
+  const int64_t KT = (K + 255) / 256, Kb = KT * 128;  // packed bytes per row
+  const int64_t MT = (M + 127) / 128, NTILE_N = (N + BN - 1) / BN;
+  if (NTILE_N * MT >= (1ll << 31)) return VQ_ERR_UNSUPPORTED;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, a, MT * 128, Kb, BM) || !make_map(&mb, b, NTILE_N * 2 * 128, Kb, BN))
+    return VQ_ERR_CUDA;
+  GemmArgs g = {};
+  g.sfa = (const uint8_t*)a_sf;
+  g.sfb = (const uint8_t*)b_sf;
+  g.bias = (const uint16_t*)bias;
+  g.out = (uint16_t*)out;
+  g.ldo = ldo;
+  g.M = (int)M;
+  g.N = (int)N;
+  g.KT = (int)KT;
+  g.MT = (int)MT;
+  g.NT128 = (int)(NTILE_N * 2);
+  g.NTILE_N = (int)NTILE_N;
+  g.MTb = (int)MT;
+  g.MT2b = (int)((M + 255) / 256);
+  g.b_step = 0;
+  g.ntiles = (int)(MT * NTILE_N);
+  g.err = d_err;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(d_err, 0, sizeof(int32_t), st) != cudaSuccess) return VQ_ERR_CUDA;
+  const int smem = F4_SMEM + 1024;
+  if (cudaFuncSetAttribute(k_gemm_nvf4, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
+    return VQ_ERR_CUDA;
+  const int grid = (int)std::min<int64_t>(g.ntiles, sm_count());
+  k_gemm_nvf4<<<grid, THREADS + 32, smem, st>>>(ma, mb, g);
+  return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
 }
 
 int vq_linear_mxf8_noalloc(const vq_tensor* a_codes, const vq_tensor* a_scale,

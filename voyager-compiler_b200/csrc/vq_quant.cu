@@ -20,6 +20,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <initializer_list>
 #include <mutex>
 
 #include "vq_numerics.cuh"
@@ -57,6 +58,45 @@ constexpr int kTableBytes = 65536 * 2;
 constexpr int kTable8Bytes = 65536 + 512;  // byte codes + bf16 palette
 // shared memory a TABLE rounder's kernels stage
 inline int table_smem(const vq_rounder& r) { return r.table8 ? kTable8Bytes : kTableBytes; }
+
+// Launch shape of a kernel that stages a table in shared memory: of the CTA
+// sizes `cands`, the one that keeps the most threads resident under the
+// shared-memory and register limits, and the resident CTAs per SM at that
+// size.  Found once per (device, kernel, shared-memory size): the host cost
+// of a launch must stay well below the kernel's tens of microseconds.
+template <typename Kern>
+int table_launch_shape(Kern kern, int smem, std::initializer_list<int> cands, int* threads,
+                       int* per_sm) {
+  struct Entry {
+    const void* fn;
+    int dev, smem, threads, per_sm;
+  };
+  static std::mutex mu;
+  static Entry cache[256];
+  static int n = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return VQ_ERR_CUDA;
+  const void* fn = reinterpret_cast<const void*>(kern);
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n; ++i)
+    if (cache[i].fn == fn && cache[i].dev == dev && cache[i].smem == smem) {
+      *threads = cache[i].threads;
+      *per_sm = cache[i].per_sm;
+      return VQ_OK;
+    }
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return VQ_ERR_CUDA;
+  int best = 0, best_t = *cands.begin(), best_per = 1;
+  for (int t : cands) {
+    int p = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&p, kern, t, smem);
+    if (p * t > best) best = p * t, best_t = t, best_per = std::max(p, 1);
+  }
+  *threads = best_t;
+  *per_sm = best_per;
+  if (n < 256) cache[n++] = {fn, dev, smem, best_t, best_per};
+  return VQ_OK;
+}
 
 // Division by a run-time invariant (Granlund-Montgomery, round-up variant):
 // q = (umulhi(n, m) + n) >> s, exact for every 32-bit n.
@@ -1347,13 +1387,9 @@ int launch_elem(ElemArgs& a, cudaStream_t st) {
   int sms = num_sms();
   int blocks;
   if (smem) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
-      return VQ_ERR_CUDA;
-    threads = 1024;  // one resident CTA per SM holds the table
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
-    blocks = sms * std::max(per_sm, 1);
+    int per_sm = 1;  // 1024-thread CTAs, each holding the table
+    if (int e = table_launch_shape(kern, smem, {1024}, &threads, &per_sm)) return e;
+    blocks = sms * per_sm;
   } else {
     blocks = sms * 8;
   }
@@ -1397,13 +1433,9 @@ int launch_2d(Elem2DArgs& a, cudaStream_t st) {
   const int smem = (!DEQ && K == VQ_R_TABLE) ? table_smem(a.qr) : 0;
   int threads = 256, sms = num_sms(), blocks;
   if (smem) {
-    threads = 1024;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
-      return VQ_ERR_CUDA;
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
-    blocks = sms * std::max(per_sm, 1);
+    int per_sm = 1;
+    if (int e = table_launch_shape(kern, smem, {1024}, &threads, &per_sm)) return e;
+    blocks = sms * per_sm;
   } else {
     blocks = sms * 8;
   }
@@ -1475,13 +1507,9 @@ int launch_rows(RowsArgs& a, cudaStream_t st) {
   const int sms = num_sms();
   int threads, blocks;
   if (smem) {
-    threads = 1024;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
-      return VQ_ERR_CUDA;
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
-    blocks = sms * std::max(per_sm, 1);
+    int per_sm = 1;
+    if (int e = table_launch_shape(kern, smem, {1024}, &threads, &per_sm)) return e;
+    blocks = sms * per_sm;
   } else {
     threads = 256;
     blocks = sms * 8;
@@ -1820,17 +1848,10 @@ int launch_qmx(QmxArgs& a, cudaStream_t st) {
   if (smem) {
     // each resident CTA holds the table: the CTA size that keeps the most
     // threads resident under the shared-memory and register limits
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
-      return VQ_ERR_CUDA;
-    int best = 0, best_per_sm = 1;
-    threads = 1024;
-    for (int t : {1024, 960, 896, 768, 640, 512}) {
-      int per_sm = 0;
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, t, smem);
-      if (per_sm * t > best) best = per_sm * t, best_per_sm = per_sm, threads = t;
-    }
-    blocks = sms * std::max(best_per_sm, 1);
+    int per_sm = 1;
+    if (int e = table_launch_shape(kern, smem, {1024, 960, 896, 768, 640, 512}, &threads, &per_sm))
+      return e;
+    blocks = sms * per_sm;
   } else {
     blocks = sms * 8;
   }

@@ -157,6 +157,13 @@ _SIGNATURES = {
                                     ctypes.c_void_p]),
     "vq_transpose_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                          ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_nvf4_pack_sizes": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                          P(ctypes.c_int64), P(ctypes.c_int64)]),
+    "vq_nvf4_pack": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_int32, ctypes.c_void_p,
+                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_gemm_nvf4": (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 3
+                     + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                        ctypes.c_void_p]),
     "vq_tp_barrier_ex": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                         ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint64,
                                         ctypes.c_void_p, ctypes.c_void_p]),

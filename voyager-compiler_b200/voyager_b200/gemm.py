@@ -8,6 +8,8 @@ Paths, chosen per call:
   * MXFP8 x MXFP8 (E4M3 codes, power-of-two block-32 scales along K on both
     operands, bf16): the tcgen05 block-scaled GEMM in ``libvoyager_b200``
     (``voyager_b200.mxgemm``), weights packed once and cached;
+  * NVFP4 x NVFP4 (E2M1 codes, E4M3 scales per 16 along K on both): the
+    tcgen05 ``kind::mxf4nvf4`` block-scaled GEMM (``mxgemm.nvf4_linear``);
   * every other bf16 operand pair: the tcgen05 bf16 GEMM
     (``voyager_b200.dqgemm``), the weight read back from palette indices in
     shared memory (or, when it does not fit that form, by this library's
@@ -90,6 +92,11 @@ def linear_mx(input, weight, bias=None, *, input_scale=None, weight_scale=None,
             out = mxgemm.linear(input, weight, bias, input_scale, weight_scale, residual=res)
             if out is not None:
                 return out
+    if sp is None and mxgemm.nvf4_applies(input, weight, input_scale, weight_scale, block_size,
+                                          input_code, weight_code, weight_layout, "linear"):
+        out = mxgemm.nvf4_linear(input, weight, bias, input_scale, weight_scale)
+        if out is not None:
+            return out
     from voyager_b200 import dqgemm
 
     out = dqgemm.linear(input, weight, bias, input_scale, weight_scale, block_size, input_code,

@@ -274,3 +274,83 @@ def matmul(a, b, input_scale, weight_scale, weight_layout):
     if CHECK_ERRORS and int(err.item()) != 0:
         raise _lib.VqError(f"matmul_mx: device wait timed out (code {int(err.item())})")
     return out
+
+
+# ---------------------------------------------------------------------------
+# NVFP4 x NVFP4 linear_mx on tcgen05 kind::mxf4nvf4
+# ---------------------------------------------------------------------------
+def nvf4_applies(input, weight, input_scale, weight_scale, block_size, input_code, weight_code,
+                 weight_layout, op) -> bool:
+    """Both operands E2M1 codes with E4M3-valued scales per 16 along K
+    (``fp4_e2m1,qs=microscaling,bs=16,ax=-1,scale=fp8_e4m3``), bf16, blocks
+    along the last dim of ``input`` [.., K] and ``weight`` [N, K]."""
+    if op != "linear" or weight_layout != "kc" or block_size != 16:
+        return False
+    if input_code is not None or weight_code is not None:
+        return False
+    if input_scale is None or weight_scale is None:
+        return False
+    ts = (input, weight, input_scale, weight_scale)
+    if any(t.dtype != torch.bfloat16 or not t.is_cuda for t in ts):
+        return False
+    if weight.dim() != 2 or input.dim() < 1 or input.shape[-1] != weight.shape[1]:
+        return False
+    K, N = weight.shape[1], weight.shape[0]
+    nkb = (K + 15) // 16
+    if tuple(weight_scale.shape) != (N, nkb):
+        return False
+    if tuple(input_scale.shape) != tuple(input.shape[:-1]) + (nkb,):
+        return False
+    return N % 8 == 0 and input.numel() > 0
+
+
+def _pack_nvf4(codes2d, scale2d, row_multiple):
+    lib = _lib.load()
+    from voyager_b200.ops import _ref, _stream, _vt
+
+    R, K = codes2d.shape
+    cb, sb = ctypes.c_int64(), ctypes.c_int64()
+    _lib.check(lib.vq_nvf4_pack_sizes(R, K, row_multiple, ctypes.byref(cb), ctypes.byref(sb)),
+               "nvf4 pack sizes")
+    dev = codes2d.device
+    pc = torch.empty(cb.value, dtype=torch.uint8, device=dev)
+    ps = torch.empty(sb.value, dtype=torch.uint8, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.check(lib.vq_nvf4_pack(_ref(_vt(codes2d)), _ref(_vt(scale2d)), row_multiple,
+                                pc.data_ptr(), ps.data_ptr(), bad.data_ptr(), _stream(dev)),
+               "quantized_ops::linear_mx (NVFP4 pack)")
+    return pc, ps, int(bad.item()) == 0
+
+
+def nvf4_linear(input, weight, bias, input_scale, weight_scale):
+    """NVFP4 linear; None when an operand is not exact E2M1 / E4M3 (the
+    caller then takes the dequantize path)."""
+    if bias is not None and (bias.dtype != torch.bfloat16 or bias.dim() != 1
+                             or bias.shape[0] != weight.shape[0] or not bias.is_cuda):
+        return None
+    key = ("nvf4", weight._version, id(weight_scale), weight_scale._version)
+    hit = _wcache.get(weight, key)
+    if hit is None:
+        hit = _wcache.put(weight, key, _pack_nvf4(weight.contiguous(),
+                                                  weight_scale.contiguous(), 256))
+    pw, pws, wok = hit
+    if not wok:
+        return None
+    K, N = weight.shape[1], weight.shape[0]
+    M = input.numel() // K
+    pa, pas, aok = _pack_nvf4(input.reshape(M, K).contiguous(),
+                              input_scale.reshape(M, input_scale.shape[-1]).contiguous(), 128)
+    if not aok:
+        return None
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=input.device)
+    err = torch.empty(1, dtype=torch.int32, device=input.device)
+    b = bias.contiguous() if bias is not None else None
+    from voyager_b200.ops import _stream
+
+    st = _lib.load().vq_gemm_nvf4(pa.data_ptr(), pas.data_ptr(), pw.data_ptr(), pws.data_ptr(),
+                                  M, N, K, b.data_ptr() if b is not None else None,
+                                  out.data_ptr(), N, err.data_ptr(), _stream(input.device))
+    _lib.check(st, "quantized_ops::linear_mx (tcgen05 NVFP4)")
+    if CHECK_ERRORS and int(err.item()) != 0:
+        raise _lib.VqError(f"linear_mx: device wait timed out (code {int(err.item())})")
+    return out.reshape(tuple(input.shape[:-1]) + (N,))
