@@ -8,7 +8,9 @@ head_dim 128, sequence lengths multiples of 128, bf16.  The scores and
 probabilities never leave the chip.
 
 Everything else runs the reference's composition on the GPU: operands
-dequantized by this library's kernels, ``torch.matmul`` / ``softmax``, the
+dequantized by this library's kernels, the two products on this library's
+tcgen05 bf16 GEMM (torch's matmul only for shapes it does not take), the
+mask and the float32 softmax with torch's elementwise ops, the
 probabilities through this library's ``quantize_mx``.
 
 The fused output is returned as a [B, H, Sq, D] view of a [B, Sq, H, D]
@@ -126,9 +128,24 @@ def _composite(query, key, value, attn_mask, is_causal, query_residual, key_resi
                value_residual, residual_mask, scale, enable_gqa, query_scale, key_scale,
                value_scale, block_size, input_code, weight_code, probs_qmap, probs_quant_max,
                probs_scale_qmap, probs_code, force_scale_power_of_two):
-    """The reference's composition (``quantized.py:716-769``) on the GPU."""
+    """The reference's composition (``quantized.py:716-769``) on the GPU: the
+    two products on this library's tcgen05 bf16 GEMM where they fit it
+    (bf16, K and N multiples of 8), torch's matmul otherwise; the mask and
+    the float32 softmax with torch's elementwise ops."""
+    from voyager_b200.dqgemm import bmm_nt, transpose_last2
     from voyager_b200.gemm import dequantize_mx
     from voyager_b200.ops import quantize_mx
+
+    def qk(a, b):  # a @ b^T
+        out = bmm_nt(a, b)
+        return out if out is not None else torch.matmul(a, b.transpose(-1, -2))
+
+    def pv(p, v):  # p @ v
+        if p.dtype == torch.bfloat16 and v.dtype == torch.bfloat16 and p.shape[-1] % 8 == 0:
+            out = bmm_nt(p, transpose_last2(v.contiguous()))
+            if out is not None:
+                return out
+        return torch.matmul(p, v)
 
     query = dequantize_mx(query, query_scale, input_code, block_size)
     key = dequantize_mx(key, key_scale, weight_code, block_size)
@@ -141,13 +158,13 @@ def _composite(query, key, value, attn_mask, is_causal, query_residual, key_resi
         if residual:
             key_residual = key_residual.repeat_interleave(group, dim=-3)
             value_residual = value_residual.repeat_interleave(group, dim=-3)
-    scores = torch.matmul(query, key.transpose(-1, -2)) * scale
+    scores = qk(query, key) * scale
     if is_causal:
         attn_mask = torch.ones(scores.shape[-2:], dtype=torch.bool, device=scores.device).tril()
     scores = _masked(scores, attn_mask)
     keys = scores.shape[-1]
     if residual:
-        rs = query_residual @ key_residual.transpose(-1, -2)
+        rs = qk(query_residual, key_residual)
         scores = torch.cat([scores, _masked(rs * scale, residual_mask)], dim=-1)
     probs = torch.softmax(scores, dim=-1)
     probs, residual_probs = probs[..., :keys], probs[..., keys:]
@@ -155,9 +172,9 @@ def _composite(query, key, value, attn_mask, is_causal, query_residual, key_resi
         ps, probs = quantize_mx(probs, probs_qmap, [-1], block_size, probs_quant_max,
                                 force_scale_power_of_two, probs_scale_qmap, probs_code)
         probs = dequantize_mx(probs, ps, input_code, block_size)
-    out = torch.matmul(probs, value)
+    out = pv(probs, value)
     if residual:
-        out = out + torch.matmul(residual_probs, value_residual)
+        out = out + pv(residual_probs, value_residual)
     return out
 
 

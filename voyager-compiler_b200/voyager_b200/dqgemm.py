@@ -311,3 +311,25 @@ def decode(pw: PackedWeight) -> torch.Tensor:
                                   pw.palette.data_ptr(), out.data_ptr(), _stream(pw.w.device))
     _lib.check(st, "dq decode")
     return out
+
+
+def bmm_nt(a: torch.Tensor, b: torch.Tensor) -> Optional[torch.Tensor]:
+    """a [.., M, K] @ b[.., N, K]^T -> [.., M, N] bf16 on the tcgen05 bf16 GEMM
+    (float32 sums, one bf16 rounding), b's leading dims equal to a's or
+    absent; None when the operands do not fit it (not bf16, K or N not a
+    multiple of 8, empty)."""
+    if not (_bf16_operand(a) and _bf16_operand(b)) or a.dim() < 2 or b.dim() < 2:
+        return None
+    M, K = a.shape[-2], a.shape[-1]
+    N = b.shape[-2]
+    if b.shape[-1] != K or K % 8 or N % 8 or a.numel() == 0 or b.numel() == 0:
+        return None
+    batch_shape = tuple(a.shape[:-2])
+    if b.dim() > 2 and tuple(b.shape[:-2]) != batch_shape:
+        return None
+    Bt = 1
+    for d in batch_shape:
+        Bt *= d
+    pw = PackedWeight(MODE_TMA, b.contiguous(), N, K)
+    out = gemm(a.reshape(Bt * M, K).contiguous(), pw, None, batch=Bt, w_shared=b.dim() == 2)
+    return out.reshape(batch_shape + (M, N))
