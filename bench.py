@@ -61,7 +61,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default=None,
-                    choices=["c1", "c2", "c3", "c4", "c5", "attn", "outlier", "spmm", "dq"],
+                    choices=["c1", "c2", "c3", "c4", "c5", "attn", "outlier", "spmm", "dq",
+                             "nvf4"],
                     help="profiling aid: run only this workload's kernels, no JSON line")
     return ap.parse_args()
 
@@ -364,8 +365,14 @@ def run_ours(args):
                "d2h_bytes_per_step": elems * 4 * 3 + ROWS * (COLS // 64) * 4}
 
     secondary = {}
+    # one weight split by rows over the ranks (strong scaling; the shards
+    # need no collective: rows are independent, the per-tensor scale is the
+    # observer's)
+    shard = run_c2_row_sharded(dev, pg, rank, world, w, si, idx_tab, posit, sp, i8, args)
     if not args.no_secondary and rank == 0:
         secondary = run_secondary(dev, hbm_peak, peaks)
+    if rank == 0:
+        secondary["c2_row_sharded"] = shard
     if not args.no_secondary and world > 1:
         tp = run_tp_linear(dev, pg, world)
         if rank == 0:
@@ -422,6 +429,45 @@ def run_ours(args):
     if pg:
         pg.barrier()
         pg.destroy_process_group()
+
+
+def run_c2_row_sharded(dev, pg, rank, world, w, si, idx_tab, posit, sp, i8, args):
+    """The C2 step on this rank's rows of the one [11008, 4096] weight
+    (rows r * 11008 / N ..): GB/s of the whole tensor over the slowest rank."""
+    import torch
+
+    Q = torch.ops.quantized_ops
+    lo, hi = rank * ROWS // world, (rank + 1) * ROWS // world
+    ws, sis = w[lo:hi], si[lo:hi]
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        Q.quantize_mx(ws, idx_tab, [-1], 64, 1.0, False)
+        Q.quantize(ws, sp, qmap=posit)
+        Q.quantize(ws, sis, qmap=i8)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    steps = max(args.steps, 10)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(int(3 * steps * 40e-6 * 2e9))
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    if pg:
+        t = torch.tensor([ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    total = ROWS * COLS * sum(BYTES_PER_ELEM.values())
+    return {"ms_per_step": round(ms, 4), "GBps": round(total / (ms / 1e3) / 1e9, 1),
+            "gpus": world, "rows_per_gpu": hi - lo,
+            "note": "one C2 weight split by rows over the GPUs (strong scaling), max over ranks"}
 
 
 def _time_ms(fn, stream, reps=10, warm=3):
@@ -975,6 +1021,16 @@ def run_only(args):
         for _ in range(args.warmup + args.steps):
             for name, c, sc, cb, bs in fmts:
                 Q.linear_mx(a, c, None, weight_scale=sc, block_size=bs, weight_code=cb)
+    elif args.only == "nvf4":
+        # C3's shape with both operands NVFP4
+        a_np, w_np = synth.c3_operands()
+        e2m1, e4m3 = get_quantization_map("fp4_e2m1", dev), get_quantization_map("fp8_e4m3", dev)
+        a = torch.from_numpy(a_np.view(np.int16)).view(torch.bfloat16).to(dev)
+        wq = torch.from_numpy(w_np.view(np.int16)).view(torch.bfloat16).to(dev)
+        sa, ca = Q.quantize_mx(a, e2m1, [-1], 16, 6.0, False, e4m3)
+        sw, cw = Q.quantize_mx(wq, e2m1, [-1], 16, 6.0, False, e4m3)
+        for _ in range(args.warmup + args.steps):
+            Q.linear_mx(ca, cw, None, input_scale=sa, weight_scale=sw, block_size=16)
     elif args.only == "c4":
         from voyager_b200 import w4a8
 

@@ -679,11 +679,28 @@ __global__ void k_dq_pack_scales(const uint16_t* scale, int wb, int N, int Npad,
   out[i] = v;
 }
 
-// Which bf16 bit patterns occur: present[bits] = 1.
+// Which bf16 bit patterns occur: present[bits] = 1.  Each CTA gathers a
+// 65,536-bit set in shared memory first (a weight holds few patterns, so
+// direct stores would pile onto the same bytes), then writes out its bits.
 __global__ void k_dq_patterns(const uint16_t* codes, int64_t n, uint8_t* present) {
+  __shared__ uint32_t bits[2048];
+  for (int i = threadIdx.x; i < 2048; i += blockDim.x) bits[i] = 0;
+  __syncthreads();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x)
-    present[codes[i]] = 1;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t b = codes[i];
+    const uint32_t m = 1u << (b & 31);
+    if (!(bits[b >> 5] & m)) atomicOr(&bits[b >> 5], m);
+  }
+  __syncthreads();
+  for (int w = threadIdx.x; w < 2048; w += blockDim.x) {
+    uint32_t v = bits[w];
+    while (v) {
+      const int j = __ffs(v) - 1;
+      v &= v - 1;
+      present[w * 32 + j] = 1;
+    }
+  }
 }
 
 // dst[b][c][r] = src[b][r][c] for bf16 [batch][rows, cols]: 32 x 32 tiles
