@@ -48,6 +48,7 @@ WORKLOAD = ("C2 fp32 [11008,4096]: NF4 g64 quantize_mx / posit8_1 per-tensor / i
 # (ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum of the C2 kernels)
 NCU_TRAFFIC = {"int8_channel": int(311.5e6), "nf4_g64": int(310.4e6),
                "posit8_tensor": int(308.9e6)}
+L2_BYTES = 126e6  # B200 L2
 BYTES_PER_ELEM = {"nf4_g64": 4 + 4 + 4.0 / 64, "posit8_tensor": 8.0, "int8_channel": 8.0}
 
 
@@ -673,6 +674,34 @@ def _time_graph_ms(fn, stream, reps=20, warm=3):
     return ms
 
 
+def _time_rotating_ms(fns, stream, replays=3):
+    """Device time per call of `fns` (calls on operands that together exceed
+    L2, so that each call reads its own from HBM), captured in one CUDA graph
+    and replayed with the host queued ahead of the device."""
+    import torch
+
+    for f in fns:
+        f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for f in fns:
+            f()
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = torch.cuda.current_stream()
+    torch.cuda._sleep(int(replays * 20e-6 * 2e9))
+    a.record(st)
+    for _ in range(replays):
+        g.replay()
+    b.record(st)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / (replays * len(fns))
+    del g
+    return ms
+
+
 def run_secondary(dev, hbm_peak, peaks):
     import torch
 
@@ -919,6 +948,8 @@ def run_c4_sweep(dev, hbm_peak, bf16_peak):
     for (k, n) in [(4096, 4096), (4096, 14336), (14336, 4096)]:
         ca0, sa0, cw, sw, a0 = c4_operands(dev, 16384, k, n, seed=k + n, keep_input=True)
         e4m3 = get_quantization_map("fp8_e4m3", dev)
+        wbytes = n * k * (0.5 + 1 / 16)
+        copies = [cw] + [cw.clone() for _ in range(int(np.ceil(2.5 * L2_BYTES / wbytes)) - 1)]
         for m in (1, 16, 128, 1024, 16384):
             # the first m tokens quantized as a batch of m (the same codes as
             # the rows of the full batch: blocks run along K)
@@ -926,9 +957,15 @@ def run_c4_sweep(dev, hbm_peak, bf16_peak):
                                                          448.0, True)
             if m == 16384:
                 ca, sa = ca0, sa0
-            reps = 20 if m <= 1024 else 5
-            # graph replay: the small-M calls take microseconds on the device
-            ms = _time_graph_ms(lambda: w4a8.linear(ca, sa, cw, sw), stream, reps=reps)
+            if m <= 16:
+                # microsecond calls that stream the weights: one graph over
+                # copies of the weights larger than L2 together, so that
+                # every call reads its copy from HBM
+                ms = _time_rotating_ms([(lambda c=c: w4a8.linear(ca, sa, c, sw))
+                                        for c in copies], stream)
+            else:
+                ms = _time_graph_ms(lambda: w4a8.linear(ca, sa, cw, sw), stream,
+                                    reps=20 if m <= 1024 else 5)
             fl = 2.0 * m * n * k
             pt = {"M": m, "K": k, "N": n, "ms": round(ms, 4),
                   "TFLOPs": round(fl / (ms / 1e3) / 1e12, 2),
@@ -941,7 +978,7 @@ def run_c4_sweep(dev, hbm_peak, bf16_peak):
             else:
                 pt["frac_bf16"] = round(pt["TFLOPs"] / bf16_peak, 3)
             res.append(pt)
-        del ca0, sa0, cw, sw, a0
+        del ca0, sa0, cw, sw, a0, copies
         torch.cuda.empty_cache()
     return res
 

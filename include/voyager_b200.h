@@ -368,7 +368,8 @@ int vq_linear_mxf8_noalloc_status(int32_t* code, void* stream);
 
 /* Sticky wait-timeout status of this library's tcgen05 and barrier kernels
  * on the current device: *code (host) = 0, or the first code any launch
- * recorded since the last clear -- GEMM 1-4, tensor-parallel barrier
+ * recorded since the last clear -- GEMM 1-4, bf16 GEMM 11-14, W4A8 21-23,
+ * tensor-parallel barrier
  * 100 + rank, attention 200 + its code.  The per-call error words report to
  * one caller; this one lets the host ask, after a batch of work, whether any
  * launch gave up.  clear != 0 resets the word.  Synchronises `stream`.  The
@@ -492,24 +493,44 @@ int vq_tp_swiglu_quantize(const void* gate_up, int64_t ld_in, int64_t up_off, in
  * the operands dequantized with their own block sizes
  * (src/voyager_compiler/ops/quantized.py:455-472, 522-586). */
 
-/* Pack bf16 E2M1 codes [N, K] (K % 128 == 0) to nibbles [N, K/2] (even k in
- * the low nibble; within each 64-byte chunk of a row, byte 16b + 4i + t
- * stored at 16t + 4b + i: the order vq_w4a8_linear_small reads) and bf16
- * E4M3 scales [N, K/16] to bytes.  *d_inexact (device, may be NULL) counts
- * entries that are not such values. */
-int vq_w4_pack_weights(const vq_tensor* codes, const vq_tensor* scales, void* wq, void* ws,
+/* Bytes of the packed form of an NVFP4 weight [N, K] (K % 128 == 0): tiles
+ * of 256 rows x 128 K, 18432 bytes each, in (row block, K chunk) order; -1
+ * for shapes the packing does not take. */
+int64_t vq_w4_packed_bytes(int64_t N, int64_t K);
+
+/* Pack bf16 E2M1 codes [N, K] and bf16 E4M3 scales [N, K/16] into
+ * vq_w4_packed_bytes(N, K) bytes at `packed` (16-byte aligned): per tile,
+ * 256 rows of 64 nibble bytes (even k in the low nibble; within a row's 64
+ * bytes, byte 16b + 4i + t stored at 16t + 4b + i, the order
+ * vq_w4a8_linear_small reads), then the rows' 8 scale bytes; rows past N
+ * zero.  *d_inexact (device, may be NULL) counts entries that are not such
+ * values. */
+int vq_w4_pack_weights(const vq_tensor* codes, const vq_tensor* scales, void* packed,
                        int32_t* d_inexact, void* stream);
+
+/* Bytes of the float32 workspace vq_w4a8_linear_small needs for a weight
+ * [N, K]: the sums of row blocks split between CTAs, [ceil(N/256) * 256]
+ * rows x 16 tokens; -1 for shapes it does not take. */
+int64_t vq_w4a8_workspace_bytes(int64_t N, int64_t K);
 
 /* out[M, N] bf16 = A . W^T (+ bias) for M <= 16 tokens in one launch from
  * MXFP8 tokens (bf16 E4M3 codes [M, K], bf16 power-of-two scales [M, K/32],
- * K % 128 == 0) and the packed weights, streamed once.
- * `workspace` (float32, >= M * N) and `counters` (int32, >= ceil(N / 256))
- * must be zero before the first call; every call leaves them zero, so a
- * caller keeps one pair per weight (calls that overlap on the GPU with the
- * same pair race). */
-int vq_w4a8_linear_small(const vq_tensor* a_codes, const vq_tensor* a_scales, const void* wq,
-                         const void* ws, int64_t N, const void* bias, float* workspace,
-                         int32_t* counters, void* out, void* stream);
+ * K % 128 == 0) and the packed weights, streamed once.  `workspace`
+ * (vq_w4a8_workspace_bytes(N, K) bytes, or more) and `counters` (int32,
+ * >= ceil(N / 256)) must be zero before the first call and every call
+ * leaves them zero, so calls that never overlap on the GPU (one stream) can
+ * share one pair sized for the largest weight; overlapping calls with the
+ * same pair race.  *d_err (device, may be NULL) receives the code of the
+ * first bounded wait that gave up (21-24; the result is then not valid).
+ * The kernel is launched with programmatic stream serialization: it may
+ * start while the previous kernel on the stream finishes and reads the
+ * packed weights before waiting for it (everything else after), so the
+ * packed weights must not be written by a kernel that is the one just
+ * before it on the stream and that triggers its dependents early
+ * (vq_w4_pack_weights does not). */
+int vq_w4a8_linear_small(const vq_tensor* a_codes, const vq_tensor* a_scales, const void* packed,
+                         int64_t N, const void* bias, float* workspace, int32_t* counters,
+                         int32_t* d_err, void* out, void* stream);
 
 /* The per-block parameters of quantized_ops::quantize_affine
  * (quantized.py:884-948): for blocks of `block_size` elements along the one

@@ -1238,6 +1238,9 @@ int sticky_tp(int* out, int clear, cudaStream_t st);
 namespace dq {
 int sticky_dq(int* out, int clear, cudaStream_t st);
 }
+namespace w4 {
+int sticky_w4(int* out, int clear, cudaStream_t st);
+}
 }  // namespace vq
 
 using namespace vq::mx;
@@ -1516,13 +1519,14 @@ int vq_linear_mxf8_noalloc_status(int32_t* code, void* stream) {
 int vq_device_errors(int32_t* code, int32_t clear, void* stream) {
   if (!code) return VQ_ERR_NULL;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  int v[4] = {0, 0, 0, 0};
+  int v[5] = {0, 0, 0, 0, 0};
   if (vq::tc::sticky_read(&v[0], clear, s) || vq::dq::sticky_dq(&v[1], clear, s) ||
-      vq::tp::sticky_tp(&v[2], clear, s) || vq::attn::sticky_attn(&v[3], clear, s))
+      vq::tp::sticky_tp(&v[2], clear, s) || vq::attn::sticky_attn(&v[3], clear, s) ||
+      vq::w4::sticky_w4(&v[4], clear, s))
     return VQ_ERR_CUDA;
-  // the first nonzero word: MXFP8 GEMM 1-4, bf16 GEMM 11-14, tensor-parallel
-  // barrier 100 + rank, attention 200 + its code
-  *code = v[0] ? v[0] : (v[1] ? v[1] : (v[2] ? v[2] : (v[3] ? 200 + v[3] : 0)));
+  // the first nonzero word: MXFP8 GEMM 1-4, bf16 GEMM 11-14, W4A8 21-23,
+  // tensor-parallel barrier 100 + rank, attention 200 + its code
+  *code = v[0] ? v[0] : (v[1] ? v[1] : (v[4] ? v[4] : (v[2] ? v[2] : (v[3] ? 200 + v[3] : 0))));
   return VQ_OK;
 }
 

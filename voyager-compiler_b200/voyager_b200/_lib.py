@@ -189,10 +189,12 @@ _SIGNATURES = {
                                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                              ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                              ctypes.c_void_p]),
+    "vq_w4_packed_bytes": (ctypes.c_int64, [ctypes.c_int64, ctypes.c_int64]),
     "vq_w4_pack_weights": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p,
-                                          ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+                                          ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_w4a8_workspace_bytes": (ctypes.c_int64, [ctypes.c_int64, ctypes.c_int64]),
     "vq_w4a8_linear_small": (ctypes.c_int, [P(VqTensor), P(VqTensor), ctypes.c_void_p,
-                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                            ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                             ctypes.c_void_p]),
     "vq_rounder_check_hw": (ctypes.c_int, [P(VqRounder), ctypes.c_void_p, ctypes.c_void_p]),

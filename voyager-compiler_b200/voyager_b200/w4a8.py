@@ -11,10 +11,12 @@ own block size (``_dequantize_mx``, ``quantized.py:455-472``), then
 
 Paths:
   * M <= 16 tokens (HBM-bound): ``vq_w4a8_linear_small`` streams the packed
-    weights (0.5625 B per weight) in one launch: 16-byte loads of rows
-    permuted at pack time, f16 mma.sync tiles on exact operands (weights
-    times their E4M3 scales, raw E4M3 token codes), token scales on the
-    float32 block sums, split-K finished by the last CTA of each row block;
+    weights (0.5625 B per weight, 18 KB tiles of 256 rows x 128 K) in one
+    launch: a persistent grid whose CTAs each take an equal run of tiles,
+    bulk copies into a shared-memory ring, f16 mma.sync tiles on exact
+    operands (weights times their E4M3 scales, token codes times their
+    power-of-two scales relative to the token's largest), row blocks split
+    between CTAs summed from float32 pieces by the CTA that adds the last;
   * larger M (compute-bound): the tcgen05 bf16 GEMM (``voyager_b200.dqgemm``)
     with the weight kept as 4-bit palette indices and its E4M3 block-16
     scales, read back in shared memory (code x scale, exact in bf16), and
@@ -33,7 +35,7 @@ from voyager_b200._cache import TensorCache
 SMALL_M = 16
 _wpack = TensorCache()
 _wdeq = TensorCache()
-_wwork = TensorCache()
+_wspace = {}
 
 
 def _packed_weight(w_codes, w_scale):
@@ -43,16 +45,15 @@ def _packed_weight(w_codes, w_scale):
         return hit
     N, K = w_codes.shape
     dev = w_codes.device
-    wq = torch.empty(N * K // 2, dtype=torch.uint8, device=dev)
-    ws = torch.empty(N * K // 16, dtype=torch.uint8, device=dev)
+    lib = _lib.load()
+    wt = torch.empty(lib.vq_w4_packed_bytes(N, K), dtype=torch.uint8, device=dev)
     bad = torch.zeros(1, dtype=torch.int32, device=dev)
-    st = _lib.load().vq_w4_pack_weights(_ops._ref(_ops._vt(w_codes.contiguous())),
-                                        _ops._ref(_ops._vt(w_scale.contiguous())),
-                                        wq.data_ptr(), ws.data_ptr(), bad.data_ptr(),
-                                        _ops._stream(dev))
+    st = lib.vq_w4_pack_weights(_ops._ref(_ops._vt(w_codes.contiguous())),
+                                _ops._ref(_ops._vt(w_scale.contiguous())), wt.data_ptr(),
+                                bad.data_ptr(), _ops._stream(dev))
     _lib.check(st, "w4a8 weight pack")
     ok = int(bad.item()) == 0
-    return _wpack.put(w_codes, key, (wq, ws, ok))
+    return _wpack.put(w_codes, key, (wt, ok))
 
 
 def _exact_tokens(a_codes, a_scale, a2, s2) -> bool:
@@ -67,15 +68,19 @@ def _exact_tokens(a_codes, a_scale, a2, s2) -> bool:
     return mxgemm._pack(a2, s2, 128, True)[2]
 
 
-def _workspace(w_codes, N):
-    """The self-cleaning split-K workspace of one weight: float32 [16 * N]
-    and the row-block counters, zero when made and left zero by each call."""
-    hit = _wwork.get(w_codes, "ws")
-    if hit is None:
-        dev = w_codes.device
-        hit = _wwork.put(w_codes, "ws", (torch.zeros(16 * N, dtype=torch.float32, device=dev),
-                                         torch.zeros((N + 255) // 256, dtype=torch.int32,
-                                                     device=dev)))
+def _workspace(dev, N, K):
+    """The workspace of the calls on the current stream: the float32 sums of
+    row blocks split between CTAs and the row-block counters, zero when
+    made and left zero by each call.  Calls on one stream never overlap, so
+    they share one pair, grown to the largest weight."""
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    need = (_lib.load().vq_w4a8_workspace_bytes(N, K) // 4, (N + 255) // 256)
+    hit = _wspace.get(key)
+    if hit is None or hit[0].numel() < need[0] or hit[1].numel() < need[1]:
+        have = (hit[0].numel(), hit[1].numel()) if hit is not None else (0, 0)
+        hit = (torch.zeros(max(need[0], have[0]), dtype=torch.float32, device=dev),
+               torch.zeros(max(need[1], have[1]), dtype=torch.int32, device=dev))
+        _wspace[key] = hit
     return hit
 
 
@@ -106,18 +111,27 @@ def linear(a_codes: torch.Tensor, a_scale: torch.Tensor, w_codes: torch.Tensor,
     M = a_codes.numel() // K
     dev = a_codes.device
     if applies_small(a_codes, w_codes):
-        wq, ws, wok = _packed_weight(w_codes, w_scale)
+        wt, wok = _packed_weight(w_codes, w_scale)
         a2 = a_codes.reshape(M, K).contiguous()
         s2 = a_scale.reshape(M, K // 32).contiguous()
         if wok and _exact_tokens(a_codes, a_scale, a2, s2):
-            acc, done = _workspace(w_codes, N)
+            from voyager_b200 import mxgemm
+
+            part, done = _workspace(dev, N, K)
             out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            # the per-call error word costs a memset between consecutive
+            # calls (no overlap of one call's start with the previous one's
+            # end): only when checking; the sticky device word always records
+            err = (torch.empty(1, dtype=torch.int32, device=dev) if mxgemm.CHECK_ERRORS
+                   else None)
             b = bias.contiguous() if bias is not None else None
             _lib.check(_lib.load().vq_w4a8_linear_small(
-                _ops._ref(_ops._vt(a2)), _ops._ref(_ops._vt(s2)), wq.data_ptr(), ws.data_ptr(),
-                N, b.data_ptr() if b is not None else None, ctypes.c_void_p(acc.data_ptr()),
-                ctypes.c_void_p(done.data_ptr()), out.data_ptr(), _ops._stream(dev)),
-                "w4a8 linear")
+                _ops._ref(_ops._vt(a2)), _ops._ref(_ops._vt(s2)), wt.data_ptr(), N,
+                b.data_ptr() if b is not None else None, ctypes.c_void_p(part.data_ptr()),
+                ctypes.c_void_p(done.data_ptr()), err.data_ptr() if err is not None else None,
+                out.data_ptr(), _ops._stream(dev)), "w4a8 linear")
+            if err is not None and int(err.item()) != 0:
+                raise _lib.VqError(f"w4a8 linear: device wait timed out (code {int(err.item())})")
             return out.reshape(tuple(lead) + (N,))
     from voyager_b200 import dqgemm
 
