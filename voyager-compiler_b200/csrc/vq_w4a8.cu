@@ -65,6 +65,8 @@ constexpr int ERR_TIMEOUT_FULL = 21;   // a compute warp waited for a tile
 constexpr int ERR_TIMEOUT_EMPTY = 22;  // the producer waited for a free stage
 constexpr int ERR_TIMEOUT_DRAIN = 23;  // the producer waited for its last copies
 constexpr int ERR_TIMEOUT_FLUSH = 24;  // the epilogue warp waited for the compute warps' sums
+constexpr int ERR_TIMEOUT_STAGED = 25;  // the producer waited for the tokens to be staged
+constexpr int FILL0 = 4;  // tiles in flight before the tokens are staged
 
 struct Args {
   const uint8_t* wt;   // packed tiles [row blocks][chunks][TILE_BYTES]
@@ -88,6 +90,21 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
   asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(r) : "r"(two_bytes));
   return r;
 }
+// The four E2M1 pairs of a word (its bytes, low first) as f16x2.
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&r)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "r"(w));
+}
+// The two E4M3 pairs of a word (its 16-bit halves, low first) as f16x2.
+__device__ __forceinline__ void e4m3x4_to_f16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 h0, h1;\n\tmov.b32 {h0, h1}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, h0;\n\tcvt.rn.f16x2.e4m3x2 %1, h1;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
   return *reinterpret_cast<uint32_t*>(&r);
@@ -108,7 +125,6 @@ __device__ __forceinline__ void consumers_sync() {  // the compute warps only
   asm volatile("bar.sync 1, %0;" ::"n"(CWARPS * 32) : "memory");
 }
 
-__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFFu; }
 // a * (b.lo, b.lo) / a * (b.hi, b.hi): the broadcast is an operand select of
 // the f16x2 multiply
 __device__ __forceinline__ uint32_t hmul2_lo(uint32_t a, uint32_t b) {
@@ -125,11 +141,6 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-// Scale bytes 2q, 2q + 1 of a row's 8 (the chunk's 16-blocks).
-__device__ __forceinline__ uint32_t scale_pair(uint2 s, int q) {
-  return q == 0 ? s.x & 0xFFFFu : q == 1 ? s.x >> 16 : q == 2 ? s.y & 0xFFFFu : s.y >> 16;
-}
 
 // Staged position of the token value at offset kk of a CTA's staged K:
 // within each 32-block, thread t's B fragments of the two MMA steps h
@@ -152,6 +163,13 @@ template <int NT, bool SCALED>
 __device__ __forceinline__ void w4a8_chunk(const uint4 (&wc)[2 * MT], const uint2 (&scc)[2 * MT], int kc,
                                            const uint16_t* tok, const float* tsc, int ks, int nkb,
                                            int g, int t, float (&acc)[2][MT][NT][4]) {
+  // the rows' 8 block scales as f16 pairs (2q, 2q + 1)
+  uint32_t scl[2 * MT][4];
+#pragma unroll
+  for (int r = 0; r < 2 * MT; ++r) {
+    e4m3x4_to_f16x2(scc[r].x, scl[r][0], scl[r][1]);
+    e4m3x4_to_f16x2(scc[r].y, scl[r][2], scl[r][3]);
+  }
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
     uint4 bt[NT];  // token g (+ 8 nt) of block b: (h0 lo, h0 hi, h1 lo, h1 hi) f16 pairs
@@ -173,18 +191,18 @@ __device__ __forceinline__ void w4a8_chunk(const uint4 (&wc)[2 * MT], const uint
     }();
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-      const uint32_t wa = (&wc[2 * mt].x)[b], wb = (&wc[2 * mt + 1].x)[b];
+      // this block's codes of rows g (A) and g + 8 (B) of m-tile mt: byte
+      // 2h + u holds the pair of MMA step h, k 2t (+8u)
+      uint32_t da[4], db[4];
+      e2m1x8_to_f16x2((&wc[2 * mt].x)[b], da);
+      e2m1x8_to_f16x2((&wc[2 * mt + 1].x)[b], db);
       // block scales 2b, 2b + 1 of the two rows as f16 pairs
-      const uint32_t pa = e4m3x2_to_f16x2(scale_pair(scc[2 * mt], b));
-      const uint32_t pb = e4m3x2_to_f16x2(scale_pair(scc[2 * mt + 1], b));
+      const uint32_t pa = scl[2 * mt][b], pb = scl[2 * mt + 1][b];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        // 16-block 2b + h of rows g (A) and g + 8 (B) of m-tile mt
         auto mul = [h](uint32_t x, uint32_t s) { return h ? hmul2_hi(x, s) : hmul2_lo(x, s); };
-        const uint32_t a0 = mul(e2m1x2_to_f16x2(byte_of(wa, 2 * h)), pa);
-        const uint32_t a2 = mul(e2m1x2_to_f16x2(byte_of(wa, 2 * h + 1)), pa);
-        const uint32_t a1 = mul(e2m1x2_to_f16x2(byte_of(wb, 2 * h)), pb);
-        const uint32_t a3 = mul(e2m1x2_to_f16x2(byte_of(wb, 2 * h + 1)), pb);
+        const uint32_t a0 = mul(da[2 * h], pa), a2 = mul(da[2 * h + 1], pa);
+        const uint32_t a1 = mul(db[2 * h], pb), a3 = mul(db[2 * h + 1], pb);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
           mma_f16(dst[mt][nt], a0, a1, a2, a3, h ? bt[nt].z : bt[nt].x, h ? bt[nt].w : bt[nt].y);
@@ -388,11 +406,12 @@ __device__ __forceinline__ void epilogue(const Args& p, int t0, int t1, uint32_t
 
 // Shared memory: the ring, then the staged tokens f16 [8 NT][L * 128 +
 // TPAD] in fragment order (tok_pos), their block scales float [8 NT][4 L],
-// the per-token exponents, a flag and the mbarriers (full, empty, flushed).
+// the per-token exponents, a flag and the mbarriers (full, empty, flushed,
+// staged).
 __host__ __device__ constexpr int tok_offset() { return STAGES * TILE_BYTES; }
 __host__ __device__ constexpr int smem_bytes(int nt, int L) {
   return STAGES * TILE_BYTES + 8 * nt * (L * 128 + TPAD) * 2 + 8 * nt * L * 4 * 4 + 16 * 4 + 16 +
-         (2 * STAGES + 2) * 8 + 8;
+         (2 * STAGES + 3) * 8 + 8;
 }
 
 // Tokens are staged once per CTA as f16 c * 2^(e - E): c the E4M3 code, 2^e
@@ -419,7 +438,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_w4a8(const __grid_constant__ Arg
   uint64_t* bars = reinterpret_cast<uint64_t*>(
       (reinterpret_cast<uintptr_t>(flags + 4) + 7) & ~uintptr_t(7));
   const uint32_t full0 = tc::smem_u32(bars), empty0 = full0 + 8 * STAGES,
-                 flushed0 = empty0 + 8 * STAGES;
+                 flushed0 = empty0 + 8 * STAGES, staged0 = flushed0 + 16;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(full0 + 8 * s, 1);
@@ -427,6 +446,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_w4a8(const __grid_constant__ Arg
     }
     tc::mbar_init(flushed0, CWARPS);
     tc::mbar_init(flushed0 + 8, CWARPS);
+    tc::mbar_init(staged0, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (threadIdx.x < 16) emax[threadIdx.x] = 0;
@@ -436,16 +456,20 @@ __global__ void __launch_bounds__(THREADS, 1) k_w4a8(const __grid_constant__ Arg
 
   if (warp == PRODUCER) {
     // ---------------- producer: the CTA's tiles, in order ----------------
-    // the first fill of the ring from one lane per stage, the rest by lane 0
-    const int n = t1 - t0, first_fill = min(n, STAGES);
+    // the first tiles from one lane each, at once (the weights are
+    // constant: before the wait for the previous grid); the rest of the
+    // ring once the tokens are staged (their loads do not queue behind the
+    // whole ring), then by lane 0 as stages free up
+    const int n = t1 - t0, first_fill = min(n, FILL0);
     if (lane < first_fill) {
       tc::mbar_expect_tx(full0 + 8 * lane, TILE_BYTES);
       tc::bulk_load(tc::smem_u32(ring + (size_t)lane * TILE_BYTES),
                     p.wt + (size_t)(t0 + lane) * TILE_BYTES, TILE_BYTES, full0 + 8 * lane);
     }
     if (lane == 0) {
-      int k = first_fill;
-      for (; k < n; ++k) {
+      int k = first_fill;  // tiles issued
+      const bool go = k >= n || tc::mbar_wait(staged0, 0, p.err, ERR_TIMEOUT_STAGED);
+      for (; go && k < n; ++k) {
         const int s = k % STAGES;
         if (!tc::mbar_wait(empty0 + 8 * s, ((uint32_t)(k / STAGES) & 1u) ^ 1u, p.err,
                            ERR_TIMEOUT_EMPTY))
@@ -470,10 +494,28 @@ __global__ void __launch_bounds__(THREADS, 1) k_w4a8(const __grid_constant__ Arg
   }
 
   // ---------------- compute warps: stage the tokens ----------------
-  // staged chunk j is K chunk (cstart + j) % chunks
+  // staged chunk j is K chunk (cstart + j) % chunks; rows M .. 8 NT - 1 are
+  // zero tokens with zero scales: their output columns (never written) add
+  // exact zeros into the shared workspace.  Item i of the codes is row
+  // i / (16 L), 8 codes at K offset 8 (i % (16 L)); every thread's code
+  // loads go out first, with the scale loads, in one round trip.
+  constexpr int NITEM = (8 * NT * LMAX * 16 + CWARPS * 32 - 1) / (CWARPS * 32);
+  const int nitem = 8 * NT * L * 16;
+  auto item = [&](int i, int& m, int& kk, int& kg) {
+    m = i / (L * 16);
+    kk = (i % (L * 16)) * 8;
+    kg = ((cstart + kk / 128) % p.chunks) * 128 + kk % 128;
+  };
+  uint4 cvv[NITEM];
+#pragma unroll
+  for (int u = 0; u < NITEM; ++u) {
+    const int i = threadIdx.x + u * CWARPS * 32;
+    cvv[u] = make_uint4(0, 0, 0, 0);
+    int m, kk, kg;
+    item(i, m, kk, kg);
+    if (i < nitem && m < p.M) cvv[u] = *reinterpret_cast<const uint4*>(p.ac + (size_t)m * p.K + kg);
+  }
   int slow = 0;
-  // rows M .. 8 NT - 1 are zero tokens with zero scales: their output
-  // columns (never written) add exact zeros into the shared workspace
   for (int i = threadIdx.x; i < 8 * NT * nkb; i += CWARPS * 32) {
     const int m = i / nkb, jb = i % nkb;
     const int kb = ((cstart + jb / 4) % p.chunks) * 4 + jb % 4;
@@ -486,11 +528,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_w4a8(const __grid_constant__ Arg
     }
   }
   consumers_sync();
-  for (int i = threadIdx.x; i < 8 * NT * L * 16; i += CWARPS * 32) {
-    const int m = i / (L * 16), kk = (i % (L * 16)) * 8;
-    const int kg = ((cstart + kk / 128) % p.chunks) * 128 + kk % 128;
-    const uint4 v = m < p.M ? *reinterpret_cast<const uint4*>(p.ac + (size_t)m * p.K + kg)
-                            : make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int u = 0; u < NITEM; ++u) {
+    const int i = threadIdx.x + u * CWARPS * 32;
+    if (i >= nitem) break;
+    int m, kk, kg;
+    item(i, m, kk, kg);
     const uint32_t sb = __float_as_uint(tsc[m * nkb + kk / 32]) >> 16;
     // 2^d, d = e - E <= 0: an E4M3 code's last bit is >= 2^-9, so c * 2^d
     // is exact in f16 for d >= -15 (and below 448 <= 65504)
@@ -500,7 +543,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_w4a8(const __grid_constant__ Arg
       if (d >= -15) f = __uint_as_float((uint32_t)(d + 127) << 23);
       else slow = 1;
     }
-    const uint32_t cv[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t cv[4] = {cvv[u].x, cvv[u].y, cvv[u].z, cvv[u].w};
     uint16_t* row = tok + m * ks;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -512,12 +555,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_w4a8(const __grid_constant__ Arg
   consumers_sync();
   slow = flags[0];
   if (slow) {  // the raw codes (exact in f16), scales applied per 32-block
-    for (int i = threadIdx.x; i < 8 * NT * L * 16; i += CWARPS * 32) {
-      const int m = i / (L * 16), kk = (i % (L * 16)) * 8;
-      const int kg = ((cstart + kk / 128) % p.chunks) * 128 + kk % 128;
-      const uint4 v = m < p.M ? *reinterpret_cast<const uint4*>(p.ac + (size_t)m * p.K + kg)
-                              : make_uint4(0, 0, 0, 0);
-      const uint32_t cv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int u = 0; u < NITEM; ++u) {
+      const int i = threadIdx.x + u * CWARPS * 32;
+      if (i >= nitem) break;
+      int m, kk, kg;
+      item(i, m, kk, kg);
+      const uint32_t cv[4] = {cvv[u].x, cvv[u].y, cvv[u].z, cvv[u].w};
       uint16_t* row = tok + m * ks;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -527,6 +571,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_w4a8(const __grid_constant__ Arg
     }
     consumers_sync();
   }
+  if (threadIdx.x == 0) tc::mbar_arrive(staged0);  // the producer may fill the rest of the ring
   // C fragment columns are tokens 8 nt + 2t, + 1; the scaled sums are 2^-E
   // of the token's
   const int t = lane & 3;
