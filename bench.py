@@ -267,10 +267,8 @@ def run_ours(args):
     idx_tab = index_table(get_quantization_map("lut4")).to(dev)
     posit = get_quantization_map("posit8_1", dev)
     i8 = get_quantization_map("int8", dev)
-    # observer scales, divided on the host as the reference's observer does
-    sp = torch.tensor(np.abs(w_host).max() / np.float32(4096.0), dtype=torch.float32).to(dev)
-    si = torch.from_numpy((np.abs(w_host).max(axis=1, keepdims=True)
-                           / np.float32(127.0)).astype(np.float32)).to(dev)
+    # the scales as calibration leaves them: the device amax observer
+    sp, si = observed_scales(w)
     stream = torch.cuda.current_stream(dev)
 
     def step():
@@ -374,6 +372,8 @@ def run_ours(args):
         secondary = run_secondary(dev, hbm_peak, peaks)
     if rank == 0:
         secondary["c2_row_sharded"] = shard
+    if not args.no_secondary and rank == 0:
+        secondary["c2_amax_observer"] = run_observer(w, stream, hbm_peak)
     if not args.no_secondary and world > 1:
         tp = run_tp_linear(dev, pg, world)
         if rank == 0:
@@ -469,6 +469,45 @@ def run_c2_row_sharded(dev, pg, rank, world, w, si, idx_tab, posit, sp, i8, args
     return {"ms_per_step": round(ms, 4), "GBps": round(total / (ms / 1e3) / 1e9, 1),
             "gpus": world, "rows_per_gpu": hi - lo,
             "note": "one C2 weight split by rows over the GPUs (strong scaling), max over ranks"}
+
+
+def observed_scales(w, hist=None):
+    """C2's per-tensor (posit8_1, quant_max 4096) and per-output-channel
+    (int8, quant_max 127) scales as the reference's calibration leaves them
+    for a constant weight: two steps of the FusedAmaxObsFakeQuantize amax
+    observer with a history of one (the first step only fills the history)."""
+    import torch
+
+    from voyager_b200.observer import update_amax_scale
+
+    dev = w.device
+    hp, sp = torch.zeros(1, device=dev), torch.ones((), device=dev)
+    hi, si = torch.zeros(1, w.shape[0], 1, device=dev), torch.ones(w.shape[0], 1, device=dev)
+    for _ in range(2):
+        update_amax_scale(w, hp, sp, 4096.0, per_channel=False)
+        update_amax_scale(w, hi, si, 127.0, per_channel=True, ch_axis=0)
+    return sp, si
+
+
+def run_observer(w, stream, hbm_peak):
+    """One amax-observer step on the C2 weight (fp32 [11008, 4096], larger
+    than L2), per output channel and per tensor: reads 180 MB each."""
+    import torch
+
+    from voyager_b200.observer import update_amax_scale
+
+    dev = w.device
+    hi, si = torch.zeros(2, w.shape[0], 1, device=dev), torch.ones(w.shape[0], 1, device=dev)
+    hp, sp = torch.zeros(2, device=dev), torch.ones((), device=dev)
+    tc = _time_ms(lambda: update_amax_scale(w, hi, si, 127.0, per_channel=True, ch_axis=0,
+                                            power_of_two=True), stream, reps=20)
+    tt = _time_ms(lambda: update_amax_scale(w, hp, sp, 4096.0, per_channel=False), stream, reps=20)
+    nbytes = w.numel() * w.element_size()
+    return {"per_channel_ms": round(tc, 4), "per_channel_GBps": round(nbytes / (tc / 1e3) / 1e9, 1),
+            "per_tensor_ms": round(tt, 4), "per_tensor_GBps": round(nbytes / (tt / 1e3) / 1e9, 1),
+            "frac_hbm_per_channel": round(nbytes / (tc / 1e3) / 1e9 / hbm_peak, 3),
+            "note": "FusedAmaxObsFakeQuantize._update_amax_scale on the device: memset, amax "
+                    "reduction, history / scale update (3 launches); bytes = the weight read once"}
 
 
 def _time_ms(fn, stream, reps=10, warm=3):
@@ -1004,9 +1043,7 @@ def run_only(args):
         w = torch.from_numpy(w_host).to(dev)
         idx_tab = index_table(get_quantization_map("lut4")).to(dev)
         posit, i8 = get_quantization_map("posit8_1", dev), get_quantization_map("int8", dev)
-        sp = torch.tensor(np.abs(w_host).max() / np.float32(4096.0)).to(dev)
-        si = torch.from_numpy((np.abs(w_host).max(axis=1, keepdims=True)
-                               / np.float32(127.0)).astype(np.float32)).to(dev)
+        sp, si = observed_scales(w)
         for _ in range(args.warmup + args.steps):
             Q.quantize_mx(w, idx_tab, [-1], 64, 1.0, False)
             Q.quantize(w, sp, qmap=posit)

@@ -544,6 +544,25 @@ int vq_quantize_affine_qparams(const vq_tensor* input, const int64_t* axes, int3
                                const vq_rounder* scale_qmap, vq_tensor* scale_out,
                                vq_tensor* zero_point_out, void* stream);
 
+/* The observer step of per-tensor / per-channel symmetric fake quantization,
+ * FusedAmaxObsFakeQuantize._update_amax_scale
+ * (src/voyager_compiler/quantization/fake_quantize.py:494-527), on the
+ * device.  input: bf16 or float32, at least one element.  C = 1 (per-tensor)
+ * or input->shape[ch_axis] (per_channel; ch_axis already reduced to
+ * 0 .. ndim - 1).  amax_history: float32 [history_len, C]; scale: float32
+ * [C]; workspace: float32 [C] scratch.  With reset != 0 the history is first
+ * set to zero and the scale to one (the reference's lazy sizing).  Then
+ *   amax     = max over the history rows as they were (NaN propagates),
+ *   history  = roll(history, -1, 0) with row 0 = amax of |input| (over every
+ *              axis, or every axis but ch_axis),
+ *   scale    = amax / quant_max where amax > 0 and finite, else unchanged,
+ *              then 2^ceil(log2(scale)) when power_of_two.
+ * Bit-exact with the reference on float32.  Two launches and one memset of
+ * the workspace. */
+int vq_amax_observe(const vq_tensor* input, int32_t per_channel, int32_t ch_axis,
+                    float* amax_history, int64_t history_len, float* scale, float quant_max,
+                    int32_t power_of_two, int32_t reset, float* workspace, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Outlier CSR side-stream (quantized.py:958-1327)
  * ------------------------------------------------------------------------- */

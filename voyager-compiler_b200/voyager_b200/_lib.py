@@ -202,6 +202,10 @@ _SIGNATURES = {
                                                   ctypes.c_int64, ctypes.c_float, ctypes.c_float,
                                                   P(VqRounder), P(VqTensor), P(VqTensor),
                                                   ctypes.c_void_p]),
+    "vq_amax_observe": (ctypes.c_int, [P(VqTensor), ctypes.c_int32, ctypes.c_int32,
+                                       ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                       ctypes.c_float, ctypes.c_int32, ctypes.c_int32,
+                                       ctypes.c_void_p, ctypes.c_void_p]),
     "vq_outlier_threshold_bits": (ctypes.c_uint32, [ctypes.c_double, ctypes.c_int32]),
     "vq_filter_outlier_workspace_bytes": (ctypes.c_size_t, [P(VqTensor)]),
     "vq_filter_outlier": (ctypes.c_int, [P(VqTensor), ctypes.c_double, ctypes.c_int64,
