@@ -284,6 +284,20 @@ int vq_gemm_dq(const void* a, int64_t batch, int64_t M, int64_t K, int32_t mode,
                int32_t w_shared, int64_t N, const void* w_scale4, const void* palette,
                const void* bias, void* out, int64_t ldo, int64_t out_batch_stride, int32_t* d_err,
                void* stream);
+/* vq_gemm_dq with each output tile's K steps split over `splits` CTA pairs
+ * (the same op, quantized.py:455-472, 522-648, for few output tiles: small M
+ * times small N).  splits == 1 is vq_gemm_dq.  splits > 1: batch 1, the K
+ * steps (ceil(K / 64)) a multiple of splits, workspace float32
+ * [splits, M, N] (16-byte aligned, no initial value needed): each slice
+ * stores its float32 sums there, then a second launch adds the slices in
+ * order, adds the bias and rounds once to bf16. */
+int vq_gemm_dq_ex(const void* a, int64_t batch, int64_t M, int64_t K, int32_t mode, const void* w,
+                  int32_t w_shared, int64_t N, const void* w_scale4, const void* palette,
+                  const void* bias, void* out, int64_t ldo, int64_t out_batch_stride,
+                  int32_t splits, float* workspace, int32_t* d_err, void* stream);
+/* The split count vq_gemm_dq_ex uses best for these sizes on this device (1:
+ * no split). */
+int32_t vq_gemm_dq_splits(int64_t batch, int64_t M, int64_t N, int64_t K);
 /* Bytes of the packed indices and quarter-step scales of wbatch weights
  * [N, K] (mode 1: 4-bit, 2: 8-bit): with KS = ceil(K / 64) and Npad = N
  * rounded up to 256, wbatch * KS * Npad * (32 | 64) and wbatch * KS * Npad * 8. */

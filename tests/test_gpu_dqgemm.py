@@ -209,3 +209,32 @@ def test_w4a8_large_m(m):
                             oracle.dequantize_mx(cw, sw, None, 16))
     got = to_np(w4a8.linear(to_dev(ca), to_dev(sa), to_dev(cw), to_dev(sw)))
     assert G.rel_l2(got, want) < 1e-3
+
+
+@pytest.mark.parametrize("fmt", ["nvfp4", "posit8_bs32", "bf16"])
+@pytest.mark.parametrize("m,k,n,splits", [(128, 4096, 4096, 4), (40, 200, 264, 2),
+                                          (130, 1024, 520, 16), (256, 14336, 512, 7)])
+def test_split_k(fmt, m, k, n, splits):
+    """K steps split over several CTA pairs per output tile (float32 slices
+    added in order by the finalize launch) against the oracle and against the
+    unsplit kernel; K and N tails, a bias, rows past M in the CTA pair."""
+    from voyager_b200 import _lib, dqgemm
+
+    rng = np.random.default_rng(m + k + n + splits)
+    a = _bf16(rng, (m, k), 1.0)
+    w = _bf16(rng, (n, k), 0.02)
+    bias = _bf16(rng, (n,), 0.1)
+    c, s, cb, bs = weight_format(fmt, w)
+    want = oracle.linear_mx(a, c, bias, weight_scale=s, block_size=bs, weight_code=cb)
+    pw = dqgemm.packed_weight(to_dev(c), to_dev(s), to_dev(cb), bs, "kc")
+    a_dev = to_dev(a)
+    one = to_np(dqgemm.gemm(a_dev, pw, to_dev(bias), splits=1)[0])
+    got = to_np(dqgemm.gemm(a_dev, pw, to_dev(bias), splits=splits)[0])
+    assert G.rel_l2(got, want) < 1e-3
+    assert G.rel_l2(got, one) < 1e-3
+    # the library's own choice for C4's M = 128 shapes splits the K steps
+    lib = _lib.load()
+    assert lib.vq_gemm_dq_splits(1, 128, 4096, 4096) > 1
+    assert lib.vq_gemm_dq_splits(1, 128, 4096, 14336) > 1
+    assert lib.vq_gemm_dq_splits(1, 8192, 11008, 4096) == 1
+    assert lib.vq_gemm_dq_splits(2, 128, 4096, 4096) == 1

@@ -137,6 +137,11 @@ struct DqArgs {
   int MT2, NTN, ntiles;   // 256-row tiles per batch, 256-column tiles, all tiles
   int w_shared;           // one weight for every batch
   int* err;
+  // split-K (one batch): unit u is K slice u % S of tile u / S, KSU steps
+  // from step (u % S) * KSU; with S > 1 the epilogue stores float32 partial
+  // sums into part [S][M][N] and k_dq_finalize adds them up
+  int S, KSU, nunits;
+  float* part;
 };
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
@@ -197,6 +202,13 @@ __device__ __forceinline__ void tile_of(const DqArgs& g, int t, int& b, int& tm,
   const int r = t - b * per_b;
   tm = r / g.NTN;
   tn = r - tm * g.NTN;
+}
+// Work unit u: its tile and its first K step (adjacent units are the K
+// slices of one tile).
+__device__ __forceinline__ void unit_of(const DqArgs& g, int u, int& b, int& tm, int& tn, int& k0) {
+  const int t = u / g.S;
+  k0 = (u - t * g.S) * g.KSU;
+  tile_of(g, t, b, tm, tn);
 }
 
 // ---- the weight decode shared by the GEMM producers and vq_dq_decode ------
@@ -323,8 +335,8 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
   const uint32_t rank = cluster_ctarank();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int pair_id = blockIdx.x / 2, npairs = gridDim.x / 2;
-  const int my_tiles = pair_id < g.ntiles ? (g.ntiles - 1 - pair_id) / npairs + 1 : 0;
-  const int nsteps = my_tiles * g.KS;  // this pair's K steps, in order
+  const int my_tiles = pair_id < g.nunits ? (g.nunits - 1 - pair_id) / npairs + 1 : 0;
+  const int nsteps = my_tiles * g.KSU;  // this pair's K steps, in order
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -368,9 +380,10 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int st = 0; st < nsteps; ++st) {
-        const int ti = st / g.KS, ks = st - ti * g.KS;
-        int b, tm, tn;
-        tile_of(g, pair_id + ti * npairs, b, tm, tn);
+        const int ti = st / g.KSU;
+        int b, tm, tn, k0;
+        unit_of(g, pair_id + ti * npairs, b, tm, tn, k0);
+        const int ks = k0 + st - ti * g.KSU;
         if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, g.err, ERR_EMPTY)) break;
         const uint32_t sb = s0 + stage * STAGE_BYTES;
         if (rank == 0)
@@ -406,7 +419,7 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
         accp ^= 1u << buf;
         tc_fence_after();
         const uint32_t dacc = tmem + buf * 256;
-        for (int ks = 0; ks < g.KS; ++ks) {
+        for (int ks = 0; ks < g.KSU; ++ks) {
           if (!wait_cluster(full0 + 8 * stage, phase, g.err, ERR_FULL)) {
             ok = false;
             break;
@@ -435,9 +448,10 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
       const uint32_t r0s = smem_u32(smem + C::RAW0);
       int issued = 0;
       for (int st = 0; st < nsteps; ++st) {
-        const int ti = st / g.KS, ks = st - ti * g.KS;
-        int b, tm, tn;
-        tile_of(g, pair_id + ti * npairs, b, tm, tn);
+        const int ti = st / g.KSU;
+        int b, tm, tn, k0;
+        unit_of(g, pair_id + ti * npairs, b, tm, tn, k0);
+        const int ks = k0 + st - ti * g.KSU;
         int slot;
         uint32_t phase;
         raw_slot<MODE>(st, slot, phase);
@@ -470,9 +484,10 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
       int slot;
       uint32_t rphase;
       raw_slot<MODE>(st, slot, rphase);
-      const int ti = st / g.KS, ks = st - ti * g.KS;
-      int b, tm, tn;
-      tile_of(g, pair_id + ti * npairs, b, tm, tn);
+      const int ti = st / g.KSU;
+      int b, tm, tn, k0;
+      unit_of(g, pair_id + ti * npairs, b, tm, tn, k0);
+      const int ks = k0 + st - ti * g.KSU;
       // the step's raw bytes: into registers, then the slot goes back
       if (!mbar_wait_warp(rfull0 + 8 * slot, rphase, g.err, ERR_FULL)) break;
       const uint8_t* rawc = smem + C::RAW0 + slot * C::RAW_BYTES;
@@ -511,8 +526,8 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     uint32_t accp = 0;
     for (int it = 0; it < my_tiles; ++it) {
       const int buf = it & 1;
-      int b, tm, tn;
-      tile_of(g, pair_id + it * npairs, b, tm, tn);
+      int b, tm, tn, k0;
+      unit_of(g, pair_id + it * npairs, b, tm, tn, k0);
       if (!mbar_wait_warp(accf0 + 8 * buf, (accp >> buf) & 1, g.err, ERR_ACC)) break;
       accp ^= 1u << buf;
       tc_fence_after();
@@ -533,6 +548,16 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
         }
         const int col0 = tn * 256 + c * 32;
         if (!row_ok || col0 >= g.N) continue;
+        if (g.S > 1) {  // this K slice's float32 sums, rows of part[k0 / KSU]
+          float4* dst = reinterpret_cast<float4*>(
+              g.part + ((int64_t)(k0 / g.KSU) * g.M + row) * g.N + col0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (col0 + 4 * i < g.N)
+              dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                   __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+          continue;
+        }
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -558,6 +583,35 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
   }
+}
+
+// Split-K: out[m, n] = bf16(sum over s of part[s][m][n], in s order, + bias[n]),
+// 8 columns per thread (N % 8 == 0).
+__global__ void k_dq_finalize(const float* part, int S, int M, int N, const uint16_t* bias,
+                              uint16_t* out, int64_t ldo) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int n8 = N / 8;
+  if (i >= (int64_t)M * n8) return;
+  const int m = (int)(i / n8), n = (int)(i % n8) * 8;
+  float v[8];
+  for (int e = 0; e < 8; ++e) v[e] = 0.f;
+  for (int sp = 0; sp < S; ++sp) {
+    const float4* q = reinterpret_cast<const float4*>(part + ((int64_t)sp * M + m) * N + n);
+    const float4 a = q[0], b = q[1];
+    v[0] += a.x, v[1] += a.y, v[2] += a.z, v[3] += a.w;
+    v[4] += b.x, v[5] += b.y, v[6] += b.z, v[7] += b.w;
+  }
+  uint32_t pk[4];
+  for (int e = 0; e < 4; ++e) {
+    float x0 = v[2 * e], x1 = v[2 * e + 1];
+    if (bias) {
+      x0 += bf2f(bias[n + 2 * e]);
+      x1 += bf2f(bias[n + 2 * e + 1]);
+    }
+    __nv_bfloat162 bb = __floats2bfloat162_rn(x0, x1);
+    pk[e] = *reinterpret_cast<uint32_t*>(&bb);
+  }
+  *reinterpret_cast<uint4*>(out + (int64_t)m * ldo + n) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
 }
 
 // The weight decode alone, for tests: out[row, k] bf16 over [rows, K].
@@ -742,7 +796,7 @@ int launch_dq(const CUtensorMap& ma, const CUtensorMap& mw, const DqArgs& g, cud
   if (cudaFuncSetAttribute(k_gemm_dq<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
       cudaSuccess)
     return VQ_ERR_CUDA;
-  const int pairs = (int)std::min<int64_t>(g.ntiles, vq::mx::sm_count() / 2);
+  const int pairs = (int)std::min<int64_t>(g.nunits, vq::mx::sm_count() / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(Cfg<MODE>::THREADS, 1, 1);
@@ -767,14 +821,53 @@ int log2_exact(int64_t v) {
 
 int64_t npad_of(int64_t N) { return (N + 255) / 256 * 256; }
 
+// K splits for one GEMM with fewer output tiles than CTA pairs: the count
+// that gives the fewest K steps on the busiest pair, a split GEMM paying in
+// step units for the finalize launch (4) and for its float32 slices written
+// and read back (about 4 MB a step: the GPU's HBM traffic in the ~0.6 us of
+// one decode-bound step); slices of at least 8 steps that divide the K steps
+// evenly; one batch only.
+int splits_for(int64_t batch, int64_t M, int64_t N, int64_t K) {
+  if (batch != 1) return 1;
+  const int64_t KS = (K + KSTEP - 1) / KSTEP, tiles = (M + 255) / 256 * ((N + 255) / 256);
+  const int64_t pairs = std::max(1, vq::mx::sm_count() / 2);
+  if (tiles >= pairs) return 1;
+  int best = 1;
+  int64_t best_cost = (tiles + pairs - 1) / pairs * KS;
+  for (int S = 2; S <= 64; ++S) {
+    if (KS % S || KS / S < 8) continue;
+    const int64_t traffic = (int64_t)(S + 1) * M * N * 8;
+    const int64_t cost =
+        (tiles * S + pairs - 1) / pairs * (KS / S) + 4 + (traffic + 3999999) / 4000000;
+    if (cost < best_cost) {
+      best = S;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
 }  // namespace
 
 extern "C" {
+
+int32_t vq_gemm_dq_splits(int64_t batch, int64_t M, int64_t N, int64_t K) {
+  if (batch <= 0 || M <= 0 || N <= 0 || K <= 0) return 1;
+  return splits_for(batch, M, N, K);
+}
 
 int vq_gemm_dq(const void* a, int64_t batch, int64_t M, int64_t K, int32_t mode, const void* w,
                int32_t w_shared, int64_t N, const void* w_scale4, const void* palette,
                const void* bias, void* out, int64_t ldo, int64_t out_batch_stride, int32_t* d_err,
                void* stream) {
+  return vq_gemm_dq_ex(a, batch, M, K, mode, w, w_shared, N, w_scale4, palette, bias, out, ldo,
+                       out_batch_stride, 1, nullptr, d_err, stream);
+}
+
+int vq_gemm_dq_ex(const void* a, int64_t batch, int64_t M, int64_t K, int32_t mode, const void* w,
+                  int32_t w_shared, int64_t N, const void* w_scale4, const void* palette,
+                  const void* bias, void* out, int64_t ldo, int64_t out_batch_stride,
+                  int32_t splits, float* workspace, int32_t* d_err, void* stream) {
   if (!a || !w || !out || !d_err) return VQ_ERR_NULL;
   if (mode < MODE_TMA || mode > MODE_LUT8) return VQ_ERR_INVALID;
   if (mode != MODE_TMA && !palette) return VQ_ERR_NULL;
@@ -809,6 +902,18 @@ int vq_gemm_dq(const void* a, int64_t batch, int64_t M, int64_t K, int32_t mode,
   g.ntiles = (int)ntiles;
   g.w_shared = w_shared ? 1 : 0;
   g.err = d_err;
+  if (splits < 1 || g.KS % splits) return VQ_ERR_INVALID;
+  if (splits > 1) {
+    if (batch != 1) return VQ_ERR_UNSUPPORTED;
+    if (!workspace) return VQ_ERR_NULL;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15) return VQ_ERR_ALIGNMENT;
+    if ((int64_t)splits * M * N >= (1ll << 40)) return VQ_ERR_UNSUPPORTED;
+  }
+  g.S = splits;
+  g.KSU = g.KS / splits;
+  if (ntiles * splits >= (1ll << 31)) return VQ_ERR_UNSUPPORTED;
+  g.nunits = (int)(ntiles * splits);
+  g.part = workspace;
   CUtensorMap ma, mw;
   if (!vq::mx::make_map(&ma, a, batch * M, K * 2, 128)) return VQ_ERR_CUDA;
   if (mode == MODE_TMA) {
@@ -818,9 +923,14 @@ int vq_gemm_dq(const void* a, int64_t batch, int64_t M, int64_t K, int32_t mode,
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(d_err, 0, sizeof(int32_t), s) != cudaSuccess) return VQ_ERR_CUDA;
-  if (mode == MODE_TMA) return launch_dq<MODE_TMA>(ma, mw, g, s);
-  if (mode == MODE_LUT4) return launch_dq<MODE_LUT4>(ma, mw, g, s);
-  return launch_dq<MODE_LUT8>(ma, mw, g, s);
+  const int rc = mode == MODE_TMA    ? launch_dq<MODE_TMA>(ma, mw, g, s)
+                 : mode == MODE_LUT4 ? launch_dq<MODE_LUT4>(ma, mw, g, s)
+                                     : launch_dq<MODE_LUT8>(ma, mw, g, s);
+  if (rc != VQ_OK || splits == 1) return rc;
+  const int64_t n = M * (N / 8);
+  k_dq_finalize<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(workspace, splits, (int)M, (int)N,
+                                                           (const uint16_t*)bias, (uint16_t*)out, ldo);
+  return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
 }
 
 int vq_dq_pack_sizes(int64_t wbatch, int64_t N, int64_t K, int32_t mode, int64_t* codes_bytes,

@@ -143,6 +143,14 @@ _SIGNATURES = {
                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                   ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                   ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_gemm_dq_ex": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                     ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
+                                     ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p,
+                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                     ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "vq_gemm_dq_splits": (ctypes.c_int32, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_int64]),
     "vq_dq_pack_sizes": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                         ctypes.c_int32, P(ctypes.c_int64), P(ctypes.c_int64)]),
     "vq_dq_pack": (ctypes.c_int, [P(VqTensor), ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,

@@ -24,6 +24,7 @@ callers keep the reference composition for them.
 """
 
 import ctypes
+import os
 from typing import Optional
 
 import numpy as np
@@ -34,6 +35,8 @@ from voyager_b200._cache import TensorCache
 
 MODE_TMA, MODE_LUT4, MODE_LUT8 = 0, 1, 2
 KSTEP = 64
+# split the K steps of few-tile GEMMs over more CTA pairs (VQ_DQ_SPLITK=0: never)
+SPLIT_K = os.environ.get("VQ_DQ_SPLITK", "1") != "0"
 _wcache = TensorCache()
 
 
@@ -218,20 +221,28 @@ def transpose_last2(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def gemm(a2: torch.Tensor, pw: PackedWeight, bias=None, batch=1, w_shared=True):
-    """out [batch, M, N] bf16 = a2 [batch * M, K] . W^T (+ bias) on the kernel."""
+def gemm(a2: torch.Tensor, pw: PackedWeight, bias=None, batch=1, w_shared=True, splits=None):
+    """out [batch, M, N] bf16 = a2 [batch * M, K] . W^T (+ bias) on the kernel;
+    ``splits`` K slices per output tile (None: the library's choice)."""
     dev = a2.device
     K = a2.shape[-1]
     M = a2.shape[0] // batch
     out = torch.empty((batch, M, pw.N), dtype=torch.bfloat16, device=dev)
     err = torch.empty(1, dtype=torch.int32, device=dev)
     b = bias.contiguous() if bias is not None else None
-    st = _lib.load().vq_gemm_dq(a2.data_ptr(), batch, M, K, pw.mode, pw.w.data_ptr(),
-                                int(bool(w_shared)), pw.N,
-                                pw.scale4.data_ptr() if pw.scale4 is not None else None,
-                                pw.palette.data_ptr() if pw.palette is not None else None,
-                                b.data_ptr() if b is not None else None, out.data_ptr(), pw.N,
-                                M * pw.N, err.data_ptr(), _stream(dev))
+    lib = _lib.load()
+    # few output tiles (small M and N): the K steps split over more CTA pairs
+    if splits is None:
+        splits = int(lib.vq_gemm_dq_splits(batch, M, pw.N, K)) if SPLIT_K else 1
+    ws = (torch.empty(splits * M * pw.N, dtype=torch.float32, device=dev) if splits > 1
+          else None)
+    st = lib.vq_gemm_dq_ex(a2.data_ptr(), batch, M, K, pw.mode, pw.w.data_ptr(),
+                           int(bool(w_shared)), pw.N,
+                           pw.scale4.data_ptr() if pw.scale4 is not None else None,
+                           pw.palette.data_ptr() if pw.palette is not None else None,
+                           b.data_ptr() if b is not None else None, out.data_ptr(), pw.N,
+                           M * pw.N, splits, ws.data_ptr() if ws is not None else None,
+                           err.data_ptr(), _stream(dev))
     _lib.check(st, "quantized_ops::linear_mx (tcgen05 bf16)")
     from voyager_b200 import mxgemm
 
