@@ -45,9 +45,11 @@ DATA = "synthetic (seeded PCG64 N(0,0.02^2))"
 WORKLOAD = ("C2 fp32 [11008,4096]: NF4 g64 quantize_mx / posit8_1 per-tensor / int8 "
             "per-channel quantize")
 # per-launch DRAM bytes (read + write) of the C2 kernels, from one ncu capture
-# (ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum of the C2 kernels)
-NCU_TRAFFIC = {"int8_channel": int(311.5e6), "nf4_g64": int(310.4e6),
-               "posit8_tensor": int(308.9e6)}
+# of the current kernels: python bench.py --only c2 --steps 1 --warmup 1, under
+# ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none
+# -k regex:"k_qmx_last|k_rows" (mean of two launches each)
+NCU_TRAFFIC = {"int8_channel": int(311.6e6), "nf4_g64": int(304.5e6),
+               "posit8_tensor": int(309.8e6)}
 L2_BYTES = 126e6  # B200 L2
 BYTES_PER_ELEM = {"nf4_g64": 4 + 4 + 4.0 / 64, "posit8_tensor": 8.0, "int8_channel": 8.0}
 
@@ -62,8 +64,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default=None,
-                    choices=["c1", "c2", "c3", "c4", "c5", "attn", "outlier", "spmm", "dq",
-                             "nvf4"],
+                    choices=["c1", "c2", "c3", "c4", "c4m128", "c5", "attn", "outlier", "spmm",
+                             "dq", "nvf4", "observer"],
                     help="profiling aid: run only this workload's kernels, no JSON line")
     return ap.parse_args()
 
@@ -510,6 +512,20 @@ def run_observer(w, stream, hbm_peak):
                     "reduction, history / scale update (3 launches); bytes = the weight read once"}
 
 
+def stream_probe(src, read_bytes, dst, write_bytes):
+    """One launch that only moves these bytes (vq_stream_probe): the least
+    time a launch doing the same traffic can take."""
+    import torch
+
+    from voyager_b200 import _lib
+
+    dev = (src if src is not None else dst).device
+    st = _lib.load().vq_stream_probe(src.data_ptr() if src is not None else None, int(read_bytes),
+                                     dst.data_ptr() if dst is not None else None,
+                                     int(write_bytes), torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(st, "stream probe")
+
+
 def _time_ms(fn, stream, reps=10, warm=3):
     import torch
 
@@ -775,6 +791,13 @@ def run_secondary(dev, hbm_peak, peaks):
                       "note": "L2 flushed (256 MB written) before every call; CUDA-graph replay "
                               "of (flush, op) minus the flush alone; eager: one op call per "
                               "launch, host launch gaps included"}
+    # the floor: one launch that only reads the input's bytes and writes the
+    # outputs' (vq_stream_probe), timed the same way
+    floor_out = torch.empty(n * 2 + n // 16 * 2 + 64, dtype=torch.uint8, device=dev)
+    tfl = _time_graph_cold_ms(lambda: stream_probe(x, n * 2, floor_out, n * 2 + n // 16 * 2), dev)
+    out["c1_cold"]["stream_floor_GBps"] = round(n * 4.125 / (tfl / 1e3) / 1e9, 1)
+    out["c1_cold"]["quantize_mx_frac_of_floor"] = round(tfl / tqc, 3)
+    out["c1_cold"]["dequantize_frac_of_floor"] = round(tfl / tdc, 3)
     # C3 MXFP8 linear
     try:
         a_np, w_np = synth.c3_operands()
@@ -1014,6 +1037,13 @@ def run_c4_sweep(dev, hbm_peak, bf16_peak):
                 byts = n * k * (0.5 + 1 / 16) + m * k * (1 + 1 / 32) + 2 * m * n
                 pt["GBps"] = round(byts / (ms / 1e3) / 1e9, 1)
                 pt["frac_hbm"] = round(pt["GBps"] / hbm_peak, 3)
+                if m == 1:
+                    # the floor of one launch reading the packed weight's bytes
+                    wb = int(n * k * (0.5 + 1 / 16)) // 16 * 16
+                    floor_ms = _time_rotating_ms([(lambda c=c: stream_probe(c, wb, None, 0))
+                                                  for c in copies], stream)
+                pt["stream_floor_ms"] = round(floor_ms, 4)
+                pt["frac_of_floor"] = round(floor_ms / ms, 3)
             else:
                 pt["frac_bf16"] = round(pt["TFLOPs"] / bf16_peak, 3)
             res.append(pt)
@@ -1111,6 +1141,17 @@ def run_only(args):
         ca, sa, cw, sw = c4_operands(dev, 16, 4096, 14336, seed=1)
         for _ in range(args.warmup + args.steps):
             w4a8.linear(ca, sa, cw, sw)
+    elif args.only == "c4m128":
+        # C4 at M = 128, K = 14336, N = 4096: the split-K dequant GEMM
+        from voyager_b200 import w4a8
+
+        ca, sa, cw, sw = c4_operands(dev, 128, 14336, 4096, seed=1)
+        for _ in range(args.warmup + args.steps):
+            w4a8.linear(ca, sa, cw, sw)
+    elif args.only == "observer":
+        w = torch.from_numpy(synth.c2_weight()).to(dev)
+        for _ in range(args.warmup + args.steps):
+            observed_scales(w)
     else:
         a_np, w_np = synth.c3_operands()
         e4m3 = get_quantization_map("fp8_e4m3", dev)

@@ -295,6 +295,13 @@ int vq_gemm_dq_ex(const void* a, int64_t batch, int64_t M, int64_t K, int32_t mo
                   int32_t w_shared, int64_t N, const void* w_scale4, const void* palette,
                   const void* bias, void* out, int64_t ldo, int64_t out_batch_stride,
                   int32_t splits, float* workspace, int32_t* d_err, void* stream);
+/* Measurement aid, no counterpart in the reference: one launch that reads
+ * read_bytes from src and writes write_bytes to dst (both multiples of 16,
+ * 16-byte aligned) and does nothing else -- the least time any one launch
+ * moving those bytes can take on this device (launch, ramp-up and drain
+ * included).  bench.py reports small kernels against it. */
+int vq_stream_probe(const void* src, int64_t read_bytes, void* dst, int64_t write_bytes,
+                    void* stream);
 /* The split count vq_gemm_dq_ex uses best for these sizes on this device (1:
  * no split). */
 int32_t vq_gemm_dq_splits(int64_t batch, int64_t M, int64_t N, int64_t K);

@@ -69,7 +69,30 @@ __global__ void __launch_bounds__(256) k_amax_runs(const __grid_constant__ ObsAr
     const int64_t n = min((int64_t)SEG, a.I - off);
     const int64_t base = run * a.I + off;
     uint32_t m = 0;
-    if (a.is_bf16) {
+    if (vec && n == SEG) {
+      // a whole aligned segment: every load of the lane in flight at once
+      constexpr int NV = SEG * 2 / (32 * 16);  // bf16: 8 x 16 bytes a lane
+      if (a.is_bf16) {
+        const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.in) + base);
+        uint4 v[NV];
+#pragma unroll
+        for (int u = 0; u < NV; ++u) v[u] = __ldcs(p + lane + 32 * u);
+#pragma unroll
+        for (int u = 0; u < NV; ++u) {
+          const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) m = max(m, max(mag_bf16(w[j] & 0xFFFFu), mag_bf16(w[j] >> 16)));
+        }
+      } else {
+        const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint32_t*>(a.in) + base);
+        uint4 v[2 * NV];
+#pragma unroll
+        for (int u = 0; u < 2 * NV; ++u) v[u] = __ldcs(p + lane + 32 * u);
+#pragma unroll
+        for (int u = 0; u < 2 * NV; ++u)
+          m = max(max(m, max(mag_f32(v[u].x), mag_f32(v[u].y))), max(mag_f32(v[u].z), mag_f32(v[u].w)));
+      }
+    } else if (a.is_bf16) {
       const uint16_t* p = static_cast<const uint16_t*>(a.in) + base;
       if (vec) {
         for (int64_t i = (int64_t)lane * 8; i < n; i += 256) {

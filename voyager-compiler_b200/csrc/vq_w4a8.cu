@@ -66,7 +66,10 @@ constexpr int ERR_TIMEOUT_EMPTY = 22;  // the producer waited for a free stage
 constexpr int ERR_TIMEOUT_DRAIN = 23;  // the producer waited for its last copies
 constexpr int ERR_TIMEOUT_FLUSH = 24;  // the epilogue warp waited for the compute warps' sums
 constexpr int ERR_TIMEOUT_STAGED = 25;  // the producer waited for the tokens to be staged
-constexpr int FILL0 = 4;  // tiles in flight before the tokens are staged
+#ifndef VQ_W4_FILL0
+#define VQ_W4_FILL0 4
+#endif
+constexpr int FILL0 = VQ_W4_FILL0;  // tiles in flight before the tokens are staged
 
 struct Args {
   const uint8_t* wt;   // packed tiles [row blocks][chunks][TILE_BYTES]
