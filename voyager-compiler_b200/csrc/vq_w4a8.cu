@@ -20,7 +20,7 @@
 // [i T / G, (i + 1) T / G) of the T tiles, so every CTA streams the same
 // number of bytes.  One producer warp copies its tiles with cp.async.bulk
 // into an 8-deep shared-memory ring (full / empty mbarriers, bounded waits);
-// 8 compute warps take 32 rows of each tile into registers, free the stage
+// 16 compute warps take 16 rows of each tile into registers, free the stage
 // and run mma.sync.m16n8k16 with f16 operands:
 //   weights  each nibble pair -> f16x2 (cvt.rn.f16x2.e2m1x2) times its E4M3
 //            block scale (exact in f16: at most 6 significant bits in
@@ -29,8 +29,8 @@
 // A row block whose chunks all fall to one CTA is written by it (bias, bf16);
 // the CTAs that share a row block add their float32 sums into a zeroed
 // workspace (vector reductions, no wait), and the CTA that adds the last
-// piece reads the rows back, writes them and leaves the workspace zero.  One
-// launch per call.
+// piece reads the rows back with its two epilogue warps, writes them and
+// leaves the workspace zero.  One launch per call.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -55,8 +55,9 @@ constexpr int TILE_W = TILE_ROWS * 64;       // nibble bytes of a tile (128 K)
 constexpr int TILE_BYTES = TILE_W + TILE_ROWS * 8;  // + scale bytes: 18432
 constexpr int STAGES = 8;
 constexpr int PRODUCER = CWARPS;            // warp: the bulk copies
-constexpr int EPILOGUE = CWARPS + 1;        // warp: row blocks shared with other CTAs
-constexpr int THREADS = (CWARPS + 2) * 32;
+constexpr int EPILOGUE = CWARPS + 1;        // first warp: row blocks shared with other CTAs
+constexpr int EWARPS = 2;                   // epilogue warps
+constexpr int THREADS = (CWARPS + 1 + EWARPS) * 32;
 constexpr int TPAD = 32;   // staged token rows padded by 64 B: rows alternate bank halves
 constexpr int LMAX = 19;   // K chunks of tokens a CTA stages (16 tokens: 4.25 KB each)
 
@@ -64,7 +65,7 @@ constexpr int LMAX = 19;   // K chunks of tokens a CTA stages (16 tokens: 4.25 K
 constexpr int ERR_TIMEOUT_FULL = 21;   // a compute warp waited for a tile
 constexpr int ERR_TIMEOUT_EMPTY = 22;  // the producer waited for a free stage
 constexpr int ERR_TIMEOUT_DRAIN = 23;  // the producer waited for its last copies
-constexpr int ERR_TIMEOUT_FLUSH = 24;  // the epilogue warp waited for the compute warps' sums
+constexpr int ERR_TIMEOUT_FLUSH = 24;  // an epilogue warp waited for the compute warps' sums
 constexpr int ERR_TIMEOUT_STAGED = 25;  // the producer waited for the tokens to be staged
 #ifndef VQ_W4_FILL0
 #define VQ_W4_FILL0 4
@@ -126,6 +127,9 @@ __device__ __forceinline__ void red_add2(float* p, float a, float b) {
 }
 __device__ __forceinline__ void consumers_sync() {  // the compute warps only
   asm volatile("bar.sync 1, %0;" ::"n"(CWARPS * 32) : "memory");
+}
+__device__ __forceinline__ void epilogue_sync() {  // the epilogue warps only
+  asm volatile("bar.sync 2, %0;" ::"n"(EWARPS * 32) : "memory");
 }
 
 // a * (b.lo, b.lo) / a * (b.hi, b.hi): the broadcast is an operand select of
@@ -244,7 +248,7 @@ __device__ __forceinline__ int range_start(int64_t i, int64_t T, int64_t G) {
 // whole row block straight to the output; this CTA's piece of a row block
 // shared with other CTAs added into the workspace, with an arrival on the
 // flush barrier of its slot (0: the CTA's first row block, 1: its last) for
-// the epilogue warp, and no wait.
+// the epilogue warps, and no wait.
 template <int NT, bool SCALED>
 __device__ __forceinline__ void consume(const Args& p, const uint8_t* ring, uint32_t full0,
                                         uint32_t empty0, int t0, int t1, int cstart,
@@ -344,16 +348,20 @@ __device__ __forceinline__ void consume(const Args& p, const uint8_t* ring, uint
   }
 }
 
-// The epilogue warp: for each row block this CTA shares with others (its
-// first and / or last), once the compute warps have added their sums, count
-// the piece in; the CTA that adds the last piece reads the row block back
-// (rows below N, tokens below M), adds the bias, writes bf16 and leaves the
-// workspace and the counter at zero.  The compute warps' additions reach the
-// whole GPU through the flush barrier (release / acquire in the CTA) and
-// this warp's device-scope fence before the counter.
+// The epilogue warps: for each row block this CTA shares with others (its
+// first and / or last), once the compute warps have added their sums, the
+// first epilogue warp counts the piece in; the CTA that adds the last piece
+// reads the row block back with all its epilogue warps (rows below N, tokens
+// below M), adds the bias, writes bf16 and leaves the workspace and the
+// counter at zero.  The compute warps' additions reach the whole GPU through
+// the flush barrier (release / acquire in the CTA) and the counting warp's
+// device-scope fence before the counter; the decision reaches the other
+// epilogue warps through shared memory and a named barrier that every
+// epilogue warp reaches, whatever its own wait gave.
 template <int NT>
-__device__ __forceinline__ void epilogue(const Args& p, int t0, int t1, uint32_t flushed0) {
-  const int lane = threadIdx.x % 32;
+__device__ __forceinline__ void epilogue(const Args& p, int t0, int t1, uint32_t flushed0,
+                                         int* last_flag) {
+  const int lane = threadIdx.x % 32, ew = threadIdx.x / 32 - EPILOGUE;
   const int64_t T = p.tiles, G = p.G;
   const int rbs[2] = {t0 / p.chunks, (t1 - 1) / p.chunks};
   for (int slot = 0; slot < 2; ++slot) {
@@ -361,47 +369,51 @@ __device__ __forceinline__ void epilogue(const Args& p, int t0, int t1, uint32_t
     if (slot == 1 && rb == rbs[0]) break;
     const int64_t first = (int64_t)rb * p.chunks, lastt = first + p.chunks - 1;
     if (first >= t0 && lastt < t1) continue;  // whole: written by the compute warps
-    if (!tc::mbar_wait_warp(flushed0 + 8 * slot, 0, p.err, ERR_TIMEOUT_FLUSH)) return;
-    __threadfence();
-    int is_last = 0;
-    if (lane == 0) {
-      const int prev = atomicAdd(p.done + rb, 1);
-      is_last = prev == cta_of(lastt, T, G) - cta_of(first, T, G);
-      if (is_last) p.done[rb] = 0;
+    const bool ok = tc::mbar_wait_warp(flushed0 + 8 * slot, 0, p.err, ERR_TIMEOUT_FLUSH);
+    if (ew == 0) {
+      int is_last = 0;
+      if (ok) {
+        __threadfence();
+        if (lane == 0) {
+          const int prev = atomicAdd(p.done + rb, 1);
+          is_last = prev == cta_of(lastt, T, G) - cta_of(first, T, G);
+          if (is_last) p.done[rb] = 0;
+        }
+        is_last = __shfl_sync(0xFFFFFFFFu, is_last, 0);
+      }
+      if (lane == 0) last_flag[slot] = is_last;
     }
-    if (!__shfl_sync(0xFFFFFFFFu, is_last, 0)) continue;
+    epilogue_sync();
+    if (!last_flag[slot]) continue;
     __threadfence();
     float* ws = p.acc + (size_t)rb * TILE_ROWS * 16;
     const int nrow = min(TILE_ROWS, p.N - rb * TILE_ROWS);
     const int nv = (p.M + 3) / 4;  // float4 of a row's sums
-    // rows lane + 32 i: 8 rows per lane, read 8 / NT at a time (all loads first)
-    constexpr int RB = 8 / NT;
-#pragma unroll 1
-    for (int i0 = 0; i0 < 8; i0 += RB) {
-      float4 q[RB][2 * NT];
+    // rows ew * 32 + lane + 32 EWARPS i, all loads first
+    constexpr int RL = TILE_ROWS / (32 * EWARPS);
+    float4 q[RL][2 * NT];
 #pragma unroll
-      for (int i = 0; i < RB; ++i) {
-        const int r = lane + 32 * (i0 + i);
+    for (int i = 0; i < RL; ++i) {
+      const int r = ew * 32 + lane + 32 * EWARPS * i;
 #pragma unroll
-        for (int v = 0; v < 2 * NT; ++v)
-          q[i][v] = r < nrow && v < nv ? __ldcg(reinterpret_cast<const float4*>(ws + r * 16) + v)
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+      for (int v = 0; v < 2 * NT; ++v)
+        q[i][v] = r < nrow && v < nv ? __ldcg(reinterpret_cast<const float4*>(ws + r * 16) + v)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 #pragma unroll
-      for (int i = 0; i < RB; ++i) {
-        const int r = lane + 32 * (i0 + i);
-        if (r >= nrow) continue;
-        const int row = rb * TILE_ROWS + r;
-        const float bv = p.bias ? bf2f(p.bias[row]) : 0.f;
+    for (int i = 0; i < RL; ++i) {
+      const int r = ew * 32 + lane + 32 * EWARPS * i;
+      if (r >= nrow) continue;
+      const int row = rb * TILE_ROWS + r;
+      const float bv = p.bias ? bf2f(p.bias[row]) : 0.f;
 #pragma unroll
-        for (int v = 0; v < 2 * NT; ++v) {
-          if (v >= nv) continue;
-          reinterpret_cast<float4*>(ws + r * 16)[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-          const float s[4] = {q[i][v].x, q[i][v].y, q[i][v].z, q[i][v].w};
+      for (int v = 0; v < 2 * NT; ++v) {
+        if (v >= nv) continue;
+        reinterpret_cast<float4*>(ws + r * 16)[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float s4[4] = {q[i][v].x, q[i][v].y, q[i][v].z, q[i][v].w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (4 * v + e < p.M) p.out[(size_t)(4 * v + e) * p.N + row] = (uint16_t)f2bf(s[e] + bv);
-        }
+        for (int e = 0; e < 4; ++e)
+          if (4 * v + e < p.M) p.out[(size_t)(4 * v + e) * p.N + row] = (uint16_t)f2bf(s4[e] + bv);
       }
     }
   }
@@ -437,7 +449,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_w4a8(const __grid_constant__ Arg
   uint16_t* tok = reinterpret_cast<uint16_t*>(smem + tok_offset());
   float* tsc = reinterpret_cast<float*>(tok + 8 * NT * ks);
   int* emax = reinterpret_cast<int*>(tsc + 8 * NT * nkb);  // per token: largest biased exponent
-  int* flags = emax + 16;                                  // [0] slow
+  int* flags = emax + 16;  // [0] slow, [1..2] last piece of the shared row block of slot 0 / 1
   uint64_t* bars = reinterpret_cast<uint64_t*>(
       (reinterpret_cast<uintptr_t>(flags + 4) + 7) & ~uintptr_t(7));
   const uint32_t full0 = tc::smem_u32(bars), empty0 = full0 + 8 * STAGES,
@@ -491,8 +503,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_w4a8(const __grid_constant__ Arg
   // the packed weights are constant: only the tokens, the workspace, the
   // counters and the output wait for the grids before this one
   pdl_wait();
-  if (warp == EPILOGUE) {
-    epilogue<NT>(p, t0, t1, flushed0);
+  if (warp >= EPILOGUE) {
+    epilogue<NT>(p, t0, t1, flushed0, flags + 1);
     return;
   }
 
