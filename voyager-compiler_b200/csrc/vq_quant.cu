@@ -235,6 +235,10 @@ struct QmxArgs {
   // outliers and quantized as +0 (filter_outlier's inliers), when mask_on
   int32_t mask_on;
   uint32_t mask_lo1;
+  // k_qmx_nvfp4: fl(1 / quant_max) when quant_max has at most 4 significant
+  // bits (then bf16(amax * rq) == bf16(amax / quant_max) for a normal
+  // quotient), else 0
+  float rq;
 };
 
 // One block of bs = TPB * VPT * VEC elements per TPB threads; lane l holds
@@ -491,10 +495,27 @@ __device__ __forceinline__ uint32_t e4m3_bf16(float v) {
   return __float_as_uint(__half2float(__ushort_as_half((unsigned short)(h & 0xFFFFu)))) >> 16;
 }
 
+// bf16 bits of the positive E4M3 code b (b < 0x7F: 4 exponent bits with bias
+// 7, 3 mantissa bits; subnormals below 2^-6)
+__device__ __forceinline__ uint32_t e4m3_code_bf16(uint32_t b) {
+  const uint32_t e = b >> 3, m = b & 7u;
+  if (e == 0) return m ? __float_as_uint((float)m * 0x1p-9f) >> 16 : 0u;
+  return ((e + 120u) << 7) | (m << 4);
+}
+
 template <bool MASK>
 __global__ void __launch_bounds__(256) k_qmx_nvfp4(const __grid_constant__ QmxArgs a) {
   __shared__ uint32_t lut[256];
+  // the positive E4M3 scale values by code: bf16 bits, and the IEEE
+  // reciprocal of each (1 for the zero code: such a block takes the scale 1)
+  __shared__ uint32_t sval[128];
+  __shared__ float srcp[128];
   if (threadIdx.x < 256) lut[threadIdx.x] = e2m1_bf16(threadIdx.x) | (e2m1_bf16(threadIdx.x >> 4) << 16);
+  if (threadIdx.x < 128) {
+    const uint32_t v = threadIdx.x == 0x7Fu ? 0u : e4m3_code_bf16(threadIdx.x);  // NaN: scale 1
+    sval[threadIdx.x] = v;
+    srcp[threadIdx.x] = v ? fdiv_rn(1.0f, __uint_as_float(v << 16)) : 1.0f;
+  }
   __syncthreads();
   const uint32_t nthr = gridDim.x * blockDim.x;
   for (uint32_t g0 = blockIdx.x * blockDim.x + threadIdx.x; g0 < a.ngroups; g0 += 2 * nthr) {
@@ -542,16 +563,24 @@ __global__ void __launch_bounds__(256) k_qmx_nvfp4(const __grid_constant__ QmxAr
         mn2 = __hmin2(mn2, *reinterpret_cast<const __nv_bfloat162*>(&ab));
       }
       const float amin = fminf(__low2float(mn2), __high2float(mn2));  // a NaN is ignored
-      // scale = e4m3(bf16(amax / quant_max)), 1 where not > 0
-      const float s0 = round_bf(fdiv_rn(bf2f(amax), a.quant_max));
-      const float sv = bf2f(e4m3_bf16(s0));
-      const float s = sv > 0.0f ? sv : 1.0f;
+      // scale = e4m3(bf16(amax / quant_max)), 1 where not > 0; the
+      // quotient by the reciprocal where that is exact in bf16 (rq != 0
+      // and a normal quotient), else the IEEE division
+      const float af = bf2f(amax);
+      float sq = __fmul_rn(af, a.rq);
+      if (!(sq >= 0x1p-126f) || isinf(sq)) sq = fdiv_rn(af, a.quant_max);
+      const float s0 = round_bf(sq);
+      uint32_t code;  // the saturating E4M3 rounding of s0 (0x7F: NaN)
+      asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e4m3x2.f32 t, %1, %1;\n\tcvt.u32.u16 %0, t;\n\t}"
+          : "=r"(code) : "f"(s0));
+      code &= 0x7Fu;
+      const uint32_t svb = sval[code];
+      const float s = svb ? __uint_as_float(svb << 16) : 1.0f;
       reinterpret_cast<uint16_t*>(a.scale)[g] = (uint16_t)f2bf(s);
-      const uint32_t e = (f2u(s) >> 23) & 0xFFu;
-      bool slow = amax > 0x7F80u || e < 1u || e > 252u;
+      bool slow = amax > 0x7F80u || code == 0x7Fu;
       uint32_t out[8];
       if (!slow) {
-        const float r = fdiv_rn(1.0f, s);
+        const float r = srcp[code];
         if (__fmul_rn(amin, r) >= 0x1p-126f) {
           // every quotient is a normal float (no zero index).  Then
           // bf16(x * fl(1/s)) == bf16(x / s): x / s = M_x / M_s * 2^E with
@@ -1911,9 +1940,16 @@ int launch_qmx_nvfp4(const vq_tensor& x, const int* blocked, int64_t bs, int pow
   if (!blocked[x.ndim - 1]) return 0;
   const int64_t C = x.shape[x.ndim - 1];
   if (C % 16 || !aligned16(x.data) || !aligned16(a.codes)) return 0;
+  if (!(a.quant_max > 0.0f) || !std::isfinite(a.quant_max)) return 0;
   const int64_t groups = numel(x) / 16;
   if (groups >= ((int64_t)1 << 31)) return 0;
   a.ngroups = (uint32_t)groups;
+  // a quant_max of at most 4 significant bits (6.0 for E2M1) divides
+  // exactly enough by its reciprocal (see k_qmx_nvfp4)
+  uint32_t qb;
+  memcpy(&qb, &a.quant_max, 4);
+  const bool normal = ((qb >> 23) & 0xFFu) != 0;
+  a.rq = normal && (qb & 0x7FFFFu) == 0 ? 1.0f / a.quant_max : 0.0f;
   const int blocks = (int)std::min<int64_t>((groups + 255) / 256, (int64_t)num_sms() * 8);
   if (a.mask_on) k_qmx_nvfp4<true><<<blocks, 256, 0, st>>>(a);
   else k_qmx_nvfp4<false><<<blocks, 256, 0, st>>>(a);
