@@ -907,12 +907,24 @@ def run_dq_linear(dev, peaks):
         ms = _time_ms(fn, stream, reps=10)
         tf = fl / (ms / 1e3) / 1e12
         res[name] = {"ms": round(ms, 4), "TFLOPs": round(tf, 1), "frac_bf16": round(tf / peak, 3),
-                     "path": {0: "tcgen05 bf16 (weight by TMA)", 1: "tcgen05 bf16, 4-bit palette "
-                              "decoded in smem", 2: "tcgen05 bf16, 8-bit palette decoded in smem"}
-                     [pw.mode] if pw is not None else "dequant + torch"}
+                     "path": dq_path(pw, 8192)}
     res["note"] = ("M=8192 K=4096 N=11008, bf16 activations; denominator: measured cuBLAS bf16 "
                    "burst")
     return res
+
+
+def dq_path(pw, m):
+    """Which kernels a linear_mx with a packed weight and m activation rows runs."""
+    from voyager_b200 import dqgemm
+
+    if pw is None:
+        return "dequant + torch"
+    if pw.mode == dqgemm.MODE_TMA:
+        return "tcgen05 bf16 (weight by TMA)"
+    bits = "4-bit" if pw.mode == dqgemm.MODE_LUT4 else "8-bit"
+    if 0 < dqgemm.DECODE_ONCE_M <= m:
+        return f"{bits} palette decoded once per call, tcgen05 bf16 (weight by TMA)"
+    return f"tcgen05 bf16, {bits} palette decoded in smem"
 
 
 def outlier_c3_operands(dev):
@@ -1022,7 +1034,7 @@ def run_c4_sweep(dev, hbm_peak, bf16_peak):
     GB/s (fraction of HBM) for the weight-streaming points M <= 16."""
     import torch
 
-    from voyager_b200 import w4a8
+    from voyager_b200 import dqgemm, w4a8
     from voyager_b200.tables import get_quantization_map
 
     stream = torch.cuda.current_stream(dev)
@@ -1052,7 +1064,7 @@ def run_c4_sweep(dev, hbm_peak, bf16_peak):
             pt = {"M": m, "K": k, "N": n, "ms": round(ms, 4),
                   "TFLOPs": round(fl / (ms / 1e3) / 1e12, 2),
                   "path": "packed-weight mma" if w4a8.applies_small(ca, cw)
-                  else "tcgen05 bf16, NVFP4 weight decoded in smem"}
+                  else dq_path(dqgemm.packed_weight(cw, sw, None, 16, "kc"), m)}
             if m <= 16:
                 byts = n * k * (0.5 + 1 / 16) + m * k * (1 + 1 / 32) + 2 * m * n
                 pt["GBps"] = round(byts / (ms / 1e3) / 1e9, 1)

@@ -238,3 +238,31 @@ def test_split_k(fmt, m, k, n, splits):
     assert lib.vq_gemm_dq_splits(1, 128, 4096, 14336) > 1
     assert lib.vq_gemm_dq_splits(1, 8192, 11008, 4096) == 1
     assert lib.vq_gemm_dq_splits(2, 128, 4096, 4096) == 1
+
+
+@pytest.mark.parametrize("fmt", ["nf4_g64", "posit8_bs32", "int8_row", "nvfp4"])
+def test_decode_once_large_m(fmt, monkeypatch):
+    """From DECODE_ONCE_M activation rows on, the packed weight is decoded
+    once into bf16 (vq_dq_decode) and multiplied by the TMA-mode kernel; both
+    that and the in-kernel decode agree with the oracle."""
+    from voyager_b200 import dqgemm
+
+    m, k, n = 1024, 1088, 520
+    if fmt == "nf4_g64":
+        k = 1024
+    rng = np.random.default_rng(k + n)
+    a = _bf16(rng, (m, k), 1.0)
+    w = _bf16(rng, (n, k), 0.02)
+    bias = _bf16(rng, (n,), 0.1)
+    c, s, cb, bs = weight_format(fmt, w)
+    want = oracle.linear_mx(a, c, bias, weight_scale=s, block_size=bs, weight_code=cb)
+    pw = dqgemm.packed_weight(to_dev(c), to_dev(s), to_dev(cb), bs, "kc")
+    assert pw.mode != dqgemm.MODE_TMA
+    monkeypatch.setattr(dqgemm, "DECODE_ONCE_M", 0)  # the in-kernel decode
+    in_kernel = to_np(dqgemm.gemm(to_dev(a), pw, to_dev(bias))[0])
+    monkeypatch.setattr(dqgemm, "DECODE_ONCE_M", m)  # decoded once
+    once = to_np(dqgemm.gemm(to_dev(a), pw, to_dev(bias))[0])
+    assert G.rel_l2(in_kernel, want) < 1e-3
+    assert G.rel_l2(once, want) < 1e-3
+    # the decoded weight is exactly what the kernel decodes in shared memory
+    assert G.rel_l2(once, in_kernel) < 1e-3

@@ -614,7 +614,13 @@ __global__ void k_dq_finalize(const float* part, int S, int M, int N, const uint
   *reinterpret_cast<uint4*>(out + (int64_t)m * ldo + n) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
 }
 
-// The weight decode alone, for tests: out[row, k] bf16 over [rows, K].
+// The weight decode on its own: out[row, k] bf16 over [rows, K] (row-major),
+// the same values the GEMM's decoder warps write into shared memory.  Used
+// for large M, where one decode per call to HBM costs less than the GEMM's
+// decode per 256-row tile of the activations, and by the tests.  Thread i
+// takes 32 elements (half h of K step ks) of row i % rows, so a warp reads
+// 32 rows' consecutive 16-byte chunks of a step and writes 32 row segments of
+// 64 bytes.
 template <int MODE>
 __global__ void k_dq_decode(const __grid_constant__ DqArgs g, int rows, uint16_t* out) {
   __shared__ uint32_t pal32[MODE == MODE_LUT8 ? 256 * 32 : 1];
@@ -622,24 +628,32 @@ __global__ void k_dq_decode(const __grid_constant__ DqArgs g, int rows, uint16_t
     for (int j = threadIdx.x; j < 256 * 32; j += blockDim.x) pal32[j] = g.pal[j >> 5];
     __syncthreads();
   }
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // (row, step, half)
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // (step, half, row)
   const int64_t total = (int64_t)rows * g.KS * 2;
   if (i >= total) return;
-  const int h = (int)(i & 1), ks = (int)((i >> 1) % g.KS);
-  const int64_t row = (i >> 1) / g.KS;
+  const int64_t row = i % rows, sh = i / rows;
+  const int h = (int)(sh & 1), ks = (int)(sh >> 1);
   Pal4 p4;
   if (MODE == MODE_LUT4) p4 = load_pal4(g.pal);
-  uint32_t raw[8], sl, sh, o[16];
+  uint32_t raw[8], sl, sh_, o[16];
   const int64_t r0 = wrow(g, 0, ks, (int)row);
   const int64_t blk0 = wrow(g, 0, ks, (int)(row & ~127ll));  // the row's 128-row block
   read32<MODE>(g.wq + blk0 * Cfg<MODE>::STEP_BYTES, (int)(row & 127), g.ws4 ? g.ws4 + r0 * 4 : nullptr,
-               h, raw, sl, sh);
+               h, raw, sl, sh_);
   const int k0 = ks * KSTEP + h * 32;
   const int valid = min(32, g.K - k0);
   if (valid <= 0) return;
-  decode32<MODE>(raw, p4, pal32, threadIdx.x & 31, sl, sh, g.ws4 != nullptr, valid, o);
-  for (int e = 0; e < valid; ++e)
-    out[row * g.K + k0 + e] = (uint16_t)((o[e / 2] >> (16 * (e & 1))) & 0xFFFFu);
+  decode32<MODE>(raw, p4, pal32, threadIdx.x & 31, sl, sh_, g.ws4 != nullptr, valid, o);
+  uint16_t* dst = out + row * g.K + k0;
+  if (valid == 32 && (g.K & 7) == 0) {  // 16-byte aligned: K % 8 == 0, k0 % 32 == 0
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      reinterpret_cast<uint4*>(dst)[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      if (e < valid) dst[e] = (uint16_t)((o[e / 2] >> (16 * (e & 1))) & 0xFFFFu);
+  }
 }
 
 // ---- packing: bf16 codes -> palette indices --------------------------------
@@ -1034,7 +1048,7 @@ int vq_dq_decode(const void* w, int64_t N, int64_t K, int32_t mode, const void* 
   if (mode != MODE_LUT4 && mode != MODE_LUT8) return VQ_ERR_INVALID;
   if (N <= 0 || K <= 0 || K >= (1 << 24) || N >= (1ll << 30)) return VQ_ERR_INVALID;
   if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(w_scale4) & 15) ||
-      (reinterpret_cast<uintptr_t>(palette) & 15))
+      (reinterpret_cast<uintptr_t>(palette) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
     return VQ_ERR_ALIGNMENT;
   DqArgs g = {};
   g.wq = (const uint8_t*)w;

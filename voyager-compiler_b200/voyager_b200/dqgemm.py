@@ -37,6 +37,11 @@ MODE_TMA, MODE_LUT4, MODE_LUT8 = 0, 1, 2
 KSTEP = 64
 # split the K steps of few-tile GEMMs over more CTA pairs (VQ_DQ_SPLITK=0: never)
 SPLIT_K = os.environ.get("VQ_DQ_SPLITK", "1") != "0"
+# from this many activation rows on, a packed weight is decoded once per call
+# into a bf16 copy (N * K * 2 bytes of scratch) multiplied by the TMA-mode
+# kernel: the in-kernel decode repeats for every 256-row tile of the
+# activations and is what bounds that kernel at large M (0 or less: never)
+DECODE_ONCE_M = int(os.environ.get("VQ_DQ_DECODE_ONCE_M", "4096"))
 _wcache = TensorCache()
 
 
@@ -227,6 +232,9 @@ def gemm(a2: torch.Tensor, pw: PackedWeight, bias=None, batch=1, w_shared=True, 
     dev = a2.device
     K = a2.shape[-1]
     M = a2.shape[0] // batch
+    if (pw.mode != MODE_TMA and DECODE_ONCE_M > 0 and batch * M >= DECODE_ONCE_M
+            and (batch == 1 or w_shared)):
+        pw = PackedWeight(MODE_TMA, decode(pw), pw.N, pw.K)
     out = torch.empty((batch, M, pw.N), dtype=torch.bfloat16, device=dev)
     err = torch.empty(1, dtype=torch.int32, device=dev)
     b = bias.contiguous() if bias is not None else None
