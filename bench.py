@@ -638,12 +638,41 @@ def run_c5(dev, pg, world, bf16_peak, reps=8, warm=2, tp=None):
     for _ in range(warm):
         dec.forward_shard(xs, seqs)
     torch.cuda.synchronize()
+    # the forward captured once as a CUDA graph and replayed: the same
+    # kernels, without the host's per-launch cost (about 150 launches per
+    # forward and rank at tp2 x dp4, where a rank's share of the work is a
+    # few ms); the barriers keep their epoch on the device, so replays stay
+    # in step.  Every rank takes the same path (eager if any capture fails).
+    graph, graph_note = None, "the NCCL form is not captured"
+    if world == 1 or columns:
+        try:
+            cg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(cg):
+                dec.forward_shard(xs, seqs)
+            graph, graph_note = cg, None
+        except Exception as e:  # report, and time the eager forward
+            graph_note = repr(e)[:160]
+    ok = torch.tensor([1 if graph is not None else 0], device=dev)
+    if pg:
+        pg.all_reduce(ok, op=pg.ReduceOp.MIN)
+    if int(ok.item()) == 0:
+        graph = None
+    torch.cuda.synchronize()
+
+    def forward():
+        if graph is not None:
+            graph.replay()
+        else:
+            dec.forward_shard(xs, seqs)
+
+    forward()
+    torch.cuda.synchronize()
     if pg:
         pg.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(reps):
-        dec.forward_shard(xs, seqs)
+        forward()
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
@@ -654,6 +683,7 @@ def run_c5(dev, pg, world, bf16_peak, reps=8, warm=2, tp=None):
     tf = cfg.flops(B, S) / (ms / 1e3) / 1e12
     peak = 2 * bf16_peak * world  # the whole job's dense FP8 denominator
     dec.check_errors()
+    del graph
     del dec, xs
     torch.cuda.empty_cache()
     if world == 1:
@@ -664,6 +694,7 @@ def run_c5(dev, pg, world, bf16_peak, reps=8, warm=2, tp=None):
         par = f"tp{tp} ({split})" + (f" x dp{dp} (sequences split across the groups)"
                                     if dp > 1 else "")
     return {"ms": round(ms, 2), "TFLOPs": round(tf, 1), "gpus": world,
+            "launch": "CUDA graph replay" if int(ok.item()) else f"eager ({graph_note})",
             "frac_fp8_dense": round(tf / peak, 3),
             "fp8_dense_peak_TFLOPs": peak,
             "peak_note": "2 x measured cuBLAS bf16 burst per GPU, times the GPUs",

@@ -481,6 +481,14 @@ int vq_tp_barrier(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int3
  * per flag (1 us .. 10 s), after which *d_err = 100 + j and the kernel ends. */
 int vq_tp_barrier_ex(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int32_t world,
                      uint32_t epoch, uint64_t timeout_ns, int32_t* d_err, void* stream);
+/* vq_tp_barrier with the epoch kept on the device: the kernel takes
+ * *d_counter + 1 (0 skipped) as the epoch and stores it back.  Every rank
+ * makes the same sequence of barrier calls, so the counters (zero at the
+ * start, like the flags) stay equal across the ranks, whether the launches
+ * are issued one by one or replayed from a captured CUDA graph.  Do not mix
+ * it with host-epoch calls on the same flags. */
+int vq_tp_barrier_dev(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int32_t world,
+                      uint32_t* d_counter, uint64_t timeout_ns, int32_t* d_err, void* stream);
 /* rows x row_bytes from src (row stride src_ld bytes) into every rank's copy
  * of a symmetric buffer through its multicast address (row stride dst_ld
  * bytes); all sizes and addresses 16-byte aligned. */

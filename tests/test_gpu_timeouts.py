@@ -64,3 +64,43 @@ def test_barrier_wait_runs_out_and_reports():
     mine[1] = 2
     assert _barrier(mine, peer, 2, 2_000_000) == 0
     voyager_b200.check_errors()
+
+
+def _barrier_dev(ptrs_list, mine, counter, rank, timeout_ns):
+    from voyager_b200 import _lib
+    from voyager_b200.ops import _stream
+
+    dev = mine.device
+    ptrs = torch.tensor(ptrs_list, dtype=torch.int64, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    st = _lib.load().vq_tp_barrier_dev(ptrs.data_ptr(), mine.data_ptr(), rank, len(ptrs_list),
+                                       counter.data_ptr(), timeout_ns, err.data_ptr(),
+                                       _stream(dev))
+    assert st == 0, _lib.STATUS.get(st, st)
+    torch.cuda.synchronize()
+    return int(err.item())
+
+
+def test_device_epoch_barrier():
+    """The barrier whose epoch lives on the device (the form a captured CUDA
+    graph can replay): one rank passes at once and advances its counter;
+    rank 0 of 2 whose peer never arrives gives up after its limit with
+    code 101, and the counter still advances by one per call."""
+    import voyager_b200
+
+    voyager_b200.check_errors()
+    mine = torch.zeros(64, dtype=torch.int32, device="cuda")
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for i in range(3):
+        assert _barrier_dev([mine.data_ptr()], mine, counter, 0, 2_000_000) == 0
+        assert int(counter.item()) == i + 1 and int(mine[0].item()) == i + 1
+    mine.zero_()
+    counter.zero_()
+    peer = torch.zeros(64, dtype=torch.int32, device="cuda")
+    assert _barrier_dev([mine.data_ptr(), peer.data_ptr()], mine, counter, 0, 2_000_000) == 101
+    assert int(counter.item()) == 1 and int(mine[0].item()) == 1 and int(peer[0].item()) == 1
+    assert _barrier_dev([mine.data_ptr(), peer.data_ptr()], mine, counter, 0, 2_000_000) == 101
+    assert int(counter.item()) == 2 and int(peer[0].item()) == 2
+    with pytest.raises(Exception):
+        voyager_b200.check_errors()  # the sticky word holds the timeout
+    voyager_b200.check_errors()

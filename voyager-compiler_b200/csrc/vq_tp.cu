@@ -90,6 +90,42 @@ __global__ void k_tp_barrier(const uint64_t* peer_flags, uint32_t* my_flags, int
   }
 }
 
+// The same barrier with the epoch kept on the device: *counter + 1 (0 is
+// skipped), stored back for the next call.  Every rank makes the same
+// sequence of barrier calls, so the counters stay equal across the ranks
+// whether the launches come from the host one by one or from a replayed
+// CUDA graph (where an epoch passed as a kernel argument would repeat).
+__global__ void k_tp_barrier_dev(const uint64_t* peer_flags, uint32_t* my_flags, int rank,
+                                 int world, uint32_t* counter, uint64_t timeout_ns, int* err) {
+  __shared__ uint32_t ep;
+  if (threadIdx.x == 0) {
+    uint32_t e = *counter + 1u;
+    if (e == 0u) e = 1u;
+    *counter = e;
+    ep = e;
+  }
+  __syncthreads();
+  const uint32_t epoch = ep;
+  const int j = threadIdx.x;
+  if (j < world) {
+    __threadfence_system();
+    uint32_t* dst = reinterpret_cast<uint32_t*>(peer_flags[j]) + rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(dst), "r"(epoch) : "memory");
+    const uint32_t* src = my_flags + j;
+    const uint64_t t0 = now_ns();
+    while (true) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(src) : "memory");
+      if ((int32_t)(v - epoch) >= 0) break;
+      if (now_ns() - t0 > timeout_ns) {
+        vq::tc::note_err(err, 100 + j);
+        break;
+      }
+    }
+    __threadfence_system();
+  }
+}
+
 // ---------------------------------------------------------------------------
 struct SumsqArgs {
   const uint16_t* x;  // bf16 [T, C] (this rank's columns)
@@ -333,6 +369,18 @@ int vq_tp_barrier_ex(const void* peer_flag_ptrs, void* my_flags, int32_t rank, i
 int vq_tp_barrier(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int32_t world,
                   uint32_t epoch, int32_t* d_err, void* stream) {
   return vq_tp_barrier_ex(peer_flag_ptrs, my_flags, rank, world, epoch, WAIT_NS, d_err, stream);
+}
+
+int vq_tp_barrier_dev(const void* peer_flag_ptrs, void* my_flags, int32_t rank, int32_t world,
+                      uint32_t* d_counter, uint64_t timeout_ns, int32_t* d_err, void* stream) {
+  if (!peer_flag_ptrs || !my_flags || !d_counter || !d_err) return VQ_ERR_NULL;
+  if (world < 1 || world > 64 || rank < 0 || rank >= world) return VQ_ERR_INVALID;
+  if (timeout_ns < 1000 || timeout_ns > 10000000000ull) return VQ_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(d_counter) & 3) return VQ_ERR_ALIGNMENT;
+  k_tp_barrier_dev<<<1, 64, 0, (cudaStream_t)stream>>>((const uint64_t*)peer_flag_ptrs,
+                                                       (uint32_t*)my_flags, rank, world, d_counter,
+                                                       timeout_ns, d_err);
+  return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
 }
 
 int vq_tp_copy_multicast(const void* src, int64_t src_ld, int64_t rows, int64_t row_bytes,

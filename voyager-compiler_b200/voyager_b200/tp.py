@@ -22,6 +22,7 @@ import torch.distributed as dist
 from voyager_b200 import _lib
 
 CHECK_ERRORS = os.environ.get("VQ_CHECK_ERRORS", "0") == "1"
+BARRIER_WAIT_NS = 2_000_000_000  # a barrier wait gives up (and records it) after 2 s
 _ALIGN = 256
 
 
@@ -91,7 +92,8 @@ class Workspace:
         peers = [p + delta for p in ptrs]
         self.peer_flags = torch.tensor(peers, dtype=torch.int64, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
-        self.epoch = 0
+        # the barrier epoch, kept on the device (graph replays advance it)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=device)
         # flags are zero everywhere before anyone signals
         torch.cuda.synchronize(device)
         dist.barrier(group)
@@ -124,9 +126,9 @@ class Workspace:
 
     # synchronisation -----------------------------------------------------
     def barrier(self, stream: int):
-        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
-        st = _lib.load().vq_tp_barrier(self.peer_flags.data_ptr(), self.base, self.rank,
-                                       self.world, self.epoch, self.err.data_ptr(), stream)
+        st = _lib.load().vq_tp_barrier_dev(self.peer_flags.data_ptr(), self.base, self.rank,
+                                           self.world, self.counter.data_ptr(), BARRIER_WAIT_NS,
+                                           self.err.data_ptr(), stream)
         _lib.check(st, "tensor-parallel barrier")
 
     def check(self):
