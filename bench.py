@@ -398,6 +398,9 @@ def run_ours(args):
         tp = run_tp_linear(dev, pg, world)
         if rank == 0:
             secondary["c3_tp_linear"] = tp
+        c4s = run_c4_sharded(dev, pg, rank, world)
+        if rank == 0:
+            secondary["c4_w4a8_n_sharded"] = c4s
     if not args.no_secondary:
         # C5 on all ranks: tensor parallel within NVLink pairs with the
         # sequences split across pairs (the split that keeps each GPU's
@@ -1076,6 +1079,50 @@ def c4_operands(dev, m, k, n, seed, keep_input=False):
     if keep_input:
         return ca, sa, cw, sw, a
     return ca, sa, cw, sw
+
+
+def run_c4_sharded(dev, pg, rank, world):
+    """C4 N-sharded over the ranks: rank r multiplies the tokens by rows
+    [r N/g, (r+1) N/g) of the NVFP4 weight (every rank makes the same weight
+    from the same seed) and keeps its output columns (a column-parallel
+    linear: no gather).  Whole-job TFLOP/s from the slowest rank's time per
+    point.  Every rank runs the same points in the same order."""
+    import torch
+
+    from voyager_b200.tables import get_quantization_map
+    from voyager_b200 import w4a8
+
+    stream = torch.cuda.current_stream(dev)
+    res = []
+    for (k, n) in [(4096, 4096), (4096, 14336), (14336, 4096)]:
+        ns = n // world
+        lo = rank * ns
+        ca0, sa0, cw, sw, a0 = c4_operands(dev, 16384, k, n, seed=k + n, keep_input=True)
+        cw, sw = cw[lo:lo + ns].contiguous(), sw[lo:lo + ns].contiguous()
+        e4m3 = get_quantization_map("fp8_e4m3", dev)
+        wbytes = ns * k * (0.5 + 1 / 16)
+        copies = [cw] + [cw.clone() for _ in range(int(np.ceil(2.5 * L2_BYTES / wbytes)) - 1)]
+        for m in (1, 16, 128, 1024, 16384):
+            sa, ca = torch.ops.quantized_ops.quantize_mx(a0[:m].contiguous(), e4m3, [-1], 32,
+                                                         448.0, True)
+            if m == 16384:
+                ca, sa = ca0, sa0
+            if m <= 16:
+                ms = _time_rotating_ms([(lambda c=c: w4a8.linear(ca, sa, c, sw)) for c in copies],
+                                       stream)
+            else:
+                ms = _time_graph_ms(lambda: w4a8.linear(ca, sa, cw, sw), stream,
+                                    reps=20 if m <= 1024 else 5)
+            t = torch.tensor([ms], device=dev)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            ms = float(t.item())
+            res.append({"M": m, "K": k, "N": n, "ms": round(ms, 4),
+                        "TFLOPs": round(2.0 * m * n * k / (ms / 1e3) / 1e12, 2)})
+        del ca0, sa0, cw, sw, a0, copies
+        torch.cuda.empty_cache()
+    return {"gpus": world, "points": res,
+            "note": "weight rows (N) split over the ranks, output columns kept sharded "
+                    "(column-parallel, no gather); max over ranks"}
 
 
 def run_c4_sweep(dev, hbm_peak, bf16_peak):
