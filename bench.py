@@ -326,6 +326,14 @@ def run_ours(args):
     kernels = {n: {"ms": round(mean_ms[n], 4),
                    "GB/s": round(elems * BYTES_PER_ELEM[n] / (mean_ms[n] / 1e3) / 1e9, 1)}
                for n in names}
+    # the floor of one launch moving the dominant kernel's bytes (its input
+    # read, its outputs written, nothing computed), timed the same way
+    rd_bytes = elems * 4  # the fp32 input, whole (w holds exactly these bytes)
+    wr_bytes = int(elems * (BYTES_PER_ELEM[dom] - 4)) // 16 * 16  # codes (+ scales)
+    floor_dst = torch.empty(wr_bytes, dtype=torch.uint8, device=dev)
+    floor_ms = _time_ms(lambda: stream_probe(w, rd_bytes, floor_dst, wr_bytes), stream, reps=20)
+    floor_gbs = (rd_bytes + wr_bytes) / (floor_ms / 1e3) / 1e9
+    del floor_dst
 
     # end-to-end through the public API with host buffers
     e2e = None
@@ -438,6 +446,10 @@ def run_ours(args):
                          "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
                          "traffic": NCU_TRAFFIC.get(dom),
+                         "stream_floor": round(floor_gbs, 1),
+                         "frac_of_floor": round(achieved / floor_gbs, 4),
+                         "floor_note": "one launch that only reads and writes the dominant "
+                                       "kernel's bytes (vq_stream_probe), timed the same way",
                          "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per "
                                          "launch from one ncu capture of this kernel; "
                                          "writes still draining from L2 at the kernel's "
