@@ -328,8 +328,11 @@ int vq_dq_pack_scales(const void* scale, int64_t wbatch, int64_t N, int64_t K, i
                       int64_t block_size, void* out, void* stream);
 /* present[bits] = 1 for every bf16 bit pattern in codes (65,536 bytes, zeroed here). */
 int vq_dq_patterns(const vq_tensor* codes, void* present, void* stream);
-/* The GEMM's weight decode alone: out bf16 [N, K] = the dequantized weight
- * (the first of the packed batches). */
+/* The GEMM's weight decode alone: out bf16 [N, K] (16-byte aligned) = the
+ * dequantized weight (the first of the packed batches), the same values the
+ * GEMM decodes in shared memory.  linear_mx decodes a packed weight this way
+ * once per call from 4096 activation rows on and multiplies it in TMA mode
+ * (quantized.py:455-472: _dequantize_mx of the weight, done once). */
 int vq_dq_decode(const void* w, int64_t N, int64_t K, int32_t mode, const void* w_scale4,
                  const void* palette, void* out, void* stream);
 /* dst[b][c][r] = src[b][r][c], bf16 [batch][rows, cols]. */
