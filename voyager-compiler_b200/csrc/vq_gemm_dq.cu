@@ -110,7 +110,10 @@ static_assert(Cfg<MODE_LUT8>::SMEM + 1024 <= 227 * 1024, "LUT8 shared memory");
 static_assert(STAGE_BYTES % 1024 == 0 && Cfg<MODE_LUT4>::RAW_BYTES % 16 == 0 &&
                   Cfg<MODE_LUT8>::RAW_BYTES % 16 == 0,
               "stages 1024-byte aligned, raw slots 16-byte aligned");
-static_assert((2 * 5 + 2 * 12 + 6) * 8 <= BAR_BYTES && (2 * 6 + 6) * 8 <= BAR_BYTES, "barrier area");
+static_assert((2 * Cfg<MODE_LUT4>::STAGES + 2 * Cfg<MODE_LUT4>::RSLOTS + 6) * 8 <= BAR_BYTES &&
+                  (2 * Cfg<MODE_LUT8>::STAGES + 2 * Cfg<MODE_LUT8>::RSLOTS + 6) * 8 <= BAR_BYTES &&
+                  (2 * Cfg<MODE_TMA>::STAGES + 6) * 8 <= BAR_BYTES,
+              "barrier area");
 // A decoder group waits on the "empty" barrier of every DQ_GROUPS-th step;
 // with at least DQ_GROUPS stages the phase it waits for is never two ahead.
 static_assert(Cfg<MODE_LUT4>::STAGES >= DQ_GROUPS && Cfg<MODE_LUT8>::STAGES >= DQ_GROUPS,
