@@ -64,8 +64,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", default=None,
-                    choices=["c1", "c2", "c3", "c4", "c4m128", "c5", "attn", "outlier", "spmm",
-                             "dq", "nvf4", "observer"],
+                    choices=["c1", "c2", "c3", "c4", "c4m128", "c4m1024", "c5", "attn", "outlier",
+                             "spmm", "dq", "nvf4", "observer"],
                     help="profiling aid: run only this workload's kernels, no JSON line")
     return ap.parse_args()
 
@@ -1284,11 +1284,13 @@ def run_only(args):
         ca, sa, cw, sw = c4_operands(dev, 16, 4096, 14336, seed=1)
         for _ in range(args.warmup + args.steps):
             w4a8.linear(ca, sa, cw, sw)
-    elif args.only == "c4m128":
-        # C4 at M = 128, K = 14336, N = 4096: the split-K dequant GEMM
+    elif args.only in ("c4m128", "c4m1024"):
+        # C4 at M = 128, K = 14336, N = 4096 (the split-K dequant GEMM) or at
+        # M = 1024, K = N = 4096 (one wave of output tiles)
         from voyager_b200 import w4a8
 
-        ca, sa, cw, sw = c4_operands(dev, 128, 14336, 4096, seed=1)
+        m, k, n = (128, 14336, 4096) if args.only == "c4m128" else (1024, 4096, 4096)
+        ca, sa, cw, sw = c4_operands(dev, m, k, n, seed=1)
         for _ in range(args.warmup + args.steps):
             w4a8.linear(ca, sa, cw, sw)
     elif args.only == "observer":
