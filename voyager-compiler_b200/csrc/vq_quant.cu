@@ -1950,9 +1950,16 @@ int launch_qmx_nvfp4(const vq_tensor& x, const int* blocked, int64_t bs, int pow
   memcpy(&qb, &a.quant_max, 4);
   const bool normal = ((qb >> 23) & 0xFFu) != 0;
   a.rq = normal && (qb & 0x7FFFFu) == 0 ? 1.0f / a.quant_max : 0.0f;
-  const int blocks = (int)std::min<int64_t>((groups + 255) / 256, (int64_t)num_sms() * 8);
-  if (a.mask_on) k_qmx_nvfp4<true><<<blocks, 256, 0, st>>>(a);
-  else k_qmx_nvfp4<false><<<blocks, 256, 0, st>>>(a);
+  // exactly the CTAs that fit at once (one wave; the grid-stride loop takes
+  // the rest), found once per device and kernel
+  auto kern = a.mask_on ? k_qmx_nvfp4<true> : k_qmx_nvfp4<false>;
+  int per_sm = 0, threads = 256;
+  if (int e = table_launch_shape(kern, 0, {256}, &threads, &per_sm)) {
+    *status = e;
+    return 1;
+  }
+  const int blocks = (int)std::min<int64_t>((groups + 255) / 256, (int64_t)num_sms() * per_sm);
+  kern<<<blocks, 256, 0, st>>>(a);
   *status = cuda_status(cudaGetLastError());
   return 1;
 }
