@@ -222,7 +222,12 @@ int vq_amax_observe(const vq_tensor* input, int32_t per_channel, int32_t ch_axis
   if (I >= 32 || C == 1) {
     a.segs_per_run = (I + SEG - 1) / SEG;
     const int64_t nseg = a.runs * a.segs_per_run;
-    const int64_t blocks = std::min<int64_t>((nseg + 7) / 8, (int64_t)sms * 8);
+    // exactly the CTAs that fit at once: the grid-stride loop takes the rest
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_amax_runs, 256, 0) != cudaSuccess ||
+        per_sm <= 0)
+      per_sm = 8;
+    const int64_t blocks = std::min<int64_t>((nseg + 7) / 8, (int64_t)sms * per_sm);
     k_amax_runs<<<(unsigned)blocks, 256, 0, st>>>(a);
   } else {
     a.W = C * I;

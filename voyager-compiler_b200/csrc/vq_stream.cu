@@ -6,8 +6,8 @@
 // linears and small quantizations sits well below the long-copy bandwidth
 // the roofline's peak is measured with.
 //
-// Eight CTAs of 256 threads per SM; each thread keeps eight 16-byte loads in
-// flight (grid-stride), folds them into one word and, where it has a store
+// Up to eight CTAs of 256 threads per SM (as many as fit at once); each
+// thread keeps eight 16-byte loads in flight (grid-stride), folds them into one word and, where it has a store
 // to make, writes 16 bytes derived from it (so no load is optimized away).
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -60,7 +60,12 @@ int vq_stream_probe(const void* src, int64_t read_bytes, void* dst, int64_t writ
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (sms <= 0) sms = 148;
   const int64_t n16 = std::max(read_bytes, write_bytes) / 16;
-  const int64_t blocks = std::min<int64_t>((int64_t)sms * 8, (n16 + 255) / 256);
+  // exactly the CTAs that fit at once (no partial second wave)
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, vq::stream::k_stream, 256, 0) !=
+          cudaSuccess || per_sm <= 0)
+    per_sm = 8;
+  const int64_t blocks = std::min<int64_t>((int64_t)sms * std::min(per_sm, 8), (n16 + 255) / 256);
   vq::stream::k_stream<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(src), read_bytes / 16, static_cast<uint4*>(dst), write_bytes / 16);
   return cudaGetLastError() == cudaSuccess ? VQ_OK : VQ_ERR_CUDA;
