@@ -103,6 +103,18 @@ int table_launch_shape(Kern kern, int smem, std::initializer_list<int> cands, in
   return VQ_OK;
 }
 
+// CTAs of `threads` threads of a kernel without dynamic shared memory that
+// fit on an SM at once (at most 8), found once per device and kernel: a
+// grid-stride launch of exactly that many per SM runs as one wave, where 8
+// per SM of a kernel that holds more than 32 registers a thread would leave a
+// partial second wave.
+template <typename Kern>
+int resident_ctas(Kern kern, int threads) {
+  int t = threads, per_sm = 8;
+  if (table_launch_shape(kern, 0, {threads}, &t, &per_sm) != VQ_OK) return 8;
+  return std::max(1, std::min(per_sm, 8));
+}
+
 // Division by a run-time invariant (Granlund-Montgomery, round-up variant):
 // q = (umulhi(n, m) + n) >> s, exact for every 32-bit n.
 struct FastDiv {
@@ -1423,7 +1435,7 @@ int launch_elem(ElemArgs& a, cudaStream_t st) {
     if (int e = table_launch_shape(kern, smem, {1024}, &threads, &per_sm)) return e;
     blocks = sms * per_sm;
   } else {
-    blocks = sms * 8;
+    blocks = sms * resident_ctas(kern, threads);
   }
   int64_t need = ((int64_t)a.nvec + threads - 1) / threads;
   if (need < blocks) blocks = (int)std::max<int64_t>(need, 1);
@@ -1469,7 +1481,7 @@ int launch_2d(Elem2DArgs& a, cudaStream_t st) {
     if (int e = table_launch_shape(kern, smem, {1024}, &threads, &per_sm)) return e;
     blocks = sms * per_sm;
   } else {
-    blocks = sms * 8;
+    blocks = sms * resident_ctas(kern, threads);
   }
   int64_t need = ((int64_t)a.nvec + (int64_t)threads * UNROLL - 1) / ((int64_t)threads * UNROLL);
   if (need < blocks) blocks = (int)std::max<int64_t>(need, 1);
@@ -1544,7 +1556,7 @@ int launch_rows(RowsArgs& a, cudaStream_t st) {
     blocks = sms * per_sm;
   } else {
     threads = 256;
-    blocks = sms * 8;
+    blocks = sms * resident_ctas(kern, threads);
   }
   if (a.vpr < threads) threads = std::max(32, (a.vpr + 31) / 32 * 32);
   if (blocks > a.nrows) blocks = std::max(a.nrows, 1);
@@ -1642,7 +1654,8 @@ int launch_deq_blocks(const vq_tensor* input, const vq_tensor* scale, const vq_t
   if (nvec >= ((int64_t)1 << 31) || nvec == 0) return 0;
   int shift = 0;
   while ((1ll << shift) < bs) ++shift;
-  const int blocks = (int)std::min<int64_t>((nvec + 255) / 256, (int64_t)num_sms() * 8);
+  const int blocks = (int)std::min<int64_t>(
+      (nvec + 255) / 256, (int64_t)num_sms() * resident_ctas(k_deq_blocks_bf16, 256));
   k_deq_blocks_bf16<<<blocks, 256, 0, st>>>((const uint16_t*)input->data,
                                             (const uint16_t*)scale->data, (uint16_t*)out->data,
                                             (uint32_t)nvec, shift);
@@ -1885,7 +1898,7 @@ int launch_qmx(QmxArgs& a, cudaStream_t st) {
       return e;
     blocks = sms * per_sm;
   } else {
-    blocks = sms * 8;
+    blocks = sms * resident_ctas(kern, threads);
   }
   int64_t need = ((int64_t)a.ngroups * TPB + threads * UNROLL - 1) / (threads * UNROLL);
   if (need < blocks) blocks = (int)std::max<int64_t>(need, 1);
