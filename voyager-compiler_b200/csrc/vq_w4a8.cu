@@ -236,10 +236,11 @@ __device__ __forceinline__ void w4a8_chunk(const uint4 (&wc)[2 * MT], const uint
 }
 
 // The CTA whose tile range holds tile x (ranges [i T / G, (i + 1) T / G)).
-__device__ __forceinline__ int cta_of(int64_t x, int64_t T, int64_t G) {
+// 32-bit unsigned arithmetic: the launcher guarantees T * G < 2^32.
+__device__ __forceinline__ int cta_of(uint32_t x, uint32_t T, uint32_t G) {
   return (int)(((x + 1) * G - 1) / T);
 }
-__device__ __forceinline__ int range_start(int64_t i, int64_t T, int64_t G) {
+__device__ __forceinline__ int range_start(uint32_t i, uint32_t T, uint32_t G) {
   return (int)(i * T / G);
 }
 
@@ -362,7 +363,7 @@ template <int NT>
 __device__ __forceinline__ void epilogue(const Args& p, int t0, int t1, uint32_t flushed0,
                                          int* last_flag) {
   const int lane = threadIdx.x % 32, ew = threadIdx.x / 32 - EPILOGUE;
-  const int64_t T = p.tiles, G = p.G;
+  const uint32_t T = p.tiles, G = p.G;
   const int rbs[2] = {t0 / p.chunks, (t1 - 1) / p.chunks};
   for (int slot = 0; slot < 2; ++slot) {
     const int rb = rbs[slot];
@@ -376,7 +377,7 @@ __device__ __forceinline__ void epilogue(const Args& p, int t0, int t1, uint32_t
         __threadfence();
         if (lane == 0) {
           const int prev = atomicAdd(p.done + rb, 1);
-          is_last = prev == cta_of(lastt, T, G) - cta_of(first, T, G);
+          is_last = prev == cta_of((uint32_t)lastt, T, G) - cta_of((uint32_t)first, T, G);
           if (is_last) p.done[rb] = 0;
         }
         is_last = __shfl_sync(0xFFFFFFFFu, is_last, 0);
@@ -441,7 +442,7 @@ template <int NT>
 __global__ void __launch_bounds__(THREADS, 1) k_w4a8(const __grid_constant__ Args p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int64_t T = p.tiles, G = p.G;
+  const uint32_t T = p.tiles, G = p.G;
   const int t0 = range_start(blockIdx.x, T, G), t1 = range_start(blockIdx.x + 1, T, G);
   const int cstart = t0 % p.chunks, L = min(t1 - t0, p.chunks);
   const int ks = L * 128 + TPAD, nkb = L * 4;
@@ -514,68 +515,98 @@ __global__ void __launch_bounds__(THREADS, 1) k_w4a8(const __grid_constant__ Arg
   // exact zeros into the shared workspace.  Item i of the codes is row
   // i / (16 L), 8 codes at K offset 8 (i % (16 L)); every thread's code
   // loads go out first, with the scale loads, in one round trip.
-  constexpr int NITEM = (8 * NT * LMAX * 16 + CWARPS * 32 - 1) / (CWARPS * 32);
-  const int nitem = 8 * NT * L * 16;
-  auto item = [&](int i, int& m, int& kk, int& kg) {
-    m = i / (L * 16);
-    kk = (i % (L * 16)) * 8;
-    kg = ((cstart + kk / 128) % p.chunks) * 128 + kk % 128;
+  // A thread's items are i = threadIdx.x + u ISTEP, u < NITEM: it steps
+  // through their (row m, remainder r = i % 16 L) pairs with no division
+  // past the first (the divisor 16 L is a runtime value); items of rows
+  // 8 NT and on are past the end.
+  constexpr int ISTEP = CWARPS * 32;
+  constexpr int NITEM = (8 * NT * LMAX * 16 + ISTEP - 1) / ISTEP;
+  const int L16 = L * 16;
+  const int im0 = threadIdx.x / L16, ir0 = threadIdx.x - im0 * L16;
+  const int im_step = ISTEP / L16, ir_step = ISTEP - im_step * L16;
+  auto next_item = [&](int& m, int& r) {
+    m += im_step;
+    r += ir_step;
+    if (r >= L16) {
+      r -= L16;
+      ++m;
+    }
+  };
+  // K of staged offset 8 r: staged chunk j = r / 16 is K chunk
+  // (cstart + j) % chunks, where cstart + j < 2 chunks
+  auto k_of = [&](int r) {
+    int c = cstart + (r >> 4);
+    if (c >= p.chunks) c -= p.chunks;
+    return c * 128 + (r & 15) * 8;
   };
   uint4 cvv[NITEM];
+  {
+    int m = im0, r = ir0;
 #pragma unroll
-  for (int u = 0; u < NITEM; ++u) {
-    const int i = threadIdx.x + u * CWARPS * 32;
-    cvv[u] = make_uint4(0, 0, 0, 0);
-    int m, kk, kg;
-    item(i, m, kk, kg);
-    if (i < nitem && m < p.M) cvv[u] = *reinterpret_cast<const uint4*>(p.ac + (size_t)m * p.K + kg);
+    for (int u = 0; u < NITEM; ++u) {
+      cvv[u] = make_uint4(0, 0, 0, 0);
+      if (m < p.M) cvv[u] = *reinterpret_cast<const uint4*>(p.ac + (size_t)m * p.K + k_of(r));
+      next_item(m, r);
+    }
   }
   int slow = 0;
-  for (int i = threadIdx.x; i < 8 * NT * nkb; i += CWARPS * 32) {
-    const int m = i / nkb, jb = i % nkb;
-    const int kb = ((cstart + jb / 4) % p.chunks) * 4 + jb % 4;
-    const uint32_t sb = m < p.M ? p.as[(size_t)m * (p.K / 32) + kb] : 0u;
-    tsc[m * nkb + jb] = __uint_as_float(sb << 16);
-    const uint32_t ef = (sb >> 7) & 0xFFu;
-    if (sb) {
-      if ((sb & 0x807Fu) || ef == 0xFFu) slow = 1;  // not a positive normal power of two
-      else atomicMax(&emax[m], (int)ef);
+  {
+    // scale i = m nkb + jb of the staged blocks, stepped the same way
+    int m = threadIdx.x / nkb, jb = threadIdx.x - m * nkb;
+    const int m_step = ISTEP / nkb, j_step = ISTEP - m_step * nkb;
+    while (m < 8 * NT) {
+      int c = cstart + (jb >> 2);
+      if (c >= p.chunks) c -= p.chunks;
+      const int kb = c * 4 + (jb & 3);
+      const uint32_t sb = m < p.M ? p.as[(size_t)m * (p.K / 32) + kb] : 0u;
+      tsc[m * nkb + jb] = __uint_as_float(sb << 16);
+      const uint32_t ef = (sb >> 7) & 0xFFu;
+      if (sb) {
+        if ((sb & 0x807Fu) || ef == 0xFFu) slow = 1;  // not a positive normal power of two
+        else atomicMax(&emax[m], (int)ef);
+      }
+      m += m_step;
+      jb += j_step;
+      if (jb >= nkb) {
+        jb -= nkb;
+        ++m;
+      }
     }
   }
   consumers_sync();
+  {
+    int m = im0, r = ir0;
 #pragma unroll
-  for (int u = 0; u < NITEM; ++u) {
-    const int i = threadIdx.x + u * CWARPS * 32;
-    if (i >= nitem) break;
-    int m, kk, kg;
-    item(i, m, kk, kg);
-    const uint32_t sb = __float_as_uint(tsc[m * nkb + kk / 32]) >> 16;
-    // 2^d, d = e - E <= 0: an E4M3 code's last bit is >= 2^-9, so c * 2^d
-    // is exact in f16 for d >= -15 (and below 448 <= 65504)
-    const int d = (int)((sb >> 7) & 0xFFu) - emax[m];
-    float f = 0.f;
-    if (sb) {
-      if (d >= -15) f = __uint_as_float((uint32_t)(d + 127) << 23);
-      else slow = 1;
-    }
-    const uint32_t cv[4] = {cvv[u].x, cvv[u].y, cvv[u].z, cvv[u].w};
-    uint16_t* row = tok + m * ks;
+    for (int u = 0; u < NITEM; ++u, next_item(m, r)) {
+      if (m >= 8 * NT) break;
+      const int kk = r * 8;
+      const uint32_t sb = __float_as_uint(tsc[m * nkb + (r >> 2)]) >> 16;
+      // 2^d, d = e - E <= 0: an E4M3 code's last bit is >= 2^-9, so c * 2^d
+      // is exact in f16 for d >= -15 (and below 448 <= 65504)
+      const int d = (int)((sb >> 7) & 0xFFu) - emax[m];
+      float f = 0.f;
+      if (sb) {
+        if (d >= -15) f = __uint_as_float((uint32_t)(d + 127) << 23);
+        else slow = 1;
+      }
+      const uint32_t cv[4] = {cvv[u].x, cvv[u].y, cvv[u].z, cvv[u].w};
+      uint16_t* row = tok + m * ks;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      __half2 h = __floats2half2_rn(bf2f(cv[q] & 0xFFFFu) * f, bf2f(cv[q] >> 16) * f);
-      *reinterpret_cast<uint32_t*>(row + tok_pos(kk + 2 * q)) = *reinterpret_cast<uint32_t*>(&h);
+      for (int q = 0; q < 4; ++q) {
+        __half2 h = __floats2half2_rn(bf2f(cv[q] & 0xFFFFu) * f, bf2f(cv[q] >> 16) * f);
+        *reinterpret_cast<uint32_t*>(row + tok_pos(kk + 2 * q)) = *reinterpret_cast<uint32_t*>(&h);
+      }
     }
   }
   if (slow) atomicOr(&flags[0], 1);
   consumers_sync();
   slow = flags[0];
   if (slow) {  // the raw codes (exact in f16), scales applied per 32-block
+    int m = im0, r = ir0;
 #pragma unroll
-    for (int u = 0; u < NITEM; ++u) {
-      const int i = threadIdx.x + u * CWARPS * 32;
-      if (i >= nitem) break;
-      int m, kk, kg;
-      item(i, m, kk, kg);
+    for (int u = 0; u < NITEM; ++u, next_item(m, r)) {
+      if (m >= 8 * NT) break;
+      const int kk = r * 8;
       const uint32_t cv[4] = {cvv[u].x, cvv[u].y, cvv[u].z, cvv[u].w};
       uint16_t* row = tok + m * ks;
 #pragma unroll
@@ -730,6 +761,9 @@ int vq_w4a8_linear_small(const vq_tensor* a_codes, const vq_tensor* a_scales, co
   const int64_t tiles = (N + TILE_ROWS - 1) / TILE_ROWS * p.chunks;
   p.tiles = (int)tiles;
   p.G = (int)grid_of(tiles);
+  // the kernel's tile ranges are 32-bit unsigned products (always true for
+  // packed weights below 2 GB: T <= 2^17, G <= max(SMs, T / LMAX))
+  if (tiles * p.G >= (1ll << 32)) return VQ_ERR_UNSUPPORTED;
   // a CTA stages at most ceil(T / G) <= LMAX chunks of tokens
   const int L = (int)std::min<int64_t>((tiles + p.G - 1) / p.G, p.chunks);
   // programmatic dependent launch: the kernel may start while the previous
