@@ -213,6 +213,30 @@ __device__ __forceinline__ void unit_of(const DqArgs& g, int u, int& b, int& tm,
   k0 = (u - t * g.S) * g.KSU;
   tile_of(g, t, b, tm, tn);
 }
+// A walk over a pair's K steps in order: step st is K step k0 + (st - ti
+// KSU) of unit pair_id + ti npairs, ti = st / KSU.  It keeps ti, the offset
+// sr within the unit and the unit's tile, and moves on by a fixed stride
+// with no division (KSU, S and the tile counts are runtime values); the
+// tile is worked out again only when the walk enters another unit.
+struct StepWalk {
+  int ti, sr, b, tm, tn, k0;
+  __device__ __forceinline__ StepWalk(const DqArgs& g, int pair_id, int npairs, int st) {
+    ti = st / g.KSU;
+    sr = st - ti * g.KSU;
+    unit_of(g, pair_id + ti * npairs, b, tm, tn, k0);
+  }
+  __device__ __forceinline__ int ks() const { return k0 + sr; }
+  __device__ __forceinline__ void advance(const DqArgs& g, int pair_id, int npairs, int stride) {
+    sr += stride;
+    if (sr >= g.KSU) {
+      do {
+        sr -= g.KSU;
+        ++ti;
+      } while (sr >= g.KSU);
+      unit_of(g, pair_id + ti * npairs, b, tm, tn, k0);
+    }
+  }
+};
 
 // ---- the weight decode shared by the GEMM producers and vq_dq_decode ------
 // A 16-entry palette as byte planes for prmt lookups: lo[i] holds the low
@@ -382,11 +406,9 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
       const uint32_t fb0 = mapa_shared(full0, 0);
       int stage = 0;
       uint32_t phase = 0;
-      for (int st = 0; st < nsteps; ++st) {
-        const int ti = st / g.KSU;
-        int b, tm, tn, k0;
-        unit_of(g, pair_id + ti * npairs, b, tm, tn, k0);
-        const int ks = k0 + st - ti * g.KSU;
+      StepWalk wk(g, pair_id, npairs, 0);
+      for (int st = 0; st < nsteps; ++st, wk.advance(g, pair_id, npairs, 1)) {
+        const int b = wk.b, tm = wk.tm, tn = wk.tn, ks = wk.ks();
         if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, g.err, ERR_EMPTY)) break;
         const uint32_t sb = s0 + stage * STAGE_BYTES;
         if (rank == 0)
@@ -450,11 +472,9 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     if (lane == 0) {
       const uint32_t r0s = smem_u32(smem + C::RAW0);
       int issued = 0;
-      for (int st = 0; st < nsteps; ++st) {
-        const int ti = st / g.KSU;
-        int b, tm, tn, k0;
-        unit_of(g, pair_id + ti * npairs, b, tm, tn, k0);
-        const int ks = k0 + st - ti * g.KSU;
+      StepWalk wk(g, pair_id, npairs, 0);
+      for (int st = 0; st < nsteps; ++st, wk.advance(g, pair_id, npairs, 1)) {
+        const int b = wk.b, tn = wk.tn, ks = wk.ks();
         int slot;
         uint32_t phase;
         raw_slot<MODE>(st, slot, phase);
@@ -482,15 +502,13 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     Pal4 p4;
     if (MODE == MODE_LUT4) p4 = load_pal4(g.pal);
     const bool scaled = g.ws4 != nullptr;
-    for (int st = grp; st < nsteps; st += DQ_GROUPS) {
+    StepWalk wk(g, pair_id, npairs, grp);
+    for (int st = grp; st < nsteps; st += DQ_GROUPS, wk.advance(g, pair_id, npairs, DQ_GROUPS)) {
       const int stage = st % S;
       int slot;
       uint32_t rphase;
       raw_slot<MODE>(st, slot, rphase);
-      const int ti = st / g.KSU;
-      int b, tm, tn, k0;
-      unit_of(g, pair_id + ti * npairs, b, tm, tn, k0);
-      const int ks = k0 + st - ti * g.KSU;
+      const int tn = wk.tn, ks = wk.ks();
       // the step's raw bytes: into registers, then the slot goes back
       if (!mbar_wait_warp(rfull0 + 8 * slot, rphase, g.err, ERR_FULL)) break;
       const uint8_t* rawc = smem + C::RAW0 + slot * C::RAW_BYTES;
