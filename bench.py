@@ -18,8 +18,9 @@ CSR), and the C5 4-layer decoder forward (tensor parallel over the ranks when
 N > 1).
 
 --impl reference times the reference algorithm's CPU restatement (the oracle
-port under oracle/) on this host's cores, on a bounded row sample of the
-same workload.
+port under oracle/) on this host's cores, on whole steps of the same
+workload (a window of rows that moves from step to step instead, should
+--steps whole ones run past REF_BUDGET_SECONDS).
 """
 
 import argparse
